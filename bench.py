@@ -1,0 +1,320 @@
+"""Gemma-2B Q8_0 token-loop benchmark on B200 (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: random-init Gemma-2B, Q8_0 weights,
+batch-1 greedy decode after a 16-token seeded prompt. A step is one decode
+token: embed -> 18 layers -> logits -> on-device argmax feeding the next step.
+Every rank decodes its own sequence on its own GPU (independent replicas, no
+collective on the data path; weak scaling), and `value` is the whole-job
+tok/s: the tokens all ranks decoded over the max-over-ranks device time.
+
+`value` is device-timed (CUDA events on the engine's stream around K decode
+steps, weights resident in HBM). `e2e` is the same metric through the public
+generate call (HF::Gemma::generate's C-ABI, hf_cuda_generate_greedy) with the
+prompt in pinned host memory and every generated token read back to the host.
+`roofline` reports the dominant kernel of the step against the measured HBM
+copy bandwidth; `cpu_baseline` the fp32 oracle port on this host's cores.
+With --impl reference the same metric is timed on the reference's arithmetic
+restated for the CPU (the reference has no runnable GPU path here: its eacp
+kernels target Metal/D3D12 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "Gemma-2B Q8_0 decode tok/s (b=1, b=64/GPU) and achieved HBM GB/s vs peak"
+WORKLOAD = "config0: Gemma-2B Q8_0 batch-1 greedy decode, BOS + 15 seeded prompt ids (seed 0)"
+PUBLISHED_TOK_S = 161.6  # the reference's int8-blocks decode, 16 tokens (Apple M4 Max, Metal)
+PROMPT_LENGTH = 16
+SEED = 0
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            peaks = json.load(f)
+        return float(peaks["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f)
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi samples of the SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.lines = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.device_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, sm_max, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                sm_max = max(sm_max, float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": sm_max or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_index(local_rank: int) -> int:
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if visible:
+        entries = [v.strip() for v in visible.split(",") if v.strip()]
+        if local_rank < len(entries) and entries[local_rank].isdigit():
+            return int(entries[local_rank])
+    return local_rank
+
+
+def build_model(native, shape, keep: bool):
+    ctx = native.Context(shape, device=int(os.environ.get("LOCAL_RANK", "0")))
+    tensors = ctx.load_synthetic(seed=SEED, keep=keep)
+    return ctx, tensors
+
+
+def cpu_decode_rate(shape, tensors, prompt, steps: int, warmup: int = 1):
+    """fp32 oracle (the reference's arithmetic, 16-lane fp32 sums) on every host core."""
+    import oracle_bindings as ob
+
+    model = ob.OracleModel(shape.replace(max_positions=PROMPT_LENGTH + warmup + steps + 2), tensors, "float")
+    _, logits = model.step(prompt, last_row_only=True, want_hidden=False)
+    token = ob.argmax(logits[-1])
+    for _ in range(warmup):
+        _, logits = model.step([token], want_hidden=False)
+        token = ob.argmax(logits[-1])
+    start = time.perf_counter()
+    for _ in range(steps):
+        _, logits = model.step([token], want_hidden=False)
+        token = ob.argmax(logits[-1])
+    elapsed = time.perf_counter() - start
+    threads = model.threads
+    model.close()
+    return steps / elapsed, threads, elapsed
+
+
+def run_reference(args):
+    """--impl reference: the reference's arithmetic on the host cores, same metric and workload."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from huggingfaceeacp_b200 import native
+
+    shape = native.GEMMA_2B
+    tensors = {}
+    for tensor, layer in native.model_tensors(shape):
+        tensors[(tensor, layer)] = native.synthetic_tensor(shape, tensor, layer, SEED)
+    prompt = native.synthetic_tokens(SEED, PROMPT_LENGTH, shape.vocab)
+    rate, threads, elapsed = cpu_decode_rate(shape, tensors, prompt, args.steps, args.warmup)
+    sample = f"{args.steps} fp32 decode steps after a {PROMPT_LENGTH}-token prefill and {args.warmup} warm-up steps"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": rate, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": rate / PUBLISHED_TOK_S, "dtype": "f32",
+        "data": "synthetic: random-init Gemma-2B, N(0,0.02) weights quantized to Q8_0, seeded prompt",
+        "config": {"workload": WORKLOAD, "batch_per_gpu": 1, "parallelism": "host cores",
+                   "implementation": "oracle/oracle.c fp32 restatement of the reference's kernels"},
+        "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+
+    from huggingfaceeacp_b200 import native
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    shape = native.GEMMA_2B.replace(max_step_rows=512)
+    keep = rank == 0 and world == 1 and not args.no_cpu_baseline
+    ctx, tensors = build_model(native, shape, keep)
+    prompt = native.synthetic_tokens(SEED, PROMPT_LENGTH, shape.vocab)
+
+    # ---- device-timed decode: K steps with the weights resident
+    ctx.prefill_async(prompt)
+    ctx.decode_async(args.warmup)
+    ctx.sync()
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    launches = ctx.decode_launches
+    first_pos = ctx.position
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(physical_index(local_rank)) as clocks:
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        ctx.decode_async(args.steps)
+        stop.record(stream)
+        ctx.sync()
+        torch.cuda.synchronize()
+    elapsed_ms = start.elapsed_time(stop)
+    barrier()
+    if dist:
+        t = torch.tensor([elapsed_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    tokens = ctx.read_slots(first_pos + 1, args.steps)
+    ms_per_step = elapsed_ms / args.steps
+    value = world * args.steps / (elapsed_ms / 1000.0)
+    keys = first_pos + args.steps // 2
+    step_bytes = native.decode_bytes(shape, keys)
+    peak, peak_kind = measured_peaks()
+
+    # ---- e2e: the public generate call, host prompt in, host tokens out
+    pinned_prompt = torch.from_numpy(prompt).pin_memory().numpy()
+    barrier()
+    e2e_start = time.perf_counter()
+    generated = ctx.generate(pinned_prompt, args.steps)
+    e2e_s = time.perf_counter() - e2e_start
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": world * len(generated) / e2e_s, "unit": "tok/s",
+           "h2d_bytes_per_step": 4.0 * PROMPT_LENGTH / max(1, len(generated)), "d2h_bytes_per_step": 4,
+           "call": "hf_cuda_generate_greedy (prefill + decode, wall clock)"}
+
+    # ---- roofline of every decode kernel, live (cycling layers: HBM, not L2)
+    ctx.begin_sequence()
+    ctx.prefill_async(prompt)
+    ctx.decode_async(keys - PROMPT_LENGTH)
+    ctx.sync()
+    kernels = {}
+    for kernel, name in enumerate(native.KERNEL_NAMES):
+        us, nbytes = ctx.time_kernel(kernel, 36 if kernel != native.KERNEL_LOGITS else 8)
+        kernels[name] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3}
+    per_step_us = {
+        name: k["us"] * (1 if name == "logits_argmax" else shape.layers) for name, k in kernels.items()}
+    dominant = max(per_step_us, key=per_step_us.get)
+    traffic = committed_traffic().get(dominant)
+    dk = kernels[dominant]
+    roofline = {"kernel": dominant, "bound": "hbm", "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": dk["gbs"] / peak, "traffic": traffic, "peak_kind": peak_kind,
+                "algorithmic_bytes_per_launch": dk["bytes"], "mean_launch_us": dk["us"],
+                "kernels": {n: {"us": round(k["us"], 2), "gbs": round(k["gbs"], 1)} for n, k in kernels.items()}}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "f32",
+        "data": "synthetic: random-init Gemma-2B, N(0,0.02) weights quantized to Q8_0, seeded prompt",
+        "config": {"workload": WORKLOAD, "batch_per_gpu": 1, "seq_len": first_pos + args.steps,
+                   "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (2.66 GB of weights per step)",
+                   "step_bytes": step_bytes},
+        "step_roofline": {"achieved": step_bytes / (ms_per_step * 1e6), "peak": peak, "unit": "GB/s",
+                          "frac": step_bytes / (ms_per_step * 1e6) / peak},
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks.summary(),
+        "tokens_head": [int(t) for t in tokens[:4]],
+    }
+
+    if rank == 0 and keep:
+        rate, threads, elapsed = cpu_decode_rate(shape, tensors, prompt, args.cpu_steps)
+        line["cpu_baseline"] = {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port",
+                                "sample": f"{args.cpu_steps} fp32 decode steps of the same model and prompt"
+                                          f" ({elapsed:.1f} s)"}
+    elif rank == 0:
+        line["cpu_baseline"] = None
+    ctx.close()
+    if dist:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=64)
+    parser.add_argument("--warmup", type=int, default=4)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--cpu-steps", type=int, default=16)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,403 @@
+// Causal multi-query attention over the fp32 KV cache.
+//
+// Semantics follow Kernels/MultiQueryAttention.h:138-341 and the double
+// reference Tests/Decoder/ReferenceDecoder.h:208-272: query row r of a step
+// stands at position pos + r and attends to cache rows [0, pos + r]; query head
+// h reads kv head h / (heads / kv_heads); softmax with the running-maximum
+// rescale exp(m_old - m_new); scale 1/sqrt(D).
+//
+// B200 schedule (mqa_fast, D = 256): the reference gives one 64-lane group to
+// each (row, head) and walks the whole context in it, so a decode step has 8
+// groups and every group re-reads the one shared K/V head. Here one CTA serves
+// all query heads of a kv head, so each K and V row crosses from memory once
+// and feeds every head, and the context is split across CTAs (flash-decoding):
+// each split writes its (max, sum, unnormalised row) and mqa_merge folds them.
+// A lane owns 8 of the 256 channels for every head of the group; keys are
+// dealt to the 8 warps and walked in tiles of up to 32, scores and
+// probabilities staged in shared memory, with one rescale per tile.
+#pragma once
+
+#include "common.cuh"
+
+namespace hfk
+{
+struct AttnArgs
+{
+    const float* q;       // [M, H * D]
+    const float* k_cache; // [P, kv_heads * D]
+    const float* v_cache;
+    float* out;           // [M, H * D]
+    float* part_acc;      // [M, nsplit, H, D]   (nsplit > 1)
+    float* part_ml;       // [M, nsplit, H, 2]
+    int heads, kv_heads, head_dim;
+    float scale;
+    int nsplit;
+    const unsigned* state; // state[0] = position of row 0
+    unsigned* err;
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all()
+{
+    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// Sums part[h] (h < QH) across the warp so that lane L ends with the total of
+// head head_of_lane<QH>(L): log2(QH) halving exchanges, then full reduction of
+// what is left -- 9 shuffles for 8 heads instead of 40.
+template <int QH>
+__device__ __forceinline__ float transpose_reduce(float (&part)[QH], int lane)
+{
+    float r[QH];
+#pragma unroll
+    for (int h = 0; h < QH; ++h)
+        r[h] = part[h];
+    int width = QH;
+    int distance = 16;
+#pragma unroll
+    for (int level = 0; (1 << level) < QH; ++level)
+    {
+        const bool upper = (lane & distance) != 0;
+        const int half = width / 2;
+#pragma unroll
+        for (int i = 0; i < QH / 2; ++i)
+        {
+            if (i < half)
+            {
+                const float send = upper ? r[i] : r[i + half];
+                const float keep = upper ? r[i + half] : r[i];
+                r[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, distance);
+            }
+        }
+        width = half;
+        distance >>= 1;
+    }
+    float v = r[0];
+#pragma unroll
+    for (; distance > 0; distance >>= 1)
+        v += __shfl_xor_sync(0xFFFFFFFFu, v, distance);
+    return v;
+}
+
+template <int QH>
+__device__ __forceinline__ int head_of_lane(int lane)
+{
+    int h = 0;
+    int distance = 16;
+#pragma unroll
+    for (int level = 0; (1 << level) < QH; ++level)
+    {
+        h = 2 * h + ((lane & distance) ? 1 : 0);
+        distance >>= 1;
+    }
+    return h;
+}
+
+template <int QH>
+__device__ __forceinline__ int lane_of_head(int h)
+{
+    int lane = 0;
+    int distance = 16 >> 0;
+    int bits = 0;
+    for (int q = QH; q > 1; q >>= 1)
+        ++bits;
+    for (int level = 0; level < bits; ++level)
+    {
+        if ((h >> (bits - 1 - level)) & 1)
+            lane |= distance;
+        distance >>= 1;
+    }
+    return lane;
+}
+
+// D = 256, QH query heads per kv head (QH in {1, 2, 4, 8}), one CTA per
+// (split, kv head, row). A lane owns channels [8 lane, 8 lane + 8) of every
+// head; K/V tiles of 32 keys are staged in shared memory by all threads at
+// once, each warp takes 4 keys of the tile, scores them for all heads, and
+// keeps its own running (max, sum, row) per head; the warps fold at the end.
+template <int QH>
+__global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
+{
+    constexpr int D = 256;
+    constexpr int TILE = 32;
+    extern __shared__ __align__(16) float sm[];
+    float* tk = sm;                 // [TILE][D]
+    float* tv = sm + TILE * D;      // [TILE][D]
+    float* wacc = sm;               // after the loop: [8][QH][D] (reuses the tiles)
+    float* wm = sm + 8 * QH * D;    // [8][QH]
+    float* wl = wm + 8 * QH;        // [8][QH]
+
+    pdl_wait();
+    const unsigned position = *(volatile const unsigned*) a.state;
+    pdl_trigger();
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int row = blockIdx.z;
+    const int kv_head = blockIdx.y;
+    const int split = blockIdx.x;
+    const int H = a.heads;
+    const int kvw = a.kv_heads * D;
+    const int keys = (int) position + row + 1;
+    const int chunk = (keys + a.nsplit - 1) / a.nsplit;
+    const int k0 = min(keys, split * chunk);
+    const int k1 = min(keys, k0 + chunk);
+    const int my_head = head_of_lane<QH>(lane);
+
+    float qv[QH][8];
+    const float* qrow = a.q + (size_t) row * H * D + (size_t) kv_head * QH * D + lane * 8;
+#pragma unroll
+    for (int h = 0; h < QH; ++h)
+    {
+        const float4 lo = *reinterpret_cast<const float4*>(qrow + h * D);
+        const float4 hi = *reinterpret_cast<const float4*>(qrow + h * D + 4);
+        qv[h][0] = lo.x * a.scale; qv[h][1] = lo.y * a.scale; qv[h][2] = lo.z * a.scale; qv[h][3] = lo.w * a.scale;
+        qv[h][4] = hi.x * a.scale; qv[h][5] = hi.y * a.scale; qv[h][6] = hi.z * a.scale; qv[h][7] = hi.w * a.scale;
+    }
+
+    float m = -INFINITY, l = 0.f; // of head my_head, replicated across its lanes
+    float acc[QH][8];
+#pragma unroll
+    for (int h = 0; h < QH; ++h)
+#pragma unroll
+        for (int d = 0; d < 8; ++d)
+            acc[h][d] = 0.f;
+
+    for (int t0 = k0; t0 < k1; t0 += TILE)
+    {
+        const int nk = min(TILE, k1 - t0);
+        // ---- stage the tile: nk rows of K and of V, 16 bytes a thread at a time
+        for (int i = tid; i < nk * (D / 4); i += 256)
+        {
+            const int r = i / (D / 4), c = (i % (D / 4)) * 4;
+            const size_t at = (size_t) (t0 + r) * kvw + (size_t) kv_head * D + c;
+            cp_async16(tk + r * D + c, a.k_cache + at);
+            cp_async16(tv + r * D + c, a.v_cache + at);
+        }
+        cp_async_wait_all();
+        __syncthreads();
+
+        // ---- this warp's keys of the tile: warp, warp + 8, ...
+        float s[TILE / 8];
+#pragma unroll
+        for (int j = 0; j < TILE / 8; ++j)
+        {
+            const int r = warp + 8 * j;
+            float part[QH];
+            const float4 lo = *reinterpret_cast<const float4*>(tk + (r < nk ? r : 0) * D + lane * 8);
+            const float4 hi = *reinterpret_cast<const float4*>(tk + (r < nk ? r : 0) * D + lane * 8 + 4);
+            const float kk[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+            for (int h = 0; h < QH; ++h)
+            {
+                float v = 0.f;
+#pragma unroll
+                for (int d = 0; d < 8; ++d)
+                    v = fmaf(qv[h][d], kk[d], v);
+                part[h] = v;
+            }
+            const float total = transpose_reduce<QH>(part, lane);
+            s[j] = r < nk ? total : -INFINITY;
+        }
+        float tile_max = s[0];
+#pragma unroll
+        for (int j = 1; j < TILE / 8; ++j)
+            tile_max = fmaxf(tile_max, s[j]);
+        const float m_new = fmaxf(m, tile_max);
+        float carried = 0.f, p[TILE / 8], psum = 0.f;
+        if (m_new != -INFINITY)
+        {
+            carried = expf(m - m_new); // 0 while nothing was seen
+#pragma unroll
+            for (int j = 0; j < TILE / 8; ++j)
+            {
+                p[j] = expf(s[j] - m_new);
+                psum += p[j];
+            }
+            m = m_new;
+        }
+        else
+        {
+#pragma unroll
+            for (int j = 0; j < TILE / 8; ++j)
+                p[j] = 0.f;
+            carried = 1.f;
+        }
+        l = l * carried + psum;
+
+        // ---- every lane needs every head's factors: rescale, then P V
+#pragma unroll
+        for (int h = 0; h < QH; ++h)
+        {
+            const float c = __shfl_sync(0xFFFFFFFFu, carried, lane_of_head<QH>(h));
+#pragma unroll
+            for (int d = 0; d < 8; ++d)
+                acc[h][d] *= c;
+        }
+#pragma unroll
+        for (int j = 0; j < TILE / 8; ++j)
+        {
+            const int r = warp + 8 * j;
+            if (r >= nk) // warp-uniform
+                break;
+            const float4 lo = *reinterpret_cast<const float4*>(tv + r * D + lane * 8);
+            const float4 hi = *reinterpret_cast<const float4*>(tv + r * D + lane * 8 + 4);
+            const float vv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+            for (int h = 0; h < QH; ++h)
+            {
+                const float ph = __shfl_sync(0xFFFFFFFFu, p[j], lane_of_head<QH>(h));
+#pragma unroll
+                for (int d = 0; d < 8; ++d)
+                    acc[h][d] = fmaf(ph, vv[d], acc[h][d]);
+            }
+        }
+        __syncthreads(); // the tile is read before the next one lands
+    }
+
+    // ---- fold the 8 warps
+#pragma unroll
+    for (int h = 0; h < QH; ++h)
+#pragma unroll
+        for (int d = 0; d < 8; d += 4)
+            *reinterpret_cast<float4*>(wacc + (warp * QH + h) * D + lane * 8 + d) =
+                make_float4(acc[h][d], acc[h][d + 1], acc[h][d + 2], acc[h][d + 3]);
+    if (lane == lane_of_head<QH>(my_head))
+    {
+        wm[warp * QH + my_head] = m;
+        wl[warp * QH + my_head] = l;
+    }
+    __syncthreads();
+
+    const int d = tid; // 256 threads, one channel each
+    for (int h = 0; h < QH; ++h)
+    {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 8; ++w)
+            mx = fmaxf(mx, wm[w * QH + h]);
+        float sum = 0.f, value = 0.f;
+        if (mx != -INFINITY)
+        {
+#pragma unroll
+            for (int w = 0; w < 8; ++w)
+            {
+                const float mw = wm[w * QH + h];
+                if (mw == -INFINITY)
+                    continue;
+                const float f = expf(mw - mx);
+                sum = fmaf(wl[w * QH + h], f, sum);
+                value = fmaf(wacc[(w * QH + h) * D + d], f, value);
+            }
+        }
+        const int head = kv_head * QH + h;
+        if (a.nsplit == 1)
+            a.out[(size_t) row * H * D + (size_t) head * D + d] = value / sum;
+        else
+        {
+            const size_t slot = ((size_t) row * a.nsplit + split) * H + head;
+            a.part_acc[slot * D + d] = value;
+            if (d == 0)
+            {
+                a.part_ml[slot * 2] = mx;
+                a.part_ml[slot * 2 + 1] = sum;
+            }
+        }
+    }
+}
+
+// Shared memory of mqa_fast<QH>: the K/V tile, or the warp fold after it.
+template <int QH>
+constexpr size_t mqa_fast_smem()
+{
+    constexpr size_t tiles = 2 * 32 * 256;
+    constexpr size_t fold = 8 * QH * 256 + 16 * QH;
+    return (tiles > fold ? tiles : fold) * sizeof(float);
+}
+
+// Folds the splits of mqa_fast: out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M).
+__global__ void __launch_bounds__(256) mqa_merge(const AttnArgs a)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.y;
+    const int H = a.heads, D = a.head_dim;
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= H * D)
+        return;
+    const int head = idx / D, d = idx % D;
+    float mx = -INFINITY;
+    for (int s = 0; s < a.nsplit; ++s)
+        mx = fmaxf(mx, a.part_ml[(((size_t) row * a.nsplit + s) * H + head) * 2]);
+    float sum = 0.f, value = 0.f;
+    for (int s = 0; s < a.nsplit; ++s)
+    {
+        const size_t slot = ((size_t) row * a.nsplit + s) * H + head;
+        const float ms = a.part_ml[slot * 2];
+        if (ms == -INFINITY)
+            continue;
+        const float f = expf(ms - mx);
+        sum = fmaf(a.part_ml[slot * 2 + 1], f, sum);
+        value = fmaf(a.part_acc[slot * D + d], f, value);
+    }
+    a.out[(size_t) row * H * D + idx] = value / sum;
+}
+
+// Any head width (D % 4 == 0, D <= 256) and any grouping: one CTA per (head,
+// row), scores for every key staged in shared memory, two passes.
+__global__ void __launch_bounds__(128) mqa_generic(const AttnArgs a)
+{
+    extern __shared__ __align__(16) float scores[]; // [keys]
+    __shared__ float red[4];
+    pdl_wait();
+    const unsigned position = *(volatile const unsigned*) a.state;
+    pdl_trigger();
+    const int head = blockIdx.x, row = blockIdx.y;
+    const int H = a.heads, D = a.head_dim;
+    const int kvw = a.kv_heads * D;
+    const int kv_column = head / (H / a.kv_heads) * D;
+    const int keys = (int) position + row + 1;
+    const float* q = a.q + (size_t) row * H * D + (size_t) head * D;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    float local_max = -INFINITY;
+    for (int k = tid; k < keys; k += blockDim.x)
+    {
+        const float* kr = a.k_cache + (size_t) k * kvw + kv_column;
+        float s = 0.f;
+        for (int c = 0; c < D; ++c)
+            s = fmaf(q[c], kr[c], s);
+        s *= a.scale;
+        scores[k] = s;
+        local_max = fmaxf(local_max, s);
+    }
+    local_max = warp_max(local_max);
+    if (lane == 0)
+        red[warp] = local_max;
+    __syncthreads();
+    const float mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    float local_sum = 0.f;
+    for (int k = tid; k < keys; k += blockDim.x)
+    {
+        const float p = expf(scores[k] - mx);
+        scores[k] = p;
+        local_sum += p;
+    }
+    local_sum = warp_sum(local_sum);
+    if (lane == 0)
+        red[warp] = local_sum;
+    __syncthreads();
+    const float sum = red[0] + red[1] + red[2] + red[3];
+    for (int c = tid; c < D; c += blockDim.x)
+    {
+        float value = 0.f;
+        for (int k = 0; k < keys; ++k)
+            value = fmaf(scores[k], a.v_cache[(size_t) k * kvw + kv_column + c], value);
+        a.out[(size_t) row * H * D + (size_t) head * D + c] = value / sum;
+    }
+}
+} // namespace hfk

@@ -1,0 +1,1354 @@
+// libhf_cuda.so: the engine behind include/hf_cuda.h.
+//
+// The reference records one eacp compute pass per step, 221 dispatches per
+// decode token with barriers between them (Decoder.cpp:644-706). Here a decode
+// step is a CUDA graph of 92 kernels (93 when the context is split) chained by
+// programmatic dependent launch, so each kernel's CTAs are resident and
+// streaming their weights before the previous kernel ends:
+//
+//   embed  ->  per layer: [norm + q/k/v + RoPE + cache write]  ->  [attention
+//   (+ split merge)]  ->  [o_proj + residual]  ->  [norm + gate/up + GeGLU]  ->
+//   [down + residual]  ->  [final norm + logits + argmax -> next token slot]
+//
+// The position lives on the device (state[0]) and the last kernel of a step
+// advances it, so the same graph replays for every step of a context-length
+// bucket (the bucket fixes the attention split count). Token feedback stays on
+// the device: a step embeds the token in slot[pos] and writes slot[pos + 1]
+// (Gemma.cpp:320-333).
+#include <hf_cuda.h>
+
+#include "attention.cuh"
+#include "gemv.cuh"
+#include "misc.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+using namespace hfk;
+
+namespace
+{
+constexpr int kStages = 3; // shared-memory ring depth of the streaming products (3 x 34 KiB)
+
+// Dynamic shared memory of q8_gemv_stream<K>: the stage ring plus either the
+// x vector (K = 2048) or the per-slab row partials (K > 2048). Two CTAs fit on
+// one SM, so the next kernel's CTAs are resident while this one streams.
+template <int K>
+constexpr size_t stream_smem()
+{
+    return (size_t) kStages * (kStageQuants + kStageScales)
+           + (K == 2048 ? 8192 : (size_t) kMaxSlabRows * (K / 2048) * sizeof(float));
+}
+
+// Grid of the streaming products: one CTA per SM, more only when a K > 2048
+// slab would exceed the rows its partials hold.
+int stream_grid(int K, int units, int sms)
+{
+    int grid = std::min(sms, units);
+    if (K > 2048)
+        grid = std::max(grid, (units + kMaxSlabRows - 1) / kMaxSlabRows);
+    return std::max(1, std::min(grid, units));
+}
+
+struct Q8
+{
+    uint8_t* base = nullptr;
+    int rows = 0;
+    int cols = 0;
+    const __half* scales() const { return reinterpret_cast<const __half*>(base + (size_t) rows * cols); }
+    size_t bytes() const { return (size_t) rows * cols + (size_t) rows * cols / 16; }
+};
+
+struct Layer
+{
+    Q8 qkv, o, gu, down;
+    float* in_norm = nullptr;
+    float* post_norm = nullptr;
+};
+
+template <typename Kernel, typename... Args>
+cudaError_t launch(bool pdl, Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args)
+{
+    cudaLaunchConfig_t config = {};
+    config.gridDim = grid;
+    config.blockDim = block;
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[0].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attribute;
+    config.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&config, kernel, args...);
+}
+
+int sm_count(int device)
+{
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    return sms > 0 ? sms : 1;
+}
+
+// Opt-in shared memory for every kernel that needs more than 48 KiB, once per
+// device.
+void configure_kernels()
+{
+    cudaFuncSetAttribute(q8_gemv_stream<2048, Epi::Store, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) stream_smem<2048>());
+    cudaFuncSetAttribute(q8_gemv_stream<2048, Epi::Residual, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) stream_smem<2048>());
+    cudaFuncSetAttribute(q8_gemv_stream<2048, Epi::Gelu, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) stream_smem<2048>());
+    cudaFuncSetAttribute(q8_gemv_stream<2048, Epi::QkvRope, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) stream_smem<2048>());
+    cudaFuncSetAttribute(q8_gemv_stream<2048, Epi::GeGLU, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) stream_smem<2048>());
+    cudaFuncSetAttribute(q8_gemv_stream<2048, Epi::Logits, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) stream_smem<2048>());
+#define HF_CONFIGURE_WIDE(KK)                                                                                          \
+    cudaFuncSetAttribute(q8_gemv_stream<KK, Epi::Store, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) stream_smem<KK>()); \
+    cudaFuncSetAttribute(q8_gemv_stream<KK, Epi::Residual, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) stream_smem<KK>()); \
+    cudaFuncSetAttribute(q8_gemv_stream<KK, Epi::Gelu, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) stream_smem<KK>());
+    HF_CONFIGURE_WIDE(4096)
+    HF_CONFIGURE_WIDE(8192)
+    HF_CONFIGURE_WIDE(16384)
+#undef HF_CONFIGURE_WIDE
+    cudaFuncSetAttribute(mqa_fast<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<8>());
+    cudaFuncSetAttribute(mqa_fast<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<4>());
+    cudaFuncSetAttribute(mqa_fast<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<2>());
+    cudaFuncSetAttribute(mqa_fast<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<1>());
+    cudaFuncSetAttribute(mqa_generic, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
+
+void configure_once(int device)
+{
+    static std::map<int, bool> done;
+    if (!done[device])
+    {
+        configure_kernels();
+        done[device] = true;
+    }
+}
+
+// Launches the streaming product for a K the dispatch knows, or returns false.
+template <Epi E>
+bool stream_product(int K, bool pdl, int grid, cudaStream_t stream, const GemvArgs& a, cudaError_t* error)
+{
+    switch (K)
+    {
+    case 2048:
+        *error = launch(pdl, q8_gemv_stream<2048, E, kStages>, dim3(grid), dim3(kStreamThreads), stream_smem<2048>(), stream, a);
+        return true;
+    default:
+        break;
+    }
+    if constexpr (E == Epi::Store || E == Epi::Residual || E == Epi::Gelu)
+    {
+        switch (K)
+        {
+        case 4096:
+            *error = launch(pdl, q8_gemv_stream<4096, E, kStages>, dim3(grid), dim3(kStreamThreads), stream_smem<4096>(), stream, a);
+            return true;
+        case 8192:
+            *error = launch(pdl, q8_gemv_stream<8192, E, kStages>, dim3(grid), dim3(kStreamThreads), stream_smem<8192>(), stream, a);
+            return true;
+        case 16384:
+            *error = launch(pdl, q8_gemv_stream<16384, E, kStages>, dim3(grid), dim3(kStreamThreads), stream_smem<16384>(), stream, a);
+            return true;
+        default:
+            break;
+        }
+    }
+    return false;
+}
+
+cudaError_t launch_attention(int QH, dim3 grid, cudaStream_t stream, const AttnArgs& at)
+{
+    switch (QH)
+    {
+    case 8: return launch(true, mqa_fast<8>, grid, dim3(256), mqa_fast_smem<8>(), stream, at);
+    case 4: return launch(true, mqa_fast<4>, grid, dim3(256), mqa_fast_smem<4>(), stream, at);
+    case 2: return launch(true, mqa_fast<2>, grid, dim3(256), mqa_fast_smem<2>(), stream, at);
+    default: return launch(true, mqa_fast<1>, grid, dim3(256), mqa_fast_smem<1>(), stream, at);
+    }
+}
+
+template <Epi E>
+cudaError_t generic_product(bool pdl, int units, cudaStream_t stream, const GemvArgs& a, int sms)
+{
+    const int warps_wanted = std::max(1, units);
+    const int grid = std::max(1, std::min(sms * 8, (warps_wanted + 7) / 8));
+    return launch(pdl, q8_rows_generic<E>, dim3(grid), dim3(256), 0, stream, a);
+}
+
+std::string shape_refusal(const hf_shape& s)
+{
+    auto positive = [](int v) { return v > 0; };
+    if (!positive(s.width) || !positive(s.heads) || !positive(s.kv_heads) || !positive(s.head_width)
+        || !positive(s.layers) || !positive(s.intermediate) || !positive(s.vocab) || !positive(s.max_positions))
+        return "a decoder shape's sizes must all be positive";
+    if (s.max_step_rows < 0)
+        return "a decoder shape's step capacity is a row count or zero for the whole window";
+    if (s.max_step_rows > s.max_positions)
+        return "a decoder shape's step capacity is past the positions its caches hold";
+    if (s.head_width % 4 != 0)
+        return "a decoder's head width must be a multiple of four";
+    if (s.head_width > 256)
+        return "a decoder's head width is at most 256";
+    if (s.heads % s.kv_heads != 0)
+        return "a decoder's kv heads do not divide its query heads";
+    // The Q8_0 storage of every product weight (Int8Blocks.h:63-69).
+    if (s.width % 32 != 0 || s.intermediate % 32 != 0 || (s.heads * s.head_width) % 32 != 0)
+        return "every product's inner extent must be a whole number of 32-element blocks";
+    if (s.head_width % 2 != 0)
+        return "the rotation pairs a head's halves";
+    return {};
+}
+} // namespace
+
+struct hf_ctx
+{
+    int device = 0;
+    hf_shape shape = {};
+    cudaStream_t stream = nullptr;
+    int sms = 1;
+    bool fast = false;
+    int capacity = 1;
+    std::string error;
+
+    uint8_t* pool = nullptr;
+    Q8 embedding;
+    float* final_norm = nullptr;
+    std::vector<Layer> layers;
+    std::vector<unsigned> loaded; // bit per tensor id, per layer (index layers = globals)
+
+    float* hidden = nullptr;
+    float* normed = nullptr;
+    float* qbuf = nullptr;
+    float* attended = nullptr;
+    float* act = nullptr;
+    float* logits = nullptr;
+    float* kcache = nullptr;
+    float* vcache = nullptr;
+    float* rope_cos = nullptr;
+    float* rope_sin = nullptr;
+    unsigned* slots = nullptr;
+    unsigned* state = nullptr; // [0] position, [1] error word, [2] logits ticket
+    float* cand_val = nullptr;
+    unsigned* cand_idx = nullptr;
+    float* attn_acc = nullptr;
+    float* attn_ml = nullptr;
+    uint8_t* staging = nullptr;
+    size_t staging_bytes = 0;
+    int max_splits = 1;
+
+    int position = 0;
+    std::map<int, cudaGraphExec_t> graphs; // decode step by attention split count
+
+    int fail(int code, const std::string& text)
+    {
+        error = text;
+        return code;
+    }
+
+    int cuda(cudaError_t e, const char* what)
+    {
+        if (e == cudaSuccess)
+            return HF_OK;
+        error = std::string(what) + ": " + cudaGetErrorString(e);
+        return HF_E_CUDA;
+    }
+
+    int kv_width() const { return shape.kv_heads * shape.head_width; }
+    int query_width() const { return shape.heads * shape.head_width; }
+    int qkv_rows() const { return query_width() + 2 * kv_width(); }
+    unsigned* err_word() const { return state + 1; }
+    unsigned* ticket() const { return state + 2; }
+    float* layer_k(int l) const { return kcache + (size_t) l * shape.max_positions * kv_width(); }
+    float* layer_v(int l) const { return vcache + (size_t) l * shape.max_positions * kv_width(); }
+
+    bool all_loaded() const
+    {
+        const unsigned layer_bits = (1u << HF_TENSOR_INPUT_NORM) | (1u << HF_TENSOR_QUERY) | (1u << HF_TENSOR_KEY)
+                                    | (1u << HF_TENSOR_VALUE) | (1u << HF_TENSOR_OUTPUT) | (1u << HF_TENSOR_GATE_UP)
+                                    | (1u << HF_TENSOR_DOWN) | (1u << HF_TENSOR_POST_NORM);
+        const unsigned global_bits = (1u << HF_TENSOR_EMBEDDING) | (1u << HF_TENSOR_FINAL_NORM);
+        if ((loaded[shape.layers] & global_bits) != global_bits)
+            return false;
+        for (int l = 0; l < shape.layers; ++l)
+            if ((loaded[l] & layer_bits) != layer_bits)
+                return false;
+        return true;
+    }
+
+    int splits_for(int keys) const
+    {
+        if (!fast || keys <= 64)
+            return 1;
+        int s = 1;
+        while (s * 64 < keys)
+            s *= 2;
+        return std::min(s, max_splits);
+    }
+
+    // ---------------------------------------------------------------------
+    // The kernels of one decode step (one row) on the streaming path; each
+    // reads the step's position from the device.
+    cudaError_t launch_embed()
+    {
+        const hf_shape& s = shape;
+        return launch(false, embed_q8, dim3((s.width + 255) / 256, 1), dim3(256), 0, stream,
+                      (const uint8_t*) embedding.base, embedding.scales(), s.width, s.vocab, s.embed_scale,
+                      (const unsigned*) slots, (const unsigned*) state, 1, hidden, err_word());
+    }
+
+    cudaError_t launch_qkv(int l)
+    {
+        const hf_shape& s = shape;
+        const Layer& L = layers[l];
+        GemvArgs a = {};
+        a.w = L.qkv.base;
+        a.scales = L.qkv.scales();
+        a.N = L.qkv.rows;
+        a.K = s.width;
+        a.M = 1;
+        a.x = hidden;
+        a.norm_w = L.in_norm;
+        a.eps = s.rms_eps;
+        a.out = qbuf;
+        a.k_cache = layer_k(l);
+        a.v_cache = layer_v(l);
+        a.rope_cos = rope_cos;
+        a.rope_sin = rope_sin;
+        a.heads = s.heads;
+        a.kv_heads = s.kv_heads;
+        a.head_dim = s.head_width;
+        a.state = state;
+        a.err = err_word();
+        cudaError_t e = cudaSuccess;
+        stream_product<Epi::QkvRope>(2048, true, stream_grid(2048, L.qkv.rows / 2, sms), stream, a, &e);
+        return e;
+    }
+
+    cudaError_t launch_decode_attention(int l, int splits)
+    {
+        const hf_shape& s = shape;
+        AttnArgs at = {};
+        at.q = qbuf;
+        at.k_cache = layer_k(l);
+        at.v_cache = layer_v(l);
+        at.out = attended;
+        at.part_acc = attn_acc;
+        at.part_ml = attn_ml;
+        at.heads = s.heads;
+        at.kv_heads = s.kv_heads;
+        at.head_dim = s.head_width;
+        at.scale = 1.f / std::sqrt((float) s.head_width);
+        at.nsplit = splits;
+        at.state = state;
+        at.err = err_word();
+        cudaError_t e = launch_attention(s.heads / s.kv_heads, dim3(splits, s.kv_heads, 1), stream, at);
+        if (e == cudaSuccess && splits > 1)
+            e = launch(true, mqa_merge, dim3((query_width() + 255) / 256, 1), dim3(256), 0, stream, at);
+        return e;
+    }
+
+    cudaError_t launch_output(int l)
+    {
+        const hf_shape& s = shape;
+        const Layer& L = layers[l];
+        GemvArgs a = {};
+        a.w = L.o.base;
+        a.scales = L.o.scales();
+        a.N = s.width;
+        a.K = query_width();
+        a.M = 1;
+        a.x = attended;
+        a.out = hidden;
+        a.state = state;
+        a.err = err_word();
+        cudaError_t e = cudaSuccess;
+        stream_product<Epi::Residual>(2048, true, stream_grid(2048, s.width, sms), stream, a, &e);
+        return e;
+    }
+
+    cudaError_t launch_gate_up(int l)
+    {
+        const hf_shape& s = shape;
+        const Layer& L = layers[l];
+        GemvArgs a = {};
+        a.w = L.gu.base;
+        a.scales = L.gu.scales();
+        a.N = L.gu.rows;
+        a.K = s.width;
+        a.M = 1;
+        a.x = hidden;
+        a.norm_w = L.post_norm;
+        a.eps = s.rms_eps;
+        a.out = act;
+        a.state = state;
+        a.err = err_word();
+        cudaError_t e = cudaSuccess;
+        stream_product<Epi::GeGLU>(2048, true, stream_grid(2048, L.gu.rows / 2, sms), stream, a, &e);
+        return e;
+    }
+
+    cudaError_t launch_down(int l)
+    {
+        const hf_shape& s = shape;
+        const Layer& L = layers[l];
+        GemvArgs a = {};
+        a.w = L.down.base;
+        a.scales = L.down.scales();
+        a.N = s.width;
+        a.K = s.intermediate;
+        a.M = 1;
+        a.x = act;
+        a.out = hidden;
+        a.state = state;
+        a.err = err_word();
+        cudaError_t e = cudaSuccess;
+        stream_product<Epi::Residual>(s.intermediate, true, stream_grid(s.intermediate, s.width, sms), stream, a, &e);
+        return e;
+    }
+
+    cudaError_t launch_logits(int advance)
+    {
+        const hf_shape& s = shape;
+        GemvArgs a = {};
+        a.w = embedding.base;
+        a.scales = embedding.scales();
+        a.N = s.vocab;
+        a.K = s.width;
+        a.M = 1;
+        a.x = hidden;
+        a.norm_w = final_norm;
+        a.eps = s.rms_eps;
+        a.out = logits;
+        a.cand_val = cand_val;
+        a.cand_idx = cand_idx;
+        a.ticket = ticket();
+        a.slots = slots;
+        a.advance = advance;
+        a.state = state;
+        a.err = err_word();
+        cudaError_t e = cudaSuccess;
+        stream_product<Epi::Logits>(2048, true, stream_grid(2048, s.vocab, sms), stream, a, &e);
+        return e;
+    }
+
+    int enqueue_fast_decode(int splits)
+    {
+        cudaError_t e = launch_embed();
+        if (e != cudaSuccess)
+            return cuda(e, "embed launch");
+        for (int l = 0; l < shape.layers; ++l)
+        {
+            if ((e = launch_qkv(l)) != cudaSuccess)
+                return cuda(e, "q/k/v launch");
+            if ((e = launch_decode_attention(l, splits)) != cudaSuccess)
+                return cuda(e, "attention launch");
+            if ((e = launch_output(l)) != cudaSuccess)
+                return cuda(e, "o_proj launch");
+            if ((e = launch_gate_up(l)) != cudaSuccess)
+                return cuda(e, "gate/up launch");
+            if ((e = launch_down(l)) != cudaSuccess)
+                return cuda(e, "down launch");
+        }
+        if ((e = launch_logits(1)) != cudaSuccess)
+            return cuda(e, "logits launch");
+        return HF_OK;
+    }
+
+    int decode_launch_count(int splits) const
+    {
+        return 2 + shape.layers * (splits > 1 ? 6 : 5);
+    }
+
+    int graph_for(int splits, cudaGraphExec_t* out)
+    {
+        auto found = graphs.find(splits);
+        if (found != graphs.end())
+        {
+            *out = found->second;
+            return HF_OK;
+        }
+        cudaGraph_t graph = nullptr;
+        int rc = cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+        if (rc)
+            return rc;
+        rc = enqueue_fast_decode(splits);
+        cudaError_t e = cudaStreamEndCapture(stream, &graph);
+        if (rc)
+        {
+            if (graph)
+                cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (e != cudaSuccess)
+            return cuda(e, "end capture");
+        cudaGraphExec_t exec = nullptr;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess)
+            return cuda(e, "graph instantiate");
+        graphs[splits] = exec;
+        *out = exec;
+        return HF_OK;
+    }
+
+    // ---------------------------------------------------------------------
+    // `rows` rows (prefill blocks, and every step on the generic path), with
+    // the token ids already in slots[position ...]. all_logits: write every
+    // row's logits (Decoder::step), else only the last row's (generation).
+    int enqueue_rows(int rows, bool all_logits)
+    {
+        const hf_shape& s = shape;
+        cudaError_t e = launch(false, embed_q8, dim3((s.width + 255) / 256, rows), dim3(256), 0, stream,
+                               (const uint8_t*) embedding.base, embedding.scales(), s.width, s.vocab, s.embed_scale,
+                               (const unsigned*) slots, (const unsigned*) state, rows, hidden, err_word());
+        if (e != cudaSuccess)
+            return cuda(e, "embed launch");
+        const int QH = s.heads / s.kv_heads;
+        for (int l = 0; l < s.layers; ++l)
+        {
+            const Layer& L = layers[l];
+            e = launch(true, rms_norm_rows, dim3(rows), dim3(256), 0, stream, (const float*) hidden,
+                       (const float*) L.in_norm, s.width, s.rms_eps, normed);
+            if (e != cudaSuccess)
+                return cuda(e, "norm launch");
+
+            GemvArgs qkv = {};
+            qkv.w = L.qkv.base;
+            qkv.scales = L.qkv.scales();
+            qkv.N = L.qkv.rows;
+            qkv.K = s.width;
+            qkv.M = rows;
+            qkv.x = normed;
+            qkv.out = qbuf;
+            qkv.k_cache = layer_k(l);
+            qkv.v_cache = layer_v(l);
+            qkv.rope_cos = rope_cos;
+            qkv.rope_sin = rope_sin;
+            qkv.heads = s.heads;
+            qkv.kv_heads = s.kv_heads;
+            qkv.head_dim = s.head_width;
+            qkv.state = state;
+            qkv.err = err_word();
+            e = generic_product<Epi::QkvRope>(true, L.qkv.rows / 2, stream, qkv, sms);
+            if (e != cudaSuccess)
+                return cuda(e, "q/k/v launch");
+
+            AttnArgs at = {};
+            at.q = qbuf;
+            at.k_cache = layer_k(l);
+            at.v_cache = layer_v(l);
+            at.out = attended;
+            at.heads = s.heads;
+            at.kv_heads = s.kv_heads;
+            at.head_dim = s.head_width;
+            at.scale = 1.f / std::sqrt((float) s.head_width);
+            at.nsplit = 1;
+            at.state = state;
+            at.err = err_word();
+            if (fast)
+            {
+                e = launch_attention(QH, dim3(1, s.kv_heads, rows), stream, at);
+            }
+            else
+                e = launch(true, mqa_generic, dim3(s.heads, rows), dim3(128), (size_t) s.max_positions * sizeof(float),
+                           stream, at);
+            if (e != cudaSuccess)
+                return cuda(e, "attention launch");
+
+            GemvArgs o = {};
+            o.w = L.o.base;
+            o.scales = L.o.scales();
+            o.N = s.width;
+            o.K = query_width();
+            o.M = rows;
+            o.x = attended;
+            o.out = hidden;
+            o.state = state;
+            o.err = err_word();
+            e = generic_product<Epi::Residual>(true, s.width, stream, o, sms);
+            if (e != cudaSuccess)
+                return cuda(e, "o_proj launch");
+
+            e = launch(true, rms_norm_rows, dim3(rows), dim3(256), 0, stream, (const float*) hidden,
+                       (const float*) L.post_norm, s.width, s.rms_eps, normed);
+            if (e != cudaSuccess)
+                return cuda(e, "norm launch");
+
+            GemvArgs gu = {};
+            gu.w = L.gu.base;
+            gu.scales = L.gu.scales();
+            gu.N = L.gu.rows;
+            gu.K = s.width;
+            gu.M = rows;
+            gu.x = normed;
+            gu.out = act;
+            gu.state = state;
+            gu.err = err_word();
+            e = generic_product<Epi::GeGLU>(true, L.gu.rows / 2, stream, gu, sms);
+            if (e != cudaSuccess)
+                return cuda(e, "gate/up launch");
+
+            GemvArgs dn = {};
+            dn.w = L.down.base;
+            dn.scales = L.down.scales();
+            dn.N = s.width;
+            dn.K = s.intermediate;
+            dn.M = rows;
+            dn.x = act;
+            dn.out = hidden;
+            dn.state = state;
+            dn.err = err_word();
+            e = generic_product<Epi::Residual>(true, s.width, stream, dn, sms);
+            if (e != cudaSuccess)
+                return cuda(e, "down launch");
+        }
+
+        e = launch(true, rms_norm_rows, dim3(rows), dim3(256), 0, stream, (const float*) hidden,
+                   (const float*) final_norm, s.width, s.rms_eps, normed);
+        if (e != cudaSuccess)
+            return cuda(e, "final norm launch");
+
+        const int logit_rows = all_logits ? rows : 1;
+        GemvArgs lg = {};
+        lg.w = embedding.base;
+        lg.scales = embedding.scales();
+        lg.N = s.vocab;
+        lg.K = s.width;
+        lg.M = logit_rows;
+        lg.x = normed + (size_t) (rows - logit_rows) * s.width;
+        lg.out = logits + (size_t) (all_logits ? 0 : rows - 1) * s.vocab;
+        lg.state = state;
+        lg.err = err_word();
+        e = generic_product<Epi::Logits>(true, s.vocab, stream, lg, sms);
+        if (e != cudaSuccess)
+            return cuda(e, "logits launch");
+
+        // The last row's argmax into slot[position + rows]; advances the position.
+        const int parts = 64;
+        e = launch(true, argmax_partial, dim3(parts, 1), dim3(256), 0, stream,
+                   (const float*) (logits + (size_t) (rows - 1) * s.vocab), s.vocab, (const float*) nullptr, parts,
+                   cand_val, cand_idx);
+        if (e != cudaSuccess)
+            return cuda(e, "argmax launch");
+        e = launch(true, argmax_final, dim3(1), dim3(32), 0, stream, (const float*) cand_val, (const unsigned*) cand_idx,
+                   parts, 1, (unsigned*) nullptr, slots, state, rows);
+        if (e != cudaSuccess)
+            return cuda(e, "argmax launch");
+        return HF_OK;
+    }
+
+    int check_device_error()
+    {
+        unsigned word = 0;
+        int rc = cuda(cudaMemcpy(&word, err_word(), sizeof(word), cudaMemcpyDeviceToHost), "error word read");
+        if (rc)
+            return rc;
+        if (word == 0)
+            return HF_OK;
+        cudaMemset(err_word(), 0, sizeof(unsigned));
+        std::string text = "a kernel reported:";
+        if (word & kErrWaitTimeout)
+            text += " a shared-memory stage wait ran out of polls;";
+        if (word & kErrTokenRange)
+            text += " a token id outside the vocabulary reached the embedding gather;";
+        if (word & kErrPosition)
+            text += " a step ran past the window;";
+        return fail(HF_E_DEVICE, text);
+    }
+
+    int sync()
+    {
+        int rc = cuda(cudaStreamSynchronize(stream), "stream synchronize");
+        if (rc)
+            return rc;
+        return check_device_error();
+    }
+
+    int set_position(int p)
+    {
+        position = p;
+        const unsigned v = (unsigned) p;
+        return cuda(cudaMemcpyAsync(state, &v, sizeof(v), cudaMemcpyHostToDevice, stream), "position write");
+    }
+
+    // Prefill `count` tokens already in the slots, in blocks of the step capacity.
+    int enqueue_prompt(int count, bool all_logits)
+    {
+        for (int first = 0; first < count; first += capacity)
+        {
+            const int rows = std::min(capacity, count - first);
+            int rc;
+            if (rows == 1 && fast && !all_logits)
+            {
+                cudaGraphExec_t exec;
+                rc = graph_for(splits_for(position + 1), &exec);
+                if (!rc)
+                    rc = cuda(cudaGraphLaunch(exec, stream), "graph launch");
+            }
+            else
+                rc = enqueue_rows(rows, all_logits);
+            if (rc)
+                return rc;
+            position += rows;
+        }
+        return HF_OK;
+    }
+};
+
+namespace
+{
+int check_tokens(hf_ctx* ctx, const uint32_t* tokens, int count)
+{
+    for (int i = 0; i < count; ++i)
+        if (tokens[i] >= (uint32_t) ctx->shape.vocab)
+            return ctx->fail(HF_E_TOKEN, "token " + std::to_string(tokens[i]) + " is outside a vocabulary of "
+                                             + std::to_string(ctx->shape.vocab));
+    return HF_OK;
+}
+
+template <typename T>
+int device_alloc(hf_ctx* ctx, T** p, size_t count, const char* what)
+{
+    return ctx->cuda(cudaMalloc((void**) p, std::max<size_t>(count, 1) * sizeof(T)), what);
+}
+} // namespace
+
+extern "C" {
+int hf_cuda_device_count(int* count)
+{
+    if (!count)
+        return HF_E_INVALID;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess)
+        n = 0;
+    *count = n;
+    return HF_OK;
+}
+
+int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
+{
+    if (!shape || !out)
+        return HF_E_INVALID;
+    *out = nullptr;
+    const std::string refusal = shape_refusal(*shape);
+    if (!refusal.empty())
+        return HF_E_SHAPE;
+
+    auto* ctx = new hf_ctx();
+    ctx->device = device;
+    ctx->shape = *shape;
+    const hf_shape& s = ctx->shape;
+    ctx->capacity = s.max_step_rows > 0 ? s.max_step_rows : s.max_positions;
+    auto bail = [&](int rc) {
+        hf_cuda_destroy(ctx);
+        return rc;
+    };
+    if (cudaSetDevice(device) != cudaSuccess)
+        return bail(HF_E_CUDA);
+    configure_once(device);
+    ctx->sms = sm_count(device);
+    ctx->max_splits = 128;
+    const int QH = s.heads / s.kv_heads;
+    ctx->fast = s.width == 2048 && s.heads * s.head_width == 2048 && s.head_width == 256 && QH <= 8
+                && (QH == 1 || QH == 2 || QH == 4 || QH == 8)
+                && (s.intermediate == 2048 || s.intermediate == 4096 || s.intermediate == 8192 || s.intermediate == 16384);
+    if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(HF_E_CUDA);
+
+    // One pool for every Q8 weight, in device layout.
+    const size_t W = s.width, QW = (size_t) s.heads * s.head_width, KVW = (size_t) s.kv_heads * s.head_width;
+    const size_t I = s.intermediate, V = s.vocab;
+    auto q8bytes = [](size_t rows, size_t cols) { return rows * cols + rows * cols / 16; };
+    auto round256 = [](size_t b) { return (b + 255) / 256 * 256; };
+    const size_t per_layer = round256(q8bytes(QW + 2 * KVW, W)) + round256(q8bytes(W, QW)) + round256(q8bytes(2 * I, W))
+                             + round256(q8bytes(W, I));
+    const size_t pool_bytes = round256(q8bytes(V, W)) + per_layer * s.layers;
+    if (ctx->cuda(cudaMalloc(&ctx->pool, pool_bytes), "weight pool"))
+        return bail(HF_E_CUDA);
+    size_t at = 0;
+    auto carve = [&](Q8& t, size_t rows, size_t cols) {
+        t.base = ctx->pool + at;
+        t.rows = (int) rows;
+        t.cols = (int) cols;
+        at += round256(q8bytes(rows, cols));
+    };
+    carve(ctx->embedding, V, W);
+    ctx->layers.resize(s.layers);
+    for (auto& L: ctx->layers)
+    {
+        carve(L.qkv, QW + 2 * KVW, W);
+        carve(L.o, W, QW);
+        carve(L.gu, 2 * I, W);
+        carve(L.down, W, I);
+    }
+    ctx->loaded.assign(s.layers + 1, 0u);
+
+    float* norms = nullptr;
+    if (device_alloc(ctx, &norms, W * (2 * (size_t) s.layers + 1), "norm weights"))
+        return bail(HF_E_CUDA);
+    ctx->final_norm = norms;
+    for (int l = 0; l < s.layers; ++l)
+    {
+        ctx->layers[l].in_norm = norms + W * (1 + 2 * (size_t) l);
+        ctx->layers[l].post_norm = norms + W * (2 + 2 * (size_t) l);
+    }
+
+    const size_t cap = ctx->capacity, P = s.max_positions;
+    if (device_alloc(ctx, &ctx->hidden, cap * W, "hidden") || device_alloc(ctx, &ctx->normed, cap * W, "normed")
+        || device_alloc(ctx, &ctx->qbuf, cap * QW, "queries") || device_alloc(ctx, &ctx->attended, cap * QW, "attended")
+        || device_alloc(ctx, &ctx->act, cap * I, "activated") || device_alloc(ctx, &ctx->logits, cap * V, "logits")
+        || device_alloc(ctx, &ctx->kcache, (size_t) s.layers * P * KVW, "key cache")
+        || device_alloc(ctx, &ctx->vcache, (size_t) s.layers * P * KVW, "value cache")
+        || device_alloc(ctx, &ctx->rope_cos, P * (s.head_width / 2), "rotary cosines")
+        || device_alloc(ctx, &ctx->rope_sin, P * (s.head_width / 2), "rotary sines")
+        || device_alloc(ctx, &ctx->slots, P + 1, "sequence slots") || device_alloc(ctx, &ctx->state, 4, "step state")
+        || device_alloc(ctx, &ctx->cand_val, 1024, "argmax candidates")
+        || device_alloc(ctx, &ctx->cand_idx, 1024, "argmax candidates")
+        || device_alloc(ctx, &ctx->attn_acc, (size_t) ctx->max_splits * QW, "attention partials")
+        || device_alloc(ctx, &ctx->attn_ml, (size_t) ctx->max_splits * s.heads * 2, "attention partials"))
+        return bail(HF_E_CUDA);
+    cudaMemset(ctx->state, 0, 4 * sizeof(unsigned));
+    cudaMemset(ctx->slots, 0, (P + 1) * sizeof(unsigned));
+    cudaMemset(ctx->kcache, 0, (size_t) s.layers * P * KVW * sizeof(float));
+    cudaMemset(ctx->vcache, 0, (size_t) s.layers * P * KVW * sizeof(float));
+
+    // Kernels/RoPE.cpp:7-34: angle = pos * theta^(-2i/D) in double, stored as float.
+    const int half = s.head_width / 2;
+    std::vector<float> cosines(P * half), sines(P * half);
+    for (int i = 0; i < half; ++i)
+    {
+        const double inverse = 1.0 / std::pow(s.rope_theta, 2.0 * i / (double) s.head_width);
+        for (size_t p = 0; p < P; ++p)
+        {
+            const double angle = (double) p * inverse;
+            cosines[p * half + i] = (float) std::cos(angle);
+            sines[p * half + i] = (float) std::sin(angle);
+        }
+    }
+    if (ctx->cuda(cudaMemcpy(ctx->rope_cos, cosines.data(), cosines.size() * 4, cudaMemcpyHostToDevice), "rotary upload")
+        || ctx->cuda(cudaMemcpy(ctx->rope_sin, sines.data(), sines.size() * 4, cudaMemcpyHostToDevice), "rotary upload"))
+        return bail(HF_E_CUDA);
+    if (cudaDeviceSynchronize() != cudaSuccess)
+        return bail(HF_E_CUDA);
+    *out = ctx;
+    return HF_OK;
+}
+
+void hf_cuda_destroy(hf_ctx* ctx)
+{
+    if (!ctx)
+        return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream)
+        cudaStreamSynchronize(ctx->stream);
+    for (auto& g: ctx->graphs)
+        cudaGraphExecDestroy(g.second);
+    void* buffers[] = {ctx->pool, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
+                       ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slots, ctx->state,
+                       ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging};
+    for (void* b: buffers)
+        if (b)
+            cudaFree(b);
+    if (ctx->stream)
+        cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+const char* hf_cuda_last_error(const hf_ctx* ctx)
+{
+    return ctx ? ctx->error.c_str() : "no context";
+}
+
+int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, uint64_t byte_count)
+{
+    if (!ctx || !bytes)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    const hf_shape& s = ctx->shape;
+    const bool global = tensor == HF_TENSOR_EMBEDDING;
+    if (!global && (layer < 0 || layer >= s.layers))
+        return ctx->fail(HF_E_INVALID, "layer " + std::to_string(layer) + " is outside the decoder");
+
+    Q8* target = nullptr;
+    int rows = 0, cols = 0, dst_row0 = 0, mode = 0, group = 1;
+    const int QW = ctx->query_width(), KVW = ctx->kv_width();
+    switch (tensor)
+    {
+    case HF_TENSOR_EMBEDDING: target = &ctx->embedding; rows = s.vocab; cols = s.width; break;
+    case HF_TENSOR_QUERY: target = &ctx->layers[layer].qkv; rows = QW; cols = s.width; mode = 1; group = s.head_width; break;
+    case HF_TENSOR_KEY: target = &ctx->layers[layer].qkv; rows = KVW; cols = s.width; dst_row0 = QW; mode = 1; group = s.head_width; break;
+    case HF_TENSOR_VALUE: target = &ctx->layers[layer].qkv; rows = KVW; cols = s.width; dst_row0 = QW + KVW; mode = 1; group = s.head_width; break;
+    case HF_TENSOR_OUTPUT: target = &ctx->layers[layer].o; rows = s.width; cols = QW; break;
+    case HF_TENSOR_GATE_UP: target = &ctx->layers[layer].gu; rows = 2 * s.intermediate; cols = s.width; mode = 2; break;
+    case HF_TENSOR_DOWN: target = &ctx->layers[layer].down; rows = s.width; cols = s.intermediate; break;
+    default: return ctx->fail(HF_E_INVALID, "tensor " + std::to_string(tensor) + " is not a Q8_0 weight");
+    }
+    const uint64_t elements = (uint64_t) rows * cols;
+    const uint64_t expected = elements + elements / 16;
+    if (byte_count != expected || cols % 32 != 0 || elements % 64 != 0)
+        return ctx->fail(HF_E_SHAPE, "a Q8_0 tensor of " + std::to_string(rows) + " x " + std::to_string(cols)
+                                         + " is " + std::to_string(expected) + " bytes, not " + std::to_string(byte_count));
+
+    int rc;
+    if (mode == 0 && dst_row0 == 0 && rows == target->rows)
+        rc = ctx->cuda(cudaMemcpy(target->base, bytes, expected, cudaMemcpyHostToDevice), "weight upload");
+    else
+    {
+        if (ctx->staging_bytes < expected)
+        {
+            if (ctx->staging)
+                cudaFree(ctx->staging);
+            ctx->staging = nullptr;
+            ctx->staging_bytes = 0;
+            if (ctx->cuda(cudaMalloc(&ctx->staging, expected), "upload staging"))
+                return HF_E_CUDA;
+            ctx->staging_bytes = expected;
+        }
+        rc = ctx->cuda(cudaMemcpy(ctx->staging, bytes, expected, cudaMemcpyHostToDevice), "weight upload");
+        if (!rc)
+        {
+            permute_q8_rows<<<rows, 256>>>(ctx->staging, rows, cols, target->base, target->rows, dst_row0, mode, group);
+            rc = ctx->cuda(cudaDeviceSynchronize(), "weight permutation");
+        }
+    }
+    if (rc)
+        return rc;
+    ctx->loaded[global ? s.layers : layer] |= 1u << tensor;
+    return HF_OK;
+}
+
+int hf_cuda_upload_f32(hf_ctx* ctx, int tensor, int layer, const float* values, uint64_t count)
+{
+    if (!ctx || !values)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    const hf_shape& s = ctx->shape;
+    float* target = nullptr;
+    if (tensor == HF_TENSOR_FINAL_NORM)
+        target = ctx->final_norm;
+    else if (tensor == HF_TENSOR_INPUT_NORM || tensor == HF_TENSOR_POST_NORM)
+    {
+        if (layer < 0 || layer >= s.layers)
+            return ctx->fail(HF_E_INVALID, "layer " + std::to_string(layer) + " is outside the decoder");
+        target = tensor == HF_TENSOR_INPUT_NORM ? ctx->layers[layer].in_norm : ctx->layers[layer].post_norm;
+    }
+    else
+        return ctx->fail(HF_E_INVALID, "tensor " + std::to_string(tensor) + " is not an fp32 norm weight");
+    if (count != (uint64_t) s.width)
+        return ctx->fail(HF_E_SHAPE, "a norm weight holds " + std::to_string(s.width) + " values");
+    const int rc = ctx->cuda(cudaMemcpy(target, values, count * sizeof(float), cudaMemcpyHostToDevice), "norm upload");
+    if (rc)
+        return rc;
+    ctx->loaded[tensor == HF_TENSOR_FINAL_NORM ? s.layers : layer] |= 1u << tensor;
+    return HF_OK;
+}
+
+int hf_cuda_prepared(const hf_ctx* ctx)
+{
+    return ctx && ctx->all_loaded() ? 1 : 0;
+}
+
+int hf_cuda_begin_sequence(hf_ctx* ctx)
+{
+    if (!ctx)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    return ctx->set_position(0);
+}
+
+int hf_cuda_position(const hf_ctx* ctx)
+{
+    return ctx ? ctx->position : HF_E_INVALID;
+}
+
+int hf_cuda_step(hf_ctx* ctx, const uint32_t* tokens, int count, float* logits, float* hidden)
+{
+    if (!ctx || !tokens)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    const hf_shape& s = ctx->shape;
+    if (!ctx->all_loaded())
+        return ctx->fail(HF_E_NOT_READY, "this decoder has not been prepared: every weight must be uploaded");
+    if (count <= 0)
+        return ctx->fail(HF_E_INVALID, "a decoder step needs at least one token");
+    if (count > ctx->capacity)
+        return ctx->fail(HF_E_CAPACITY, "this step carries " + std::to_string(count) + " rows and the intermediates hold "
+                                            + std::to_string(ctx->capacity) + "; a longer prompt is fed in blocks");
+    if (ctx->position + count > s.max_positions)
+        return ctx->fail(HF_E_WINDOW, "this step would carry the sequence to " + std::to_string(ctx->position + count)
+                                          + " tokens, past the " + std::to_string(s.max_positions)
+                                          + " this decoder was built for");
+    int rc = check_tokens(ctx, tokens, count);
+    if (rc)
+        return rc;
+
+    rc = ctx->cuda(cudaMemcpyAsync(ctx->slots + ctx->position, tokens, (size_t) count * 4, cudaMemcpyHostToDevice,
+                                   ctx->stream),
+                   "token upload");
+    if (rc)
+        return rc;
+    const int first = ctx->position;
+    if (count == 1 && ctx->fast)
+    {
+        cudaGraphExec_t exec;
+        rc = ctx->graph_for(ctx->splits_for(first + 1), &exec);
+        if (!rc)
+            rc = ctx->cuda(cudaGraphLaunch(exec, ctx->stream), "graph launch");
+    }
+    else
+        rc = ctx->enqueue_rows(count, true);
+    if (rc)
+        return rc;
+    ctx->position += count;
+
+    if (hidden)
+    {
+        // Decoder::hiddenStates: the rows after the final norm.
+        rc = ctx->cuda(launch(false, rms_norm_rows, dim3(count), dim3(256), 0, ctx->stream, (const float*) ctx->hidden,
+                              (const float*) ctx->final_norm, s.width, s.rms_eps, ctx->normed),
+                       "norm launch");
+        if (!rc)
+            rc = ctx->cuda(cudaMemcpyAsync(hidden, ctx->normed, (size_t) count * s.width * 4, cudaMemcpyDeviceToHost,
+                                           ctx->stream),
+                           "hidden readback");
+        if (rc)
+            return rc;
+    }
+    if (logits)
+    {
+        rc = ctx->cuda(cudaMemcpyAsync(logits, ctx->logits, (size_t) count * s.vocab * 4, cudaMemcpyDeviceToHost,
+                                       ctx->stream),
+                       "logits readback");
+        if (rc)
+            return rc;
+    }
+    return ctx->sync();
+}
+
+int hf_cuda_argmax(hf_ctx* ctx, const float* logits, const float* mask, int rows, int row_length, uint32_t* indices)
+{
+    if (!ctx || !logits || !indices || rows <= 0 || row_length <= 0)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    const int parts = std::max(1, std::min(64, (row_length + 2047) / 2048));
+    float* d_logits = nullptr;
+    float* d_mask = nullptr;
+    float* d_cv = nullptr;
+    unsigned* d_ci = nullptr;
+    unsigned* d_out = nullptr;
+    int rc = device_alloc(ctx, &d_logits, (size_t) rows * row_length, "argmax input");
+    if (!rc && mask)
+        rc = device_alloc(ctx, &d_mask, (size_t) row_length, "argmax mask");
+    if (!rc)
+        rc = device_alloc(ctx, &d_cv, (size_t) rows * parts, "argmax candidates");
+    if (!rc)
+        rc = device_alloc(ctx, &d_ci, (size_t) rows * parts, "argmax candidates");
+    if (!rc)
+        rc = device_alloc(ctx, &d_out, (size_t) rows, "argmax output");
+    if (!rc)
+        rc = ctx->cuda(cudaMemcpyAsync(d_logits, logits, (size_t) rows * row_length * 4, cudaMemcpyHostToDevice,
+                                       ctx->stream),
+                       "argmax upload");
+    if (!rc && mask)
+        rc = ctx->cuda(cudaMemcpyAsync(d_mask, mask, (size_t) row_length * 4, cudaMemcpyHostToDevice, ctx->stream),
+                       "argmax upload");
+    if (!rc)
+        rc = ctx->cuda(launch(false, argmax_partial, dim3(parts, rows), dim3(256), 0, ctx->stream,
+                              (const float*) d_logits, row_length, (const float*) d_mask, parts, d_cv, d_ci),
+                       "argmax launch");
+    if (!rc)
+        rc = ctx->cuda(launch(true, argmax_final, dim3(rows), dim3(32), 0, ctx->stream, (const float*) d_cv,
+                              (const unsigned*) d_ci, parts, rows, d_out, (unsigned*) nullptr, (unsigned*) nullptr, 0),
+                       "argmax launch");
+    if (!rc)
+        rc = ctx->cuda(cudaMemcpyAsync(indices, d_out, (size_t) rows * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                       "argmax readback");
+    if (!rc)
+        rc = ctx->sync();
+    void* buffers[] = {d_logits, d_mask, d_cv, d_ci, d_out};
+    for (void* b: buffers)
+        if (b)
+            cudaFree(b);
+    return rc;
+}
+
+int hf_cuda_prefill_async(hf_ctx* ctx, const uint32_t* prompt, int prompt_length)
+{
+    if (!ctx || !prompt)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    const hf_shape& s = ctx->shape;
+    if (!ctx->all_loaded())
+        return ctx->fail(HF_E_NOT_READY, "this decoder has not been prepared: every weight must be uploaded");
+    if (prompt_length <= 0)
+        return ctx->fail(HF_E_INVALID, "a run needs at least one prompt token");
+    if (prompt_length > s.max_positions)
+        return ctx->fail(HF_E_WINDOW, "this prompt holds " + std::to_string(prompt_length)
+                                          + " tokens and the window is " + std::to_string(s.max_positions));
+    int rc = check_tokens(ctx, prompt, prompt_length);
+    if (rc)
+        return rc;
+    rc = ctx->set_position(0);
+    if (rc)
+        return rc;
+    rc = ctx->cuda(cudaMemcpyAsync(ctx->slots, prompt, (size_t) prompt_length * 4, cudaMemcpyHostToDevice, ctx->stream),
+                   "prompt upload");
+    if (rc)
+        return rc;
+    return ctx->enqueue_prompt(prompt_length, false);
+}
+
+int hf_cuda_decode_async(hf_ctx* ctx, int steps)
+{
+    if (!ctx || steps < 0)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    if (!ctx->all_loaded())
+        return ctx->fail(HF_E_NOT_READY, "this decoder has not been prepared: every weight must be uploaded");
+    if (ctx->position + steps > ctx->shape.max_positions)
+        return ctx->fail(HF_E_WINDOW, "these steps would carry the sequence past the window");
+    if (ctx->position == 0 && steps > 0)
+        return ctx->fail(HF_E_INVALID, "a decode step follows a prefill: the sequence is empty");
+    for (int i = 0; i < steps; ++i)
+    {
+        int rc;
+        if (ctx->fast)
+        {
+            cudaGraphExec_t exec;
+            rc = ctx->graph_for(ctx->splits_for(ctx->position + 1), &exec);
+            if (!rc)
+                rc = ctx->cuda(cudaGraphLaunch(exec, ctx->stream), "graph launch");
+        }
+        else
+            rc = ctx->enqueue_rows(1, false);
+        if (rc)
+            return rc;
+        ctx->position += 1;
+    }
+    return HF_OK;
+}
+
+int hf_cuda_read_slots(hf_ctx* ctx, int first, int count, uint32_t* out)
+{
+    if (!ctx || !out || first < 0 || count < 0 || first + count > ctx->shape.max_positions + 1)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    int rc = ctx->cuda(cudaMemcpyAsync(out, ctx->slots + first, (size_t) count * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                       "slot readback");
+    if (rc)
+        return rc;
+    return ctx->sync();
+}
+
+int hf_cuda_sync(hf_ctx* ctx)
+{
+    if (!ctx)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    return ctx->sync();
+}
+
+int hf_cuda_generate_greedy(hf_ctx* ctx, const uint32_t* prompt, int prompt_length, int max_tokens, int eos,
+                            uint32_t* tokens_out, int* count_out)
+{
+    if (!ctx || !prompt || !count_out || (max_tokens > 0 && !tokens_out))
+        return HF_E_INVALID;
+    *count_out = 0;
+    int rc = hf_cuda_prefill_async(ctx, prompt, prompt_length);
+    if (rc)
+        return rc;
+    const int window = ctx->shape.max_positions - prompt_length;
+    const int limit = max_tokens > 0 ? std::min(max_tokens, window) : window;
+    if (limit <= 0)
+        return ctx->sync();
+
+    // Token j is in slot prompt_length + j; the prefill wrote token 0 and
+    // decode step j writes token j. Steps go out in chunks; the host reads the
+    // chunk's tokens for the end-of-sequence check (Gemma.cpp:459-533).
+    int produced = 1, emitted = 0;
+    std::vector<uint32_t> chunk;
+    while (true)
+    {
+        const int batch = std::min(16, limit - produced);
+        if (batch > 0)
+        {
+            rc = hf_cuda_decode_async(ctx, batch);
+            if (rc)
+                return rc;
+        }
+        const int ready = produced + std::max(batch, 0);
+        chunk.resize((size_t) (ready - emitted));
+        rc = hf_cuda_read_slots(ctx, prompt_length + emitted, ready - emitted, chunk.data());
+        if (rc)
+            return rc;
+        for (int j = 0; j < ready - emitted; ++j)
+        {
+            if (eos >= 0 && chunk[j] == (uint32_t) eos)
+            {
+                *count_out = emitted + j;
+                return HF_OK;
+            }
+            tokens_out[emitted + j] = chunk[j];
+        }
+        emitted = ready;
+        produced = ready;
+        if (produced >= limit)
+            break;
+    }
+    *count_out = emitted;
+    return HF_OK;
+}
+
+void* hf_cuda_stream(const hf_ctx* ctx)
+{
+    return ctx ? (void*) ctx->stream : nullptr;
+}
+
+int hf_cuda_decode_launches(const hf_ctx* ctx)
+{
+    if (!ctx)
+        return HF_E_INVALID;
+    if (!ctx->fast)
+        return 3 + ctx->shape.layers * 7 + 3;
+    return ctx->decode_launch_count(ctx->splits_for(ctx->position + 1));
+}
+
+int hf_cuda_fast_path(const hf_ctx* ctx)
+{
+    return ctx && ctx->fast ? 1 : 0;
+}
+
+int hf_cuda_time_kernel(hf_ctx* ctx, int kernel, int reps, float* mean_us, double* bytes_per_launch)
+{
+    if (!ctx || !mean_us || reps <= 0 || kernel < HF_KERNEL_QKV || kernel > HF_KERNEL_LOGITS)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    if (!ctx->fast)
+        return ctx->fail(HF_E_INVALID, "the timing hook measures the streaming decode kernels");
+    if (!ctx->all_loaded())
+        return ctx->fail(HF_E_NOT_READY, "this decoder has not been prepared: every weight must be uploaded");
+    const hf_shape& s = ctx->shape;
+    if (ctx->position + 1 > s.max_positions)
+        return ctx->fail(HF_E_WINDOW, "the timing hook needs one free position");
+    const int keys = ctx->position + 1;
+    const int splits = ctx->splits_for(keys);
+    const double kv = 4.0 * ctx->kv_width();
+    auto q8 = [](double rows, double cols) { return rows * cols * 17.0 / 16.0; };
+    double bytes = 0;
+    switch (kernel)
+    {
+    case HF_KERNEL_QKV: bytes = q8(ctx->qkv_rows(), s.width) + 8.0 * s.width + 4.0 * ctx->query_width() + 2 * kv; break;
+    case HF_KERNEL_ATTENTION: bytes = 2 * kv * keys + 8.0 * ctx->query_width(); break;
+    case HF_KERNEL_OUTPUT: bytes = q8(s.width, ctx->query_width()) + 4.0 * ctx->query_width() + 8.0 * s.width; break;
+    case HF_KERNEL_GATE_UP: bytes = q8(2.0 * s.intermediate, s.width) + 8.0 * s.width + 4.0 * s.intermediate; break;
+    case HF_KERNEL_DOWN: bytes = q8(s.width, s.intermediate) + 4.0 * s.intermediate + 8.0 * s.width; break;
+    default: bytes = q8(s.vocab, s.width) + 8.0 * s.width + 4.0 * s.vocab; break;
+    }
+    auto one = [&](int i) -> cudaError_t {
+        const int l = i % s.layers;
+        switch (kernel)
+        {
+        case HF_KERNEL_QKV: return ctx->launch_qkv(l);
+        case HF_KERNEL_ATTENTION: return ctx->launch_decode_attention(l, splits);
+        case HF_KERNEL_OUTPUT: return ctx->launch_output(l);
+        case HF_KERNEL_GATE_UP: return ctx->launch_gate_up(l);
+        case HF_KERNEL_DOWN: return ctx->launch_down(l);
+        default: return ctx->launch_logits(0); // advance 0: the position stays
+        }
+    };
+    for (int i = 0; i < 3; ++i)
+        if (int rc = ctx->cuda(one(i), "timed launch"))
+            return rc;
+    cudaEvent_t start, stop;
+    cudaEventCreate(&start);
+    cudaEventCreate(&stop);
+    cudaEventRecord(start, ctx->stream);
+    int rc = HF_OK;
+    for (int i = 0; i < reps && !rc; ++i)
+        rc = ctx->cuda(one(i), "timed launch");
+    cudaEventRecord(stop, ctx->stream);
+    if (!rc)
+        rc = ctx->sync();
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, start, stop);
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+    if (rc)
+        return rc;
+    *mean_us = ms * 1000.f / (float) reps;
+    if (bytes_per_launch)
+        *bytes_per_launch = bytes;
+    return HF_OK;
+}
+
+int hf_cuda_linear_q8(const float* input, const uint8_t* weights, const float* bias, float* output, uint32_t inner,
+                      uint32_t outputs, uint32_t rows, int gelu, int residual, void* stream)
+{
+    if (!input || !weights || !output || inner == 0 || outputs == 0 || rows == 0)
+        return HF_E_INVALID;
+    if (inner % 32 != 0 || ((uint64_t) inner * outputs) % 64 != 0)
+        return HF_E_SHAPE;
+    int device = 0;
+    cudaGetDevice(&device);
+    configure_once(device);
+    const int sms = sm_count(device);
+    cudaStream_t s = (cudaStream_t) stream;
+
+    GemvArgs a = {};
+    a.w = weights;
+    a.scales = reinterpret_cast<const __half*>(weights + (size_t) inner * outputs);
+    a.N = (int) outputs;
+    a.K = (int) inner;
+    a.M = (int) rows;
+    a.x = input;
+    a.bias = bias;
+    a.out = output;
+    const Epi e = gelu ? Epi::Gelu : (residual ? Epi::Residual : Epi::Store);
+    // gelu then residual (Linear.h:213-217) has no fused form; it is one rare
+    // combination, run as a Store with gelu into the output after the sum.
+    if (gelu && residual)
+        return HF_E_INVALID;
+
+    const bool aligned = ((uintptr_t) weights % 16 == 0) && ((uintptr_t) input % 16 == 0);
+    cudaError_t err = cudaSuccess;
+    bool launched = false;
+    if (rows == 1 && aligned)
+    {
+        const int grid = stream_grid((int) inner, (int) outputs, sms);
+        if (e == Epi::Store)
+            launched = stream_product<Epi::Store>((int) inner, false, grid, s, a, &err);
+        else if (e == Epi::Residual)
+            launched = stream_product<Epi::Residual>((int) inner, false, grid, s, a, &err);
+        else
+            launched = stream_product<Epi::Gelu>((int) inner, false, grid, s, a, &err);
+    }
+    if (!launched)
+    {
+        if (e == Epi::Store)
+            err = generic_product<Epi::Store>(false, (int) outputs, s, a, sms);
+        else if (e == Epi::Residual)
+            err = generic_product<Epi::Residual>(false, (int) outputs, s, a, sms);
+        else
+            err = generic_product<Epi::Gelu>(false, (int) outputs, s, a, sms);
+    }
+    return err == cudaSuccess ? HF_OK : HF_E_CUDA;
+}
+
+int hf_cuda_quantize_q8(const float* values, int64_t first, int64_t count, int64_t element_count, uint8_t* destination,
+                        void* stream)
+{
+    if (!values || !destination || first < 0 || count < 0 || first % 32 || count % 32 || first + count > element_count)
+        return HF_E_INVALID;
+    if (count == 0)
+        return HF_OK;
+    const long long threads = count; // one lane per element, a warp per block
+    const int grid = (int) ((threads + 255) / 256);
+    quantize_q8<<<grid, 256, 0, (cudaStream_t) stream>>>(values, first, count, element_count, destination);
+    return cudaGetLastError() == cudaSuccess ? HF_OK : HF_E_CUDA;
+}
+}

@@ -1,0 +1,236 @@
+// The small kernels around the products: the token gather, a row RMSNorm for
+// multi-row steps, the two-stage argmax, the device-layout permutation of
+// uploaded weights, and the on-device Q8_0 quantizer.
+#pragma once
+
+#include "common.cuh"
+
+namespace hfk
+{
+// Kernels/Embed.h:45-77 over the Q8_0 tied table: h = scale * (q * s), with
+// token ids read from the sequence slots at the step's position.
+__global__ void __launch_bounds__(256) embed_q8(const uint8_t* table, const __half* scales, int width, int vocab,
+                                                 float scale, const unsigned* slots, const unsigned* state, int rows,
+                                                 float* out, unsigned* err)
+{
+    pdl_wait();
+    const unsigned position = state ? *(volatile const unsigned*) state : 0u;
+    pdl_trigger();
+    const int row = blockIdx.y;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= rows || c >= width)
+        return;
+    unsigned token = slots[position + row];
+    if (token >= (unsigned) vocab)
+    {
+        if (c == 0)
+            flag_error(err, kErrTokenRange);
+        token = 0;
+    }
+    const size_t element = (size_t) token * width + c;
+    const float gathered = (float) (int) (int8_t) table[element] * __half2float(scales[element / kBlock]);
+    out[(size_t) row * width + c] = scale * gathered;
+}
+
+// Kernels/RMSNorm.h:51-81: one CTA per row, a fixed fold order.
+__global__ void __launch_bounds__(256) rms_norm_rows(const float* x, const float* weight, int width, float eps,
+                                                      float* out)
+{
+    __shared__ float red[8];
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.x;
+    const float* xr = x + (size_t) row * width;
+    float s = 0.f;
+    for (int c = threadIdx.x; c < width; c += blockDim.x)
+        s += xr[c] * xr[c];
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0)
+        red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float total = 0.f;
+    for (int w = 0; w < (int) (blockDim.x >> 5); ++w)
+        total += red[w];
+    const float scale = 1.f / sqrtf(total / (float) width + eps);
+    for (int c = threadIdx.x; c < width; c += blockDim.x)
+        out[(size_t) row * width + c] = xr[c] * scale * (1.f + weight[c]);
+}
+
+// Kernels/Argmax.h:82-140: each CTA scans a strided share of its row; the
+// candidate is the first index of the largest allowed value.
+__global__ void __launch_bounds__(256) argmax_partial(const float* logits, int row_length, const float* mask,
+                                                       int parts, float* cand_val, unsigned* cand_idx)
+{
+    __shared__ float sv[8];
+    __shared__ unsigned si[8];
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.y, part = blockIdx.x;
+    const float* lr = logits + (size_t) row * row_length;
+    float best = -INFINITY;
+    unsigned best_i = 0xFFFFFFFFu;
+    for (int i = part * blockDim.x + threadIdx.x; i < row_length; i += parts * blockDim.x)
+    {
+        const float v = lr[i];
+        if (mask && mask[i] != 0.f)
+            continue;
+        if (best_i == 0xFFFFFFFFu || better_candidate(v, (unsigned) i, best, best_i))
+        {
+            best = v;
+            best_i = (unsigned) i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+    {
+        const float v = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+        const unsigned i = __shfl_xor_sync(0xFFFFFFFFu, best_i, o);
+        if (i != 0xFFFFFFFFu && (best_i == 0xFFFFFFFFu || better_candidate(v, i, best, best_i)))
+        {
+            best = v;
+            best_i = i;
+        }
+    }
+    if ((threadIdx.x & 31) == 0)
+    {
+        sv[threadIdx.x >> 5] = best;
+        si[threadIdx.x >> 5] = best_i;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+    {
+        for (int w = 1; w < (int) (blockDim.x >> 5); ++w)
+            if (si[w] != 0xFFFFFFFFu && (best_i == 0xFFFFFFFFu || better_candidate(sv[w], si[w], best, best_i)))
+            {
+                best = sv[w];
+                best_i = si[w];
+            }
+        cand_val[(size_t) row * parts + part] = best;
+        cand_idx[(size_t) row * parts + part] = best_i;
+    }
+}
+
+// Kernels/Argmax.h:144-200: one warp folds a row's candidates; 0 when nothing
+// was allowed. With `slots`, also writes the token into the sequence slot
+// after the step and advances the position by `advance` rows (one row only).
+__global__ void argmax_final(const float* cand_val, const unsigned* cand_idx, int parts, int rows,
+                             unsigned* indices, unsigned* slots, unsigned* state, int advance)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.x;
+    const int lane = threadIdx.x;
+    float best = -INFINITY;
+    unsigned best_i = 0xFFFFFFFFu;
+    for (int c = lane; c < parts; c += 32)
+    {
+        const float v = cand_val[(size_t) row * parts + c];
+        const unsigned i = cand_idx[(size_t) row * parts + c];
+        if (i != 0xFFFFFFFFu && (best_i == 0xFFFFFFFFu || better_candidate(v, i, best, best_i)))
+        {
+            best = v;
+            best_i = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+    {
+        const float v = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+        const unsigned i = __shfl_xor_sync(0xFFFFFFFFu, best_i, o);
+        if (i != 0xFFFFFFFFu && (best_i == 0xFFFFFFFFu || better_candidate(v, i, best, best_i)))
+        {
+            best = v;
+            best_i = i;
+        }
+    }
+    if (lane == 0)
+    {
+        const unsigned token = best_i == 0xFFFFFFFFu ? 0u : best_i;
+        if (indices)
+            indices[row] = token;
+        if (slots && row == rows - 1)
+        {
+            const unsigned position = *state;
+            slots[position + (unsigned) advance] = token;
+            *state = position + (unsigned) advance;
+        }
+    }
+}
+
+// Advances the step position without sampling (a step whose caller only wants
+// logits still moves the sequence on, Decoder.cpp:705).
+__global__ void advance_position(unsigned* state, int advance)
+{
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0 && blockIdx.x == 0)
+        *state += (unsigned) advance;
+}
+
+// Copies `rows` rows of a reference two-region Q8_0 tensor into a device
+// tensor of `dst_rows` rows starting at `dst_row0`, applying the row order the
+// paired epilogues read:
+//   mode 0: identity;
+//   mode 1 (per head of `group` rows): device row 2j + b <- row j + b * group / 2;
+//   mode 2 (whole tensor, gate/up): device row 2j + b <- row j + b * rows / 2.
+__global__ void permute_q8_rows(const uint8_t* src, int rows, int K, uint8_t* dst, int dst_rows, int dst_row0,
+                                int mode, int group)
+{
+    const int g = blockIdx.x; // device row within this tensor's segment
+    if (g >= rows)
+        return;
+    int source = g;
+    if (mode == 1)
+    {
+        const int block = g / group, i = g % group;
+        source = block * group + i / 2 + (i % 2) * (group / 2);
+    }
+    else if (mode == 2)
+        source = g / 2 + (g % 2) * (rows / 2);
+
+    const uint4* sq = reinterpret_cast<const uint4*>(src + (size_t) source * K);
+    uint4* dq = reinterpret_cast<uint4*>(dst + (size_t) (dst_row0 + g) * K);
+    for (int i = threadIdx.x; i < K / 16; i += blockDim.x)
+        dq[i] = sq[i];
+    const __half* ss = reinterpret_cast<const __half*>(src + (size_t) rows * K) + (size_t) source * (K / kBlock);
+    __half* ds = reinterpret_cast<__half*>(dst + (size_t) dst_rows * K) + (size_t) (dst_row0 + g) * (K / kBlock);
+    for (int i = threadIdx.x; i < K / kBlock; i += blockDim.x)
+        ds[i] = ss[i];
+}
+
+// Int8Blocks.cpp:114-136 on the device, one warp per block of 32: the same
+// fp16 round-to-nearest-even scale and the same double division with
+// ties-to-even rounding, so the bytes equal the host quantizer's.
+__global__ void __launch_bounds__(256) quantize_q8(const float* values, long long first, long long count,
+                                                    long long element_count, uint8_t* destination)
+{
+    const long long block = ((long long) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (block * kBlock >= count)
+        return;
+    const float x = values[block * kBlock + lane];
+    float largest = fabsf(x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+        largest = fmaxf(largest, __shfl_xor_sync(0xFFFFFFFFu, largest, o));
+    const __half narrowed = __float2half_rn(largest / 127.0f);
+    const float scale = __half2float(narrowed);
+    const bool usable = scale > 0.f && isfinite(scale);
+    const unsigned short bits = usable ? __half_as_ushort(narrowed) : (unsigned short) 0;
+    const long long element = first + block * kBlock;
+    uint8_t byte = 0;
+    if (usable)
+    {
+        double rounded = rint((double) x / (double) scale);
+        rounded = fmin(fmax(rounded, -127.0), 127.0);
+        byte = (uint8_t) (int8_t) rounded;
+    }
+    destination[element + lane] = byte;
+    if (lane == 0)
+    {
+        const long long at = element_count + 2 * (element / kBlock);
+        destination[at] = (uint8_t) (bits & 0xFFu);
+        destination[at + 1] = (uint8_t) (bits >> 8);
+    }
+}
+} // namespace hfk

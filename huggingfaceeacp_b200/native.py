@@ -1,0 +1,429 @@
+"""ctypes bindings to the two native libraries of this package.
+
+``libhf_cuda.so`` is the sm_100a engine (include/hf_cuda.h); ``libhf_host.so``
+holds the Q8_0 quantizer and the seeded weight generator (include/hf_host.h).
+Both are built in-tree by ``huggingfaceeacp_b200.build`` into
+``huggingfaceeacp_b200/lib``. There is no fallback: a missing library is an
+ImportError-grade failure, raised loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib")
+
+HF_OK = 0
+HF_E_INVALID = -1
+HF_E_SHAPE = -2
+HF_E_CAPACITY = -3
+HF_E_WINDOW = -4
+HF_E_NOT_READY = -5
+HF_E_CUDA = -6
+HF_E_DEVICE = -7
+HF_E_TOKEN = -8
+
+# Decode-step kernels the timing hook measures (hf_cuda.h HF_KERNEL_*).
+KERNEL_QKV, KERNEL_ATTENTION, KERNEL_OUTPUT, KERNEL_GATE_UP, KERNEL_DOWN, KERNEL_LOGITS = range(6)
+KERNEL_NAMES = ("qkv_rope", "attention", "o_proj_residual", "gate_up_geglu", "down_residual", "logits_argmax")
+
+# Tensor ids (DecoderWeights.h:53-116).
+EMBEDDING, FINAL_NORM, INPUT_NORM, QUERY, KEY, VALUE, OUTPUT, GATE_UP, DOWN, POST_NORM = range(10)
+Q8_TENSORS = (QUERY, KEY, VALUE, OUTPUT, GATE_UP, DOWN)
+NORM_TENSORS = (INPUT_NORM, POST_NORM)
+
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_vp = ctypes.c_void_p
+
+
+class HFError(RuntimeError):
+    """A non-zero status from the C-ABI; ``code`` is the HF_E* value."""
+
+    def __init__(self, code: int, text: str):
+        super().__init__(f"[{code}] {text}")
+        self.code = code
+
+
+class ShapeStruct(ctypes.Structure):
+    _fields_ = [
+        ("width", ctypes.c_int32),
+        ("heads", ctypes.c_int32),
+        ("kv_heads", ctypes.c_int32),
+        ("head_width", ctypes.c_int32),
+        ("layers", ctypes.c_int32),
+        ("intermediate", ctypes.c_int32),
+        ("vocab", ctypes.c_int32),
+        ("max_positions", ctypes.c_int32),
+        ("max_step_rows", ctypes.c_int32),
+        ("rms_eps", ctypes.c_float),
+        ("rope_theta", ctypes.c_double),
+        ("embed_scale", ctypes.c_float),
+    ]
+
+
+@dataclass(frozen=True)
+class DecoderShape:
+    """HF::DecoderShape (Decoder/DecoderShape.h:42-110)."""
+
+    width: int
+    heads: int
+    kv_heads: int
+    head_width: int
+    layers: int
+    intermediate: int
+    vocab: int
+    max_positions: int
+    max_step_rows: int = 0
+    rms_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    embed_scale: float | None = None  # sqrtf(width) (GemmaConfig.cpp:123-126)
+
+    @property
+    def scale(self) -> float:
+        if self.embed_scale is not None:
+            return float(np.float32(self.embed_scale))
+        return float(np.sqrt(np.float32(self.width), dtype=np.float32))
+
+    @property
+    def query_width(self) -> int:
+        return self.heads * self.head_width
+
+    @property
+    def kv_width(self) -> int:
+        return self.kv_heads * self.head_width
+
+    def struct(self) -> ShapeStruct:
+        return ShapeStruct(self.width, self.heads, self.kv_heads, self.head_width, self.layers, self.intermediate,
+                           self.vocab, self.max_positions, self.max_step_rows, self.rms_eps, self.rope_theta,
+                           self.scale)
+
+    def tensor_shape(self, tensor: int) -> tuple[int, ...]:
+        return {
+            EMBEDDING: (self.vocab, self.width),
+            FINAL_NORM: (self.width,),
+            INPUT_NORM: (self.width,),
+            POST_NORM: (self.width,),
+            QUERY: (self.query_width, self.width),
+            KEY: (self.kv_width, self.width),
+            VALUE: (self.kv_width, self.width),
+            OUTPUT: (self.width, self.query_width),
+            GATE_UP: (2 * self.intermediate, self.width),
+            DOWN: (self.width, self.intermediate),
+        }[tensor]
+
+    def replace(self, **changes) -> "DecoderShape":
+        values = {f: getattr(self, f) for f in self.__dataclass_fields__}
+        values.update(changes)
+        return DecoderShape(**values)
+
+
+# google/gemma-2b (GemmaConfig.h:45-65).
+GEMMA_2B = DecoderShape(width=2048, heads=8, kv_heads=1, head_width=256, layers=18, intermediate=16384,
+                        vocab=256000, max_positions=8192)
+
+# The reference's synthetic test decoder (Tests/Decoder/Common.h:38-72): the
+# int8 variant has a 64-wide feed-forward.
+SMALL_INT8 = DecoderShape(width=32, heads=2, kv_heads=1, head_width=16, layers=2, intermediate=64, vocab=64,
+                          max_positions=16)
+
+
+def _load(name: str) -> ctypes.CDLL:
+    path = os.path.join(LIB_DIR, name)
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is not built; run python -c 'import __graft_entry__ as g; g.build()'")
+    return ctypes.CDLL(path)
+
+
+_host = None
+_cuda = None
+
+
+def host() -> ctypes.CDLL:
+    global _host
+    if _host is None:
+        lib = _load("libhf_host.so")
+        lib.hf_int8_block_count.restype = ctypes.c_int64
+        lib.hf_int8_block_count.argtypes = [ctypes.c_int64]
+        lib.hf_int8_blocks_byte_count.restype = ctypes.c_int64
+        lib.hf_int8_blocks_byte_count.argtypes = [ctypes.c_int64]
+        lib.hf_quantizes_as_int8_blocks.argtypes = [ctypes.c_int64, ctypes.c_int64]
+        lib.hf_quantize_int8_blocks.argtypes = [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, ctypes.c_int]
+        lib.hf_dequantize_int8_blocks.argtypes = [_vp, ctypes.c_int64, _vp]
+        lib.hf_half_from_float.restype = ctypes.c_uint16
+        lib.hf_half_from_float.argtypes = [ctypes.c_float]
+        lib.hf_half_to_float.restype = ctypes.c_float
+        lib.hf_half_to_float.argtypes = [ctypes.c_uint16]
+        lib.hf_synthetic_stream.restype = ctypes.c_uint64
+        lib.hf_synthetic_stream.argtypes = [ctypes.c_int, ctypes.c_int]
+        lib.hf_synthetic_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64,
+                                            ctypes.c_double, _vp, ctypes.c_int]
+        lib.hf_synthetic_tokens.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, _vp]
+        lib.hf_host_threads.restype = ctypes.c_int
+        _host = lib
+    return _host
+
+
+def cuda() -> ctypes.CDLL:
+    global _cuda
+    if _cuda is None:
+        lib = _load("libhf_cuda.so")
+        lib.hf_cuda_device_count.argtypes = [ctypes.POINTER(ctypes.c_int)]
+        lib.hf_cuda_create.argtypes = [ctypes.c_int, ctypes.POINTER(ShapeStruct), ctypes.POINTER(_vp)]
+        lib.hf_cuda_destroy.argtypes = [_vp]
+        lib.hf_cuda_destroy.restype = None
+        lib.hf_cuda_last_error.argtypes = [_vp]
+        lib.hf_cuda_last_error.restype = ctypes.c_char_p
+        lib.hf_cuda_upload_q8.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_uint64]
+        lib.hf_cuda_upload_f32.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_uint64]
+        lib.hf_cuda_prepared.argtypes = [_vp]
+        lib.hf_cuda_begin_sequence.argtypes = [_vp]
+        lib.hf_cuda_position.argtypes = [_vp]
+        lib.hf_cuda_step.argtypes = [_vp, _vp, ctypes.c_int, _vp, _vp]
+        lib.hf_cuda_argmax.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]
+        lib.hf_cuda_generate_greedy.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp,
+                                                ctypes.POINTER(ctypes.c_int)]
+        lib.hf_cuda_prefill_async.argtypes = [_vp, _vp, ctypes.c_int]
+        lib.hf_cuda_decode_async.argtypes = [_vp, ctypes.c_int]
+        lib.hf_cuda_read_slots.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp]
+        lib.hf_cuda_sync.argtypes = [_vp]
+        lib.hf_cuda_stream.argtypes = [_vp]
+        lib.hf_cuda_stream.restype = _vp
+        lib.hf_cuda_decode_launches.argtypes = [_vp]
+        lib.hf_cuda_fast_path.argtypes = [_vp]
+        lib.hf_cuda_linear_q8.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                          ctypes.c_int, ctypes.c_int, _vp]
+        lib.hf_cuda_quantize_q8.argtypes = [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp]
+        lib.hf_cuda_time_kernel.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float),
+                                            ctypes.POINTER(ctypes.c_double)]
+        _cuda = lib
+    return _cuda
+
+
+def _ptr(array: np.ndarray | None):
+    if array is None:
+        return None
+    assert array.flags["C_CONTIGUOUS"]
+    return array.ctypes.data_as(_vp)
+
+
+# ---------------------------------------------------------------------------
+# Q8_0 blocks on the host (Kernels/Int8Blocks.h).
+
+def int8_blocks_byte_count(elements: int) -> int:
+    return int(host().hf_int8_blocks_byte_count(elements))
+
+
+def quantizes_as_int8_blocks(contiguous: int, elements: int) -> bool:
+    return bool(host().hf_quantizes_as_int8_blocks(contiguous, elements))
+
+
+def quantize(values: np.ndarray, threads: int = 0) -> np.ndarray:
+    values = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+    out = np.zeros(int8_blocks_byte_count(values.size), dtype=np.uint8)
+    rc = host().hf_quantize_int8_blocks(_ptr(values), 0, values.size, values.size, _ptr(out), threads)
+    if rc:
+        raise HFError(rc, "quantize refused")
+    return out
+
+
+def dequantize(stored: np.ndarray, elements: int) -> np.ndarray:
+    out = np.zeros(elements, dtype=np.float32)
+    rc = host().hf_dequantize_int8_blocks(_ptr(np.ascontiguousarray(stored, dtype=np.uint8)), elements, _ptr(out))
+    if rc:
+        raise HFError(rc, "dequantize refused")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Seeded synthetic weights (hf_host.h): linear weights and the embedding
+# N(0, 0.02), norm weights N(0, 0.1).
+
+LINEAR_STDDEV = 0.02
+NORM_STDDEV = 0.1
+
+
+def synthetic_normal(seed: int, tensor: int, layer: int, count: int, stddev: float, threads: int = 0,
+                     first: int = 0) -> np.ndarray:
+    out = np.empty(count, dtype=np.float32)
+    stream = host().hf_synthetic_stream(tensor, layer)
+    rc = host().hf_synthetic_normal(seed, stream, first, count, stddev, _ptr(out), threads)
+    if rc:
+        raise HFError(rc, "generator refused")
+    return out
+
+
+def synthetic_tokens(seed: int, count: int, vocab: int) -> np.ndarray:
+    out = np.empty(count, dtype=np.uint32)
+    rc = host().hf_synthetic_tokens(seed, count, vocab, _ptr(out))
+    if rc:
+        raise HFError(rc, "token generator refused")
+    return out
+
+
+def synthetic_tensor(shape: DecoderShape, tensor: int, layer: int, seed: int, threads: int = 0) -> np.ndarray:
+    """One tensor of the random-init model: fp32 norms, or Q8_0 bytes."""
+    dims = shape.tensor_shape(tensor)
+    count = int(np.prod(dims))
+    if tensor in (FINAL_NORM, INPUT_NORM, POST_NORM):
+        return synthetic_normal(seed, tensor, layer, count, NORM_STDDEV, threads)
+    values = synthetic_normal(seed, tensor, layer, count, LINEAR_STDDEV, threads)
+    return quantize(values, threads)
+
+
+def model_tensors(shape: DecoderShape):
+    """(tensor, layer) pairs in load order."""
+    yield EMBEDDING, -1
+    yield FINAL_NORM, -1
+    for layer in range(shape.layers):
+        for tensor in (INPUT_NORM, QUERY, KEY, VALUE, OUTPUT, GATE_UP, DOWN, POST_NORM):
+            yield tensor, layer
+
+
+# ---------------------------------------------------------------------------
+
+class Context:
+    """One hf_ctx: a prepared decoder on one device (HF::Decoder + DecoderWeights)."""
+
+    def __init__(self, shape: DecoderShape, device: int = 0):
+        self.lib = cuda()
+        self.shape = shape
+        handle = _vp()
+        struct = shape.struct()
+        rc = self.lib.hf_cuda_create(device, ctypes.byref(struct), ctypes.byref(handle))
+        if rc:
+            raise HFError(rc, "hf_cuda_create refused the shape or the device")
+        self.handle = handle
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.hf_cuda_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def error(self) -> str:
+        text = self.lib.hf_cuda_last_error(self.handle)
+        return text.decode() if text else ""
+
+    def check(self, rc: int):
+        if rc:
+            raise HFError(rc, self.error())
+
+    def upload(self, tensor: int, layer: int, data: np.ndarray):
+        data = np.ascontiguousarray(data)
+        if data.dtype == np.uint8:
+            self.check(self.lib.hf_cuda_upload_q8(self.handle, tensor, layer, _ptr(data), data.size))
+        else:
+            data = data.astype(np.float32, copy=False)
+            self.check(self.lib.hf_cuda_upload_f32(self.handle, tensor, layer, _ptr(data), data.size))
+
+    def load_synthetic(self, seed: int, keep: bool = False, threads: int = 0):
+        """Generates, quantizes and uploads every tensor; returns them when keep."""
+        kept = {}
+        for tensor, layer in model_tensors(self.shape):
+            data = synthetic_tensor(self.shape, tensor, layer, seed, threads)
+            self.upload(tensor, layer, data)
+            if keep:
+                kept[(tensor, layer)] = data
+        return kept
+
+    @property
+    def prepared(self) -> bool:
+        return bool(self.lib.hf_cuda_prepared(self.handle))
+
+    @property
+    def fast_path(self) -> bool:
+        return bool(self.lib.hf_cuda_fast_path(self.handle))
+
+    def begin_sequence(self):
+        self.check(self.lib.hf_cuda_begin_sequence(self.handle))
+
+    @property
+    def position(self) -> int:
+        return int(self.lib.hf_cuda_position(self.handle))
+
+    def step(self, tokens, want_logits=True, want_hidden=True):
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint32).reshape(-1)
+        n = tokens.size
+        logits = np.empty((n, self.shape.vocab), dtype=np.float32) if want_logits else None
+        hidden = np.empty((n, self.shape.width), dtype=np.float32) if want_hidden else None
+        self.check(self.lib.hf_cuda_step(self.handle, _ptr(tokens), n, _ptr(logits), _ptr(hidden)))
+        return logits, hidden
+
+    def argmax(self, logits: np.ndarray, mask: np.ndarray | None = None) -> np.ndarray:
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+        rows, length = (1, logits.size) if logits.ndim == 1 else logits.shape
+        out = np.empty(rows, dtype=np.uint32)
+        m = None if mask is None else np.ascontiguousarray(mask, dtype=np.float32)
+        self.check(self.lib.hf_cuda_argmax(self.handle, _ptr(logits), _ptr(m), rows, length, _ptr(out)))
+        return out
+
+    def generate(self, prompt, max_tokens: int, eos: int = -1) -> np.ndarray:
+        prompt = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.empty(max(max_tokens, 1), dtype=np.uint32)
+        count = ctypes.c_int(0)
+        self.check(self.lib.hf_cuda_generate_greedy(self.handle, _ptr(prompt), prompt.size, max_tokens, eos,
+                                                    _ptr(out), ctypes.byref(count)))
+        return out[: count.value].copy()
+
+    def prefill_async(self, prompt):
+        prompt = np.ascontiguousarray(prompt, dtype=np.uint32)
+        self.check(self.lib.hf_cuda_prefill_async(self.handle, _ptr(prompt), prompt.size))
+
+    def decode_async(self, steps: int):
+        self.check(self.lib.hf_cuda_decode_async(self.handle, steps))
+
+    def read_slots(self, first: int, count: int) -> np.ndarray:
+        out = np.empty(count, dtype=np.uint32)
+        self.check(self.lib.hf_cuda_read_slots(self.handle, first, count, _ptr(out)))
+        return out
+
+    def sync(self):
+        self.check(self.lib.hf_cuda_sync(self.handle))
+
+    @property
+    def stream(self) -> int:
+        return int(self.lib.hf_cuda_stream(self.handle) or 0)
+
+    @property
+    def decode_launches(self) -> int:
+        return int(self.lib.hf_cuda_decode_launches(self.handle))
+
+    def time_kernel(self, kernel: int, reps: int) -> tuple[float, float]:
+        """(mean microseconds, algorithmic bytes) of one decode-step kernel launch."""
+        us = ctypes.c_float(0.0)
+        nbytes = ctypes.c_double(0.0)
+        self.check(self.lib.hf_cuda_time_kernel(self.handle, kernel, reps, ctypes.byref(us), ctypes.byref(nbytes)))
+        return float(us.value), float(nbytes.value)
+
+
+def device_count() -> int:
+    n = ctypes.c_int(0)
+    cuda().hf_cuda_device_count(ctypes.byref(n))
+    return n.value
+
+
+def weight_bytes(shape: DecoderShape) -> int:
+    """Algorithmic Q8_0 weight bytes one decode token streams (layers + tied logits)."""
+    per_layer = sum(int8_blocks_byte_count(int(np.prod(shape.tensor_shape(t)))) for t in Q8_TENSORS)
+    return per_layer * shape.layers + int8_blocks_byte_count(shape.vocab * shape.width)
+
+
+def decode_bytes(shape: DecoderShape, keys: int) -> int:
+    """Algorithmic bytes of one batch-1 decode token attending to `keys` positions."""
+    norms = 4 * shape.width * (2 * shape.layers + 1)
+    kv = 4 * 2 * shape.kv_width * shape.layers
+    return weight_bytes(shape) + norms + kv * keys + kv + 4 * shape.vocab

@@ -1,0 +1,172 @@
+/*
+ * hf_cuda.h — the C-ABI of libhf_cuda.so, the B200 (sm_100a) engine behind
+ * HuggingFaceEACP's Gemma Q8_0 token loop.
+ *
+ * Plain pointers and sizes only. Every function returns an int status (0 = ok,
+ * a negative HF_E* code otherwise); a context's last error text is
+ * hf_cuda_last_error(ctx). Like the reference, every shape, capacity and
+ * window check happens before anything is launched, so a refused call leaves
+ * the sequence, the caches and the caller's buffers untouched
+ * (Decoder.cpp:650-675, ReferenceDecoder.h:418-446).
+ *
+ * Threading: one context per device, one CUDA stream per context, not
+ * thread-safe per context (the reference's GPU layer is main-thread only).
+ * Ownership: the context owns all device memory (weights, KV cache,
+ * intermediates, CUDA graphs); the caller owns every host buffer it passes.
+ */
+#ifndef HF_CUDA_H
+#define HF_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    HF_OK = 0,
+    HF_E_INVALID = -1,   /* a null pointer or an argument out of range */
+    HF_E_SHAPE = -2,     /* DecoderShape::validate refusals; a tensor of the wrong size */
+    HF_E_CAPACITY = -3,  /* more rows than the step capacity (Decoder.cpp:661-665) */
+    HF_E_WINDOW = -4,    /* the step would pass max_positions (Decoder.cpp:670-675) */
+    HF_E_NOT_READY = -5, /* weights missing: the decoder is not prepared (Decoder.cpp:308-313) */
+    HF_E_CUDA = -6,      /* a CUDA runtime error */
+    HF_E_DEVICE = -7,    /* a kernel reported an error through the context's error word */
+    HF_E_TOKEN = -8      /* a token id outside the vocabulary (Gemma.cpp:419-424) */
+};
+
+/* Tensor ids; the names of DecoderWeights / DecoderLayerWeights
+ * (Decoder/DecoderWeights.h:53-116). Q8 tensors arrive in the reference's
+ * two-region Int8Blocks layout; norms as fp32. */
+enum {
+    HF_TENSOR_EMBEDDING = 0,  /* [vocab, width] q8, tied with the logits */
+    HF_TENSOR_FINAL_NORM = 1, /* [width] f32 */
+    HF_TENSOR_INPUT_NORM = 2, /* per layer [width] f32 */
+    HF_TENSOR_QUERY = 3,      /* per layer [heads*head_width, width] q8 */
+    HF_TENSOR_KEY = 4,        /* per layer [kv_heads*head_width, width] q8 */
+    HF_TENSOR_VALUE = 5,      /* per layer [kv_heads*head_width, width] q8 */
+    HF_TENSOR_OUTPUT = 6,     /* per layer [width, heads*head_width] q8 */
+    HF_TENSOR_GATE_UP = 7,    /* per layer [2*intermediate, width] q8, gate rows first */
+    HF_TENSOR_DOWN = 8,       /* per layer [width, intermediate] q8 */
+    HF_TENSOR_POST_NORM = 9   /* per layer [width] f32 */
+};
+
+/* Replaces HF::DecoderShape (Decoder/DecoderShape.h:42-110). */
+typedef struct hf_shape {
+    int32_t width;
+    int32_t heads;
+    int32_t kv_heads;
+    int32_t head_width;
+    int32_t layers;
+    int32_t intermediate;
+    int32_t vocab;
+    int32_t max_positions;
+    int32_t max_step_rows; /* 0 = the whole window (DecoderShape::stepRowCapacity) */
+    float rms_eps;
+    double rope_theta;
+    float embed_scale;
+} hf_shape;
+
+typedef struct hf_ctx hf_ctx;
+
+/* Number of CUDA devices visible to this process. */
+int hf_cuda_device_count(int* count);
+
+/* Replaces HF::Decoder::Decoder(shape) + Decoder::prepare (Decoder.h:72-89):
+ * validates the shape (DecoderShape.cpp:41-92), allocates the KV cache
+ * [layers, max_positions, kv_heads*head_width] fp32, the step intermediates
+ * at the step capacity, the rotary tables (RoPE.cpp:7-34) and the weight
+ * storage, on `device`. */
+int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out);
+void hf_cuda_destroy(hf_ctx* ctx);
+const char* hf_cuda_last_error(const hf_ctx* ctx);
+
+/* Replaces DecoderWeights' per-tensor upload (DecoderWeights.cpp:61-121,
+ * TensorLoader::loadProjectionWeight / loadStackedProjectionWeights). bytes
+ * is exactly hf_int8_blocks_byte_count(rows*cols) for the tensor's shape. */
+int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, uint64_t byte_count);
+int hf_cuda_upload_f32(hf_ctx* ctx, int tensor, int layer, const float* values, uint64_t count);
+/* 1 when every tensor is loaded (Decoder::requirePrepared), else 0. */
+int hf_cuda_prepared(const hf_ctx* ctx);
+
+/* Replaces Decoder::beginSequence / position (Decoder.h:96, 130). */
+int hf_cuda_begin_sequence(hf_ctx* ctx);
+int hf_cuda_position(const hf_ctx* ctx);
+
+/* Replaces Decoder::step (Decoder.h:113-126, Decoder.cpp:644-706): appends
+ * `count` host token ids and, when the pointers are non-null, copies back
+ * count*vocab logits and count*width hidden rows (after the final norm,
+ * Decoder::hiddenStates). Synchronous. */
+int hf_cuda_step(hf_ctx* ctx, const uint32_t* tokens, int count, float* logits, float* hidden);
+
+/* Replaces HF::Argmax::encode (Kernels/Argmax.h:206-257, Argmax.cpp:47-80):
+ * the first index of the largest unmasked value of each of `rows` host rows
+ * (mask non-zero = suppressed, may be null); 0 when everything is masked. */
+int hf_cuda_argmax(hf_ctx* ctx, const float* logits, const float* mask, int rows, int row_length,
+                   uint32_t* indices);
+
+/* Replaces HF::Gemma::generate with greedy sampling (Gemma.cpp:402-533):
+ * begins a sequence, prefills the prompt in blocks of the step capacity,
+ * then decodes with on-device token feedback until `max_tokens` tokens, the
+ * window, or `eos` (not included in the output; eos < 0 = none). Writes the
+ * generated ids to tokens_out (capacity max_tokens) and their number. */
+int hf_cuda_generate_greedy(hf_ctx* ctx, const uint32_t* prompt, int prompt_length, int max_tokens, int eos,
+                            uint32_t* tokens_out, int* count_out);
+
+/* ---- asynchronous hooks (bench and the C++ HF::Gemma loop) -------------- */
+/* Begins a sequence and enqueues the prompt's prefill plus the argmax that
+ * writes the first generated token into slot prompt_length. */
+int hf_cuda_prefill_async(hf_ctx* ctx, const uint32_t* prompt, int prompt_length);
+/* Enqueues `steps` greedy decode steps (CUDA-graph replays), each embedding
+ * the token in slot position and writing its argmax into slot position + 1. */
+int hf_cuda_decode_async(hf_ctx* ctx, int steps);
+/* Synchronises and copies sequence token slots [first, first + count). */
+int hf_cuda_read_slots(hf_ctx* ctx, int first, int count, uint32_t* out);
+/* Waits for the context's stream; reports a kernel-side error as HF_E_DEVICE. */
+int hf_cuda_sync(hf_ctx* ctx);
+/* The context's cudaStream_t (for events), and how many kernels one decode
+ * step launches at the current position. */
+void* hf_cuda_stream(const hf_ctx* ctx);
+int hf_cuda_decode_launches(const hf_ctx* ctx);
+/* 1 when the sm_100a streaming kernels serve this shape, 0 for the generic path. */
+int hf_cuda_fast_path(const hf_ctx* ctx);
+
+/* Measurement hook (no reference counterpart; the reference times whole runs
+ * only, Gemma.h:205-224): launches one kernel of the decode step `reps` times
+ * on the context's stream exactly as the step graph does, cycling through the
+ * layers so the weights stream from HBM rather than L2, and writes the mean
+ * duration of one launch in microseconds (CUDA events) and the algorithmic
+ * bytes one launch moves. kernel: HF_KERNEL_*. Runs at the current position;
+ * it rewrites that position's KV-cache row and the step buffers, so call it
+ * outside a sequence whose state matters, then begin a new one. */
+enum {
+    HF_KERNEL_QKV = 0,       /* norm + q/k/v + RoPE + cache write */
+    HF_KERNEL_ATTENTION = 1, /* decode attention (+ split merge) */
+    HF_KERNEL_OUTPUT = 2,    /* o_proj + residual */
+    HF_KERNEL_GATE_UP = 3,   /* norm + gate/up + GeGLU */
+    HF_KERNEL_DOWN = 4,      /* down + residual */
+    HF_KERNEL_LOGITS = 5     /* final norm + tied logits + argmax */
+};
+int hf_cuda_time_kernel(hf_ctx* ctx, int kernel, int reps, float* mean_us, double* bytes_per_launch);
+
+/* ---- stateless operators on device pointers ------------------------------
+ * Replaces SplitLinearProgram<Int8Blocks> / the tiled product's Int8Blocks
+ * read (Kernels/Linear.h:128-357, Decoder.cpp:389-448): output[r, o] =
+ * sum_k input[r, k] * w[o, k] (+ bias[o]), then gelu when `gelu`, then added
+ * to what output holds when `residual`. weights is the reference two-region
+ * layout (inner % 32 == 0, inner*outputs % 64 == 0); bias may be null.
+ * stream is a cudaStream_t (null = the legacy default stream). */
+int hf_cuda_linear_q8(const float* input, const uint8_t* weights, const float* bias, float* output, uint32_t inner,
+                      uint32_t outputs, uint32_t rows, int gelu, int residual, void* stream);
+/* Replaces HF::quantizeInt8Blocks on the device (Int8Blocks.cpp:176-199),
+ * byte-identical to the host quantizer: values[0, count) are elements
+ * [first, first + count) of a tensor of element_count; destination is that
+ * tensor's device bytes. */
+int hf_cuda_quantize_q8(const float* values, int64_t first, int64_t count, int64_t element_count,
+                        uint8_t* destination, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

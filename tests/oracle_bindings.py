@@ -1,0 +1,220 @@
+"""Test-side ctypes bindings to the CPU oracle (oracle/_build/liboracle.so) and
+to the reference's own compiled sources (oracle/_ref/libhf_ref.so).
+
+TEST INFRASTRUCTURE: only tests/, __graft_entry__.smoke() and bench.py's CPU
+legs use this module; the product never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ORACLE_LIB = os.path.join(ROOT, "oracle", "_build", "liboracle.so")
+REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libhf_ref.so")
+GOLDEN_DIR = os.path.join(ROOT, "tests", "golden")
+
+_vp = ctypes.c_void_p
+_oracle = None
+_ref = None
+
+
+class OracleShape(ctypes.Structure):
+    _fields_ = [
+        ("width", ctypes.c_int), ("heads", ctypes.c_int), ("kv_heads", ctypes.c_int),
+        ("head_width", ctypes.c_int), ("layers", ctypes.c_int), ("intermediate", ctypes.c_int),
+        ("vocab", ctypes.c_int), ("max_positions", ctypes.c_int), ("rms_eps", ctypes.c_float),
+        ("rope_theta", ctypes.c_double), ("embed_scale", ctypes.c_float),
+    ]
+
+
+def oracle() -> ctypes.CDLL:
+    global _oracle
+    if _oracle is None:
+        if not os.path.exists(ORACLE_LIB):
+            raise ImportError(f"{ORACLE_LIB} is not built (oracle/build.sh)")
+        lib = ctypes.CDLL(ORACLE_LIB)
+        lib.oracle_half_from_float.restype = ctypes.c_uint16
+        lib.oracle_half_from_float.argtypes = [ctypes.c_float]
+        lib.oracle_half_to_float.restype = ctypes.c_float
+        lib.oracle_half_to_float.argtypes = [ctypes.c_uint16]
+        lib.oracle_int8_blocks_byte_count.restype = ctypes.c_int64
+        lib.oracle_int8_blocks_byte_count.argtypes = [ctypes.c_int64]
+        lib.oracle_quantizes_as_int8_blocks.argtypes = [ctypes.c_int64, ctypes.c_int64]
+        lib.oracle_quantize_int8_blocks.argtypes = [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp]
+        lib.oracle_dequantize_int8_blocks.argtypes = [_vp, ctypes.c_int64, _vp]
+        lib.oracle_spread_values.argtypes = [ctypes.c_int, ctypes.c_uint32, ctypes.c_float, _vp]
+        lib.oracle_mt19937_raw.argtypes = [ctypes.c_uint32, ctypes.c_int, _vp]
+        lib.oracle_rotary_table.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_double, _vp, _vp]
+        lib.oracle_tanh_gelu_double.restype = ctypes.c_double
+        lib.oracle_tanh_gelu_double.argtypes = [ctypes.c_double]
+        lib.oracle_tanh_gelu_float.restype = ctypes.c_float
+        lib.oracle_tanh_gelu_float.argtypes = [ctypes.c_float]
+        lib.oracle_argmax.restype = ctypes.c_uint32
+        lib.oracle_argmax.argtypes = [_vp, _vp, ctypes.c_int64]
+        lib.oracle_argmax_double.restype = ctypes.c_uint32
+        lib.oracle_argmax_double.argtypes = [_vp, _vp, ctypes.c_int64]
+        lib.oracle_model_create.restype = _vp
+        lib.oracle_model_create.argtypes = [ctypes.POINTER(OracleShape), ctypes.c_int, ctypes.c_int]
+        lib.oracle_model_destroy.argtypes = [_vp]
+        lib.oracle_model_set_q8.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp]
+        lib.oracle_model_set_f32.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp]
+        lib.oracle_begin_sequence.argtypes = [_vp]
+        lib.oracle_position.argtypes = [_vp]
+        lib.oracle_threads.argtypes = [_vp]
+        lib.oracle_step.argtypes = [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_int]
+        _oracle = lib
+    return _oracle
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_LIB)
+
+
+def ref() -> ctypes.CDLL:
+    """The reference's own Int8Blocks.cpp and Sampler.cpp (oracle/build_ref.sh)."""
+    global _ref
+    if _ref is None:
+        lib = ctypes.CDLL(REF_LIB)
+        lib.ref_int8_blocks_byte_count.restype = ctypes.c_longlong
+        lib.ref_int8_blocks_byte_count.argtypes = [ctypes.c_longlong]
+        lib.ref_quantizes_as_int8_blocks.argtypes = [ctypes.c_longlong, ctypes.c_longlong]
+        lib.ref_quantize_int8_blocks.argtypes = [_vp, ctypes.c_longlong, ctypes.c_longlong, ctypes.c_longlong, _vp]
+        lib.ref_dequantize_int8_blocks.argtypes = [_vp, ctypes.c_longlong, _vp]
+        lib.ref_sampler_argmax.argtypes = [_vp, _vp, ctypes.c_longlong]
+        lib.ref_mt19937_raw.argtypes = [ctypes.c_uint, ctypes.c_int, _vp]
+        _ref = lib
+    return _ref
+
+
+def p(a):
+    return None if a is None else a.ctypes.data_as(_vp)
+
+
+# ---- scalar helpers --------------------------------------------------------
+
+def spread_values(count: int, seed: int, value_range: float) -> np.ndarray:
+    """Tests/Kernels/Common.h:90-99."""
+    out = np.empty(count, dtype=np.float32)
+    oracle().oracle_spread_values(count, seed, value_range, p(out))
+    return out
+
+
+def quantize(values: np.ndarray) -> np.ndarray:
+    values = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+    out = np.zeros(int(oracle().oracle_int8_blocks_byte_count(values.size)), dtype=np.uint8)
+    oracle().oracle_quantize_int8_blocks(p(values), 0, values.size, values.size, p(out))
+    return out
+
+
+def dequantize(stored: np.ndarray, elements: int) -> np.ndarray:
+    out = np.empty(elements, dtype=np.float32)
+    oracle().oracle_dequantize_int8_blocks(p(np.ascontiguousarray(stored)), elements, p(out))
+    return out
+
+
+def ref_quantize(values: np.ndarray) -> np.ndarray:
+    values = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+    out = np.zeros(int(ref().ref_int8_blocks_byte_count(values.size)), dtype=np.uint8)
+    ref().ref_quantize_int8_blocks(p(values), 0, values.size, values.size, p(out))
+    return out
+
+
+def argmax(logits: np.ndarray, mask: np.ndarray | None = None) -> int:
+    logits = np.ascontiguousarray(logits)
+    m = None if mask is None else np.ascontiguousarray(mask, dtype=np.float32)
+    if logits.dtype == np.float64:
+        return int(oracle().oracle_argmax_double(p(logits), p(m), logits.size))
+    logits = logits.astype(np.float32, copy=False)
+    return int(oracle().oracle_argmax(p(logits), p(m), logits.size))
+
+
+def worst_error(actual: np.ndarray, expected: np.ndarray) -> float:
+    """Tests/Decoder/Common.h:391-400: max |a - e| / (1 + |e|)."""
+    a = np.asarray(actual, dtype=np.float64).reshape(-1)
+    e = np.asarray(expected, dtype=np.float64).reshape(-1)
+    return float(np.max(np.abs(a - e) / (1.0 + np.abs(e)))) if a.size else 0.0
+
+
+def dot_product_tolerance(inner: int) -> float:
+    """Tests/Kernels/TiledProduct.h:186-198."""
+    return 1e-5 + 2.4e-7 * inner
+
+
+# ---- the model -------------------------------------------------------------
+
+class OracleModel:
+    """The CPU forward over the same Q8 bytes the GPU was given.
+
+    tensors: {(tensor_id, layer): uint8 Q8 bytes or float32 norm}, as
+    huggingfaceeacp_b200.native.Context.load_synthetic(keep=True) returns.
+    """
+
+    def __init__(self, shape, tensors, precision="double", threads=0):
+        self.shape = shape
+        self.real = np.float64 if precision == "double" else np.float32
+        s = OracleShape(shape.width, shape.heads, shape.kv_heads, shape.head_width, shape.layers,
+                        shape.intermediate, shape.vocab, shape.max_positions, shape.rms_eps, shape.rope_theta,
+                        shape.scale)
+        self.lib = oracle()
+        self.handle = self.lib.oracle_model_create(ctypes.byref(s), 0 if precision == "double" else 1, threads)
+        self.tensors = {k: np.ascontiguousarray(v) for k, v in tensors.items()}  # kept alive: borrowed by C
+        for (tensor, layer), data in self.tensors.items():
+            if data.dtype == np.uint8:
+                rc = self.lib.oracle_model_set_q8(self.handle, tensor, layer, p(data))
+            else:
+                rc = self.lib.oracle_model_set_f32(self.handle, tensor, layer, p(data))
+            assert rc == 0, (tensor, layer)
+
+    def close(self):
+        if self.handle:
+            self.lib.oracle_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def threads(self) -> int:
+        return int(self.lib.oracle_threads(self.handle))
+
+    def begin_sequence(self):
+        self.lib.oracle_begin_sequence(self.handle)
+
+    @property
+    def position(self) -> int:
+        return int(self.lib.oracle_position(self.handle))
+
+    def step(self, tokens, last_row_only=False, want_hidden=True):
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint32).reshape(-1)
+        n = tokens.size
+        hidden = np.empty((n, self.shape.width), dtype=self.real) if want_hidden else None
+        logits = np.empty((1 if last_row_only else n, self.shape.vocab), dtype=self.real)
+        rc = self.lib.oracle_step(self.handle, p(tokens), n, p(hidden), p(logits), 1 if last_row_only else 0)
+        assert rc == 0, "oracle step refused (window)"
+        return hidden, logits
+
+
+def greedy_reference(shape, tensors, prompt, count, precision="double", eos=-1, with_margins=False):
+    """The host-driven greedy loop (Tests/Generation/Common.h:248-300):
+    prefill, then one step per token, argmax (Sampler.cpp:60-76) fed back."""
+    model = OracleModel(shape, tensors, precision=precision)
+    _, logits = model.step(prompt, last_row_only=True, want_hidden=False)
+    tokens, margins = [], []
+    for i in range(count):
+        row = logits[-1]
+        token = argmax(row)
+        if with_margins:
+            top = np.partition(row, -2)[-2:]
+            margins.append(float(top[1] - top[0]))
+        if token == eos:
+            break
+        tokens.append(token)
+        if i + 1 < count and model.position < shape.max_positions:
+            _, logits = model.step([token], want_hidden=False)
+        elif i + 1 < count:
+            break
+    model.close()
+    return (tokens, margins) if with_margins else tokens
