@@ -26,6 +26,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1075,6 +1076,64 @@ int hf_cuda_argmax(hf_ctx* ctx, const float* logits, const float* mask, int rows
         if (b)
             cudaFree(b);
     return rc;
+}
+
+} // extern "C"
+
+namespace
+{
+// The argmax candidates of hf_cuda_argmax_noalloc: HF_ARGMAX_SCRATCH_CANDIDATES
+// float values followed by as many uint32 indices (64 KiB). Every device that
+// loads this library holds one copy until the process exits. Nothing in it has
+// to start at zero: the partial stage writes every candidate slot a call uses
+// before the final stage of the same call reads it.
+static __device__ __align__(256) unsigned char g_argmax_scratch[HF_ARGMAX_SCRATCH_CANDIDATES * 8];
+
+// In host code g_argmax_scratch names a host-side stand-in, not device memory:
+// the device address is looked up once per device, with that device current.
+constexpr int kScratchDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_address[kScratchDevices] = {};
+
+int argmax_scratch(int device, void** out)
+{
+    if (device < 0 || device >= kScratchDevices)
+        return HF_E_INVALID;
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_address[device])
+    {
+        void* address = nullptr;
+        if (cudaGetSymbolAddress(&address, g_argmax_scratch) != cudaSuccess || !address)
+            return HF_E_CUDA;
+        g_scratch_address[device] = address;
+    }
+    *out = g_scratch_address[device];
+    return HF_OK;
+}
+} // namespace
+
+extern "C" {
+int hf_cuda_argmax_noalloc(const float* logits, const float* mask, int rows, int row_length, uint32_t* indices,
+                           void* stream)
+{
+    if (!logits || !indices || rows <= 0 || row_length <= 0)
+        return HF_E_INVALID;
+    const int parts = std::max(1, std::min(64, (row_length + 2047) / 2048)); // as hf_cuda_argmax
+    if ((long long) rows * parts > HF_ARGMAX_SCRATCH_CANDIDATES)
+        return HF_E_CAPACITY;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess)
+        return HF_E_CUDA;
+    void* scratch = nullptr;
+    if (const int rc = argmax_scratch(device, &scratch))
+        return rc;
+    float* cand_values = static_cast<float*>(scratch);
+    unsigned* cand_indices = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(scratch)
+                                                         + HF_ARGMAX_SCRATCH_CANDIDATES * sizeof(float));
+    cudaStream_t s = (cudaStream_t) stream;
+    argmax_partial<<<dim3(parts, rows), 256, 0, s>>>(logits, row_length, mask, parts, cand_values, cand_indices);
+    argmax_final<<<rows, 32, 0, s>>>(cand_values, cand_indices, parts, rows, indices, nullptr, nullptr, 0);
+    return cudaGetLastError() == cudaSuccess ? HF_OK : HF_E_CUDA;
 }
 
 int hf_cuda_prefill_async(hf_ctx* ctx, const uint32_t* prompt, int prompt_length)

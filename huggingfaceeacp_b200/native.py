@@ -199,6 +199,7 @@ def cuda() -> ctypes.CDLL:
         lib.hf_cuda_linear_q8.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
                                           ctypes.c_int, ctypes.c_int, _vp]
         lib.hf_cuda_quantize_q8.argtypes = [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp]
+        lib.hf_cuda_argmax_noalloc.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp]
         lib.hf_cuda_time_kernel.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float),
                                             ctypes.POINTER(ctypes.c_double)]
         _cuda = lib

@@ -106,6 +106,24 @@ int hf_cuda_step(hf_ctx* ctx, const uint32_t* tokens, int count, float* logits, 
 int hf_cuda_argmax(hf_ctx* ctx, const float* logits, const float* mask, int rows, int row_length,
                    uint32_t* indices);
 
+/* No counterpart in the reference. The same argmax for callers that must not
+ * allocate device memory: a host application that owns every byte of device
+ * memory and hands this library ready buffers, or a thread with a latency
+ * budget (an audio or render callback) where cudaMalloc/cudaFree, which can
+ * synchronise the whole device, are not allowed. Nothing is allocated here:
+ * logits [rows, row_length], the optional mask [row_length] and indices [rows]
+ * are the caller's DEVICE pointers, and the per-row candidates live in a
+ * file-scope device array of HF_ARGMAX_SCRATCH_CANDIDATES entries, so
+ * rows * ceil(row_length / 2048) (at most 64 per row) must not exceed it, else
+ * HF_E_CAPACITY and nothing is launched. The first call on a device looks up
+ * that array's address on the current device (make that first call before any
+ * stream capture). Every call shares the one array: calls that overlap on the
+ * GPU (different streams, or different host threads) race on it. Asynchronous
+ * on `stream` (a cudaStream_t, null = the legacy default stream). */
+#define HF_ARGMAX_SCRATCH_CANDIDATES 8192
+int hf_cuda_argmax_noalloc(const float* logits, const float* mask, int rows, int row_length, uint32_t* indices,
+                           void* stream);
+
 /* Replaces HF::Gemma::generate with greedy sampling (Gemma.cpp:402-533):
  * begins a sequence, prefills the prompt in blocks of the step capacity,
  * then decodes with on-device token feedback until `max_tokens` tokens, the
