@@ -212,7 +212,8 @@ def run_ours(args):
     ctx.decode_async(args.warmup)
     ctx.sync()
     stream = torch.cuda.ExternalStream(ctx.stream)
-    launches = ctx.decode_launches
+    launches = ctx.decode_launches(args.steps)
+    path = ctx.decode_path
     first_pos = ctx.position
     barrier()
     torch.cuda.synchronize()
@@ -259,15 +260,24 @@ def run_ours(args):
     for kernel, name in enumerate(native.KERNEL_NAMES):
         us, nbytes = ctx.time_kernel(kernel, 36 if kernel != native.KERNEL_LOGITS else 8)
         kernels[name] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3}
-    per_step_us = {
-        name: k["us"] * (1 if name == "logits_argmax" else shape.layers) for name, k in kernels.items()}
-    dominant = max(per_step_us, key=per_step_us.get)
+    graph_kernels = {n: {"us": round(k["us"], 2), "gbs": round(k["gbs"], 1)} for n, k in kernels.items()}
+    if path == native.DECODE_PERSISTENT:
+        # One cooperative launch runs all K steps: the dominant (only) kernel.
+        dominant = "decode_persistent"
+        launch_bytes = step_bytes * args.steps
+        launch_us = elapsed_ms * 1000.0
+        achieved = launch_bytes / launch_us / 1e3
+    else:
+        per_step_us = {
+            name: k["us"] * (1 if name == "logits_argmax" else shape.layers) for name, k in kernels.items()}
+        dominant = max(per_step_us, key=per_step_us.get)
+        launch_bytes, launch_us = kernels[dominant]["bytes"], kernels[dominant]["us"]
+        achieved = kernels[dominant]["gbs"]
     traffic = committed_traffic().get(dominant)
-    dk = kernels[dominant]
-    roofline = {"kernel": dominant, "bound": "hbm", "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": dk["gbs"] / peak, "traffic": traffic, "peak_kind": peak_kind,
-                "algorithmic_bytes_per_launch": dk["bytes"], "mean_launch_us": dk["us"],
-                "kernels": {n: {"us": round(k["us"], 2), "gbs": round(k["gbs"], 1)} for n, k in kernels.items()}}
+    roofline = {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                "algorithmic_bytes_per_launch": launch_bytes, "mean_launch_us": launch_us,
+                "graph_path_kernels": graph_kernels}
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -281,7 +291,8 @@ def run_ours(args):
                           "frac": step_bytes / (ms_per_step * 1e6) / peak},
         "roofline": roofline,
         "e2e": e2e,
-        "gpu_launches": launches * args.steps,
+        "gpu_launches": launches,
+        "decode_path": {0: "generic", 1: "graph", 2: "persistent"}[path],
         "clocks": clocks.summary(),
         "tokens_head": [int(t) for t in tokens[:4]],
     }

@@ -114,31 +114,25 @@ __device__ __forceinline__ int lane_of_head(int h)
     return lane;
 }
 
-// D = 256, QH query heads per kv head (QH in {1, 2, 4, 8}), one CTA per
-// (split, kv head, row). A lane owns channels [8 lane, 8 lane + 8) of every
-// head; K/V tiles of 32 keys are staged in shared memory by all threads at
-// once, each warp takes 4 keys of the tile, scores them for all heads, and
-// keeps its own running (max, sum, row) per head; the warps fold at the end.
-template <int QH>
-__global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
+// D = 256, QH query heads in one CTA's group (all reading kv head `kv_head`),
+// one CTA per (split, head group, row). A lane owns channels [8 lane, 8 lane + 8)
+// of every head of the group; K/V tiles of TILE keys are staged in shared
+// memory by the 256 threads at once, each warp takes TILE / 8 keys of the tile,
+// scores them for all heads, and keeps its own running (max, sum, row) per head;
+// the warps fold at the end. `sync` is the barrier of the 256 threads.
+// Shared memory: max(2 TILE, 8 QH) x 256 floats + 16 QH.
+template <int QH, int TILE, typename Sync>
+__device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int head0, int kv_head, int split,
+                          float* sm, Sync sync)
 {
     constexpr int D = 256;
-    constexpr int TILE = 32;
-    extern __shared__ __align__(16) float sm[];
     float* tk = sm;                 // [TILE][D]
     float* tv = sm + TILE * D;      // [TILE][D]
     float* wacc = sm;               // after the loop: [8][QH][D] (reuses the tiles)
-    float* wm = sm + 8 * QH * D;    // [8][QH]
+    float* wm = sm + (2 * TILE > 8 * QH ? 2 * TILE : 8 * QH) * D; // [8][QH]
     float* wl = wm + 8 * QH;        // [8][QH]
 
-    pdl_wait();
-    const unsigned position = *(volatile const unsigned*) a.state;
-    pdl_trigger();
-
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int row = blockIdx.z;
-    const int kv_head = blockIdx.y;
-    const int split = blockIdx.x;
     const int H = a.heads;
     const int kvw = a.kv_heads * D;
     const int keys = (int) position + row + 1;
@@ -148,12 +142,12 @@ __global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
     const int my_head = head_of_lane<QH>(lane);
 
     float qv[QH][8];
-    const float* qrow = a.q + (size_t) row * H * D + (size_t) kv_head * QH * D + lane * 8;
+    const float* qrow = a.q + (size_t) row * H * D + (size_t) head0 * D + lane * 8;
 #pragma unroll
     for (int h = 0; h < QH; ++h)
     {
-        const float4 lo = *reinterpret_cast<const float4*>(qrow + h * D);
-        const float4 hi = *reinterpret_cast<const float4*>(qrow + h * D + 4);
+        const float4 lo = __ldcg(reinterpret_cast<const float4*>(qrow + h * D));
+        const float4 hi = __ldcg(reinterpret_cast<const float4*>(qrow + h * D + 4));
         qv[h][0] = lo.x * a.scale; qv[h][1] = lo.y * a.scale; qv[h][2] = lo.z * a.scale; qv[h][3] = lo.w * a.scale;
         qv[h][4] = hi.x * a.scale; qv[h][5] = hi.y * a.scale; qv[h][6] = hi.z * a.scale; qv[h][7] = hi.w * a.scale;
     }
@@ -178,7 +172,7 @@ __global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
             cp_async16(tv + r * D + c, a.v_cache + at);
         }
         cp_async_wait_all();
-        __syncthreads();
+        sync();
 
         // ---- this warp's keys of the tile: warp, warp + 8, ...
         float s[TILE / 8];
@@ -255,7 +249,7 @@ __global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
                     acc[h][d] = fmaf(ph, vv[d], acc[h][d]);
             }
         }
-        __syncthreads(); // the tile is read before the next one lands
+        sync(); // the tile is read before the next one lands
     }
 
     // ---- fold the 8 warps
@@ -270,7 +264,7 @@ __global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
         wm[warp * QH + my_head] = m;
         wl[warp * QH + my_head] = l;
     }
-    __syncthreads();
+    sync();
 
     const int d = tid; // 256 threads, one channel each
     for (int h = 0; h < QH; ++h)
@@ -293,7 +287,7 @@ __global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
                 value = fmaf(wacc[(w * QH + h) * D + d], f, value);
             }
         }
-        const int head = kv_head * QH + h;
+        const int head = head0 + h;
         if (a.nsplit == 1)
             a.out[(size_t) row * H * D + (size_t) head * D + d] = value / sum;
         else
@@ -309,13 +303,26 @@ __global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
     }
 }
 
-// Shared memory of mqa_fast<QH>: the K/V tile, or the warp fold after it.
+// The standalone decode/prefill attention: grid (nsplit, kv_heads, rows), 256
+// threads, all query heads of a kv head in one CTA, 32-key tiles.
 template <int QH>
+__global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
+{
+    extern __shared__ __align__(16) float sm[];
+    pdl_wait();
+    const unsigned position = *(volatile const unsigned*) a.state;
+    pdl_trigger();
+    mqa_block<QH, 32>(a, position, blockIdx.z, blockIdx.y * QH, blockIdx.y, blockIdx.x, sm, [] { __syncthreads(); });
+}
+
+
+// Shared memory of mqa_fast<QH>: the K/V tile, or the warp fold after it.
+template <int QH, int TILE = 32>
 constexpr size_t mqa_fast_smem()
 {
-    constexpr size_t tiles = 2 * 32 * 256;
-    constexpr size_t fold = 8 * QH * 256 + 16 * QH;
-    return (tiles > fold ? tiles : fold) * sizeof(float);
+    constexpr size_t tiles = 2 * TILE * 256;
+    constexpr size_t fold = 8 * QH * 256;
+    return ((tiles > fold ? tiles : fold) + 16 * QH) * sizeof(float);
 }
 
 // Folds the splits of mqa_fast: out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M).

@@ -11,7 +11,7 @@
 namespace hfk
 {
 constexpr int kBlock = 32;            // Q8_0 block: 32 elements, one fp16 scale
-constexpr unsigned kSpinLimit = 1u << 26; // bounded waits give up after this many polls
+constexpr unsigned kSpinLimit = 1u << 20; // bounded waits give up after this many polls (tens of ms at least)
 
 // Device-side error bits, OR-ed into the context's error word.
 enum : unsigned
@@ -92,6 +92,13 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned b
             smem_addr(dst)),
         "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
         : "memory");
+}
+
+// Starts moving `bytes` (a multiple of 16, 16-byte aligned) of global memory
+// into L2 without waiting for or tracking it.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ uint64_t evict_first_policy()

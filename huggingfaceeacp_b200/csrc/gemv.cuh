@@ -59,6 +59,8 @@ struct GemvArgs
     float* v_cache;
     const float* rope_cos;  // [P, D/2]
     const float* rope_sin;
+    const float* rope_cos_row; // this position's D/2 cosines (e.g. staged in shared memory), or null
+    const float* rope_sin_row;
     int heads, kv_heads, head_dim;
     // Logits
     const float* mask;      // [N] suppression (non-zero = suppressed) or null
@@ -88,8 +90,8 @@ __device__ __forceinline__ void qkv_pair_store(const GemvArgs& a, unsigned unit,
     const int kvw = a.kv_heads * D;
     if (block < a.heads + a.kv_heads)
     {
-        const float c = a.rope_cos[(size_t) position * half + pair];
-        const float s = a.rope_sin[(size_t) position * half + pair];
+        const float c = a.rope_cos_row ? a.rope_cos_row[pair] : a.rope_cos[(size_t) position * half + pair];
+        const float s = a.rope_sin_row ? a.rope_sin_row[pair] : a.rope_sin[(size_t) position * half + pair];
         const float r0 = v0 * c - v1 * s;
         const float r1 = v1 * c + v0 * s;
         if (block < a.heads)
@@ -119,7 +121,7 @@ __device__ __forceinline__ float plain_epilogue(Epi e, float acc, const float* b
     if (e == Epi::Gelu)
         v = tanh_gelu(v);
     if (e == Epi::Residual)
-        v += *y;
+        v += __ldcg(y);
     *y = v;
     return v;
 }
@@ -220,23 +222,296 @@ __device__ __forceinline__ float row_slab_dot(const uint8_t* q, const __half* sc
     return warp_sum(acc);
 }
 
-template <int K>
-constexpr int stream_rows_per_stage()
+// The shared-memory ring a producer warp fills and the consumer warps drain.
+struct Ring
 {
-    return kStageQuants / K;
+    uint8_t* quants;  // [NST][kStageQuants]
+    uint8_t* scales;  // [NST][kStageScales]
+    uint64_t* full;   // [NST], one arrival + the stage's transaction bytes
+    uint64_t* empty;  // [NST], one arrival per consumer warp
+};
+
+// The rows [r0, r1) a CTA owns of a product with N weight rows split over
+// `ctas` CTAs (in whole pairs for the paired epilogues).
+struct Slab
+{
+    int r0, r1;
+};
+
+__device__ __forceinline__ Slab cta_slab(int N, bool pairs, int cta, int ctas)
+{
+    const int units = pairs ? N / 2 : N;
+    const int u0 = (int) ((long long) units * cta / ctas);
+    const int u1 = (int) ((long long) units * (cta + 1) / ctas);
+    return pairs ? Slab {2 * u0, 2 * u1} : Slab {u0, u1};
 }
 
-template <int K, Epi E, int NST>
-__global__ void __launch_bounds__(kStreamThreads, 2) q8_gemv_stream(const GemvArgs a)
+__device__ __forceinline__ void init_ring(const Ring& ring, int nst)
 {
-    constexpr int WPR = K / 2048;                 // warps sharing one weight row
-    constexpr int RPS = kStageQuants / K;         // weight rows per stage
-    constexpr int RPW = 2;                        // rows each warp's row group takes per stage
+    for (int s = 0; s < nst; ++s)
+    {
+        mbar_init(&ring.full[s], 1);
+        mbar_init(&ring.empty[s], kConsumerWarps);
+    }
+    mbar_fence_init();
+}
+
+// Producer lane: streams the slab's stages into the ring. `seq` counts every
+// stage this CTA has ever streamed, so one ring serves a sequence of products.
+template <int K, int NST>
+__device__ bool produce_slab(const uint8_t* w, const __half* scales, Slab slab, const Ring& ring, unsigned& seq,
+                             uint64_t policy, unsigned* err)
+{
+    constexpr int RPS = kStageQuants / K;
+    const uint8_t* scale_bytes = reinterpret_cast<const uint8_t*>(scales);
+    const int stages = (slab.r1 - slab.r0 + RPS - 1) / RPS;
+    for (int s = 0; s < stages; ++s, ++seq)
+    {
+        const int b = (int) (seq % NST);
+        if (seq >= NST && !mbar_wait(&ring.empty[b], (seq / NST - 1) & 1u))
+        {
+            flag_error(err, kErrWaitTimeout);
+            return false;
+        }
+        const int first = slab.r0 + s * RPS;
+        const int rows = min(RPS, slab.r1 - first);
+        const unsigned qb = (unsigned) rows * K;
+        const unsigned sb = (unsigned) rows * (K / 16);
+        mbar_expect_tx(&ring.full[b], qb + sb);
+        bulk_load(ring.quants + b * kStageQuants, w + (size_t) first * K, qb, &ring.full[b], policy);
+        bulk_load(ring.scales + b * kStageScales, scale_bytes + (size_t) first * (K / 16), sb, &ring.full[b], policy);
+    }
+    return true;
+}
+
+// Consumer threads: the 2048-float x of a K = 2048 product into shared memory,
+// RMS-normalised (Kernels/RMSNorm.h:51-81, one fixed fold order so every CTA
+// normalises identically) when norm_w is given; then the lane's slice into
+// registers. x is read through L2 (it was written by other CTAs); a null x
+// means it is already in sx.
+__device__ __forceinline__ void stage_x_2048(const float* x, const float* norm_w, float eps, float* sx,
+                                             float* reduce, int tid, float* xr, const float* norm_regs = nullptr)
+{
+    const int lane = tid & 31, warp = tid >> 5;
+    float ss_part = 0.f;
+    for (int i = tid; i < 512; i += kConsumerWarps * 32)
+    {
+        const float4 v = x ? __ldcg(reinterpret_cast<const float4*>(x) + i) : reinterpret_cast<const float4*>(sx)[i];
+        if (x)
+            reinterpret_cast<float4*>(sx)[i] = v;
+        ss_part += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    if (norm_w)
+    {
+        ss_part = warp_sum(ss_part);
+        if (lane == 0)
+            reduce[warp] = ss_part;
+        consumer_sync();
+        float total = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w)
+            total += reduce[w];
+        const float scale = 1.f / sqrtf(total / 2048.f + eps);
+        if (norm_regs)
+        {
+#pragma unroll
+            for (int k = 0; k < 2048 / (kConsumerWarps * 32); ++k)
+            {
+                float& v = sx[tid + k * kConsumerWarps * 32];
+                v = v * scale * (1.f + norm_regs[k]);
+            }
+        }
+        else
+            for (int i = tid; i < 2048; i += kConsumerWarps * 32)
+                sx[i] = sx[i] * scale * (1.f + norm_w[i]);
+    }
+    consumer_sync();
+    load_x_slice(sx, lane, xr);
+}
+
+// The norm weights thread `tid` applies in stage_x_2048, loaded ahead of time.
+__device__ __forceinline__ void load_norm_regs(const float* norm_w, int tid, float* norm_regs)
+{
+#pragma unroll
+    for (int k = 0; k < 2048 / (kConsumerWarps * 32); ++k)
+        norm_regs[k] = __ldg(norm_w + tid + k * kConsumerWarps * 32);
+}
+
+// Consumer warp w's 64-column x slice of slab (w % WPR) of a K > 2048 product.
+template <int K>
+__device__ __forceinline__ void load_x_wide(const float* x, int tid, float* xr)
+{
+    constexpr int WPR = K / 2048;
+    const int lane = tid & 31, warp = tid >> 5;
+    const float* xs = x + 2048 * (warp % WPR);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int t = 0; t < 16; t += 4)
+        {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(xs + 16 * lane + 512 * j + t));
+            xr[16 * j + t] = v.x;
+            xr[16 * j + t + 1] = v.y;
+            xr[16 * j + t + 2] = v.z;
+            xr[16 * j + t + 3] = v.w;
+        }
+}
+
+// Consumer warps: drain the slab's stages and apply the epilogue. With WPR > 1
+// the rows' slab partials collect in `spart` and are reduced at the end (a
+// consumer-wide barrier). Logits candidates accumulate in best/best_i (lane 0).
+template <int K, Epi E, int NST>
+__device__ bool consume_slab(const GemvArgs& a, Slab slab, const Ring& ring, unsigned& seq, const float* xr,
+                             float* spart, unsigned position, float& best, unsigned& best_i)
+{
+    constexpr int WPR = K / 2048;
+    constexpr int RPS = kStageQuants / K;
+    constexpr int RPW = 2;
     constexpr bool PAIRS = E == Epi::QkvRope || E == Epi::GeGLU;
     static_assert(K % 2048 == 0 && WPR >= 1 && WPR <= 8 && 8 % WPR == 0, "K must be 2048 * {1,2,4,8}");
     static_assert(RPS == (kConsumerWarps / WPR) * RPW, "stage geometry");
     static_assert(!PAIRS || WPR == 1, "paired epilogues need a whole row per warp");
 
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int group = warp / WPR; // row group within a stage
+    const int slab_col = warp % WPR;
+    const int stages = (slab.r1 - slab.r0 + RPS - 1) / RPS;
+    bool ok = true;
+
+    for (int s = 0; s < stages; ++s, ++seq)
+    {
+        const int b = (int) (seq % NST);
+        if (ok && !mbar_wait(&ring.full[b], (seq / NST) & 1u))
+        {
+            if (lane == 0)
+                flag_error(a.err, kErrWaitTimeout);
+            ok = false;
+        }
+        if (!ok)
+            continue; // keep `seq` in step with the producer
+        const int first = slab.r0 + s * RPS;
+        const int rows = min(RPS, slab.r1 - first);
+        const uint8_t* qs = ring.quants + b * kStageQuants;
+        const __half* scs = reinterpret_cast<const __half*>(ring.scales + b * kStageScales);
+
+        float v[RPW];
+#pragma unroll
+        for (int i = 0; i < RPW; ++i)
+        {
+            const int rr = group * RPW + i;
+            v[i] = rr < rows ? row_slab_dot(qs + rr * K + 2048 * slab_col, scs + rr * (K / 32) + 64 * slab_col, lane, xr)
+                             : 0.f;
+        }
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(&ring.empty[b]);
+
+        if (lane != 0)
+            continue;
+        if constexpr (WPR == 1)
+        {
+            const int row0 = first + group * RPW;
+            if constexpr (PAIRS)
+            {
+                if (group * RPW < rows)
+                {
+                    const unsigned unit = (unsigned) (row0 / 2);
+                    if constexpr (E == Epi::QkvRope)
+                        qkv_pair_store(a, unit, v[0], v[1], position, 0);
+                    else
+                        a.out[unit] = tanh_gelu(v[0]) * v[1];
+                }
+            }
+            else
+            {
+#pragma unroll
+                for (int i = 0; i < RPW; ++i)
+                {
+                    const int row = row0 + i;
+                    if (group * RPW + i >= rows)
+                        break;
+                    if constexpr (E == Epi::Logits)
+                    {
+                        const float value = v[i] + (a.bias ? a.bias[row] : 0.f);
+                        a.out[row] = value;
+                        const bool allowed = !a.mask || a.mask[row] == 0.f;
+                        if (allowed && (best_i == 0xFFFFFFFFu || better_candidate(value, (unsigned) row, best, best_i)))
+                        {
+                            best = value;
+                            best_i = (unsigned) row;
+                        }
+                    }
+                    else
+                        plain_epilogue(E, v[i], a.bias, row, a.out + row);
+                }
+            }
+        }
+        else
+        {
+#pragma unroll
+            for (int i = 0; i < RPW; ++i)
+                if (group * RPW + i < rows)
+                    spart[(first + group * RPW + i - slab.r0) * WPR + slab_col] = v[i];
+        }
+    }
+
+    if constexpr (WPR > 1)
+    {
+        consumer_sync();
+        for (int local = tid; local < slab.r1 - slab.r0; local += kConsumerWarps * 32)
+        {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < WPR; ++w)
+                v += spart[local * WPR + w];
+            if constexpr (E == Epi::Store || E == Epi::Residual || E == Epi::Gelu)
+                plain_epilogue(E, v, a.bias, slab.r0 + local, a.out + slab.r0 + local);
+        }
+        consumer_sync(); // spart is reused by the next product
+    }
+    return ok;
+}
+
+// The CTA's logits candidate (folded over the consumer warps), then the grid's
+// through a ticket: the last CTA folds every CTA's candidate in CTA order.
+// Returns true in the CTA that did the final fold.
+__device__ bool logits_fold(const GemvArgs& a, unsigned position, float best, unsigned best_i, float* cand_v,
+                            unsigned* cand_i, unsigned* last_cta)
+{
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (lane == 0)
+    {
+        cand_v[warp] = best;
+        cand_i[warp] = best_i;
+    }
+    consumer_sync();
+    if (tid == 0)
+    {
+        for (int w = 0; w < kConsumerWarps; ++w)
+            if (cand_i[w] != 0xFFFFFFFFu && (best_i == 0xFFFFFFFFu || better_candidate(cand_v[w], cand_i[w], best, best_i)))
+            {
+                best = cand_v[w];
+                best_i = cand_i[w];
+            }
+        a.cand_val[blockIdx.x] = best;
+        a.cand_idx[blockIdx.x] = best_i;
+        __threadfence();
+        *last_cta = atomicAdd(a.ticket, 1u) == gridDim.x - 1 ? 1u : 0u;
+    }
+    consumer_sync();
+    const bool last = *last_cta != 0;
+    if (last && warp == 0)
+    {
+        __threadfence();
+        logits_finish(a, position, (int) gridDim.x);
+    }
+    return last;
+}
+
+template <int K, Epi E, int NST>
+__global__ void __launch_bounds__(kStreamThreads, 2) q8_gemv_stream(const GemvArgs a)
+{
+    constexpr bool PAIRS = E == Epi::QkvRope || E == Epi::GeGLU;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[NST];
     __shared__ uint64_t empty[NST];
@@ -245,232 +520,40 @@ __global__ void __launch_bounds__(kStreamThreads, 2) q8_gemv_stream(const GemvAr
     __shared__ unsigned cand_i[kConsumerWarps];
     __shared__ unsigned last_cta;
 
-    uint8_t* sq = smem;
-    uint8_t* ss = smem + NST * kStageQuants;
-    float* sx = reinterpret_cast<float*>(ss + NST * kStageScales); // WPR == 1: 2048 floats of x
-    float* spart = sx;                                              // WPR > 1: [rows][WPR] partials
-
+    const Ring ring {smem, smem + NST * kStageQuants, full, empty};
+    float* sx = reinterpret_cast<float*>(smem + NST * (kStageQuants + kStageScales)); // x, or WPR > 1 partials
     const int tid = threadIdx.x;
-    const int warp = tid >> 5;
-    const int lane = tid & 31;
-
-    const int units = PAIRS ? a.N / 2 : a.N;
-    const int u0 = (int) ((long long) units * blockIdx.x / gridDim.x);
-    const int u1 = (int) ((long long) units * (blockIdx.x + 1) / gridDim.x);
-    const int r0 = PAIRS ? 2 * u0 : u0;
-    const int r1 = PAIRS ? 2 * u1 : u1;
-    const int stages = (r1 - r0 + RPS - 1) / RPS;
+    const Slab slab = cta_slab(a.N, PAIRS, blockIdx.x, gridDim.x);
 
     if (tid == 0)
-    {
-        for (int s = 0; s < NST; ++s)
-        {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
-        }
-        mbar_fence_init();
-    }
+        init_ring(ring, NST);
     __syncthreads();
 
-    if (warp == kConsumerWarps)
+    unsigned seq = 0;
+    if (tid >= kConsumerWarps * 32)
     {
-        // ---- producer: the weights do not depend on the previous kernel, so the
-        // first NST stages go out before anything waits on it.
-        if (lane == 0)
-        {
-            const uint64_t policy = evict_first_policy();
-            const uint8_t* scale_bytes = reinterpret_cast<const uint8_t*>(a.scales);
-            for (int s = 0; s < stages; ++s)
-            {
-                const int b = s % NST;
-                if (s >= NST && !mbar_wait(&empty[b], (unsigned) (s / NST - 1) & 1u))
-                {
-                    flag_error(a.err, kErrWaitTimeout);
-                    break;
-                }
-                const int first = r0 + s * RPS;
-                const int rows = min(RPS, r1 - first);
-                const unsigned qb = (unsigned) rows * K;
-                const unsigned sb = (unsigned) rows * (K / 16);
-                mbar_expect_tx(&full[b], qb + sb);
-                bulk_load(sq + b * kStageQuants, a.w + (size_t) first * K, qb, &full[b], policy);
-                bulk_load(ss + b * kStageScales, scale_bytes + (size_t) first * (K / 16), sb, &full[b], policy);
-            }
-        }
+        // The weights do not depend on the previous kernel: stream them now.
+        if (tid == kConsumerWarps * 32)
+            produce_slab<K, NST>(a.w, a.scales, slab, ring, seq, evict_first_policy(), a.err);
         pdl_wait();
         pdl_trigger();
         return;
     }
 
-    // ---- consumers
     pdl_wait();
     const unsigned position = step_position(a);
-
     float xr[64];
-    if constexpr (WPR == 1)
-    {
-        const float4* x4 = reinterpret_cast<const float4*>(a.x);
-        float ss_part = 0.f;
-        for (int i = tid; i < 512; i += kConsumerWarps * 32)
-        {
-            const float4 v = x4[i];
-            reinterpret_cast<float4*>(sx)[i] = v;
-            ss_part += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        }
-        if (a.norm_w)
-        {
-            // Kernels/RMSNorm.h:51-81, folded in one fixed order so every CTA
-            // normalises identically.
-            ss_part = warp_sum(ss_part);
-            if (lane == 0)
-                reduce[warp] = ss_part;
-            consumer_sync();
-            float total = 0.f;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w)
-                total += reduce[w];
-            const float scale = 1.f / sqrtf(total / 2048.f + a.eps);
-            for (int i = tid; i < 2048; i += kConsumerWarps * 32)
-                sx[i] = sx[i] * scale * (1.f + a.norm_w[i]);
-        }
-        consumer_sync();
-        load_x_slice(sx, lane, xr);
-    }
+    if constexpr (K == 2048)
+        stage_x_2048(a.x, a.norm_w, a.eps, sx, reduce, tid, xr);
     else
-        load_x_slice(a.x + 2048 * (warp % WPR), lane, xr);
+        load_x_wide<K>(a.x, tid, xr);
     pdl_trigger();
 
-    const int group = warp / WPR; // row group within a stage
-    const int slab = warp % WPR;  // 2048-column slab within a row
     float best = -INFINITY;
     unsigned best_i = 0xFFFFFFFFu;
-
-    for (int s = 0; s < stages; ++s)
-    {
-        const int b = s % NST;
-        const bool ok = mbar_wait(&full[b], (unsigned) (s / NST) & 1u);
-        if (!ok)
-        {
-            if (lane == 0)
-                flag_error(a.err, kErrWaitTimeout);
-            break;
-        }
-        const int first = r0 + s * RPS;
-        const int rows = min(RPS, r1 - first);
-        const uint8_t* qs = sq + b * kStageQuants;
-        const __half* scs = reinterpret_cast<const __half*>(ss + b * kStageScales);
-
-        float v[RPW];
-#pragma unroll
-        for (int i = 0; i < RPW; ++i)
-        {
-            const int rr = group * RPW + i; // row within the stage
-            v[i] = rr < rows ? row_slab_dot(qs + rr * K + 2048 * slab, scs + rr * (K / 32) + 64 * slab, lane, xr)
-                             : 0.f;
-        }
-        __syncwarp();
-        if (lane == 0)
-            mbar_arrive(&empty[b]);
-
-        // ---- epilogue (lane 0 holds both rows' sums)
-        if (lane == 0)
-        {
-            if constexpr (WPR == 1)
-            {
-                const int row0 = first + group * RPW;
-                if constexpr (PAIRS)
-                {
-                    if (group * RPW < rows)
-                    {
-                        const unsigned unit = (unsigned) (row0 / 2);
-                        if constexpr (E == Epi::QkvRope)
-                            qkv_pair_store(a, unit, v[0], v[1], position, 0);
-                        else
-                            a.out[unit] = tanh_gelu(v[0]) * v[1];
-                    }
-                }
-                else
-                {
-#pragma unroll
-                    for (int i = 0; i < RPW; ++i)
-                    {
-                        const int row = row0 + i;
-                        if (group * RPW + i >= rows)
-                            break;
-                        if constexpr (E == Epi::Logits)
-                        {
-                            const float value = v[i] + (a.bias ? a.bias[row] : 0.f);
-                            a.out[row] = value;
-                            const bool allowed = !a.mask || a.mask[row] == 0.f;
-                            if (allowed && (best_i == 0xFFFFFFFFu || better_candidate(value, (unsigned) row, best, best_i)))
-                            {
-                                best = value;
-                                best_i = (unsigned) row;
-                            }
-                        }
-                        else
-                            plain_epilogue(E, v[i], a.bias, row, a.out + row);
-                    }
-                }
-            }
-            else
-            {
-#pragma unroll
-                for (int i = 0; i < RPW; ++i)
-                {
-                    const int local = first + group * RPW + i - r0;
-                    if (group * RPW + i < rows)
-                        spart[local * WPR + slab] = v[i];
-                }
-            }
-        }
-    }
-
-    if constexpr (WPR > 1)
-    {
-        // Rows reduced over their WPR slabs in slab order.
-        consumer_sync();
-        for (int local = tid; local < r1 - r0; local += kConsumerWarps * 32)
-        {
-            float v = 0.f;
-#pragma unroll
-            for (int w = 0; w < WPR; ++w)
-                v += spart[local * WPR + w];
-            const int row = r0 + local;
-            if constexpr (E == Epi::Store || E == Epi::Residual || E == Epi::Gelu)
-                plain_epilogue(E, v, a.bias, row, a.out + row);
-        }
-    }
-
+    consume_slab<K, E, NST>(a, slab, ring, seq, xr, sx, position, best, best_i);
     if constexpr (E == Epi::Logits)
-    {
-        if (lane == 0)
-        {
-            cand_v[warp] = best;
-            cand_i[warp] = best_i;
-        }
-        consumer_sync();
-        if (tid == 0)
-        {
-            for (int w = 0; w < kConsumerWarps; ++w)
-                if (cand_i[w] != 0xFFFFFFFFu
-                    && (best_i == 0xFFFFFFFFu || better_candidate(cand_v[w], cand_i[w], best, best_i)))
-                {
-                    best = cand_v[w];
-                    best_i = cand_i[w];
-                }
-            a.cand_val[blockIdx.x] = best;
-            a.cand_idx[blockIdx.x] = best_i;
-            __threadfence();
-            last_cta = atomicAdd(a.ticket, 1u) == gridDim.x - 1 ? 1u : 0u;
-        }
-        consumer_sync();
-        if (last_cta && warp == 0)
-        {
-            __threadfence();
-            logits_finish(a, position, (int) gridDim.x);
-        }
-    }
+        logits_fold(a, position, best, best_i, cand_v, cand_i, &last_cta);
 }
 
 // ============================================================================

@@ -20,6 +20,7 @@
 #include "attention.cuh"
 #include "gemv.cuh"
 #include "misc.cuh"
+#include "persistent.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -118,6 +119,8 @@ void configure_kernels()
     cudaFuncSetAttribute(mqa_fast<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<2>());
     cudaFuncSetAttribute(mqa_fast<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<1>());
     cudaFuncSetAttribute(mqa_generic, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(decode_persistent<kPersistentStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int) persistent_smem<kPersistentStages>());
 }
 
 void configure_once(int device)
@@ -241,6 +244,9 @@ struct hf_ctx
     uint8_t* staging = nullptr;
     size_t staging_bytes = 0;
     int max_splits = 1;
+    bool persistent_ok = false; // the cooperative whole-loop kernel serves this shape on this device
+    int decode_path = HF_DECODE_AUTO;
+    LayerDev* layer_dev = nullptr;
 
     int position = 0;
     std::map<int, cudaGraphExec_t> graphs; // decode step by attention split count
@@ -264,6 +270,12 @@ struct hf_ctx
     int qkv_rows() const { return query_width() + 2 * kv_width(); }
     unsigned* err_word() const { return state + 1; }
     unsigned* ticket() const { return state + 2; }
+    unsigned* barrier_counter() const { return state + 3; }
+    unsigned* exit_ticket() const { return state + 4; }
+    bool use_persistent() const
+    {
+        return persistent_ok && decode_path != HF_DECODE_GRAPH;
+    }
     float* layer_k(int l) const { return kcache + (size_t) l * shape.max_positions * kv_width(); }
     float* layer_v(int l) const { return vcache + (size_t) l * shape.max_positions * kv_width(); }
 
@@ -457,6 +469,85 @@ struct hf_ctx
         }
         if ((e = launch_logits(1)) != cudaSuccess)
             return cuda(e, "logits launch");
+        return HF_OK;
+    }
+
+    // `steps` decode steps in one cooperative launch of the whole-loop kernel.
+    int enqueue_persistent(int steps, unsigned long long* trace = nullptr)
+    {
+        const hf_shape& s = shape;
+        PersistentArgs p = {};
+        p.layers = layer_dev;
+        p.n_layers = s.layers;
+        p.embed = embedding.base;
+        p.embed_scales = embedding.scales();
+        p.final_norm = final_norm;
+        p.heads = s.heads;
+        p.head_dim = s.head_width;
+        p.intermediate = s.intermediate;
+        p.vocab = s.vocab;
+        p.qkv_rows = qkv_rows();
+        p.eps = s.rms_eps;
+        p.embed_scale = s.embed_scale;
+        p.attn_scale = 1.f / std::sqrt((float) s.head_width);
+        p.hidden = hidden;
+        p.qbuf = qbuf;
+        p.attended = attended;
+        p.act = act;
+        p.logits = logits;
+        p.attn_acc = attn_acc;
+        p.attn_ml = attn_ml;
+        p.max_splits = max_splits;
+        p.rope_cos = rope_cos;
+        p.rope_sin = rope_sin;
+        p.slots = slots;
+        p.state = state;
+        p.err = err_word();
+        p.cand_val = cand_val;
+        p.cand_idx = cand_idx;
+        p.ticket = ticket();
+        p.barrier = barrier_counter();
+        p.exit_ticket = exit_ticket();
+        p.steps = steps;
+        p.trace = trace;
+        cudaLaunchConfig_t config = {};
+        config.gridDim = dim3(2 * sms);
+        config.blockDim = dim3(kStreamThreads);
+        config.dynamicSmemBytes = persistent_smem<kPersistentStages>();
+        config.stream = stream;
+        cudaLaunchAttribute attribute[1];
+        attribute[0].id = cudaLaunchAttributeCooperative;
+        attribute[0].val.cooperative = 1;
+        config.attrs = attribute;
+        config.numAttrs = 1;
+        return cuda(cudaLaunchKernelEx(&config, decode_persistent<kPersistentStages>, p), "persistent launch");
+    }
+
+    // One decode step at the current position on the chosen path.
+    int enqueue_decode_steps(int steps)
+    {
+        if (use_persistent())
+            return enqueue_persistent(steps);
+        for (int i = 0; i < steps; ++i)
+        {
+            int rc;
+            if (fast)
+            {
+                cudaGraphExec_t exec;
+                rc = graph_for(splits_for(position + i + 1), &exec);
+                if (!rc)
+                    rc = cuda(cudaGraphLaunch(exec, stream), "graph launch");
+            }
+            else
+            {
+                const int saved = position;
+                position += i;
+                rc = enqueue_rows(1, false);
+                position = saved;
+            }
+            if (rc)
+                return rc;
+        }
         return HF_OK;
     }
 
@@ -685,12 +776,7 @@ struct hf_ctx
             const int rows = std::min(capacity, count - first);
             int rc;
             if (rows == 1 && fast && !all_logits)
-            {
-                cudaGraphExec_t exec;
-                rc = graph_for(splits_for(position + 1), &exec);
-                if (!rc)
-                    rc = cuda(cudaGraphLaunch(exec, stream), "graph launch");
-            }
+                rc = enqueue_decode_steps(1);
             else
                 rc = enqueue_rows(rows, all_logits);
             if (rc)
@@ -807,13 +893,13 @@ int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
         || device_alloc(ctx, &ctx->vcache, (size_t) s.layers * P * KVW, "value cache")
         || device_alloc(ctx, &ctx->rope_cos, P * (s.head_width / 2), "rotary cosines")
         || device_alloc(ctx, &ctx->rope_sin, P * (s.head_width / 2), "rotary sines")
-        || device_alloc(ctx, &ctx->slots, P + 1, "sequence slots") || device_alloc(ctx, &ctx->state, 4, "step state")
+        || device_alloc(ctx, &ctx->slots, P + 1, "sequence slots") || device_alloc(ctx, &ctx->state, 8, "step state")
         || device_alloc(ctx, &ctx->cand_val, 1024, "argmax candidates")
         || device_alloc(ctx, &ctx->cand_idx, 1024, "argmax candidates")
         || device_alloc(ctx, &ctx->attn_acc, (size_t) ctx->max_splits * QW, "attention partials")
         || device_alloc(ctx, &ctx->attn_ml, (size_t) ctx->max_splits * s.heads * 2, "attention partials"))
         return bail(HF_E_CUDA);
-    cudaMemset(ctx->state, 0, 4 * sizeof(unsigned));
+    cudaMemset(ctx->state, 0, 8 * sizeof(unsigned));
     cudaMemset(ctx->slots, 0, (P + 1) * sizeof(unsigned));
     cudaMemset(ctx->kcache, 0, (size_t) s.layers * P * KVW * sizeof(float));
     cudaMemset(ctx->vcache, 0, (size_t) s.layers * P * KVW * sizeof(float));
@@ -834,6 +920,28 @@ int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
     if (ctx->cuda(cudaMemcpy(ctx->rope_cos, cosines.data(), cosines.size() * 4, cudaMemcpyHostToDevice), "rotary upload")
         || ctx->cuda(cudaMemcpy(ctx->rope_sin, sines.data(), sines.size() * 4, cudaMemcpyHostToDevice), "rotary upload"))
         return bail(HF_E_CUDA);
+    // The whole-loop kernel: Gemma's grouping (8 query heads over 1 kv head),
+    // the 16384-wide feed-forward its schedule is written for, cooperative
+    // launch, and two resident CTAs per SM.
+    if (ctx->fast && s.heads == 8 && s.kv_heads == 1 && s.intermediate == 16384)
+    {
+        std::vector<LayerDev> table(s.layers);
+        for (int l = 0; l < s.layers; ++l)
+        {
+            const Layer& L = ctx->layers[l];
+            table[l] = {L.qkv.base, L.qkv.scales(), L.o.base, L.o.scales(), L.gu.base, L.gu.scales(), L.down.base,
+                        L.down.scales(), L.in_norm, L.post_norm, ctx->layer_k(l), ctx->layer_v(l)};
+        }
+        if (device_alloc(ctx, &ctx->layer_dev, table.size(), "layer table")
+            || ctx->cuda(cudaMemcpy(ctx->layer_dev, table.data(), table.size() * sizeof(LayerDev), cudaMemcpyHostToDevice),
+                         "layer table upload"))
+            return bail(HF_E_CUDA);
+        int cooperative = 0, resident = 0;
+        cudaDeviceGetAttribute(&cooperative, cudaDevAttrCooperativeLaunch, device);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, decode_persistent<kPersistentStages>, kStreamThreads,
+                                                      persistent_smem<kPersistentStages>());
+        ctx->persistent_ok = cooperative && resident >= 2;
+    }
     if (cudaDeviceSynchronize() != cudaSuccess)
         return bail(HF_E_CUDA);
     *out = ctx;
@@ -851,7 +959,7 @@ void hf_cuda_destroy(hf_ctx* ctx)
         cudaGraphExecDestroy(g.second);
     void* buffers[] = {ctx->pool, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
                        ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slots, ctx->state,
-                       ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging};
+                       ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev};
     for (void* b: buffers)
         if (b)
             cudaFree(b);
@@ -995,12 +1103,7 @@ int hf_cuda_step(hf_ctx* ctx, const uint32_t* tokens, int count, float* logits, 
         return rc;
     const int first = ctx->position;
     if (count == 1 && ctx->fast)
-    {
-        cudaGraphExec_t exec;
-        rc = ctx->graph_for(ctx->splits_for(first + 1), &exec);
-        if (!rc)
-            rc = ctx->cuda(cudaGraphLaunch(exec, ctx->stream), "graph launch");
-    }
+        rc = ctx->enqueue_decode_steps(1);
     else
         rc = ctx->enqueue_rows(count, true);
     if (rc)
@@ -1173,22 +1276,12 @@ int hf_cuda_decode_async(hf_ctx* ctx, int steps)
         return ctx->fail(HF_E_WINDOW, "these steps would carry the sequence past the window");
     if (ctx->position == 0 && steps > 0)
         return ctx->fail(HF_E_INVALID, "a decode step follows a prefill: the sequence is empty");
-    for (int i = 0; i < steps; ++i)
-    {
-        int rc;
-        if (ctx->fast)
-        {
-            cudaGraphExec_t exec;
-            rc = ctx->graph_for(ctx->splits_for(ctx->position + 1), &exec);
-            if (!rc)
-                rc = ctx->cuda(cudaGraphLaunch(exec, ctx->stream), "graph launch");
-        }
-        else
-            rc = ctx->enqueue_rows(1, false);
-        if (rc)
-            return rc;
-        ctx->position += 1;
-    }
+    if (steps == 0)
+        return HF_OK;
+    const int rc = ctx->enqueue_decode_steps(steps);
+    if (rc)
+        return rc;
+    ctx->position += steps;
     return HF_OK;
 }
 
@@ -1268,13 +1361,43 @@ void* hf_cuda_stream(const hf_ctx* ctx)
     return ctx ? (void*) ctx->stream : nullptr;
 }
 
-int hf_cuda_decode_launches(const hf_ctx* ctx)
+int hf_cuda_decode_launches(const hf_ctx* ctx, int steps)
+{
+    if (!ctx || steps < 0)
+        return HF_E_INVALID;
+    if (steps == 0)
+        return 0;
+    if (ctx->use_persistent())
+        return 1;
+    if (!ctx->fast)
+        return steps * (1 + ctx->shape.layers * 7 + 4);
+    int total = 0;
+    for (int i = 0; i < steps; ++i)
+        total += ctx->decode_launch_count(ctx->splits_for(ctx->position + i + 1));
+    return total;
+}
+
+int hf_cuda_set_decode_path(hf_ctx* ctx, int path)
+{
+    if (!ctx || path < HF_DECODE_AUTO || path > HF_DECODE_PERSISTENT)
+        return HF_E_INVALID;
+    if (path == HF_DECODE_PERSISTENT && !ctx->persistent_ok)
+        return ctx->fail(HF_E_INVALID, "the whole-loop kernel does not serve this shape or device");
+    if (path == HF_DECODE_GRAPH && !ctx->fast)
+        return ctx->fail(HF_E_INVALID, "the graph path needs the streaming kernels' shapes");
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    ctx->decode_path = path;
+    return HF_OK;
+}
+
+int hf_cuda_decode_path(const hf_ctx* ctx)
 {
     if (!ctx)
         return HF_E_INVALID;
-    if (!ctx->fast)
-        return 3 + ctx->shape.layers * 7 + 3;
-    return ctx->decode_launch_count(ctx->splits_for(ctx->position + 1));
+    if (ctx->use_persistent())
+        return HF_DECODE_PERSISTENT;
+    return ctx->fast ? HF_DECODE_GRAPH : HF_DECODE_AUTO;
 }
 
 int hf_cuda_fast_path(const hf_ctx* ctx)
@@ -1343,6 +1466,42 @@ int hf_cuda_time_kernel(hf_ctx* ctx, int kernel, int reps, float* mean_us, doubl
     if (bytes_per_launch)
         *bytes_per_launch = bytes;
     return HF_OK;
+}
+
+int hf_cuda_trace_decode(hf_ctx* ctx, int steps, uint64_t* stamps, int capacity, int* ctas, int* events)
+{
+    if (!ctx || !stamps || !ctas || !events || steps <= 0)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    if (!ctx->use_persistent())
+        return ctx->fail(HF_E_INVALID, "phase tracing covers the whole-loop kernel");
+    if (!ctx->all_loaded())
+        return ctx->fail(HF_E_NOT_READY, "this decoder has not been prepared: every weight must be uploaded");
+    if (ctx->position == 0 || ctx->position + steps > ctx->shape.max_positions)
+        return ctx->fail(HF_E_WINDOW, "tracing decodes `steps` tokens after a prefill, inside the window");
+    const int grid = 2 * ctx->sms;
+    if ((long long) capacity < (long long) grid * kTraceEvents)
+        return ctx->fail(HF_E_CAPACITY, "the stamp buffer holds fewer than 2 x SMs x 256 entries");
+    unsigned long long* trace = nullptr;
+    int rc = device_alloc(ctx, &trace, (size_t) grid * kTraceEvents, "trace buffer");
+    if (!rc)
+        rc = ctx->cuda(cudaMemsetAsync(trace, 0, (size_t) grid * kTraceEvents * 8, ctx->stream), "trace clear");
+    if (!rc)
+        rc = ctx->enqueue_persistent(steps, trace);
+    if (!rc)
+    {
+        ctx->position += steps;
+        rc = ctx->cuda(cudaMemcpyAsync(stamps, trace, (size_t) grid * kTraceEvents * 8, cudaMemcpyDeviceToHost,
+                                       ctx->stream),
+                       "trace readback");
+    }
+    if (!rc)
+        rc = ctx->sync();
+    if (trace)
+        cudaFree(trace);
+    *ctas = grid;
+    *events = kTraceEvents;
+    return rc;
 }
 
 int hf_cuda_linear_q8(const float* input, const uint8_t* weights, const float* bias, float* output, uint32_t inner,

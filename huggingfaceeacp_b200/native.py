@@ -27,6 +27,9 @@ HF_E_CUDA = -6
 HF_E_DEVICE = -7
 HF_E_TOKEN = -8
 
+# Decode paths (hf_cuda.h HF_DECODE_*).
+DECODE_AUTO, DECODE_GRAPH, DECODE_PERSISTENT = 0, 1, 2
+
 # Decode-step kernels the timing hook measures (hf_cuda.h HF_KERNEL_*).
 KERNEL_QKV, KERNEL_ATTENTION, KERNEL_OUTPUT, KERNEL_GATE_UP, KERNEL_DOWN, KERNEL_LOGITS = range(6)
 KERNEL_NAMES = ("qkv_rope", "attention", "o_proj_residual", "gate_up_geglu", "down_residual", "logits_argmax")
@@ -194,7 +197,11 @@ def cuda() -> ctypes.CDLL:
         lib.hf_cuda_sync.argtypes = [_vp]
         lib.hf_cuda_stream.argtypes = [_vp]
         lib.hf_cuda_stream.restype = _vp
-        lib.hf_cuda_decode_launches.argtypes = [_vp]
+        lib.hf_cuda_decode_launches.argtypes = [_vp, ctypes.c_int]
+        lib.hf_cuda_set_decode_path.argtypes = [_vp, ctypes.c_int]
+        lib.hf_cuda_trace_decode.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
+                                             ctypes.POINTER(ctypes.c_int)]
+        lib.hf_cuda_decode_path.argtypes = [_vp]
         lib.hf_cuda_fast_path.argtypes = [_vp]
         lib.hf_cuda_linear_q8.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
                                           ctypes.c_int, ctypes.c_int, _vp]
@@ -399,9 +406,24 @@ class Context:
     def stream(self) -> int:
         return int(self.lib.hf_cuda_stream(self.handle) or 0)
 
+    def decode_launches(self, steps: int) -> int:
+        """Kernel launches that decode_async(steps) makes from the current position."""
+        return int(self.lib.hf_cuda_decode_launches(self.handle, steps))
+
+    def trace_decode(self, steps: int, max_ctas: int = 1024) -> np.ndarray:
+        """[ctas, events] %globaltimer stamps (ns) of the first traced step (hf_cuda_trace_decode)."""
+        stamps = np.zeros(max_ctas * 256, dtype=np.uint64)
+        ctas, events = ctypes.c_int(0), ctypes.c_int(0)
+        self.check(self.lib.hf_cuda_trace_decode(self.handle, steps, _ptr(stamps), stamps.size, ctypes.byref(ctas),
+                                                 ctypes.byref(events)))
+        return stamps[: ctas.value * events.value].reshape(ctas.value, events.value)
+
+    def set_decode_path(self, path: int):
+        self.check(self.lib.hf_cuda_set_decode_path(self.handle, path))
+
     @property
-    def decode_launches(self) -> int:
-        return int(self.lib.hf_cuda_decode_launches(self.handle))
+    def decode_path(self) -> int:
+        return int(self.lib.hf_cuda_decode_path(self.handle))
 
     def time_kernel(self, kernel: int, reps: int) -> tuple[float, float]:
         """(mean microseconds, algorithmic bytes) of one decode-step kernel launch."""

@@ -136,17 +136,38 @@ int hf_cuda_generate_greedy(hf_ctx* ctx, const uint32_t* prompt, int prompt_leng
 /* Begins a sequence and enqueues the prompt's prefill plus the argmax that
  * writes the first generated token into slot prompt_length. */
 int hf_cuda_prefill_async(hf_ctx* ctx, const uint32_t* prompt, int prompt_length);
-/* Enqueues `steps` greedy decode steps (CUDA-graph replays), each embedding
- * the token in slot position and writing its argmax into slot position + 1. */
+/* Enqueues `steps` greedy decode steps (one whole-loop launch, or one CUDA
+ * graph per step; hf_cuda_set_decode_path), each embedding the token in slot
+ * position and writing its argmax into slot position + 1. */
 int hf_cuda_decode_async(hf_ctx* ctx, int steps);
 /* Synchronises and copies sequence token slots [first, first + count). */
 int hf_cuda_read_slots(hf_ctx* ctx, int first, int count, uint32_t* out);
 /* Waits for the context's stream; reports a kernel-side error as HF_E_DEVICE. */
 int hf_cuda_sync(hf_ctx* ctx);
-/* The context's cudaStream_t (for events), and how many kernels one decode
- * step launches at the current position. */
+/* The context's cudaStream_t (for events), and how many kernels
+ * hf_cuda_decode_async(ctx, steps) launches from the current position. */
 void* hf_cuda_stream(const hf_ctx* ctx);
-int hf_cuda_decode_launches(const hf_ctx* ctx);
+int hf_cuda_decode_launches(const hf_ctx* ctx, int steps);
+
+/* Which kernels run a decode step (no reference counterpart; the reference
+ * has one kernel sequence): HF_DECODE_PERSISTENT, one cooperative kernel that
+ * runs every step of an hf_cuda_decode_async call with 2 resident CTAs per SM
+ * and grid barriers between phases (Gemma's MQA grouping and feed-forward);
+ * HF_DECODE_GRAPH, one CUDA graph of PDL-chained kernels per step (any shape
+ * the streaming kernels serve); HF_DECODE_AUTO picks the first that serves
+ * the shape. Both compute the same arithmetic. hf_cuda_decode_path reports the
+ * path in use (HF_DECODE_AUTO there means the generic kernels). */
+enum { HF_DECODE_AUTO = 0, HF_DECODE_GRAPH = 1, HF_DECODE_PERSISTENT = 2 };
+int hf_cuda_set_decode_path(hf_ctx* ctx, int path);
+int hf_cuda_decode_path(const hf_ctx* ctx);
+
+/* Phase tracing of the whole-loop kernel (the reference has wall-clock
+ * timings only, Gemma.h:205-224): decodes `steps` tokens like
+ * hf_cuda_decode_async, synchronously, and writes the first step's
+ * %globaltimer stamps (ns): stamps[cta * events + e], thread 0 of every CTA,
+ * e = 0 kernel start, 1 embed done, then entry and exit of every grid barrier
+ * in phase order (unused entries 0). capacity >= 2 * SMs * 256. */
+int hf_cuda_trace_decode(hf_ctx* ctx, int steps, uint64_t* stamps, int capacity, int* ctas, int* events);
 /* 1 when the sm_100a streaming kernels serve this shape, 0 for the generic path. */
 int hf_cuda_fast_path(const hf_ctx* ctx);
 

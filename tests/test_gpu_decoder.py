@@ -238,3 +238,54 @@ def test_decoding_is_deterministic_across_runs():
         b = [ctx.step(PROMPT)[0]] + [ctx.step([t])[0] for t in (7, 8, 9)]
         for x, y in zip(a, b):
             np.testing.assert_array_equal(x, y)
+
+
+# ---- the two fast decode paths -----------------------------------------------
+
+MINI_PERSISTENT = MINI.replace(intermediate=16384)
+
+
+def test_persistent_path_matches_reference_across_context_splits():
+    """The whole-loop kernel (one cooperative launch per call) on a shape it
+    serves, token by token across 1, 2, 4 and 8 attention splits."""
+    p = Pair(MINI_PERSISTENT, seed=13)
+    try:
+        assert p.ctx.decode_path == native.DECODE_PERSISTENT
+        prompt = native.synthetic_tokens(13, 60, MINI_PERSISTENT.vocab)
+        worst = p.step(prompt)
+        for i in range(210):
+            worst = max(worst, p.step([int(prompt[(7 * i) % 60])]))
+        assert worst <= TOLERANCE, worst
+    finally:
+        p.close()
+
+
+def test_graph_and_persistent_paths_agree():
+    with native.Context(MINI_PERSISTENT) as ctx:
+        ctx.load_synthetic(seed=21)
+        rows = {}
+        for path in (native.DECODE_GRAPH, native.DECODE_PERSISTENT):
+            ctx.set_decode_path(path)
+            ctx.begin_sequence()
+            out = [ctx.step(PROMPT)]
+            out += [ctx.step([t]) for t in (3, 1, 4, 1, 5, 9, 2, 6)]
+            rows[path] = out
+        for (lg, hd), (lp, hp) in zip(rows[native.DECODE_GRAPH], rows[native.DECODE_PERSISTENT]):
+            assert ob.worst_error(lp, lg) <= TOLERANCE
+            assert ob.worst_error(hp, hd) <= TOLERANCE
+
+
+def test_persistent_multi_step_launches_feed_tokens_back():
+    """decode_async with many steps per launch: the token each step writes is
+    the one the next step embeds, inside the kernel."""
+    shape = MINI_PERSISTENT.replace(embed_scale=1.0)
+    with native.Context(shape) as ctx:
+        tensors = ctx.load_synthetic(seed=5, keep=True)
+        assert ctx.decode_path == native.DECODE_PERSISTENT
+        expected = ob.greedy_reference(shape, tensors, PROMPT, 40)
+        assert len(set(expected)) > 3
+        assert list(ctx.generate(PROMPT, 40)) == expected
+        ctx.prefill_async(PROMPT)
+        ctx.decode_async(39)  # one launch
+        assert ctx.decode_launches(5) == 1
+        assert list(ctx.read_slots(len(PROMPT), 40)) == expected
