@@ -225,10 +225,12 @@ __device__ __forceinline__ float row_slab_dot(const uint8_t* q, const __half* sc
 // The shared-memory ring a producer warp fills and the consumer warps drain.
 struct Ring
 {
-    uint8_t* quants;  // [NST][kStageQuants]
-    uint8_t* scales;  // [NST][kStageScales]
+    uint8_t* quants;  // [NST][quant_stride]
+    uint8_t* scales;  // [NST][scale_stride]
     uint64_t* full;   // [NST], one arrival + the stage's transaction bytes
     uint64_t* empty;  // [NST], one arrival per consumer warp
+    int quant_stride = kStageQuants;
+    int scale_stride = kStageScales;
 };
 
 // The rows [r0, r1) a CTA owns of a product with N weight rows split over
@@ -278,8 +280,9 @@ __device__ bool produce_slab(const uint8_t* w, const __half* scales, Slab slab, 
         const unsigned qb = (unsigned) rows * K;
         const unsigned sb = (unsigned) rows * (K / 16);
         mbar_expect_tx(&ring.full[b], qb + sb);
-        bulk_load(ring.quants + b * kStageQuants, w + (size_t) first * K, qb, &ring.full[b], policy);
-        bulk_load(ring.scales + b * kStageScales, scale_bytes + (size_t) first * (K / 16), sb, &ring.full[b], policy);
+        bulk_load(ring.quants + b * ring.quant_stride, w + (size_t) first * K, qb, &ring.full[b], policy);
+        bulk_load(ring.scales + b * ring.scale_stride, scale_bytes + (size_t) first * (K / 16), sb, &ring.full[b],
+                  policy);
     }
     return true;
 }
@@ -326,7 +329,8 @@ __device__ __forceinline__ void stage_x_2048(const float* x, const float* norm_w
                 sx[i] = sx[i] * scale * (1.f + norm_w[i]);
     }
     consumer_sync();
-    load_x_slice(sx, lane, xr);
+    if (xr)
+        load_x_slice(sx, lane, xr);
 }
 
 // The norm weights thread `tid` applies in stage_x_2048, loaded ahead of time.
@@ -391,8 +395,8 @@ __device__ bool consume_slab(const GemvArgs& a, Slab slab, const Ring& ring, uns
             continue; // keep `seq` in step with the producer
         const int first = slab.r0 + s * RPS;
         const int rows = min(RPS, slab.r1 - first);
-        const uint8_t* qs = ring.quants + b * kStageQuants;
-        const __half* scs = reinterpret_cast<const __half*>(ring.scales + b * kStageScales);
+        const uint8_t* qs = ring.quants + b * ring.quant_stride;
+        const __half* scs = reinterpret_cast<const __half*>(ring.scales + b * ring.scale_stride);
 
         float v[RPW];
 #pragma unroll

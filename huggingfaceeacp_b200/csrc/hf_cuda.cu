@@ -25,6 +25,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -245,6 +246,7 @@ struct hf_ctx
     size_t staging_bytes = 0;
     int max_splits = 1;
     bool persistent_ok = false; // the cooperative whole-loop kernel serves this shape on this device
+    int prefetch_stages = kPrefetchStages; // HF_PREFETCH_STAGES overrides (a tuning knob)
     int decode_path = HF_DECODE_AUTO;
     LayerDev* layer_dev = nullptr;
 
@@ -509,6 +511,7 @@ struct hf_ctx
         p.barrier = barrier_counter();
         p.exit_ticket = exit_ticket();
         p.steps = steps;
+        p.prefetch_stages = prefetch_stages;
         p.trace = trace;
         cudaLaunchConfig_t config = {};
         config.gridDim = dim3(2 * sms);
@@ -839,6 +842,8 @@ int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
         return bail(HF_E_CUDA);
     configure_once(device);
     ctx->sms = sm_count(device);
+    if (const char* knob = std::getenv("HF_PREFETCH_STAGES"))
+        ctx->prefetch_stages = std::max(0, std::atoi(knob));
     ctx->max_splits = 128;
     const int QH = s.heads / s.kv_heads;
     ctx->fast = s.width == 2048 && s.heads * s.head_width == 2048 && s.head_width == 256 && QH <= 8
@@ -1481,7 +1486,7 @@ int hf_cuda_trace_decode(hf_ctx* ctx, int steps, uint64_t* stamps, int capacity,
         return ctx->fail(HF_E_WINDOW, "tracing decodes `steps` tokens after a prefill, inside the window");
     const int grid = 2 * ctx->sms;
     if ((long long) capacity < (long long) grid * kTraceEvents)
-        return ctx->fail(HF_E_CAPACITY, "the stamp buffer holds fewer than 2 x SMs x 256 entries");
+        return ctx->fail(HF_E_CAPACITY, "the stamp buffer holds fewer than 2 x SMs x 384 entries");
     unsigned long long* trace = nullptr;
     int rc = device_alloc(ctx, &trace, (size_t) grid * kTraceEvents, "trace buffer");
     if (!rc)

@@ -23,6 +23,7 @@
 
 #include "attention.cuh"
 #include "gemv.cuh"
+#include "limb_gemv.cuh"
 
 namespace hfk
 {
@@ -80,13 +81,14 @@ struct PersistentArgs
     unsigned* barrier;      // grid barrier counter (zero at launch)
     unsigned* exit_ticket;  // zero at launch
     int steps;
+    int prefetch_stages;       // stages of L2 prefetch ahead of the ring (0 = none)
     unsigned long long* trace; // [gridDim.x][kTraceEvents] first-step phase stamps, or null
 };
 
 // Phase tracing: thread 0 of every CTA stamps %globaltimer (ns) at kernel
 // start, after the embed, and on entering and leaving every grid barrier of
 // the launch's first step.
-constexpr int kTraceEvents = 256;
+constexpr int kTraceEvents = 384;
 
 __device__ __forceinline__ unsigned long long global_ns()
 {
@@ -158,16 +160,22 @@ struct StageRef
     const uint8_t* quants;
     const uint8_t* scales;
     unsigned quant_bytes, scale_bytes;
+    bool tile; // 16 rows of K = 2048 copied row by row to the padded tile pitch
 };
+
+// One ring slot holds either stage format: a 16-row tile (rows at a 2064-byte
+// pitch, scales at 144) or 32 KiB of contiguous K = 16384 rows.
+constexpr int kSlotQuants = kTileQuantBytes > kStageQuants ? kTileQuantBytes : kStageQuants;
+constexpr int kSlotScales = kTileScaleBytes > kStageScales ? kTileScaleBytes : kStageScales;
 
 __device__ __forceinline__ Plan make_plan(const PersistentArgs& p, int cta, int ctas)
 {
     Plan plan;
-    plan.slab[0] = cta_slab(p.qkv_rows, true, cta, ctas);
-    plan.slab[1] = cta_slab(2048, false, cta, ctas);
-    plan.slab[2] = cta_slab(2 * p.intermediate, true, cta, ctas);
+    plan.slab[0] = cta_tiles(p.qkv_rows, cta, ctas);
+    plan.slab[1] = cta_tiles(2048, cta, ctas);
+    plan.slab[2] = cta_tiles(2 * p.intermediate, cta, ctas);
     plan.slab[3] = cta_slab(2048, false, cta, ctas);
-    plan.slab[4] = cta_slab(p.vocab, false, cta, ctas);
+    plan.slab[4] = cta_tiles(p.vocab, cta, ctas);
     const int rps[5] = {16, 16, 16, 2, 16}; // rows per 32 KiB stage at K = 2048 and 16384
     for (int i = 0; i < 5; ++i)
         plan.stages[i] = (plan.slab[i].r1 - plan.slab[i].r0 + rps[i] - 1) / rps[i];
@@ -205,14 +213,16 @@ __device__ __forceinline__ StageRef plan_stage(const PersistentArgs& p, const Pl
     ref.scales = reinterpret_cast<const uint8_t*>(sc) + (size_t) first * (K / 16);
     ref.quant_bytes = (unsigned) rows * K;
     ref.scale_bytes = (unsigned) rows * (K / 16);
+    ref.tile = K == 2048;
     return ref;
 }
 
-// Stages the producer keeps in flight to L2 beyond the shared-memory ring.
-// While the consumers wait at a grid barrier the ring fills within a few
-// microseconds; these prefetches keep HBM streaming the next products' weights
-// into L2 meanwhile (296 CTAs x 6 x 34 KiB, about 60 MB ahead).
-constexpr int kPrefetchStages = 6;
+// Default stages the producer keeps in flight to L2 beyond the shared-memory
+// ring (PersistentArgs::prefetch_stages, HF_PREFETCH_STAGES). Measured on B200
+// at Gemma-2B sizes: 0 stages 1127 us/token, 2: 1135, 6: 1195, 12: 1379; the
+// prefetched lines were partly evicted before use (DRAM reads grew 7%), so
+// the default is off.
+constexpr int kPrefetchStages = 0;
 
 template <int NST>
 __device__ void persistent_producer(const PersistentArgs& p, const Ring& ring)
@@ -223,7 +233,7 @@ __device__ void persistent_producer(const PersistentArgs& p, const Ring& ring)
     long long prefetched = NST;
     for (long long k = 0; k < total; ++k)
     {
-        const long long until = min(total, k + NST + kPrefetchStages);
+        const long long until = min(total, k + NST + p.prefetch_stages);
         for (; prefetched < until; ++prefetched)
         {
             const StageRef ahead = plan_stage(p, plan, prefetched);
@@ -238,8 +248,21 @@ __device__ void persistent_producer(const PersistentArgs& p, const Ring& ring)
         }
         const StageRef stage = plan_stage(p, plan, k);
         mbar_expect_tx(&ring.full[b], stage.quant_bytes + stage.scale_bytes);
-        bulk_load(ring.quants + b * kStageQuants, stage.quants, stage.quant_bytes, &ring.full[b], policy);
-        bulk_load(ring.scales + b * kStageScales, stage.scales, stage.scale_bytes, &ring.full[b], policy);
+        uint8_t* quants = ring.quants + b * ring.quant_stride;
+        uint8_t* scales = ring.scales + b * ring.scale_stride;
+        if (stage.tile)
+        {
+            for (int r = 0; r < kTileRows; ++r)
+            {
+                bulk_load(quants + r * kTilePitch, stage.quants + r * 2048, 2048, &ring.full[b], policy);
+                bulk_load(scales + r * kScalePitch, stage.scales + r * 128, 128, &ring.full[b], policy);
+            }
+        }
+        else
+        {
+            bulk_load(quants, stage.quants, stage.quant_bytes, &ring.full[b], policy);
+            bulk_load(scales, stage.scales, stage.scale_bytes, &ring.full[b], policy);
+        }
     }
 }
 
@@ -255,10 +278,13 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
     __shared__ unsigned last_cta;
     __shared__ unsigned abort_flag;
     __shared__ float rope_row[256]; // this step's cosines [0, 128) and sines [128, 256)
+    __shared__ float xexp[64];      // per k-block 2^(e - 30) of the limb form of x
+    __shared__ float red[2 * 8 * kTileRows];
 
-    const Ring ring {smem, smem + NST * kStageQuants, full, empty};
-    float* sx = reinterpret_cast<float*>(smem + NST * (kStageQuants + kStageScales)); // x (8 KiB) or down partials
-    float* sattn = sx + 2048;                                                           // attention tile / fold
+    const Ring ring {smem, smem + NST * kSlotQuants, full, empty, kSlotQuants, kSlotScales};
+    float* sx = reinterpret_cast<float*>(smem + NST * (kSlotQuants + kSlotScales)); // x (8 KiB) or down partials
+    float* sattn = sx + 2048;                                                        // attention tile / fold
+    uint2* frags = reinterpret_cast<uint2*>(sattn); // limb B fragments (8 KiB), outside the attention phase
 
     const int tid = threadIdx.x;
     if (tid == 0)
@@ -284,6 +310,14 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
         if (p.trace && tid == 0 && trace_at < kTraceEvents)
             p.trace[(size_t) cta * kTraceEvents + trace_at] = global_ns();
         ++trace_at;
+    };
+    uint32_t bfrag[8][2];
+    float bfactor[8];
+    // x of a K = 2048 product, normalised in sx, into this warp's limb B fragments.
+    auto limbs = [&]() {
+        make_limb_frags(sx, frags, xexp, tid);
+        consumer_sync();
+        load_limb_frags(frags, xexp, tid >> 5, tid & 31, bfrag, bfactor);
     };
     auto barrier = [&]() {
         stamp();
@@ -350,8 +384,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
                 a.kv_heads = 1;
                 a.head_dim = p.head_dim;
                 a.err = p.err;
-                stage_x_2048(l == 0 ? nullptr : p.hidden, L.in_norm, p.eps, sx, reduce, tid, xr, norm_regs);
-                consume_slab<2048, Epi::QkvRope, NST>(a, cta_slab(p.qkv_rows, true, cta, ctas), ring, seq, xr, sx,
+                stage_x_2048(l == 0 ? nullptr : p.hidden, L.in_norm, p.eps, sx, reduce, tid, nullptr, norm_regs);
+                limbs();
+                stamp();
+                consume_tiles<Epi::QkvRope, NST>(a, cta_tiles(p.qkv_rows, cta, ctas), ring, seq, bfrag, bfactor, red,
                                                       position, best, best_i);
             }
             if (!barrier())
@@ -418,8 +454,10 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
                 a.N = 2048;
                 a.out = p.hidden;
                 a.err = p.err;
-                stage_x_2048(p.attended, nullptr, p.eps, sx, reduce, tid, xr);
-                consume_slab<2048, Epi::Residual, NST>(a, cta_slab(2048, false, cta, ctas), ring, seq, xr, sx,
+                stage_x_2048(p.attended, nullptr, p.eps, sx, reduce, tid, nullptr);
+                limbs();
+                stamp();
+                consume_tiles<Epi::Residual, NST>(a, cta_tiles(2048, cta, ctas), ring, seq, bfrag, bfactor, red,
                                                        position, best, best_i);
             }
             load_norm_regs(L.post_norm, tid, norm_regs);
@@ -434,9 +472,11 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
                 a.N = 2 * p.intermediate;
                 a.out = p.act;
                 a.err = p.err;
-                stage_x_2048(p.hidden, L.post_norm, p.eps, sx, reduce, tid, xr, norm_regs);
-                consume_slab<2048, Epi::GeGLU, NST>(a, cta_slab(2 * p.intermediate, true, cta, ctas), ring, seq, xr,
-                                                    sx, position, best, best_i);
+                stage_x_2048(p.hidden, L.post_norm, p.eps, sx, reduce, tid, nullptr, norm_regs);
+                limbs();
+                stamp();
+                consume_tiles<Epi::GeGLU, NST>(a, cta_tiles(2 * p.intermediate, cta, ctas), ring, seq, bfrag, bfactor,
+                                                    red, position, best, best_i);
             }
             if (!barrier())
                 return;
@@ -450,6 +490,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
                 a.out = p.hidden;
                 a.err = p.err;
                 load_x_wide<16384>(p.act, tid, xr);
+                stamp();
                 consume_slab<16384, Epi::Residual, NST>(a, cta_slab(2048, false, cta, ctas), ring, seq, xr, sx,
                                                         position, best, best_i);
             }
@@ -474,9 +515,12 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
             a.err = p.err;
             float best = -INFINITY;
             unsigned best_i = 0xFFFFFFFFu;
-            stage_x_2048(p.hidden, p.final_norm, p.eps, sx, reduce, tid, xr, norm_regs);
-            consume_slab<2048, Epi::Logits, NST>(a, cta_slab(p.vocab, false, cta, ctas), ring, seq, xr, sx, position,
+            stage_x_2048(p.hidden, p.final_norm, p.eps, sx, reduce, tid, nullptr, norm_regs);
+            limbs();
+            stamp();
+            consume_tiles<Epi::Logits, NST>(a, cta_tiles(p.vocab, cta, ctas), ring, seq, bfrag, bfactor, red, position,
                                                  best, best_i);
+            warp_best(best, best_i);
             logits_fold(a, position, best, best_i, cand_v, cand_i, &last_cta);
         }
         if (!barrier()) // the next step embeds the token just written
@@ -504,7 +548,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
 template <int NST>
 constexpr size_t persistent_smem()
 {
-    return (size_t) NST * (kStageQuants + kStageScales) + 2048 * sizeof(float)
-           + mqa_fast_smem<kAttnHeads, kAttnTile>();
+    constexpr size_t attention = mqa_fast_smem<kAttnHeads, kAttnTile>();
+    return (size_t) NST * (kSlotQuants + kSlotScales) + 2048 * sizeof(float)
+           + (attention > (size_t) kLimbFragBytes ? attention : (size_t) kLimbFragBytes);
 }
 } // namespace hfk

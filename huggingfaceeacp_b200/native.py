@@ -412,7 +412,7 @@ class Context:
 
     def trace_decode(self, steps: int, max_ctas: int = 1024) -> np.ndarray:
         """[ctas, events] %globaltimer stamps (ns) of the first traced step (hf_cuda_trace_decode)."""
-        stamps = np.zeros(max_ctas * 256, dtype=np.uint64)
+        stamps = np.zeros(max_ctas * 384, dtype=np.uint64)
         ctas, events = ctypes.c_int(0), ctypes.c_int(0)
         self.check(self.lib.hf_cuda_trace_decode(self.handle, steps, _ptr(stamps), stamps.size, ctypes.byref(ctas),
                                                  ctypes.byref(events)))

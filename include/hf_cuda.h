@@ -166,7 +166,8 @@ int hf_cuda_decode_path(const hf_ctx* ctx);
  * hf_cuda_decode_async, synchronously, and writes the first step's
  * %globaltimer stamps (ns): stamps[cta * events + e], thread 0 of every CTA,
  * e = 0 kernel start, 1 embed done, then entry and exit of every grid barrier
- * in phase order (unused entries 0). capacity >= 2 * SMs * 256. */
+ * in phase order, with a stamp where each product starts streaming (unused
+ * entries 0). capacity >= 2 * SMs * 384. */
 int hf_cuda_trace_decode(hf_ctx* ctx, int steps, uint64_t* stamps, int capacity, int* ctas, int* events);
 /* 1 when the sm_100a streaming kernels serve this shape, 0 for the generic path. */
 int hf_cuda_fast_path(const hf_ctx* ctx);
