@@ -94,13 +94,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned b
         : "memory");
 }
 
-// Starts moving `bytes` (a multiple of 16, 16-byte aligned) of global memory
-// into L2 without waiting for or tracking it.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes)
-{
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 __device__ __forceinline__ uint64_t evict_first_policy()
 {
     uint64_t policy;

@@ -187,6 +187,12 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar)
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// `count` arrivals at once.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar, unsigned count)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ void consumer_sync()
 {
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
@@ -248,12 +254,13 @@ __device__ __forceinline__ Slab cta_slab(int N, bool pairs, int cta, int ctas)
     return pairs ? Slab {2 * u0, 2 * u1} : Slab {u0, u1};
 }
 
-__device__ __forceinline__ void init_ring(const Ring& ring, int nst)
+// `arrivals`: the consumer-warp arrivals that release a slot.
+__device__ __forceinline__ void init_ring(const Ring& ring, int nst, int arrivals = kConsumerWarps)
 {
     for (int s = 0; s < nst; ++s)
     {
         mbar_init(&ring.full[s], 1);
-        mbar_init(&ring.empty[s], kConsumerWarps);
+        mbar_init(&ring.empty[s], arrivals);
     }
     mbar_fence_init();
 }
@@ -476,9 +483,10 @@ __device__ bool consume_slab(const GemvArgs& a, Slab slab, const Ring& ring, uns
     return ok;
 }
 
-// The CTA's logits candidate (folded over the consumer warps), then the grid's
+// The CTA's logits candidate (folded over its WARPS consumer warps, barrier 1), then the grid's
 // through a ticket: the last CTA folds every CTA's candidate in CTA order.
 // Returns true in the CTA that did the final fold.
+template <int WARPS = kConsumerWarps>
 __device__ bool logits_fold(const GemvArgs& a, unsigned position, float best, unsigned best_i, float* cand_v,
                             unsigned* cand_i, unsigned* last_cta)
 {
@@ -488,10 +496,10 @@ __device__ bool logits_fold(const GemvArgs& a, unsigned position, float best, un
         cand_v[warp] = best;
         cand_i[warp] = best_i;
     }
-    consumer_sync();
+    asm volatile("bar.sync 1, %0;" ::"n"(WARPS * 32) : "memory");
     if (tid == 0)
     {
-        for (int w = 0; w < kConsumerWarps; ++w)
+        for (int w = 0; w < WARPS; ++w)
             if (cand_i[w] != 0xFFFFFFFFu && (best_i == 0xFFFFFFFFu || better_candidate(cand_v[w], cand_i[w], best, best_i)))
             {
                 best = cand_v[w];
@@ -502,7 +510,7 @@ __device__ bool logits_fold(const GemvArgs& a, unsigned position, float best, un
         __threadfence();
         *last_cta = atomicAdd(a.ticket, 1u) == gridDim.x - 1 ? 1u : 0u;
     }
-    consumer_sync();
+    asm volatile("bar.sync 1, %0;" ::"n"(WARPS * 32) : "memory");
     const bool last = *last_cta != 0;
     if (last && warp == 0)
     {

@@ -61,6 +61,7 @@ int stream_grid(int K, int units, int sms)
 struct Q8
 {
     uint8_t* base = nullptr;
+    uint8_t* records = nullptr; // the stage-record copy the whole-loop kernel streams, or null
     int rows = 0;
     int cols = 0;
     const __half* scales() const { return reinterpret_cast<const __half*>(base + (size_t) rows * cols); }
@@ -221,6 +222,7 @@ struct hf_ctx
     std::string error;
 
     uint8_t* pool = nullptr;
+    uint8_t* record_pool = nullptr; // stage records of every Q8 weight (the whole-loop kernel's copy)
     Q8 embedding;
     float* final_norm = nullptr;
     std::vector<Layer> layers;
@@ -246,7 +248,7 @@ struct hf_ctx
     size_t staging_bytes = 0;
     int max_splits = 1;
     bool persistent_ok = false; // the cooperative whole-loop kernel serves this shape on this device
-    int prefetch_stages = kPrefetchStages; // HF_PREFETCH_STAGES overrides (a tuning knob)
+    int gate_point = 1; // HF_GATE overrides (a tuning knob of the whole-loop kernel)
     int decode_path = HF_DECODE_AUTO;
     LayerDev* layer_dev = nullptr;
 
@@ -274,6 +276,12 @@ struct hf_ctx
     unsigned* ticket() const { return state + 2; }
     unsigned* barrier_counter() const { return state + 3; }
     unsigned* exit_ticket() const { return state + 4; }
+    // The whole-loop kernel runs one CTA per SM.
+    int persistent_grid() const
+    {
+        return sms;
+    }
+
     bool use_persistent() const
     {
         return persistent_ok && decode_path != HF_DECODE_GRAPH;
@@ -483,6 +491,7 @@ struct hf_ctx
         p.n_layers = s.layers;
         p.embed = embedding.base;
         p.embed_scales = embedding.scales();
+        p.embed_records = embedding.records;
         p.final_norm = final_norm;
         p.heads = s.heads;
         p.head_dim = s.head_width;
@@ -511,11 +520,11 @@ struct hf_ctx
         p.barrier = barrier_counter();
         p.exit_ticket = exit_ticket();
         p.steps = steps;
-        p.prefetch_stages = prefetch_stages;
+        p.gate_point = gate_point;
         p.trace = trace;
         cudaLaunchConfig_t config = {};
-        config.gridDim = dim3(2 * sms);
-        config.blockDim = dim3(kStreamThreads);
+        config.gridDim = dim3(persistent_grid());
+        config.blockDim = dim3(kPThreads);
         config.dynamicSmemBytes = persistent_smem<kPersistentStages>();
         config.stream = stream;
         cudaLaunchAttribute attribute[1];
@@ -842,8 +851,8 @@ int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
         return bail(HF_E_CUDA);
     configure_once(device);
     ctx->sms = sm_count(device);
-    if (const char* knob = std::getenv("HF_PREFETCH_STAGES"))
-        ctx->prefetch_stages = std::max(0, std::atoi(knob));
+    if (const char* knob = std::getenv("HF_GATE"))
+        ctx->gate_point = std::max(0, std::min(2, std::atoi(knob)));
     ctx->max_splits = 128;
     const int QH = s.heads / s.kv_heads;
     ctx->fast = s.width == 2048 && s.heads * s.head_width == 2048 && s.head_width == 256 && QH <= 8
@@ -926,16 +935,31 @@ int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
         || ctx->cuda(cudaMemcpy(ctx->rope_sin, sines.data(), sines.size() * 4, cudaMemcpyHostToDevice), "rotary upload"))
         return bail(HF_E_CUDA);
     // The whole-loop kernel: Gemma's grouping (8 query heads over 1 kv head),
-    // the 16384-wide feed-forward its schedule is written for, cooperative
-    // launch, and two resident CTAs per SM.
-    if (ctx->fast && s.heads == 8 && s.kv_heads == 1 && s.intermediate == 16384)
+    // the 16384-wide feed-forward its schedule is written for, a vocabulary of
+    // whole 16-row records, enough SMs for the down product's per-CTA limit,
+    // cooperative launch, and one resident CTA per SM. It streams its own copy
+    // of every weight as stage records (build_records), at the same offsets in
+    // a second pool.
+    if (ctx->fast && s.heads == 8 && s.kv_heads == 1 && s.intermediate == 16384 && s.vocab % kTileRows == 0
+        && ctx->sms * kMaxDownRecords >= s.width / 2)
     {
+        if (ctx->cuda(cudaMalloc(&ctx->record_pool, pool_bytes), "record pool"))
+            return bail(HF_E_CUDA);
+        auto mirror = [&](Q8& t) { t.records = ctx->record_pool + (t.base - ctx->pool); };
+        mirror(ctx->embedding);
+        for (auto& L: ctx->layers)
+        {
+            mirror(L.qkv);
+            mirror(L.o);
+            mirror(L.gu);
+            mirror(L.down);
+        }
         std::vector<LayerDev> table(s.layers);
         for (int l = 0; l < s.layers; ++l)
         {
             const Layer& L = ctx->layers[l];
-            table[l] = {L.qkv.base, L.qkv.scales(), L.o.base, L.o.scales(), L.gu.base, L.gu.scales(), L.down.base,
-                        L.down.scales(), L.in_norm, L.post_norm, ctx->layer_k(l), ctx->layer_v(l)};
+            table[l] = {L.qkv.records, L.o.records, L.gu.records, L.down.records, L.in_norm, L.post_norm,
+                        ctx->layer_k(l), ctx->layer_v(l)};
         }
         if (device_alloc(ctx, &ctx->layer_dev, table.size(), "layer table")
             || ctx->cuda(cudaMemcpy(ctx->layer_dev, table.data(), table.size() * sizeof(LayerDev), cudaMemcpyHostToDevice),
@@ -943,9 +967,9 @@ int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
             return bail(HF_E_CUDA);
         int cooperative = 0, resident = 0;
         cudaDeviceGetAttribute(&cooperative, cudaDevAttrCooperativeLaunch, device);
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, decode_persistent<kPersistentStages>, kStreamThreads,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, decode_persistent<kPersistentStages>, kPThreads,
                                                       persistent_smem<kPersistentStages>());
-        ctx->persistent_ok = cooperative && resident >= 2;
+        ctx->persistent_ok = cooperative && resident >= 1;
     }
     if (cudaDeviceSynchronize() != cudaSuccess)
         return bail(HF_E_CUDA);
@@ -962,7 +986,7 @@ void hf_cuda_destroy(hf_ctx* ctx)
         cudaStreamSynchronize(ctx->stream);
     for (auto& g: ctx->graphs)
         cudaGraphExecDestroy(g.second);
-    void* buffers[] = {ctx->pool, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
+    void* buffers[] = {ctx->pool, ctx->record_pool, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
                        ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slots, ctx->state,
                        ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev};
     for (void* b: buffers)
@@ -1029,6 +1053,15 @@ int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, 
             permute_q8_rows<<<rows, 256>>>(ctx->staging, rows, cols, target->base, target->rows, dst_row0, mode, group);
             rc = ctx->cuda(cudaDeviceSynchronize(), "weight permutation");
         }
+    }
+    if (!rc && target->records)
+    {
+        // Rebuild the tensor's records (q/k/v arrive in three uploads: each
+        // rebuild covers the whole tensor).
+        const int rows_per_record = 32768 / target->cols;
+        build_records<<<target->rows / rows_per_record, 256>>>(target->base, target->rows, target->cols,
+                                                               target->records);
+        rc = ctx->cuda(cudaDeviceSynchronize(), "record build");
     }
     if (rc)
         return rc;
@@ -1484,9 +1517,9 @@ int hf_cuda_trace_decode(hf_ctx* ctx, int steps, uint64_t* stamps, int capacity,
         return ctx->fail(HF_E_NOT_READY, "this decoder has not been prepared: every weight must be uploaded");
     if (ctx->position == 0 || ctx->position + steps > ctx->shape.max_positions)
         return ctx->fail(HF_E_WINDOW, "tracing decodes `steps` tokens after a prefill, inside the window");
-    const int grid = 2 * ctx->sms;
+    const int grid = ctx->persistent_grid();
     if ((long long) capacity < (long long) grid * kTraceEvents)
-        return ctx->fail(HF_E_CAPACITY, "the stamp buffer holds fewer than 2 x SMs x 384 entries");
+        return ctx->fail(HF_E_CAPACITY, "the stamp buffer holds fewer than SMs x 1024 entries");
     unsigned long long* trace = nullptr;
     int rc = device_alloc(ctx, &trace, (size_t) grid * kTraceEvents, "trace buffer");
     if (!rc)

@@ -16,70 +16,65 @@
 // accumulation across blocks; the activation itself is represented to
 // 2^-31 of its block's largest magnitude, finer than its own fp32 significand.
 //
-// Shared-memory stage: 16 weight rows x 2048 k, each row copied by its own
-// 1-D bulk copy to a 2064-byte pitch (2048 + 16), so the eight row addresses
-// of every `ldmatrix` fall in distinct banks; the rows' 64 fp16 scales at a
-// 144-byte pitch for the same reason. A warp owns k-blocks [8w, 8w + 8) of the
-// stage and keeps their B fragments (x limbs) in 16 registers for a whole
-// product.
+// Stage records. The persistent decode streams K = 2048 weights as records
+// of 16 rows (34,816 bytes, one bulk copy each): 32,768 bytes of quants, row
+// r at r * 2048, its 16-byte chunk c stored at chunk c ^ (r & 7) (so the eight
+// row addresses of every `ldmatrix` fall in distinct banks), then the 1,024
+// fp16 scales k-block-major, scale (r, kb) at kb * 16 + r. A warp owns
+// k-blocks [8w, 8w + 8) of the stage and keeps their B fragments (x limbs) in
+// 16 registers for a whole product.
 #pragma once
 
 #include "gemv.cuh"
 
 namespace hfk
 {
-constexpr int kTileRows = 16;                                  // weight rows per stage
-constexpr int kTilePitch = 2048 + 16;                          // shared-memory bytes per row of quants
-constexpr int kScalePitch = 128 + 16;                          // shared-memory bytes per row of scales
-constexpr int kTileQuantBytes = kTileRows * kTilePitch;        // 33,024
-constexpr int kTileScaleBytes = kTileRows * kScalePitch;       // 2,304
-constexpr int kLimbFragBytes = 64 * 16 * 8;                    // B fragments of one 2048-wide x: 8 KiB
+constexpr int kTileRows = 16;                                    // weight rows per K = 2048 record
+constexpr int kRecordQuants = 32768;                             // quants of one record (either kind)
+constexpr int kRecordBytes = kRecordQuants + kRecordQuants / 16; // with their scales: 34,816
+constexpr int kLimbFragBytes = 64 * 16 * 8;                      // B fragments of one 2048-wide x: 8 KiB
 
-// x in [0, 2048) (shared memory) -> per k-block exponent factors 2^(e-30)
-// and the B fragments of its limbs: frags[kb][lane16] = (b0, b1) for lanes
-// g*4 + t with g < 4 (limb g); lanes g >= 4 read zeros. 256 consumer threads:
-// thread = 4 * kb + t owns x[kb*32 + 4t + i] and x[kb*32 + 16 + 4t + i].
-__device__ __forceinline__ void make_limb_frags(const float* sx, uint2* frags, float* xexp, int tid)
+// The limb form of a 2048-wide x held one float4 per thread of 512 (x[4 tid,
+// 4 tid + 4)): per k-block factors xexp[kb] = 2^(e - 30) and the B fragments
+// frags[kb][lane16] = (b0, b1) for lanes g * 4 + t with g < 4 (limb g): b0
+// packs limb g of x[kb*32 + 4t .. + 3], b1 of x[kb*32 + 16 + 4t .. + 3]. The
+// eight lanes 8 kb .. 8 kb + 7 hold k-block kb; its exponent e (largest |x| <
+// 2^e) is frexp's exponent of the largest magnitude, read from its exponent
+// bits, and at least -96 (zero and subnormal blocks take -96, as frexp's
+// exponent clamped there does), which keeps 2^(30 - e) a normal float.
+__device__ __forceinline__ void limbs_from_regs(float4 v, uint2* frags, float* xexp, int tid)
 {
-    const int kb = tid >> 2, t = tid & 3;
-    float v[8];
+    const int kb = tid >> 3, j = tid & 7;
+    float largest = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    largest = fmaxf(largest, __shfl_xor_sync(0xFFFFFFFFu, largest, 1));
+    largest = fmaxf(largest, __shfl_xor_sync(0xFFFFFFFFu, largest, 2));
+    largest = fmaxf(largest, __shfl_xor_sync(0xFFFFFFFFu, largest, 4));
+    const int e = max((int) ((__float_as_uint(largest) >> 23) & 0xFFu) - 126, -96);
+    const float up = __uint_as_float((unsigned) (30 - e + 127) << 23); // 2^(30 - e)
+    if (j == 0)
+        xexp[kb] = __uint_as_float((unsigned) (e - 30 + 127) << 23); // 2^(e - 30)
+    const float vals[4] = {v.x, v.y, v.z, v.w};
+    uint32_t packed[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
     for (int i = 0; i < 4; ++i)
     {
-        v[i] = sx[kb * 32 + 4 * t + i];
-        v[4 + i] = sx[kb * 32 + 16 + 4 * t + i];
-    }
-    float largest = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        largest = fmaxf(largest, fabsf(v[i]));
-    largest = fmaxf(largest, __shfl_xor_sync(0xFFFFFFFFu, largest, 1));
-    largest = fmaxf(largest, __shfl_xor_sync(0xFFFFFFFFu, largest, 2));
-    int e = 0;
-    frexpf(largest, &e); // largest < 2^e (0 -> e = 0: X = 0)
-    e = max(e, -96);      // keeps 2^(30 - e) finite for blocks below 2^-96
-    const float up = ldexpf(1.f, 30 - e);
-    if (t == 0)
-        xexp[kb] = ldexpf(1.f, e - 30);
-    uint32_t packed[4][2] = {};
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-    {
-        int X = __float2int_rn(v[i] * up);
+        int X = __float2int_rn(vals[i] * up);
         const int l0 = ((X + 128) & 0xFF) - 128;
         X = (X - l0) >> 8;
         const int l1 = ((X + 128) & 0xFF) - 128;
         X = (X - l1) >> 8;
         const int l2 = ((X + 128) & 0xFF) - 128;
         const int l3 = (X - l2) >> 8;
-        const int limbs[4] = {l0, l1, l2, l3};
-#pragma unroll
-        for (int g = 0; g < 4; ++g)
-            packed[g][i >> 2] |= ((uint32_t) limbs[g] & 0xFFu) << (8 * (i & 3));
+        packed[0] |= ((uint32_t) l0 & 0xFFu) << (8 * i);
+        packed[1] |= ((uint32_t) l1 & 0xFFu) << (8 * i);
+        packed[2] |= ((uint32_t) l2 & 0xFFu) << (8 * i);
+        packed[3] |= ((uint32_t) l3 & 0xFFu) << (8 * i);
     }
+    uint32_t* words = reinterpret_cast<uint32_t*>(frags);
+    const int t = j & 3, half = j >> 2; // x[kb*32 + 4j ..] is word (t, half) of the fragment
 #pragma unroll
     for (int g = 0; g < 4; ++g)
-        frags[kb * 16 + g * 4 + t] = make_uint2(packed[g][0], packed[g][1]);
+        words[(kb * 16 + g * 4 + t) * 2 + half] = packed[g];
 }
 
 // One warp's B fragments for its eight k-blocks, and the per-k-block factors
@@ -115,29 +110,28 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], const uint32_t (&a)[4], uint
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
 
-// This warp's partial dot products of the stage's 16 rows over its 256
+// This warp's partial dot products of the record's 16 rows over its 256
 // columns: rows g (first) and g + 8 (second), valid in lanes with t == 0
 // after the quad reduction.
-__device__ __forceinline__ float2 tile_partial(const uint8_t* quants, const uint8_t* scales, int warp, int lane,
+__device__ __forceinline__ float2 tile_partial(const uint8_t* quants, const __half* scales, int warp, int lane,
                                                const uint32_t (&b)[8][2], const float (&factor)[8])
 {
     const int g = lane >> 2;
     const int m = lane >> 3;                                  // the ldmatrix matrix this lane addresses
-    const int row = (lane & 7) + 8 * (m & 1), chunk = m >> 1; // its row and 16-byte k-chunk
-    const uint8_t* a_row = quants + row * kTilePitch + chunk * 16;
-    const __half* s_g = reinterpret_cast<const __half*>(scales + g * kScalePitch);
-    const __half* s_g8 = reinterpret_cast<const __half*>(scales + (g + 8) * kScalePitch);
+    const int row = (lane & 7) + 8 * (m & 1), chunk = m >> 1; // its row and 16-byte half of the k-block
+    const uint8_t* a_row = quants + row * 2048;
+    const int swizzle = row & 7;
     float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
     {
         const int kb = 8 * warp + j;
         uint32_t a[4];
-        ldmatrix_x4(a, a_row + kb * 32);
+        ldmatrix_x4(a, a_row + (((2 * kb + chunk) ^ swizzle) << 4));
         int c[4];
         mma_s8(c, a, b[j][0], b[j][1]);
-        acc0 = fmaf((float) (c[0] + 256 * c[1]), factor[j] * __half2float(s_g[kb]), acc0);
-        acc1 = fmaf((float) (c[2] + 256 * c[3]), factor[j] * __half2float(s_g8[kb]), acc1);
+        acc0 = fmaf((float) (c[0] + 256 * c[1]), factor[j] * __half2float(scales[kb * kTileRows + g]), acc0);
+        acc1 = fmaf((float) (c[2] + 256 * c[3]), factor[j] * __half2float(scales[kb * kTileRows + g + 8]), acc1);
     }
     acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
     acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
@@ -192,11 +186,12 @@ __device__ bool consume_tiles(const GemvArgs& a, Slab slab, const Ring& ring, un
         }
         float2 part = make_float2(0.f, 0.f);
         if (ok)
-            part = tile_partial(ring.quants + buf * ring.quant_stride, ring.scales + buf * ring.scale_stride, warp,
-                                lane, b, factor);
+            part = tile_partial(ring.quants + buf * ring.quant_stride,
+                                reinterpret_cast<const __half*>(ring.scales + buf * ring.scale_stride), warp, lane, b,
+                                factor);
         __syncwarp();
         if (lane == 0)
-            mbar_arrive(&ring.empty[buf]);
+            mbar_arrive(&ring.empty[buf], (unsigned) GROUPS); // a slot takes kConsumerWarps * GROUPS arrivals
         float* r = gred + (mine & 1) * 8 * kTileRows;
         if ((lane & 3) == 0)
         {

@@ -198,6 +198,46 @@ __global__ void permute_q8_rows(const uint8_t* src, int rows, int K, uint8_t* ds
         ds[i] = ss[i];
 }
 
+// The stage records the persistent decode streams, built from a tensor in
+// device layout (quants [rows][K], then scales [rows][K / 32]); one CTA per
+// record.
+//   K = 2048: 16 rows; quants row r at r * 2048 with 16-byte chunk c stored at
+//     chunk c ^ (r & 7); then the scales k-block-major, (r, kb) at kb * 16 + r.
+//   K > 2048: 32768 / K rows; quants row-major, then the rows' scales
+//     row-major: a plain concatenation.
+__global__ void __launch_bounds__(256) build_records(const uint8_t* src, int rows, int K, uint8_t* dst)
+{
+    const int rows_per_record = 32768 / K;
+    const int first = blockIdx.x * rows_per_record;
+    if (first + rows_per_record > rows)
+        return;
+    const uint4* sq = reinterpret_cast<const uint4*>(src + (size_t) first * K);
+    const __half* ss = reinterpret_cast<const __half*>(src + (size_t) rows * K) + (size_t) first * (K / kBlock);
+    uint8_t* record = dst + (size_t) blockIdx.x * (32768 + 2048);
+    uint4* dq = reinterpret_cast<uint4*>(record);
+    __half* ds = reinterpret_cast<__half*>(record + 32768);
+    if (K == 2048)
+    {
+        for (int i = threadIdx.x; i < 2048; i += blockDim.x)
+        {
+            const int r = i >> 7, c = i & 127;
+            dq[r * 128 + (c ^ (r & 7))] = sq[i];
+        }
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x)
+        {
+            const int kb = i >> 4, r = i & 15;
+            ds[i] = ss[r * 64 + kb];
+        }
+    }
+    else
+    {
+        for (int i = threadIdx.x; i < 2048; i += blockDim.x)
+            dq[i] = sq[i];
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x)
+            ds[i] = ss[i];
+    }
+}
+
 // Int8Blocks.cpp:114-136 on the device, one warp per block of 32: the same
 // fp16 round-to-nearest-even scale and the same double division with
 // ties-to-even rounding, so the bytes equal the host quantizer's.

@@ -2,23 +2,27 @@
 //
 // The graph-of-kernels step (hf_cuda.cu) pays a fixed cost at each of its ~92
 // kernel boundaries: the next kernel's CTAs launch, fetch their first weights
-// and ramp while HBM idles. Here 2 CTAs per SM stay resident for `steps`
-// decode steps. Each CTA's producer warp streams its row slab of every weight
-// matrix of every layer and step, in order, into a 2-stage shared-memory ring;
-// it never waits for activations, so while the consumer warps sit at a grid
-// barrier (every product needs the whole previous activation vector) the next
-// product's weights are already landing. The per-step phases, each ended by a
-// grid barrier:
+// and ramp while HBM idles. Here one CTA per SM stays resident for `steps`
+// decode steps. Its producer thread streams the CTA's share of every weight
+// matrix of every layer and step, in order, as stage records (build_records:
+// 34,816 bytes, one bulk copy each) into a 4-slot shared-memory ring; it never
+// waits for activations, so while the consumers sit at a grid barrier (every
+// product needs the whole previous activation vector) the next products'
+// weights are already landing. Sixteen consumer warps form two groups of eight
+// that take alternate records. The per-step phases, each ended by a grid
+// barrier:
 //
 //   embed (every CTA, locally) | per layer: q/k/v + RoPE + cache write |
-//   attention (2 CTAs per context split, 4 heads each) | [split merge] |
-//   o_proj + residual | gate/up + GeGLU | down + residual | then logits +
-//   argmax (ticket fold writes the next token's slot)
+//   attention (one CTA per 16-key context split, a group per four heads) |
+//   [split merge, long contexts only] | o_proj + residual (short contexts fold
+//   the splits while staging x) | gate/up + GeGLU | down + residual | then
+//   logits + argmax (ticket fold writes the next token's slot)
 //
-// Phase work and arithmetic are those of the standalone kernels
-// (q8_gemv_stream, mqa_block), so results are identical to the graph path.
 // Every cross-CTA read goes through L2 (ld.global.cg / cp.async.cg): an SM's L1
-// may hold lines of an activation from an earlier phase.
+// may hold lines of an activation from an earlier phase. Small values that
+// every thread of every CTA needs (a position, a token, the splits' softmax
+// statistics) are read once per CTA and shared through shared memory: read by
+// every warp they would queue on the single L2 line that holds them.
 #pragma once
 
 #include "attention.cuh"
@@ -27,9 +31,20 @@
 
 namespace hfk
 {
-constexpr int kPersistentStages = 2;
-constexpr int kAttnTile = 16;
-constexpr int kAttnHeads = 4; // query heads per attention CTA (two CTAs per split)
+constexpr int kPersistentStages = 4;                        // ring slots
+constexpr int kPGroups = 2;                                 // consumer groups of eight warps
+constexpr int kPWarps = kPGroups * kConsumerWarps;          // 16 consumer warps
+constexpr int kPConsumers = kPWarps * 32;                   // 512 consumer threads
+constexpr int kPThreads = kPConsumers + 32;                 // and the producer warp
+constexpr int kAttnTile = 16;                               // keys per attention tile
+constexpr int kAttnKeysPerSplit = kAttnTile;                // context rows per split: one tile
+constexpr int kAttnHeads = 4;                               // query heads per consumer group
+constexpr int kAttnTileFloats = 2 * kAttnTile * 256;        // the K rows, then the V rows
+constexpr int kAttnFoldFloats = 8 * kAttnHeads * 256 + 2 * 8 * kAttnHeads; // one group's warp fold
+constexpr int kAttnAreaFloats = kPGroups * kAttnFoldFloats; // the tile, then (reusing it) both folds
+static_assert(kAttnAreaFloats >= kAttnTileFloats, "the fold area holds the tile");
+constexpr int kFusedMergeSplits = 8;                        // splits folded inside the o_proj x staging
+constexpr int kMaxDownRecords = 8;                          // 2-row down records a CTA may own
 constexpr unsigned kBarrierSpinLimit = 1u << 20;
 enum : unsigned
 {
@@ -37,16 +52,14 @@ enum : unsigned
 };
 constexpr unsigned kErrAbort = kErrWaitTimeout | kErrBarrierTimeout; // a wait gave up: every CTA leaves
 
+// A layer's weights as stage records (build_records): q/k/v, o and gate/up as
+// 16-row K = 2048 records, down as 2-row K = 16384 records.
 struct LayerDev
 {
     const uint8_t* qkv;
-    const __half* qkv_scales;
     const uint8_t* o;
-    const __half* o_scales;
     const uint8_t* gu;
-    const __half* gu_scales;
     const uint8_t* down;
-    const __half* down_scales;
     const float* in_norm;
     const float* post_norm;
     float* k_cache;
@@ -55,10 +68,11 @@ struct LayerDev
 
 struct PersistentArgs
 {
-    const LayerDev* layers; // device array [layers]
+    const LayerDev* layers;       // device array [layers]
     int n_layers;
-    const uint8_t* embed;   // tied table, Q8_0
+    const uint8_t* embed;         // tied table, Q8_0 in device layout (the token gather)
     const __half* embed_scales;
+    const uint8_t* embed_records; // the same table as 16-row records (the logits)
     const float* final_norm;
     int heads, head_dim, intermediate, vocab, qkv_rows;
     float eps, embed_scale, attn_scale;
@@ -81,14 +95,53 @@ struct PersistentArgs
     unsigned* barrier;      // grid barrier counter (zero at launch)
     unsigned* exit_ticket;  // zero at launch
     int steps;
-    int prefetch_stages;       // stages of L2 prefetch ahead of the ring (0 = none)
+    int gate_point;            // where a layer's gate/up records are released: 0 never held, 1 after the
+                               // attention phase, 2 after the o_proj staging
     unsigned long long* trace; // [gridDim.x][kTraceEvents] first-step phase stamps, or null
 };
 
-// Phase tracing: thread 0 of every CTA stamps %globaltimer (ns) at kernel
-// start, after the embed, and on entering and leaving every grid barrier of
-// the launch's first step.
-constexpr int kTraceEvents = 384;
+// Phase tracing: thread 0 of every CTA stamps %globaltimer (ns) into fixed
+// slots of its row during the launch's first step: slot 0 kernel start, 1
+// embed done, then layer l's events at 2 + 32 l + TraceEvent, then the logits
+// events at 2 + 32 layers + TraceLogits. Slots past kTraceEvents are dropped;
+// unused slots stay zero.
+constexpr int kTraceEvents = 1024;
+constexpr int kTraceLayerSlots = 32;
+enum TraceEvent : int
+{
+    kTrQkvStaged = 0, // limb form of the normalised x in shared memory
+    kTrQkvLimbs,      // this warp's fragments in registers
+    kTrQkvDone,       // records consumed; barrier entry
+    kTrQkvLeft,       // barrier exit
+    kTrAttnLoaded,    // q and the first K/V tile in shared memory (attention CTAs)
+    kTrAttnScored,    // every tile scored and accumulated
+    kTrAttnDone,      // output written; barrier entry
+    kTrAttnLeft,
+    kTrMergeDone,     // split merge (long contexts); barrier entry
+    kTrMergeLeft,
+    kTrOStaged,       // limb form of the attended x
+    kTrOLimbs,
+    kTrODone,
+    kTrOLeft,
+    kTrGuStaged,
+    kTrGuLimbs,
+    kTrGuDone,
+    kTrGuLeft,
+    kTrDownStaged,    // activation slice in registers
+    kTrDownDone,
+    kTrDownLeft,
+    kTrMergeMl,       // o_proj staging: the splits' (max, sum) in shared memory
+    kTrMergeRows,     // the splits' rows landed
+    kTrMergeFolded,   // folded, before the limb form
+    kTrAttnDots       // attention: the first tile's scores reduced
+};
+enum TraceLogits : int
+{
+    kTrLogitsStaged = 0,
+    kTrLogitsLimbs,
+    kTrLogitsDone,
+    kTrLogitsLeft
+};
 
 __device__ __forceinline__ unsigned long long global_ns()
 {
@@ -104,69 +157,503 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p)
     return v;
 }
 
-// All consumer warps of all CTAs meet. Thread 0 of each CTA publishes the
-// CTA's writes (release), arrives, and polls the monotonic counter (acquire);
-// the CTA's consumer barrier extends the ordering to its other threads.
-// Returns false when any CTA has given up a wait (the error word says which):
-// the caller then leaves, so one failure ends the launch instead of making
-// every later wait time out in turn.
+__device__ __forceinline__ unsigned ld_relaxed(const unsigned* p)
+{
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v)
+{
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// The 512 consumer threads of the CTA (named barrier 1; 2 and 3 are the groups').
+__device__ __forceinline__ void consumers_sync()
+{
+    named_sync(1, kPConsumers);
+}
+
+// All consumers of all CTAs meet. Thread 0 of each CTA arrives with a release
+// add (publishing the CTA's writes, which the CTA barrier before it orders)
+// and polls the monotonic counter with acquire loads, reading the error word
+// in the same poll. Returns false when any CTA has given up a wait (the error
+// word says which): the caller then leaves, so one failure ends the launch
+// instead of making every later wait time out in turn.
 __device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch, unsigned* err, unsigned* abort)
 {
-    consumer_sync();
+    consumers_sync();
     ++epoch;
     if (threadIdx.x == 0)
     {
-        __threadfence();
-        atomicAdd(counter, 1u);
+        red_release_add(counter, 1u);
         const unsigned target = epoch * gridDim.x;
-        for (unsigned spin = 0; ld_acquire(counter) < target; ++spin)
+        unsigned errs = 0;
+        for (unsigned spin = 0;; ++spin)
         {
+            const unsigned arrived = ld_acquire(counter);
+            errs = ld_relaxed(err);
+            if (arrived >= target || (errs & kErrAbort))
+                break;
             if (spin > kBarrierSpinLimit)
             {
                 flag_error(err, kErrBarrierTimeout);
+                errs |= kErrBarrierTimeout;
                 break;
             }
-            if (ld_acquire(err) & kErrAbort)
-                break;
-            __nanosleep(32);
         }
-        __threadfence();
-        *abort = ld_acquire(err) & kErrAbort;
+        *abort = errs & kErrAbort;
     }
-    consumer_sync();
+    consumers_sync();
     return *abort == 0;
 }
 
+// Context splits of a decode step: one 16-key tile each, one CTA each.
 __device__ __forceinline__ int attention_splits(int keys, int max_splits)
 {
-    const int splits = (keys + 63) / 64;
-    return splits < 1 ? 1 : (splits > max_splits ? max_splits : splits);
+    const int limit = min(max_splits, (int) gridDim.x);
+    const int splits = (keys + kAttnKeysPerSplit - 1) / kAttnKeysPerSplit;
+    return splits < 1 ? 1 : (splits > limit ? limit : splits);
+}
+
+// x (one float4 per consumer thread), RMS-normalised with the (1 + w)
+// weights `nw` when `norm` (Kernels/RMSNorm.h:51-81; one fixed fold order, so
+// every CTA normalises identically), into the limb form; returns after the
+// CTA's fragments are complete (a consumer barrier).
+__device__ __forceinline__ void stage_limbs(float4 v, bool norm, float4 nw, float eps, float* reduce, uint2* frags,
+                                            float* xexp, int tid)
+{
+    if (norm)
+    {
+        const float ss = warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w);
+        if ((tid & 31) == 0)
+            reduce[tid >> 5] = ss;
+        consumers_sync();
+        float total = 0.f;
+#pragma unroll
+        for (int w = 0; w < kPWarps; ++w)
+            total += reduce[w];
+        const float scale = 1.f / sqrtf(total / 2048.f + eps);
+        v.x = v.x * scale * (1.f + nw.x);
+        v.y = v.y * scale * (1.f + nw.y);
+        v.z = v.z * scale * (1.f + nw.z);
+        v.w = v.w * scale * (1.f + nw.w);
+    }
+    limbs_from_regs(v, frags, xexp, tid);
+    consumers_sync();
+}
+
+// Long contexts: four attended outputs (quad q = channels 4q .. 4q + 3 of
+// H * D) folded by one warp whose lanes walk the splits; mqa_merge's fold in a
+// tree order across lanes.
+__device__ __forceinline__ void merge_splits_warp(const float* acc, const float* ml, int splits, int heads, int quad,
+                                                  int lane, float* out)
+{
+    const int head = (4 * quad) / 256, d = (4 * quad) % 256;
+    float mx = -INFINITY;
+    for (int s = lane; s < splits; s += 32)
+        mx = fmaxf(mx, __ldcg(ml + ((size_t) s * heads + head) * 2));
+    mx = warp_max(mx);
+    float sum = 0.f;
+    float4 value = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = lane; s < splits; s += 32)
+    {
+        const size_t slot = (size_t) s * heads + head;
+        const float ms = __ldcg(ml + slot * 2);
+        if (ms == -INFINITY)
+            continue;
+        const float f = expf(ms - mx);
+        sum = fmaf(__ldcg(ml + slot * 2 + 1), f, sum);
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(acc + slot * 256 + d));
+        value.x = fmaf(a.x, f, value.x);
+        value.y = fmaf(a.y, f, value.y);
+        value.z = fmaf(a.z, f, value.z);
+        value.w = fmaf(a.w, f, value.w);
+    }
+    sum = warp_sum(sum);
+    value.x = warp_sum(value.x);
+    value.y = warp_sum(value.y);
+    value.z = warp_sum(value.z);
+    value.w = warp_sum(value.w);
+    if (lane == 0)
+        reinterpret_cast<float4*>(out)[quad] = make_float4(value.x / sum, value.y / sum, value.z / sum, value.w / sum);
+}
+
+// The thread's four attended outputs (channels 4 tid .. 4 tid + 3 of H * D)
+// from up to kFusedMergeSplits context splits: out = sum_s acc_s e^(m_s - M) /
+// sum_s l_s e^(m_s - M), folded in split order like mqa_merge. The split rows
+// land in shared memory (`land`: four splits x 2048 floats; each thread reads
+// back only what it copied) by cp.async, four splits per round trip; the
+// (max, sum) pairs are fetched once per CTA into `sml` ([splits][heads][2]).
+template <typename Stamp>
+__device__ __forceinline__ float4 merged_attention(const float* acc, const float* ml, int splits, int heads,
+                                                   float* land, float* sml, int tid, Stamp stamp)
+{
+    const int head = (4 * tid) >> 8;
+    const int first = min(splits, 4);
+    for (int s = 0; s < first; ++s)
+        cp_async16(land + s * 2048 + 4 * tid, acc + (size_t) s * heads * 256 + 4 * tid);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (tid < splits * heads * 2)
+        sml[tid] = __ldcg(ml + tid);
+    consumers_sync();
+    float ms[kFusedMergeSplits], ls[kFusedMergeSplits];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < kFusedMergeSplits; ++s)
+    {
+        ms[s] = -INFINITY;
+        ls[s] = 0.f;
+        if (s < splits)
+        {
+            ms[s] = sml[(s * heads + head) * 2];
+            ls[s] = sml[(s * heads + head) * 2 + 1];
+        }
+        mx = fmaxf(mx, ms[s]);
+    }
+    stamp(kTrMergeMl);
+    float sum = 0.f;
+    float4 value = make_float4(0.f, 0.f, 0.f, 0.f);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    stamp(kTrMergeRows);
+#pragma unroll
+    for (int s = 0; s < kFusedMergeSplits; ++s)
+    {
+        if (s == 4 && splits > 4)
+        {
+            for (int r = 4; r < splits; ++r)
+                cp_async16(land + (r - 4) * 2048 + 4 * tid, acc + (size_t) r * heads * 256 + 4 * tid);
+            cp_async_wait_all();
+        }
+        if (s >= splits || ms[s] == -INFINITY)
+            continue;
+        const float f = expf(ms[s] - mx);
+        sum = fmaf(ls[s], f, sum);
+        const float4 a = *reinterpret_cast<const float4*>(land + (s & 3) * 2048 + 4 * tid);
+        value.x = fmaf(a.x, f, value.x);
+        value.y = fmaf(a.y, f, value.y);
+        value.z = fmaf(a.z, f, value.z);
+        value.w = fmaf(a.w, f, value.w);
+    }
+    const float4 out = make_float4(value.x / sum, value.y / sum, value.z / sum, value.w / sum);
+    stamp(kTrMergeFolded);
+    return out;
+}
+
+// K/V cache rows [r0, r1) into the attention tile, row r at r - base
+// (cp.async through L2; the caller waits).
+__device__ __forceinline__ void load_kv_rows(const float* k_cache, const float* v_cache, int base, int r0, int r1,
+                                             float* tile, int tid)
+{
+    for (int i = tid; i < (r1 - r0) * 64; i += kPConsumers)
+    {
+        const int r = r0 + (i >> 6), c = (i & 63) * 4;
+        cp_async16(tile + (r - base) * 256 + c, k_cache + (size_t) r * 256 + c);
+        cp_async16(tile + kAttnTile * 256 + (r - base) * 256 + c, v_cache + (size_t) r * 256 + c);
+    }
+}
+
+// The context rows [k0, k1) of split `split` (the mqa_block partition).
+__device__ __forceinline__ void split_range(unsigned position, int split, int splits, int& k0, int& k1)
+{
+    const int keys = (int) position + 1;
+    const int chunk = (keys + splits - 1) / splits;
+    k0 = min(keys, split * chunk);
+    k1 = min(keys, k0 + chunk);
+}
+
+// Rows of the split's first tile that are final before this step's q/k/v
+// phase ends (every row but the newest), fetched while the grid barrier runs.
+__device__ __forceinline__ void prefetch_split(const LayerDev& L, unsigned position, int split, int splits, float* tile,
+                                               int tid)
+{
+    int k0, k1;
+    split_range(position, split, splits, k0, k1);
+    const int end = min(min(k1, k0 + kAttnTile), (int) position);
+    load_kv_rows(L.k_cache, L.v_cache, k0, k0, max(k0, end), tile, tid);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Decode attention of one context split over all eight query heads
+// (Kernels/MultiQueryAttention.h:138-341 semantics; the partition, fold and
+// outputs of mqa_block). Consumer group g takes heads 4g .. 4g + 3, its warp w
+// keys w and w + 8 of every 16-key tile, which both groups share in `area`. A
+// lane owns channels [4 lane, 4 lane + 4) and [128 + 4 lane, 128 + 4 lane + 4)
+// of the group's four heads (consecutive lanes read consecutive 16-byte words
+// of a row, free of bank conflicts, and each K/V row is read by two warps),
+// and keeps the running (max, sum) of head head_of_lane<4>(lane) with the
+// four heads' unnormalised rows. The eight warps of a group fold at the end
+// through `area`, which then holds both groups' folds. Writes the attended row
+// (one split) or the split's (max, sum, unnormalised row).
+template <typename Stamp>
+__device__ void attend_split(const PersistentArgs& p, const LayerDev& L, unsigned position, int split, int splits,
+                             float* area, int tid, Stamp stamp)
+{
+    constexpr int D = 256, QH = kAttnHeads;
+    const int group = tid >> 8, warp = (tid >> 5) & 7, lane = tid & 31;
+    const int head0 = group * QH;
+    const int c0 = 4 * lane, c1 = 128 + 4 * lane;
+    const int my_head = head_of_lane<QH>(lane);
+    int k0, k1;
+    split_range(position, split, splits, k0, k1);
+
+    float q[QH][8];
+#pragma unroll
+    for (int h = 0; h < QH; ++h)
+    {
+        const float* qrow = p.qbuf + (head0 + h) * D;
+        const float4 lo = __ldcg(reinterpret_cast<const float4*>(qrow + c0));
+        const float4 hi = __ldcg(reinterpret_cast<const float4*>(qrow + c1));
+        q[h][0] = lo.x * p.attn_scale;
+        q[h][1] = lo.y * p.attn_scale;
+        q[h][2] = lo.z * p.attn_scale;
+        q[h][3] = lo.w * p.attn_scale;
+        q[h][4] = hi.x * p.attn_scale;
+        q[h][5] = hi.y * p.attn_scale;
+        q[h][6] = hi.z * p.attn_scale;
+        q[h][7] = hi.w * p.attn_scale;
+    }
+    float m = -INFINITY, l = 0.f; // of head my_head, replicated across its lanes
+    float acc[QH][8];
+#pragma unroll
+    for (int h = 0; h < QH; ++h)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            acc[h][i] = 0.f;
+
+    const float* tk = area;
+    const float* tv = area + kAttnTile * D;
+    for (int t0 = k0; t0 < k1; t0 += kAttnTile)
+    {
+        const int nk = min(kAttnTile, k1 - t0);
+        // The first tile's final rows were prefetched before the barrier.
+        const int from = t0 == k0 ? max(k0, min(t0 + nk, (int) position)) : t0;
+        load_kv_rows(L.k_cache, L.v_cache, t0, from, t0 + nk, area, tid);
+        cp_async_wait_all();
+        consumers_sync();
+        if (t0 == k0)
+            stamp(kTrAttnLoaded);
+
+        float sc[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+        {
+            const int r = warp + 8 * j;
+            const int rr = min(r, nk - 1); // rows past the tile repeat a valid one, then drop out
+            const float4 lo = *reinterpret_cast<const float4*>(tk + rr * D + c0);
+            const float4 hi = *reinterpret_cast<const float4*>(tk + rr * D + c1);
+            const float kk[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+            float part[QH];
+#pragma unroll
+            for (int h = 0; h < QH; ++h)
+            {
+                float v = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    v = fmaf(q[h][i], kk[i], v);
+                part[h] = v;
+            }
+            const float total = transpose_reduce<QH>(part, lane);
+            sc[j] = r < nk ? total : -INFINITY;
+        }
+        if (t0 == k0)
+            stamp(kTrAttnDots);
+        const float m_new = fmaxf(m, fmaxf(sc[0], sc[1]));
+        float carried = 1.f, pj[2] = {0.f, 0.f};
+        if (m_new != -INFINITY)
+        {
+            carried = expf(m - m_new); // 0 while nothing was seen
+            pj[0] = expf(sc[0] - m_new);
+            pj[1] = expf(sc[1] - m_new);
+            m = m_new;
+        }
+        l = l * carried + (pj[0] + pj[1]);
+#pragma unroll
+        for (int h = 0; h < QH; ++h)
+        {
+            const float c = __shfl_sync(0xFFFFFFFFu, carried, lane_of_head<QH>(h));
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                acc[h][i] *= c;
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+        {
+            const int r = warp + 8 * j;
+            float ph[QH];
+#pragma unroll
+            for (int h = 0; h < QH; ++h)
+                ph[h] = __shfl_sync(0xFFFFFFFFu, pj[j], lane_of_head<QH>(h));
+            if (r >= nk) // warp-uniform
+                break;
+            const float4 lo = *reinterpret_cast<const float4*>(tv + r * D + c0);
+            const float4 hi = *reinterpret_cast<const float4*>(tv + r * D + c1);
+            const float vv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+            for (int h = 0; h < QH; ++h)
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    acc[h][i] = fmaf(ph[h], vv[i], acc[h][i]);
+        }
+        consumers_sync(); // the tile is read before it is refilled or reused
+    }
+    stamp(kTrAttnScored);
+
+    // ---- fold the group's eight warps
+    float* wacc = area + group * kAttnFoldFloats; // [8 warps][QH][D]
+    float* wm = wacc + 8 * QH * D;                // [8][QH]
+    float* wl = wm + 8 * QH;                      // [8][QH]
+#pragma unroll
+    for (int h = 0; h < QH; ++h)
+    {
+        *reinterpret_cast<float4*>(wacc + (warp * QH + h) * D + c0) =
+            make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+        *reinterpret_cast<float4*>(wacc + (warp * QH + h) * D + c1) =
+            make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+    }
+    if (lane == lane_of_head<QH>(my_head))
+    {
+        wm[warp * QH + my_head] = m;
+        wl[warp * QH + my_head] = l;
+    }
+    named_sync(2 + group, 256);
+    // Every warp derives the 32 (head, warp) weights itself, lane h * 8 + w:
+    // f = e^(m_w - M_h) (0 for a warp that saw no key), and each head's sum.
+    const int fh = lane >> 3, fw = lane & 7;
+    const float mw = wm[fw * QH + fh];
+    float mx = mw;
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 4));
+    const float f = mw == -INFINITY ? 0.f : expf(mw - mx);
+    float lsum = wl[fw * QH + fh] * f;
+    lsum += __shfl_xor_sync(0xFFFFFFFFu, lsum, 1);
+    lsum += __shfl_xor_sync(0xFFFFFFFFu, lsum, 2);
+    lsum += __shfl_xor_sync(0xFFFFFFFFu, lsum, 4);
+    const int d = tid & 255;
+#pragma unroll
+    for (int h = 0; h < QH; ++h)
+    {
+        float value = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w)
+            value = fmaf(wacc[(w * QH + h) * D + d], __shfl_sync(0xFFFFFFFFu, f, h * 8 + w), value);
+        const float sum = __shfl_sync(0xFFFFFFFFu, lsum, h * 8);
+        const float head_max = __shfl_sync(0xFFFFFFFFu, mx, h * 8);
+        const int head = head0 + h;
+        if (splits == 1)
+            p.attended[head * D + d] = value / sum;
+        else
+        {
+            const size_t slot = (size_t) split * p.heads + head;
+            p.attn_acc[slot * D + d] = value;
+            if (d == 0)
+            {
+                p.attn_ml[slot * 2] = head_max;
+                p.attn_ml[slot * 2 + 1] = sum;
+            }
+        }
+    }
+}
+
+// ---- down + residual ---------------------------------------------------------
+// Every 2-row K = 16384 record is read by all sixteen consumer warps, warp w
+// taking columns [1024 w, 1024 w + 1024) of both rows, so a lane keeps 32
+// values of the activation in registers.
+
+// The lane's 32 activation values of warp w's columns: [1024 w + 16 lane +
+// 512 j, + 16) for j = 0, 1.
+__device__ __forceinline__ void load_down_x(const float* act, int warp, int lane, float (&xr)[32])
+{
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int t = 0; t < 16; t += 4)
+        {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(act + 1024 * warp + 16 * lane + 512 * j + t));
+            xr[16 * j + t] = v.x;
+            xr[16 * j + t + 1] = v.y;
+            xr[16 * j + t + 2] = v.z;
+            xr[16 * j + t + 3] = v.w;
+        }
+}
+
+// Drains the slab's records (rows [r0, r1), whole pairs, at most
+// kMaxDownRecords): every warp releases a slot on its own after reading its
+// slices (a slot takes sixteen arrivals) and keeps per-lane partial sums of
+// every row; the warp sums go to `spart` ([row][16 warps]) at the end and are
+// folded in warp order into the residual stream.
+template <int NST>
+__device__ bool consume_down(const GemvArgs& a, Slab slab, const Ring& ring, unsigned& seq, const float (&xr)[32],
+                             float* spart)
+{
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int records = (slab.r1 - slab.r0) / 2;
+    bool ok = true;
+    float part[2 * kMaxDownRecords];
+#pragma unroll
+    for (int s = 0; s < kMaxDownRecords; ++s)
+    {
+        part[2 * s] = 0.f;
+        part[2 * s + 1] = 0.f;
+        if (s >= records)
+            continue;
+        const int buf = (int) ((seq + s) % NST);
+        if (ok && !mbar_wait(&ring.full[buf], ((seq + s) / NST) & 1u))
+        {
+            if (lane == 0)
+                flag_error(a.err, kErrWaitTimeout);
+            ok = false;
+        }
+        if (ok)
+        {
+            const uint8_t* qs = ring.quants + buf * ring.quant_stride + 1024 * warp;
+            const __half* scs = reinterpret_cast<const __half*>(ring.scales + buf * ring.scale_stride) + 32 * warp;
+            const uint4 w0 = *reinterpret_cast<const uint4*>(qs + 16 * lane);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(qs + 16 * lane + 512);
+            const uint4 w2 = *reinterpret_cast<const uint4*>(qs + 16384 + 16 * lane);
+            const uint4 w3 = *reinterpret_cast<const uint4*>(qs + 16384 + 16 * lane + 512);
+            const float s0 = __half2float(scs[lane / 2]), s1 = __half2float(scs[lane / 2 + 16]);
+            const float s2 = __half2float(scs[512 + lane / 2]), s3 = __half2float(scs[512 + lane / 2 + 16]);
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&ring.empty[buf]);
+            part[2 * s] = fmaf(dot16(w1, xr + 16), s1, dot16(w0, xr) * s0);
+            part[2 * s + 1] = fmaf(dot16(w3, xr + 16), s3, dot16(w2, xr) * s2);
+        }
+    }
+    seq += (unsigned) records;
+#pragma unroll
+    for (int r = 0; r < 2 * kMaxDownRecords; ++r)
+    {
+        const float v = warp_sum(part[r]);
+        if (lane == 0 && r < 2 * records)
+            spart[r * kPWarps + warp] = v;
+    }
+    consumers_sync();
+    if (ok)
+        for (int local = tid; local < slab.r1 - slab.r0; local += kPConsumers)
+        {
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < kPWarps; ++w)
+                v += spart[local * kPWarps + w];
+            plain_epilogue(Epi::Residual, v, nullptr, slab.r0 + local, a.out + slab.r0 + local);
+        }
+    return ok;
 }
 
 // A CTA's weight schedule: its slab of every product of every layer and step,
-// in the order the consumer warps drain them. Stage k of the schedule is a
-// pure function of k, so the producer can run a prefetch cursor ahead of the
-// stage it copies into the ring.
+// in the order the consumer warps drain them, one record per stage. Stage k
+// of the schedule is a pure function of k.
 struct Plan
 {
-    Slab slab[5];   // q/k/v, o, gate/up, down, logits
+    Slab slab[5]; // rows of q/k/v, o, gate/up, down, logits
     int stages[5];
     int per_layer;
     int per_step;
 };
-
-struct StageRef
-{
-    const uint8_t* quants;
-    const uint8_t* scales;
-    unsigned quant_bytes, scale_bytes;
-    bool tile; // 16 rows of K = 2048 copied row by row to the padded tile pitch
-};
-
-// One ring slot holds either stage format: a 16-row tile (rows at a 2064-byte
-// pitch, scales at 144) or 32 KiB of contiguous K = 16384 rows.
-constexpr int kSlotQuants = kTileQuantBytes > kStageQuants ? kTileQuantBytes : kStageQuants;
-constexpr int kSlotScales = kTileScaleBytes > kStageScales ? kTileScaleBytes : kStageScales;
 
 __device__ __forceinline__ Plan make_plan(const PersistentArgs& p, int cta, int ctas)
 {
@@ -174,22 +661,24 @@ __device__ __forceinline__ Plan make_plan(const PersistentArgs& p, int cta, int 
     plan.slab[0] = cta_tiles(p.qkv_rows, cta, ctas);
     plan.slab[1] = cta_tiles(2048, cta, ctas);
     plan.slab[2] = cta_tiles(2 * p.intermediate, cta, ctas);
-    plan.slab[3] = cta_slab(2048, false, cta, ctas);
+    plan.slab[3] = cta_slab(2048, true, cta, ctas); // whole 2-row records
     plan.slab[4] = cta_tiles(p.vocab, cta, ctas);
-    const int rps[5] = {16, 16, 16, 2, 16}; // rows per 32 KiB stage at K = 2048 and 16384
+    const int rows_per_record[5] = {kTileRows, kTileRows, kTileRows, 2, kTileRows};
     for (int i = 0; i < 5; ++i)
-        plan.stages[i] = (plan.slab[i].r1 - plan.slab[i].r0 + rps[i] - 1) / rps[i];
+        plan.stages[i] = (plan.slab[i].r1 - plan.slab[i].r0) / rows_per_record[i];
     plan.per_layer = plan.stages[0] + plan.stages[1] + plan.stages[2] + plan.stages[3];
     plan.per_step = p.n_layers * plan.per_layer + plan.stages[4];
     return plan;
 }
 
-__device__ __forceinline__ StageRef plan_stage(const PersistentArgs& p, const Plan& plan, long long k)
+// The record stage k of the schedule streams, with its product (0 q/k/v, 1 o,
+// 2 gate/up, 3 down, 4 logits) and its index within the CTA's slab.
+__device__ __forceinline__ const uint8_t* plan_stage(const PersistentArgs& p, const Plan& plan, long long k,
+                                                     int& product, int& index)
 {
     int r = (int) (k % plan.per_step);
-    int product = 4;
-    const uint8_t* w = p.embed;
-    const __half* sc = p.embed_scales;
+    product = 4;
+    const uint8_t* records = p.embed_records;
     if (r < p.n_layers * plan.per_layer)
     {
         const LayerDev& L = p.layers[r / plan.per_layer];
@@ -197,168 +686,174 @@ __device__ __forceinline__ StageRef plan_stage(const PersistentArgs& p, const Pl
         product = 0;
         while (r >= plan.stages[product])
             r -= plan.stages[product++];
-        const uint8_t* ws[4] = {L.qkv, L.o, L.gu, L.down};
-        const __half* ss[4] = {L.qkv_scales, L.o_scales, L.gu_scales, L.down_scales};
-        w = ws[product];
-        sc = ss[product];
+        const uint8_t* rs[4] = {L.qkv, L.o, L.gu, L.down};
+        records = rs[product];
     }
     else
         r -= p.n_layers * plan.per_layer;
-    const int K = product == 3 ? 16384 : 2048;
-    const int rps = 32768 / K;
-    const int first = plan.slab[product].r0 + r * rps;
-    const int rows = min(rps, plan.slab[product].r1 - first);
-    StageRef ref;
-    ref.quants = w + (size_t) first * K;
-    ref.scales = reinterpret_cast<const uint8_t*>(sc) + (size_t) first * (K / 16);
-    ref.quant_bytes = (unsigned) rows * K;
-    ref.scale_bytes = (unsigned) rows * (K / 16);
-    ref.tile = K == 2048;
-    return ref;
+    index = r;
+    const int rows_per_record = product == 3 ? 2 : kTileRows;
+    const int record = plan.slab[product].r0 / rows_per_record + r;
+    return records + (size_t) record * kRecordBytes;
 }
 
-// Default stages the producer keeps in flight to L2 beyond the shared-memory
-// ring (PersistentArgs::prefetch_stages, HF_PREFETCH_STAGES). Measured on B200
-// at Gemma-2B sizes: 0 stages 1127 us/token, 2: 1135, 6: 1195, 12: 1379; the
-// prefetched lines were partly evicted before use (DRAM reads grew 7%), so
-// the default is off.
-constexpr int kPrefetchStages = 0;
-
+// The producer: one thread streams the schedule's records into the ring, a
+// single bulk copy per stage, as soon as the consumers release a slot. A
+// layer's gate/up records wait at `gate` (gate_point) until the consumers have
+// finished the layer's attention: issued earlier (during the q/k/v ->
+// attention chain, while the ring has room) their data queues ahead of that
+// chain's latency-bound loads and lengthens it; issued at the gate they still
+// fill the ring before the gate/up phase begins.
 template <int NST>
-__device__ void persistent_producer(const PersistentArgs& p, const Ring& ring)
+__device__ void persistent_producer(const PersistentArgs& p, const Ring& ring, uint64_t* gate)
 {
     const uint64_t policy = evict_first_policy();
     const Plan plan = make_plan(p, blockIdx.x, gridDim.x);
     const long long total = (long long) p.steps * plan.per_step;
-    long long prefetched = NST;
+    unsigned gates = 0;
     for (long long k = 0; k < total; ++k)
     {
-        const long long until = min(total, k + NST + p.prefetch_stages);
-        for (; prefetched < until; ++prefetched)
-        {
-            const StageRef ahead = plan_stage(p, plan, prefetched);
-            bulk_prefetch_l2(ahead.quants, ahead.quant_bytes);
-            bulk_prefetch_l2(ahead.scales, ahead.scale_bytes);
-        }
         const int b = (int) (k % NST);
         if (k >= NST && !mbar_wait(&ring.empty[b], (unsigned) (k / NST - 1) & 1u))
         {
             flag_error(p.err, kErrWaitTimeout);
             return;
         }
-        const StageRef stage = plan_stage(p, plan, k);
-        mbar_expect_tx(&ring.full[b], stage.quant_bytes + stage.scale_bytes);
-        uint8_t* quants = ring.quants + b * ring.quant_stride;
-        uint8_t* scales = ring.scales + b * ring.scale_stride;
-        if (stage.tile)
+        int product, index;
+        const uint8_t* record = plan_stage(p, plan, k, product, index);
+        if (product == 2 && index == 0 && p.gate_point != 0)
         {
-            for (int r = 0; r < kTileRows; ++r)
+            if (!mbar_wait(gate, gates & 1u))
             {
-                bulk_load(quants + r * kTilePitch, stage.quants + r * 2048, 2048, &ring.full[b], policy);
-                bulk_load(scales + r * kScalePitch, stage.scales + r * 128, 128, &ring.full[b], policy);
+                flag_error(p.err, kErrWaitTimeout);
+                return;
             }
+            ++gates;
         }
-        else
-        {
-            bulk_load(quants, stage.quants, stage.quant_bytes, &ring.full[b], policy);
-            bulk_load(scales, stage.scales, stage.scale_bytes, &ring.full[b], policy);
-        }
+        mbar_expect_tx(&ring.full[b], kRecordBytes);
+        bulk_load(ring.quants + b * kRecordBytes, record, kRecordBytes, &ring.full[b], policy);
     }
 }
 
 template <int NST>
-__global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const PersistentArgs p)
+__global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const PersistentArgs p)
 {
+    // Stage seq goes to group seq % 2 and to slot seq % NST. With NST even a
+    // slot always serves the same group, which waits on its uses in order;
+    // with NST odd a slot alternates between the groups, and a group can poll
+    // a slot whose previous use (the other group's) is still in flight --
+    // where the parity wait reports the use before that as complete.
+    static_assert(NST % kPGroups == 0, "each ring slot must serve one consumer group");
+
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[NST];
     __shared__ uint64_t empty[NST];
-    __shared__ float reduce[kConsumerWarps];
-    __shared__ float cand_v[kConsumerWarps];
-    __shared__ unsigned cand_i[kConsumerWarps];
+    __shared__ uint64_t gate; // one arrival per layer: its gate/up records may stream
+    __shared__ float reduce[kPWarps];
+    __shared__ float cand_v[kPWarps];
+    __shared__ unsigned cand_i[kPWarps];
     __shared__ unsigned last_cta;
     __shared__ unsigned abort_flag;
-    __shared__ float rope_row[256]; // this step's cosines [0, 128) and sines [128, 256)
-    __shared__ float xexp[64];      // per k-block 2^(e - 30) of the limb form of x
-    __shared__ float red[2 * 8 * kTileRows];
+    __shared__ unsigned shared_word; // the launch's position, then each step's token, read once per CTA
+    __shared__ float rope_row[256];  // this step's cosines [0, 128) and sines [128, 256)
+    __shared__ float xexp[64];       // per k-block 2^(e - 30) of the limb form of x
+    __shared__ float red[kPGroups * 2 * 8 * kTileRows];
 
-    const Ring ring {smem, smem + NST * kSlotQuants, full, empty, kSlotQuants, kSlotScales};
-    float* sx = reinterpret_cast<float*>(smem + NST * (kSlotQuants + kSlotScales)); // x (8 KiB) or down partials
-    float* sattn = sx + 2048;                                                        // attention tile / fold
-    uint2* frags = reinterpret_cast<uint2*>(sattn); // limb B fragments (8 KiB), outside the attention phase
+    const Ring ring {smem, smem + kRecordQuants, full, empty, kRecordBytes, kRecordBytes}; // a record per slot
+    float* sx = reinterpret_cast<float*>(smem + NST * kRecordBytes); // down partials
+    uint2* frags = reinterpret_cast<uint2*>(sx + 2048);             // limb B fragments (8 KiB)
+    float* attn_area = sx + 4096; // attention K/V tile and folds; the merge's landing area
 
     const int tid = threadIdx.x;
     if (tid == 0)
-        init_ring(ring, NST);
+    {
+        mbar_init(&gate, 1);
+        init_ring(ring, NST, kPWarps);
+    }
     __syncthreads();
 
-    if (tid >= kConsumerWarps * 32)
+    if (tid >= kPConsumers)
     {
-        if (tid == kConsumerWarps * 32)
-            persistent_producer<NST>(p, ring);
+        if (tid == kPConsumers)
+            persistent_producer<NST>(p, ring, &gate);
         return;
     }
 
     // ---- consumers
     const int cta = blockIdx.x, ctas = gridDim.x;
-    const unsigned position0 = *(volatile const unsigned*) p.state;
+    const int group = tid >> 8;
+    if (tid == 0)
+        shared_word = *(volatile const unsigned*) p.state;
+    consumers_sync();
+    const unsigned position0 = shared_word;
     unsigned seq = 0, epoch = 0;
-    float xr[64];
-    float norm_regs[2048 / (kConsumerWarps * 32)];
+    float xr[32];
+    float4 nw;
 
-    int trace_at = 0;
-    auto stamp = [&]() {
-        if (p.trace && tid == 0 && trace_at < kTraceEvents)
-            p.trace[(size_t) cta * kTraceEvents + trace_at] = global_ns();
-        ++trace_at;
+    unsigned long long* trace_row = p.trace && tid == 0 ? p.trace + (size_t) cta * kTraceEvents : nullptr;
+    auto stamp = [&](int slot) {
+        if (trace_row && slot < kTraceEvents)
+            trace_row[slot] = global_ns();
     };
     uint32_t bfrag[8][2];
     float bfactor[8];
-    // x of a K = 2048 product, normalised in sx, into this warp's limb B fragments.
-    auto limbs = [&]() {
-        make_limb_frags(sx, frags, xexp, tid);
-        consumer_sync();
-        load_limb_frags(frags, xexp, tid >> 5, tid & 31, bfrag, bfactor);
+    // x of a K = 2048 product (one float4 per thread) into the limb form, then
+    // each warp's B fragments into registers; stamps both points.
+    auto stage = [&](float4 v, bool norm, int slot) {
+        stage_limbs(v, norm, nw, p.eps, reduce, frags, xexp, tid);
+        stamp(slot);
+        load_limb_frags(frags, xexp, (tid >> 5) & 7, tid & 31, bfrag, bfactor);
+        stamp(slot + 1);
     };
-    auto barrier = [&]() {
-        stamp();
+    const float4* hidden4 = reinterpret_cast<const float4*>(p.hidden);
+    auto barrier = [&](int entry_slot, int exit_slot) {
+        stamp(entry_slot);
         const bool alive = grid_barrier(p.barrier, epoch, p.err, &abort_flag);
-        stamp();
+        stamp(exit_slot);
         return alive;
     };
-    stamp();
+    auto load_norm = [&](const float* w) { nw = __ldg(reinterpret_cast<const float4*>(w) + tid); };
+    stamp(0);
     auto run = [&]() {
     for (int step = 0; step < p.steps; ++step)
     {
+        if (step == 1)
+            trace_row = nullptr; // the first step only
         const unsigned position = position0 + (unsigned) step;
+        const int keys = (int) position + 1;
+        const int splits = attention_splits(keys, p.max_splits);
 
-        // ---- embed: every CTA gathers the row into sx; CTA 0 also writes the
-        // residual stream (Kernels/Embed.h:45-77). The step's rotary row and
-        // layer 0's norm weights come along.
+        // ---- embed: every CTA gathers the row; CTA 0 also writes the residual
+        // stream (Kernels/Embed.h:45-77). The step's rotary row and layer 0's
+        // norm weights come along.
+        float4 embedded;
         {
             if (tid < p.head_dim / 2)
             {
                 rope_row[tid] = p.rope_cos[(size_t) position * (p.head_dim / 2) + tid];
                 rope_row[128 + tid] = p.rope_sin[(size_t) position * (p.head_dim / 2) + tid];
             }
-            load_norm_regs(p.layers[0].in_norm, tid, norm_regs);
-            unsigned token = __ldcg(p.slots + position);
+            load_norm(p.layers[0].in_norm);
+            if (tid == 0)
+                shared_word = __ldcg(p.slots + position);
+            consumers_sync();
+            unsigned token = shared_word;
             if (token >= (unsigned) p.vocab)
             {
                 if (tid == 0)
                     flag_error(p.err, kErrTokenRange);
                 token = 0;
             }
-            for (int c = tid; c < 2048; c += kConsumerWarps * 32)
-            {
-                const size_t element = (size_t) token * 2048 + c;
-                const float v = p.embed_scale * ((float) (int) (int8_t) p.embed[element]
-                                                 * __half2float(p.embed_scales[element / kBlock]));
-                sx[c] = v;
-                if (cta == 0)
-                    p.hidden[c] = v;
-            }
-            consumer_sync();
-            stamp();
+            const size_t element = (size_t) token * 2048 + 4 * tid;
+            const uint32_t q4 = *reinterpret_cast<const uint32_t*>(p.embed + element);
+            const float scale = __half2float(p.embed_scales[element / kBlock]);
+            embedded.x = p.embed_scale * ((float) (int) (int8_t) (q4 & 0xFFu) * scale);
+            embedded.y = p.embed_scale * ((float) (int) (int8_t) ((q4 >> 8) & 0xFFu) * scale);
+            embedded.z = p.embed_scale * ((float) (int) (int8_t) ((q4 >> 16) & 0xFFu) * scale);
+            embedded.w = p.embed_scale * ((float) (int) (int8_t) (q4 >> 24) * scale);
+            if (cta == 0)
+                reinterpret_cast<float4*>(p.hidden)[tid] = embedded;
+            stamp(1);
         }
 
         for (int l = 0; l < p.n_layers; ++l)
@@ -366,12 +861,11 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
             const LayerDev& L = p.layers[l];
             float best = -INFINITY;
             unsigned best_i = 0xFFFFFFFFu;
+            const int ts = 2 + kTraceLayerSlots * l; // this layer's trace slots
 
             // ---- q/k/v with RMSNorm, RoPE and the cache write
             {
                 GemvArgs a = {};
-                a.w = L.qkv;
-                a.scales = L.qkv_scales;
                 a.N = p.qkv_rows;
                 a.out = p.qbuf;
                 a.k_cache = L.k_cache;
@@ -384,126 +878,85 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
                 a.kv_heads = 1;
                 a.head_dim = p.head_dim;
                 a.err = p.err;
-                stage_x_2048(l == 0 ? nullptr : p.hidden, L.in_norm, p.eps, sx, reduce, tid, nullptr, norm_regs);
-                limbs();
-                stamp();
-                consume_tiles<Epi::QkvRope, NST>(a, cta_tiles(p.qkv_rows, cta, ctas), ring, seq, bfrag, bfactor, red,
-                                                      position, best, best_i);
+                stage(l == 0 ? embedded : __ldcg(hidden4 + tid), true, ts + kTrQkvStaged);
+                consume_tiles<Epi::QkvRope, NST, kPGroups>(a, cta_tiles(p.qkv_rows, cta, ctas), ring, seq, bfrag,
+                                                           bfactor, red, position, best, best_i, group, 2 + group);
             }
-            if (!barrier())
+            if (cta < splits)
+                prefetch_split(L, position, cta, splits, attn_area, tid);
+            if (!barrier(ts + kTrQkvDone, ts + kTrQkvLeft))
                 return;
 
-            // ---- attention: CTA pairs per context split, four heads each
-            const int keys = (int) position + 1;
-            const int splits = attention_splits(keys, p.max_splits);
-            {
-                AttnArgs at = {};
-                at.q = p.qbuf;
-                at.k_cache = L.k_cache;
-                at.v_cache = L.v_cache;
-                at.out = p.attended;
-                at.part_acc = p.attn_acc;
-                at.part_ml = p.attn_ml;
-                at.heads = p.heads;
-                at.kv_heads = 1;
-                at.head_dim = p.head_dim;
-                at.scale = p.attn_scale;
-                at.nsplit = splits;
-                at.err = p.err;
-                const int groups = p.heads / kAttnHeads;
-                if (cta < splits * groups)
-                    mqa_block<kAttnHeads, kAttnTile>(at, position, 0, (cta % groups) * kAttnHeads, 0, cta / groups,
-                                                     sattn, [] { consumer_sync(); });
-            }
-            if (!barrier())
+            // ---- attention: one CTA per context split, all eight heads
+            if (cta < splits)
+                attend_split(p, L, position, cta, splits, attn_area, tid, [&](int event) { stamp(ts + event); });
+            if (!barrier(ts + kTrAttnDone, ts + kTrAttnLeft))
                 return;
-            if (splits > 1)
+            if (tid == 0 && p.gate_point == 1)
+                mbar_arrive(&gate); // the producer may stream this layer's gate/up records now
+            const bool fused_merge = splits > 1 && splits <= kFusedMergeSplits;
+            if (splits > kFusedMergeSplits)
             {
-                // mqa_merge's fold, each CTA taking a slice of the H * D outputs.
-                const int outputs = p.heads * p.head_dim;
-                const int begin = (int) ((long long) outputs * cta / ctas);
-                const int end = (int) ((long long) outputs * (cta + 1) / ctas);
-                for (int idx = begin + tid; idx < end; idx += kConsumerWarps * 32)
-                {
-                    const int head = idx / p.head_dim, d = idx % p.head_dim;
-                    float mx = -INFINITY;
-                    for (int s = 0; s < splits; ++s)
-                        mx = fmaxf(mx, __ldcg(p.attn_ml + ((size_t) s * p.heads + head) * 2));
-                    float sum = 0.f, value = 0.f;
-                    for (int s = 0; s < splits; ++s)
-                    {
-                        const size_t slot = (size_t) s * p.heads + head;
-                        const float ms = __ldcg(p.attn_ml + slot * 2);
-                        if (ms == -INFINITY)
-                            continue;
-                        const float f = expf(ms - mx);
-                        sum = fmaf(__ldcg(p.attn_ml + slot * 2 + 1), f, sum);
-                        value = fmaf(__ldcg(p.attn_acc + slot * p.head_dim + d), f, value);
-                    }
-                    p.attended[idx] = value / sum;
-                }
-                if (!barrier())
+                // Long contexts: the fold as its own phase, one warp per four
+                // outputs, its lanes over the splits.
+                const int quad = cta * kPWarps + (tid >> 5);
+                if (quad < 512)
+                    merge_splits_warp(p.attn_acc, p.attn_ml, splits, p.heads, quad, tid & 31, p.attended);
+                if (!barrier(ts + kTrMergeDone, ts + kTrMergeLeft))
                     return;
             }
 
             // ---- o_proj + residual
             {
                 GemvArgs a = {};
-                a.w = L.o;
-                a.scales = L.o_scales;
                 a.N = 2048;
                 a.out = p.hidden;
                 a.err = p.err;
-                stage_x_2048(p.attended, nullptr, p.eps, sx, reduce, tid, nullptr);
-                limbs();
-                stamp();
-                consume_tiles<Epi::Residual, NST>(a, cta_tiles(2048, cta, ctas), ring, seq, bfrag, bfactor, red,
-                                                       position, best, best_i);
+                stage(fused_merge ? merged_attention(p.attn_acc, p.attn_ml, splits, p.heads, attn_area, red, tid,
+                                                     [&](int event) { stamp(ts + event); })
+                                  : __ldcg(reinterpret_cast<const float4*>(p.attended) + tid),
+                      false, ts + kTrOStaged);
+                if (tid == 0 && p.gate_point == 2)
+                    mbar_arrive(&gate);
+                consume_tiles<Epi::Residual, NST, kPGroups>(a, cta_tiles(2048, cta, ctas), ring, seq, bfrag, bfactor,
+                                                            red, position, best, best_i, group, 2 + group);
             }
-            load_norm_regs(L.post_norm, tid, norm_regs);
-            if (!barrier())
+            load_norm(L.post_norm);
+            if (!barrier(ts + kTrODone, ts + kTrOLeft))
                 return;
 
             // ---- RMSNorm + gate/up + GeGLU
             {
                 GemvArgs a = {};
-                a.w = L.gu;
-                a.scales = L.gu_scales;
                 a.N = 2 * p.intermediate;
                 a.out = p.act;
                 a.err = p.err;
-                stage_x_2048(p.hidden, L.post_norm, p.eps, sx, reduce, tid, nullptr, norm_regs);
-                limbs();
-                stamp();
-                consume_tiles<Epi::GeGLU, NST>(a, cta_tiles(2 * p.intermediate, cta, ctas), ring, seq, bfrag, bfactor,
-                                                    red, position, best, best_i);
+                stage(__ldcg(hidden4 + tid), true, ts + kTrGuStaged);
+                consume_tiles<Epi::GeGLU, NST, kPGroups>(a, cta_tiles(2 * p.intermediate, cta, ctas), ring, seq, bfrag,
+                                                         bfactor, red, position, best, best_i, group, 2 + group);
             }
-            if (!barrier())
+            if (!barrier(ts + kTrGuDone, ts + kTrGuLeft))
                 return;
 
             // ---- down + residual
             {
                 GemvArgs a = {};
-                a.w = L.down;
-                a.scales = L.down_scales;
                 a.N = 2048;
                 a.out = p.hidden;
                 a.err = p.err;
-                load_x_wide<16384>(p.act, tid, xr);
-                stamp();
-                consume_slab<16384, Epi::Residual, NST>(a, cta_slab(2048, false, cta, ctas), ring, seq, xr, sx,
-                                                        position, best, best_i);
+                load_down_x(p.act, tid >> 5, tid & 31, xr);
+                stamp(ts + kTrDownStaged);
+                consume_down<NST>(a, cta_slab(2048, true, cta, ctas), ring, seq, xr, sx);
             }
-            load_norm_regs(l + 1 < p.n_layers ? p.layers[l + 1].in_norm : p.final_norm, tid, norm_regs);
-            if (!barrier())
+            load_norm(l + 1 < p.n_layers ? p.layers[l + 1].in_norm : p.final_norm);
+            if (!barrier(ts + kTrDownDone, ts + kTrDownLeft))
                 return;
         }
 
         // ---- final RMSNorm + tied logits + argmax into slot position + 1
+        const int ts = 2 + kTraceLayerSlots * p.n_layers;
         {
             GemvArgs a = {};
-            a.w = p.embed;
-            a.scales = p.embed_scales;
             a.N = p.vocab;
             a.out = p.logits;
             a.cand_val = p.cand_val;
@@ -515,15 +968,13 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
             a.err = p.err;
             float best = -INFINITY;
             unsigned best_i = 0xFFFFFFFFu;
-            stage_x_2048(p.hidden, p.final_norm, p.eps, sx, reduce, tid, nullptr, norm_regs);
-            limbs();
-            stamp();
-            consume_tiles<Epi::Logits, NST>(a, cta_tiles(p.vocab, cta, ctas), ring, seq, bfrag, bfactor, red, position,
-                                                 best, best_i);
+            stage(__ldcg(hidden4 + tid), true, ts + kTrLogitsStaged);
+            consume_tiles<Epi::Logits, NST, kPGroups>(a, cta_tiles(p.vocab, cta, ctas), ring, seq, bfrag, bfactor, red,
+                                                      position, best, best_i, group, 2 + group);
             warp_best(best, best_i);
-            logits_fold(a, position, best, best_i, cand_v, cand_i, &last_cta);
+            logits_fold<kPWarps>(a, position, best, best_i, cand_v, cand_i, &last_cta);
         }
-        if (!barrier()) // the next step embeds the token just written
+        if (!barrier(ts + kTrLogitsDone, ts + kTrLogitsLeft)) // the next step embeds the token just written
             return;
     }
     };
@@ -544,12 +995,12 @@ __global__ void __launch_bounds__(kStreamThreads, 2) decode_persistent(const Per
     }
 }
 
-// Dynamic shared memory: the ring, x (8 KiB), and the attention tile / fold.
+// Dynamic shared memory: the ring, the down partials (8 KiB), the limb
+// fragments (8 KiB) and the attention area (the K/V tile, then the warp folds:
+// 66 KiB).
 template <int NST>
 constexpr size_t persistent_smem()
 {
-    constexpr size_t attention = mqa_fast_smem<kAttnHeads, kAttnTile>();
-    return (size_t) NST * (kSlotQuants + kSlotScales) + 2048 * sizeof(float)
-           + (attention > (size_t) kLimbFragBytes ? attention : (size_t) kLimbFragBytes);
+    return (size_t) NST * kRecordBytes + 2048 * sizeof(float) + kLimbFragBytes + kAttnAreaFloats * sizeof(float);
 }
 } // namespace hfk

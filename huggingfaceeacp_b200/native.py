@@ -30,6 +30,15 @@ HF_E_TOKEN = -8
 # Decode paths (hf_cuda.h HF_DECODE_*).
 DECODE_AUTO, DECODE_GRAPH, DECODE_PERSISTENT = 0, 1, 2
 
+# Stamp slots per CTA of hf_cuda_trace_decode: 0 start, 1 embed, 2 + 32 l + event.
+TRACE_SLOTS = 1024
+TRACE_LAYER_SLOTS = 32
+TRACE_EVENTS = ("qkv.staged", "qkv.limbs", "qkv.done", "qkv.left", "attn.loaded", "attn.scored", "attn.done",
+                "attn.left", "merge.done", "merge.left", "o.staged", "o.limbs", "o.done", "o.left", "gu.staged",
+                "gu.limbs", "gu.done", "gu.left", "down.staged", "down.done", "down.left", "merge.ml", "merge.rows",
+                "merge.folded", "attn.dots")
+TRACE_LOGITS_EVENTS = ("logits.staged", "logits.limbs", "logits.done", "logits.left")
+
 # Decode-step kernels the timing hook measures (hf_cuda.h HF_KERNEL_*).
 KERNEL_QKV, KERNEL_ATTENTION, KERNEL_OUTPUT, KERNEL_GATE_UP, KERNEL_DOWN, KERNEL_LOGITS = range(6)
 KERNEL_NAMES = ("qkv_rope", "attention", "o_proj_residual", "gate_up_geglu", "down_residual", "logits_argmax")
@@ -412,7 +421,7 @@ class Context:
 
     def trace_decode(self, steps: int, max_ctas: int = 1024) -> np.ndarray:
         """[ctas, events] %globaltimer stamps (ns) of the first traced step (hf_cuda_trace_decode)."""
-        stamps = np.zeros(max_ctas * 384, dtype=np.uint64)
+        stamps = np.zeros(max_ctas * TRACE_SLOTS, dtype=np.uint64)
         ctas, events = ctypes.c_int(0), ctypes.c_int(0)
         self.check(self.lib.hf_cuda_trace_decode(self.handle, steps, _ptr(stamps), stamps.size, ctypes.byref(ctas),
                                                  ctypes.byref(events)))

@@ -164,10 +164,12 @@ int hf_cuda_decode_path(const hf_ctx* ctx);
 /* Phase tracing of the whole-loop kernel (the reference has wall-clock
  * timings only, Gemma.h:205-224): decodes `steps` tokens like
  * hf_cuda_decode_async, synchronously, and writes the first step's
- * %globaltimer stamps (ns): stamps[cta * events + e], thread 0 of every CTA,
- * e = 0 kernel start, 1 embed done, then entry and exit of every grid barrier
- * in phase order, with a stamp where each product starts streaming (unused
- * entries 0). capacity >= 2 * SMs * 384. */
+ * %globaltimer stamps (ns) of thread 0 of every CTA: stamps[cta * events + e]
+ * with e = 0 kernel start, 1 embed done, 2 + 32 l + k event k of layer l
+ * (per product: staged, fragments ready, consumed / barrier entry, barrier
+ * exit; attention: loaded, scored, reduced; the split merge's steps), then
+ * the logits events at 2 + 32 layers (unused entries 0).
+ * capacity >= SMs * 1024. */
 int hf_cuda_trace_decode(hf_ctx* ctx, int steps, uint64_t* stamps, int capacity, int* ctas, int* events);
 /* 1 when the sm_100a streaming kernels serve this shape, 0 for the generic path. */
 int hf_cuda_fast_path(const hf_ctx* ctx);
