@@ -312,6 +312,31 @@ def run_ours(args):
     return 0
 
 
+def run_profile_case(args):
+    """A small case of the bench's decode kernel for ncu captures (not a bench
+    line): Gemma-2B's layer and head shapes with 4 layers and a 32,000-token
+    vocabulary (0.54 GB of weights per decode step, above L2), two launches of
+    `--steps` decode steps after the seeded prompt; capture the second launch
+    (`-k regex:decode_persistent -s 1 -c 1`). Prints the case's algorithmic
+    bytes per launch so DRAM traffic can be compared and scaled."""
+    from huggingfaceeacp_b200 import native
+
+    shape = native.GEMMA_2B.replace(layers=4, vocab=32000, max_positions=256, max_step_rows=16)
+    with native.Context(shape) as ctx:
+        ctx.load_synthetic(seed=SEED)
+        prompt = native.synthetic_tokens(SEED, PROMPT_LENGTH, shape.vocab)
+        ctx.prefill_async(prompt)
+        ctx.decode_async(args.steps)
+        ctx.sync()
+        first = ctx.position
+        ctx.decode_async(args.steps)
+        ctx.sync()
+        launch_bytes = sum(native.decode_bytes(shape, first + i + 1) for i in range(args.steps))
+    print(json.dumps({"profile_case": "Gemma-2B shapes, 4 layers, vocab 32000", "steps_per_launch": args.steps,
+                      "algorithmic_bytes_per_launch": launch_bytes}), flush=True)
+    return 0
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -320,8 +345,12 @@ def main():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--cpu-steps", type=int, default=16)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--profile-case", action="store_true",
+                        help="run the small ncu capture case of the decode kernel instead of the bench")
     args = parser.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.profile_case:
+        return run_profile_case(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
