@@ -1,0 +1,71 @@
+"""The C++ HF surface (include/HF/*.h over libhf.so): HF::Decoder, HF::Gemma,
+HF::Argmax, HF::Sampler and HF::DecoderWeights with the reference's names
+(Decoder/Decoder.h:72-136, Generation/Gemma.h:65-251, Kernels/Argmax.h:206-257,
+Sampling/Sampler.h:70, Decoder/DecoderWeights.h:53-116), driven by
+tests/cpp/hf_surface_test.cpp and checked against the Python binding over the
+same engine and the same seeded weights.
+"""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from huggingfaceeacp_b200 import build, native
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+SOURCE = os.path.join(ROOT, "tests", "cpp", "hf_surface_test.cpp")
+SHAPE = native.DecoderShape(width=2048, heads=8, kv_heads=1, head_width=256, layers=2, intermediate=4096, vocab=8192,
+                            max_positions=64, max_step_rows=16, embed_scale=1.0)
+SEED = 31
+PROMPT = [2, 5, 41, 3, 17, 28, 9, 60]
+
+
+@pytest.fixture(scope="module")
+def program(tmp_path_factory):
+    lib = build.build_cpp_surface()
+    assert lib and os.path.exists(lib)
+    out = str(tmp_path_factory.mktemp("cpp") / "hf_surface_test")
+    subprocess.run(["g++", "-std=c++20", "-O2", f"-I{os.path.join(ROOT, 'include')}", SOURCE,
+                    f"-L{os.path.dirname(lib)}", "-lhf", f"-Wl,-rpath,{os.path.dirname(lib)}", "-o", out], check=True)
+    return out
+
+
+def test_surface_compiles_and_links(program):
+    assert os.path.exists(program)
+
+
+@pytest.mark.gpu
+def test_cpp_surface_matches_the_python_binding(program, tmp_path):
+    out = str(tmp_path / "out.bin")
+    s = SHAPE
+    subprocess.run([program, out, str(s.width), str(s.heads), str(s.kv_heads), str(s.head_width), str(s.layers),
+                    str(s.intermediate), str(s.vocab), str(s.max_positions), str(SEED)], check=True)
+    raw = np.fromfile(out, dtype=np.uint8)
+    at = 4
+    rows = np.frombuffer(raw[at:at + 16 * s.vocab], np.float32).reshape(4, s.vocab)
+    at += 16 * s.vocab
+    hidden = np.frombuffer(raw[at:at + 4 * s.width], np.float32)
+    at += 4 * s.width
+    picks = np.frombuffer(raw[at:at + 16], np.uint32)
+    host = np.frombuffer(raw[at + 16:at + 32], np.uint32)
+    at += 32
+    count = int(np.frombuffer(raw[at:at + 4], np.int32)[0])
+    generated = np.frombuffer(raw[at + 4:at + 4 + 4 * count], np.uint32)
+    refusals = np.frombuffer(raw[at + 4 + 4 * count:], np.int32)
+
+    with native.Context(s) as ctx:
+        ctx.load_synthetic(seed=SEED)
+        ctx.begin_sequence()
+        lg, _ = ctx.step(PROMPT)
+        expected = [lg[-1]]
+        for t in (7, 11, 13):
+            lg, hd = ctx.step([t])
+            expected.append(lg[-1])
+        np.testing.assert_array_equal(rows, np.stack(expected))
+        np.testing.assert_array_equal(hidden, hd[-1])
+        reference_tokens = ctx.generate(np.array(PROMPT, np.uint32), 12)
+    np.testing.assert_array_equal(picks, [int(np.argmax(r)) for r in rows])
+    np.testing.assert_array_equal(host, picks)
+    np.testing.assert_array_equal(generated, reference_tokens)
+    assert list(refusals) == [1, 1, 1, 1, 1]
