@@ -936,12 +936,10 @@ int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
         return bail(HF_E_CUDA);
     // The whole-loop kernel: Gemma's grouping (8 query heads over 1 kv head),
     // the 16384-wide feed-forward its schedule is written for, a vocabulary of
-    // whole 16-row records, enough SMs for the down product's per-CTA limit,
-    // cooperative launch, and one resident CTA per SM. It streams its own copy
+    // whole 16-row records, cooperative launch, and one resident CTA per SM. It streams its own copy
     // of every weight as stage records (build_records), at the same offsets in
     // a second pool.
-    if (ctx->fast && s.heads == 8 && s.kv_heads == 1 && s.intermediate == 16384 && s.vocab % kTileRows == 0
-        && ctx->sms * kMaxDownRecords >= s.width / 2)
+    if (ctx->fast && s.heads == 8 && s.kv_heads == 1 && s.intermediate == 16384 && s.vocab % kTileRows == 0)
     {
         if (ctx->cuda(cudaMalloc(&ctx->record_pool, pool_bytes), "record pool"))
             return bail(HF_E_CUDA);
@@ -1058,9 +1056,8 @@ int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, 
     {
         // Rebuild the tensor's records (q/k/v arrive in three uploads: each
         // rebuild covers the whole tensor).
-        const int rows_per_record = 32768 / target->cols;
-        build_records<<<target->rows / rows_per_record, 256>>>(target->base, target->rows, target->cols,
-                                                               target->records);
+        build_records<<<(target->rows / 16) * (target->cols / 2048), 256>>>(target->base, target->rows,
+                                                                            target->cols, target->records);
         rc = ctx->cuda(cudaDeviceSynchronize(), "record build");
     }
     if (rc)

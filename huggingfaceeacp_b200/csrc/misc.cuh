@@ -198,43 +198,33 @@ __global__ void permute_q8_rows(const uint8_t* src, int rows, int K, uint8_t* ds
         ds[i] = ss[i];
 }
 
-// The stage records the persistent decode streams, built from a tensor in
-// device layout (quants [rows][K], then scales [rows][K / 32]); one CTA per
-// record.
-//   K = 2048: 16 rows; quants row r at r * 2048 with 16-byte chunk c stored at
-//     chunk c ^ (r & 7); then the scales k-block-major, (r, kb) at kb * 16 + r.
-//   K > 2048: 32768 / K rows; quants row-major, then the rows' scales
-//     row-major: a plain concatenation.
+// The stage records the persistent decode and the multi-row products stream,
+// built from a tensor in device layout (quants [rows][K], then scales
+// [rows][K / 32]); one CTA per record. A record is 16 rows x 2048 columns: the
+// row-tile t, column chunk c (K / 2048 chunks a tile, record t * chunks + c):
+// quants row r at r * 2048 with its 16-byte chunk j stored at chunk j ^ (r & 7);
+// then the 1,024 fp16 scales k-block-major, scale (r, kb) at kb * 16 + r.
 __global__ void __launch_bounds__(256) build_records(const uint8_t* src, int rows, int K, uint8_t* dst)
 {
-    const int rows_per_record = 32768 / K;
-    const int first = blockIdx.x * rows_per_record;
-    if (first + rows_per_record > rows)
+    const int chunks = K / 2048;
+    const int tile = blockIdx.x / chunks, c = blockIdx.x % chunks;
+    if ((tile + 1) * 16 > rows)
         return;
-    const uint4* sq = reinterpret_cast<const uint4*>(src + (size_t) first * K);
-    const __half* ss = reinterpret_cast<const __half*>(src + (size_t) rows * K) + (size_t) first * (K / kBlock);
+    const uint8_t* quants = src + (size_t) tile * 16 * K + (size_t) c * 2048;
+    const __half* ss = reinterpret_cast<const __half*>(src + (size_t) rows * K) + (size_t) tile * 16 * (K / kBlock)
+                       + (size_t) c * 64;
     uint8_t* record = dst + (size_t) blockIdx.x * (32768 + 2048);
     uint4* dq = reinterpret_cast<uint4*>(record);
     __half* ds = reinterpret_cast<__half*>(record + 32768);
-    if (K == 2048)
+    for (int i = threadIdx.x; i < 2048; i += blockDim.x)
     {
-        for (int i = threadIdx.x; i < 2048; i += blockDim.x)
-        {
-            const int r = i >> 7, c = i & 127;
-            dq[r * 128 + (c ^ (r & 7))] = sq[i];
-        }
-        for (int i = threadIdx.x; i < 1024; i += blockDim.x)
-        {
-            const int kb = i >> 4, r = i & 15;
-            ds[i] = ss[r * 64 + kb];
-        }
+        const int r = i >> 7, j = i & 127;
+        dq[r * 128 + (j ^ (r & 7))] = *reinterpret_cast<const uint4*>(quants + (size_t) r * K + 16 * j);
     }
-    else
+    for (int i = threadIdx.x; i < 1024; i += blockDim.x)
     {
-        for (int i = threadIdx.x; i < 2048; i += blockDim.x)
-            dq[i] = sq[i];
-        for (int i = threadIdx.x; i < 1024; i += blockDim.x)
-            ds[i] = ss[i];
+        const int kb = i >> 4, r = i & 15;
+        ds[i] = ss[(size_t) r * (K / kBlock) + kb];
     }
 }
 

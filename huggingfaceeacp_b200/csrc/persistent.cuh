@@ -43,8 +43,8 @@ constexpr int kAttnTileFloats = 2 * kAttnTile * 256;        // the K rows, then 
 constexpr int kAttnFoldFloats = 8 * kAttnHeads * 256 + 2 * 8 * kAttnHeads; // one group's warp fold
 constexpr int kAttnAreaFloats = kPGroups * kAttnFoldFloats; // the tile, then (reusing it) both folds
 static_assert(kAttnAreaFloats >= kAttnTileFloats, "the fold area holds the tile");
+static_assert(kAttnAreaFloats * 4 >= 8 * kLimbFragBytes, "the attention area holds the down fragments");
 constexpr int kFusedMergeSplits = 8;                        // splits folded inside the o_proj x staging
-constexpr int kMaxDownRecords = 8;                          // 2-row down records a CTA may own
 constexpr unsigned kBarrierSpinLimit = 1u << 20;
 enum : unsigned
 {
@@ -52,8 +52,8 @@ enum : unsigned
 };
 constexpr unsigned kErrAbort = kErrWaitTimeout | kErrBarrierTimeout; // a wait gave up: every CTA leaves
 
-// A layer's weights as stage records (build_records): q/k/v, o and gate/up as
-// 16-row K = 2048 records, down as 2-row K = 16384 records.
+// A layer's weights as stage records (build_records): 16 rows x 2048 columns
+// each; the down matrix's tiles in eight column chunks.
 struct LayerDev
 {
     const uint8_t* qkv;
@@ -127,7 +127,7 @@ enum TraceEvent : int
     kTrGuLimbs,
     kTrGuDone,
     kTrGuLeft,
-    kTrDownStaged,    // activation slice in registers
+    kTrDownStaged,    // limb form of the activation, eight chunks
     kTrDownDone,
     kTrDownLeft,
     kTrMergeMl,       // o_proj staging: the splits' (max, sum) in shared memory
@@ -558,89 +558,92 @@ __device__ void attend_split(const PersistentArgs& p, const LayerDev& L, unsigne
 }
 
 // ---- down + residual ---------------------------------------------------------
-// Every 2-row K = 16384 record is read by all sixteen consumer warps, warp w
-// taking columns [1024 w, 1024 w + 1024) of both rows, so a lane keeps 32
-// values of the activation in registers.
+// The down matrix streams as (16-row tile, 2048-column chunk) records, a
+// tile's eight chunks consecutive, on the limb MMA like the other products. A
+// CTA owns whole tiles (one or none at Gemma's sizes); the activation (16384
+// values) is put into the limb form chunk by chunk: eight fragment sets
+// (64 KiB, in the attention area) and their k-block factors.
+constexpr int kDownChunks = 8;
 
-// The lane's 32 activation values of warp w's columns: [1024 w + 16 lane +
-// 512 j, + 16) for j = 0, 1.
-__device__ __forceinline__ void load_down_x(const float* act, int warp, int lane, float (&xr)[32])
+__device__ __forceinline__ void stage_down_limbs(const float* act, uint2* frags8, float* xexp8, int tid)
 {
+    float4 v[kDownChunks];
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int c = 0; c < kDownChunks; ++c)
+        v[c] = __ldcg(reinterpret_cast<const float4*>(act) + c * 512 + tid);
 #pragma unroll
-        for (int t = 0; t < 16; t += 4)
-        {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(act + 1024 * warp + 16 * lane + 512 * j + t));
-            xr[16 * j + t] = v.x;
-            xr[16 * j + t + 1] = v.y;
-            xr[16 * j + t + 2] = v.z;
-            xr[16 * j + t + 3] = v.w;
-        }
+    for (int c = 0; c < kDownChunks; ++c)
+        limbs_from_regs(v[c], frags8 + c * 1024, xexp8 + c * 64, tid);
+    consumers_sync();
 }
 
-// Drains the slab's records (rows [r0, r1), whole pairs, at most
-// kMaxDownRecords): every warp releases a slot on its own after reading its
-// slices (a slot takes sixteen arrivals) and keeps per-lane partial sums of
-// every row; the warp sums go to `spart` ([row][16 warps]) at the end and are
-// folded in warp order into the residual stream.
+// Drains the CTA's down tiles [r0, r1): the two groups take alternate chunk
+// records, each folds a record's 16 row sums over its warps (red, as
+// consume_tiles does) and adds them to its running sums (`rowsum`, [2][16],
+// zero on entry); at a tile's end the two groups' sums (group 0's first) are
+// added to the residual stream.
 template <int NST>
-__device__ bool consume_down(const GemvArgs& a, Slab slab, const Ring& ring, unsigned& seq, const float (&xr)[32],
-                             float* spart)
+__device__ bool consume_down_tiles(const GemvArgs& a, Slab tiles, const Ring& ring, unsigned& seq,
+                                   const uint2* frags8, const float* xexp8, float* red, float* rowsum, int group)
 {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int records = (slab.r1 - slab.r0) / 2;
+    const int tid = threadIdx.x, lane = tid & 31, warp = (tid >> 5) & 7;
+    float* gred = red + group * 2 * 8 * kTileRows;
     bool ok = true;
-    float part[2 * kMaxDownRecords];
-#pragma unroll
-    for (int s = 0; s < kMaxDownRecords; ++s)
+    int mine = 0;
+    for (int r0 = tiles.r0; r0 < tiles.r1; r0 += kTileRows)
     {
-        part[2 * s] = 0.f;
-        part[2 * s + 1] = 0.f;
-        if (s >= records)
-            continue;
-        const int buf = (int) ((seq + s) % NST);
-        if (ok && !mbar_wait(&ring.full[buf], ((seq + s) / NST) & 1u))
+        for (int c = 0; c < kDownChunks; ++c, ++seq)
         {
-            if (lane == 0)
-                flag_error(a.err, kErrWaitTimeout);
-            ok = false;
-        }
-        if (ok)
-        {
-            const uint8_t* qs = ring.quants + buf * ring.quant_stride + 1024 * warp;
-            const __half* scs = reinterpret_cast<const __half*>(ring.scales + buf * ring.scale_stride) + 32 * warp;
-            const uint4 w0 = *reinterpret_cast<const uint4*>(qs + 16 * lane);
-            const uint4 w1 = *reinterpret_cast<const uint4*>(qs + 16 * lane + 512);
-            const uint4 w2 = *reinterpret_cast<const uint4*>(qs + 16384 + 16 * lane);
-            const uint4 w3 = *reinterpret_cast<const uint4*>(qs + 16384 + 16 * lane + 512);
-            const float s0 = __half2float(scs[lane / 2]), s1 = __half2float(scs[lane / 2 + 16]);
-            const float s2 = __half2float(scs[512 + lane / 2]), s3 = __half2float(scs[512 + lane / 2 + 16]);
+            if ((int) (seq & 1u) != group)
+                continue;
+            const int buf = (int) (seq % NST);
+            if (ok && !mbar_wait(&ring.full[buf], (seq / NST) & 1u))
+            {
+                if (lane == 0)
+                    flag_error(a.err, kErrWaitTimeout);
+                ok = false;
+            }
+            float2 part = make_float2(0.f, 0.f);
+            if (ok)
+            {
+                uint32_t b[8][2];
+                float factor[8];
+                load_limb_frags(frags8 + c * 1024, xexp8 + c * 64, warp, lane, b, factor);
+                part = tile_partial(ring.quants + buf * ring.quant_stride,
+                                    reinterpret_cast<const __half*>(ring.scales + buf * ring.scale_stride), warp, lane,
+                                    b, factor);
+            }
             __syncwarp();
             if (lane == 0)
-                mbar_arrive(&ring.empty[buf]);
-            part[2 * s] = fmaf(dot16(w1, xr + 16), s1, dot16(w0, xr) * s0);
-            part[2 * s + 1] = fmaf(dot16(w3, xr + 16), s3, dot16(w2, xr) * s2);
-        }
-    }
-    seq += (unsigned) records;
+                mbar_arrive(&ring.empty[buf], 2u);
+            float* r = gred + (mine & 1) * 8 * kTileRows;
+            if ((lane & 3) == 0)
+            {
+                r[warp * kTileRows + (lane >> 2)] = part.x;
+                r[warp * kTileRows + (lane >> 2) + 8] = part.y;
+            }
+            named_sync(2 + group, 256);
+            if (warp == (mine & 7) && lane < kTileRows)
+            {
+                float v = 0.f;
 #pragma unroll
-    for (int r = 0; r < 2 * kMaxDownRecords; ++r)
-    {
-        const float v = warp_sum(part[r]);
-        if (lane == 0 && r < 2 * records)
-            spart[r * kPWarps + warp] = v;
-    }
-    consumers_sync();
-    if (ok)
-        for (int local = tid; local < slab.r1 - slab.r0; local += kPConsumers)
+                for (int w = 0; w < kConsumerWarps; ++w)
+                    v += r[w * kTileRows + lane];
+                rowsum[group * kTileRows + lane] += v;
+            }
+            ++mine;
+        }
+        consumers_sync(); // both groups' sums are in
+        if (tid < kTileRows)
         {
-            float v = 0.f;
-#pragma unroll
-            for (int w = 0; w < kPWarps; ++w)
-                v += spart[local * kPWarps + w];
-            plain_epilogue(Epi::Residual, v, nullptr, slab.r0 + local, a.out + slab.r0 + local);
+            const float v = rowsum[tid] + rowsum[kTileRows + tid];
+            rowsum[tid] = 0.f;
+            rowsum[kTileRows + tid] = 0.f;
+            if (ok)
+                plain_epilogue(Epi::Residual, v, nullptr, r0 + tid, a.out + r0 + tid);
         }
+        consumers_sync(); // zeroed before the next tile's sums
+    }
     return ok;
 }
 
@@ -661,11 +664,10 @@ __device__ __forceinline__ Plan make_plan(const PersistentArgs& p, int cta, int 
     plan.slab[0] = cta_tiles(p.qkv_rows, cta, ctas);
     plan.slab[1] = cta_tiles(2048, cta, ctas);
     plan.slab[2] = cta_tiles(2 * p.intermediate, cta, ctas);
-    plan.slab[3] = cta_slab(2048, true, cta, ctas); // whole 2-row records
+    plan.slab[3] = cta_tiles(2048, cta, ctas); // whole tiles, kDownChunks records each
     plan.slab[4] = cta_tiles(p.vocab, cta, ctas);
-    const int rows_per_record[5] = {kTileRows, kTileRows, kTileRows, 2, kTileRows};
     for (int i = 0; i < 5; ++i)
-        plan.stages[i] = (plan.slab[i].r1 - plan.slab[i].r0) / rows_per_record[i];
+        plan.stages[i] = (plan.slab[i].r1 - plan.slab[i].r0) / kTileRows * (i == 3 ? kDownChunks : 1);
     plan.per_layer = plan.stages[0] + plan.stages[1] + plan.stages[2] + plan.stages[3];
     plan.per_step = p.n_layers * plan.per_layer + plan.stages[4];
     return plan;
@@ -692,8 +694,7 @@ __device__ __forceinline__ const uint8_t* plan_stage(const PersistentArgs& p, co
     else
         r -= p.n_layers * plan.per_layer;
     index = r;
-    const int rows_per_record = product == 3 ? 2 : kTileRows;
-    const int record = plan.slab[product].r0 / rows_per_record + r;
+    const int record = plan.slab[product].r0 / kTileRows * (product == 3 ? kDownChunks : 1) + r;
     return records + (size_t) record * kRecordBytes;
 }
 
@@ -760,9 +761,11 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
     __shared__ float red[kPGroups * 2 * 8 * kTileRows];
 
     const Ring ring {smem, smem + kRecordQuants, full, empty, kRecordBytes, kRecordBytes}; // a record per slot
-    float* sx = reinterpret_cast<float*>(smem + NST * kRecordBytes); // down partials
+    float* sx = reinterpret_cast<float*>(smem + NST * kRecordBytes); // down: k-block factors, row sums
     uint2* frags = reinterpret_cast<uint2*>(sx + 2048);             // limb B fragments (8 KiB)
-    float* attn_area = sx + 4096; // attention K/V tile and folds; the merge's landing area
+    float* attn_area = sx + 4096; // attention K/V tile and folds; the merge's landing; the down fragments
+    float* down_xexp = sx;        // [kDownChunks][64]
+    float* down_rowsum = sx + kDownChunks * 64; // [2 groups][16]
 
     const int tid = threadIdx.x;
     if (tid == 0)
@@ -786,8 +789,9 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
         shared_word = *(volatile const unsigned*) p.state;
     consumers_sync();
     const unsigned position0 = shared_word;
+    if (tid < 2 * kTileRows)
+        down_rowsum[tid] = 0.f; // ordered before its first use by the barriers between
     unsigned seq = 0, epoch = 0;
-    float xr[32];
     float4 nw;
 
     unsigned long long* trace_row = p.trace && tid == 0 ? p.trace + (size_t) cta * kTraceEvents : nullptr;
@@ -944,9 +948,10 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
                 a.N = 2048;
                 a.out = p.hidden;
                 a.err = p.err;
-                load_down_x(p.act, tid >> 5, tid & 31, xr);
+                stage_down_limbs(p.act, reinterpret_cast<uint2*>(attn_area), down_xexp, tid);
                 stamp(ts + kTrDownStaged);
-                consume_down<NST>(a, cta_slab(2048, true, cta, ctas), ring, seq, xr, sx);
+                consume_down_tiles<NST>(a, cta_tiles(2048, cta, ctas), ring, seq, reinterpret_cast<const uint2*>(attn_area),
+                                        down_xexp, red, down_rowsum, group);
             }
             load_norm(l + 1 < p.n_layers ? p.layers[l + 1].in_norm : p.final_norm);
             if (!barrier(ts + kTrDownDone, ts + kTrDownLeft))
@@ -995,9 +1000,9 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
     }
 }
 
-// Dynamic shared memory: the ring, the down partials (8 KiB), the limb
-// fragments (8 KiB) and the attention area (the K/V tile, then the warp folds:
-// 66 KiB).
+// Dynamic shared memory: the ring, the down factors and row sums (8 KiB), the
+// limb fragments (8 KiB) and the attention area (the K/V tile, then the warp
+// folds, then the down fragments: 66 KiB).
 template <int NST>
 constexpr size_t persistent_smem()
 {
