@@ -21,6 +21,7 @@
 #include "gemv.cuh"
 #include "misc.cuh"
 #include "persistent.cuh"
+#include "rows_mma.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -116,6 +117,11 @@ void configure_kernels()
     HF_CONFIGURE_WIDE(8192)
     HF_CONFIGURE_WIDE(16384)
 #undef HF_CONFIGURE_WIDE
+    cudaFuncSetAttribute(q8_rows_mma<Epi::QkvRope, 2048>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
+    cudaFuncSetAttribute(q8_rows_mma<Epi::Residual, 2048>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
+    cudaFuncSetAttribute(q8_rows_mma<Epi::GeGLU, 2048>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
+    cudaFuncSetAttribute(q8_rows_mma<Epi::Logits, 2048>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
+    cudaFuncSetAttribute(q8_rows_mma<Epi::Residual, 16384>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
     cudaFuncSetAttribute(mqa_fast<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<8>());
     cudaFuncSetAttribute(mqa_fast<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<4>());
     cudaFuncSetAttribute(mqa_fast<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<2>());
@@ -176,6 +182,22 @@ cudaError_t launch_attention(int QH, dim3 grid, cudaStream_t stream, const AttnA
     case 2: return launch(true, mqa_fast<2>, grid, dim3(256), mqa_fast_smem<2>(), stream, at);
     default: return launch(true, mqa_fast<1>, grid, dim3(256), mqa_fast_smem<1>(), stream, at);
     }
+}
+
+// A product of a.M rows of x on the int8 tensor cores over the weight's stage
+// records, in blocks of kRowsBlock rows.
+template <Epi E, int K>
+cudaError_t rows_mma_product(bool pdl, const uint8_t* records, cudaStream_t stream, const GemvArgs& a, int sms)
+{
+    const int grid = std::max(1, std::min(sms, a.N / kTileRows));
+    for (int m0 = 0; m0 < a.M; m0 += kRowsBlock)
+    {
+        const cudaError_t e = launch(pdl, q8_rows_mma<E, K>, dim3(grid), dim3(kStreamThreads), rows_mma_smem(), stream,
+                                     a, records, m0, std::min(kRowsBlock, a.M - m0));
+        if (e != cudaSuccess)
+            return e;
+    }
+    return cudaSuccess;
 }
 
 template <Epi E>
@@ -638,7 +660,8 @@ struct hf_ctx
             qkv.head_dim = s.head_width;
             qkv.state = state;
             qkv.err = err_word();
-            e = generic_product<Epi::QkvRope>(true, L.qkv.rows / 2, stream, qkv, sms);
+            e = L.qkv.records ? rows_mma_product<Epi::QkvRope, 2048>(true, L.qkv.records, stream, qkv, sms)
+                              : generic_product<Epi::QkvRope>(true, L.qkv.rows / 2, stream, qkv, sms);
             if (e != cudaSuccess)
                 return cuda(e, "q/k/v launch");
 
@@ -674,7 +697,8 @@ struct hf_ctx
             o.out = hidden;
             o.state = state;
             o.err = err_word();
-            e = generic_product<Epi::Residual>(true, s.width, stream, o, sms);
+            e = L.o.records ? rows_mma_product<Epi::Residual, 2048>(true, L.o.records, stream, o, sms)
+                            : generic_product<Epi::Residual>(true, s.width, stream, o, sms);
             if (e != cudaSuccess)
                 return cuda(e, "o_proj launch");
 
@@ -693,7 +717,8 @@ struct hf_ctx
             gu.out = act;
             gu.state = state;
             gu.err = err_word();
-            e = generic_product<Epi::GeGLU>(true, L.gu.rows / 2, stream, gu, sms);
+            e = L.gu.records ? rows_mma_product<Epi::GeGLU, 2048>(true, L.gu.records, stream, gu, sms)
+                             : generic_product<Epi::GeGLU>(true, L.gu.rows / 2, stream, gu, sms);
             if (e != cudaSuccess)
                 return cuda(e, "gate/up launch");
 
@@ -707,7 +732,8 @@ struct hf_ctx
             dn.out = hidden;
             dn.state = state;
             dn.err = err_word();
-            e = generic_product<Epi::Residual>(true, s.width, stream, dn, sms);
+            e = L.down.records ? rows_mma_product<Epi::Residual, 16384>(true, L.down.records, stream, dn, sms)
+                               : generic_product<Epi::Residual>(true, s.width, stream, dn, sms);
             if (e != cudaSuccess)
                 return cuda(e, "down launch");
         }
@@ -728,7 +754,8 @@ struct hf_ctx
         lg.out = logits + (size_t) (all_logits ? 0 : rows - 1) * s.vocab;
         lg.state = state;
         lg.err = err_word();
-        e = generic_product<Epi::Logits>(true, s.vocab, stream, lg, sms);
+        e = embedding.records ? rows_mma_product<Epi::Logits, 2048>(true, embedding.records, stream, lg, sms)
+                              : generic_product<Epi::Logits>(true, s.vocab, stream, lg, sms);
         if (e != cudaSuccess)
             return cuda(e, "logits launch");
 
