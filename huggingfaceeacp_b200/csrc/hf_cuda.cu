@@ -626,7 +626,12 @@ struct hf_ctx
     // `rows` rows (prefill blocks, and every step on the generic path), with
     // the token ids already in slots[position ...]. all_logits: write every
     // row's logits (Decoder::step), else only the last row's (generation).
-    int enqueue_rows(int rows, bool all_logits)
+    // A block of a prompt that more blocks follow (sample false) ends after
+    // the last layer: it only moves the position on,
+    // since its logits are never read and the slot after it holds the next
+    // prompt token, not a sampled one (only the last block's last row is
+    // sampled, Gemma.cpp:341-380).
+    int enqueue_rows(int rows, bool all_logits, bool sample = true)
     {
         const hf_shape& s = shape;
         cudaError_t e = launch(false, embed_q8, dim3((s.width + 255) / 256, rows), dim3(256), 0, stream,
@@ -738,6 +743,11 @@ struct hf_ctx
                 return cuda(e, "down launch");
         }
 
+        if (!sample)
+        {
+            e = launch(true, advance_position, dim3(1), dim3(32), 0, stream, state, rows);
+            return e != cudaSuccess ? cuda(e, "position launch") : HF_OK;
+        }
         e = launch(true, rms_norm_rows, dim3(rows), dim3(256), 0, stream, (const float*) hidden,
                    (const float*) final_norm, s.width, s.rms_eps, normed);
         if (e != cudaSuccess)
@@ -813,11 +823,12 @@ struct hf_ctx
         for (int first = 0; first < count; first += capacity)
         {
             const int rows = std::min(capacity, count - first);
+            const bool last = first + rows == count;
             int rc;
-            if (rows == 1 && fast && !all_logits)
+            if (rows == 1 && last && fast && !all_logits)
                 rc = enqueue_decode_steps(1);
             else
-                rc = enqueue_rows(rows, all_logits);
+                rc = enqueue_rows(rows, all_logits, last);
             if (rc)
                 return rc;
             position += rows;

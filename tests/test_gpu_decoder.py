@@ -209,6 +209,18 @@ def test_greedy_generation_equals_the_host_driven_reference_loop(shape):
             assert len(set(expected)) > 3  # the feedback path sees real token changes
 
 
+@pytest.mark.parametrize("capacity,length", [(64, 70), (4, 10), (1, 5)])
+def test_prompt_longer_than_a_step_generates_like_the_reference(capacity, length):
+    """A prompt fed in several blocks (Gemma.cpp:341-380): every block but the
+    last leaves the next prompt token in its slot; only the last one samples."""
+    shape = MINI.replace(intermediate=16384, embed_scale=1.0, max_positions=96, max_step_rows=capacity)
+    with native.Context(shape) as ctx:
+        tensors = ctx.load_synthetic(seed=41, keep=True)
+        prompt = native.synthetic_tokens(100, length, shape.vocab)
+        expected = ob.greedy_reference(shape, tensors, prompt, 12)
+        assert list(ctx.generate(prompt, 12)) == expected
+
+
 def test_generation_stops_at_end_of_sequence_and_at_the_window():
     shape = VARIED
     with native.Context(shape) as ctx:
