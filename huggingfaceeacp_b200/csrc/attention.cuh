@@ -34,6 +34,10 @@ struct AttnArgs
     int nsplit;
     const unsigned* state; // state[0] = position of row 0
     unsigned* err;
+    // Batched decode: row r is sequence r, every row at state[0], its caches at
+    // k_cache / v_cache + r * cache_seq_stride. 0: the rows are consecutive
+    // positions of one sequence.
+    size_t cache_seq_stride;
 };
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src)
@@ -135,7 +139,9 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int H = a.heads;
     const int kvw = a.kv_heads * D;
-    const int keys = (int) position + row + 1;
+    const int keys = (int) position + (a.cache_seq_stride ? 0 : row) + 1;
+    const float* k_cache = a.k_cache + (size_t) row * a.cache_seq_stride;
+    const float* v_cache = a.v_cache + (size_t) row * a.cache_seq_stride;
     const int chunk = (keys + a.nsplit - 1) / a.nsplit;
     const int k0 = min(keys, split * chunk);
     const int k1 = min(keys, k0 + chunk);
@@ -168,8 +174,8 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
         {
             const int r = i / (D / 4), c = (i % (D / 4)) * 4;
             const size_t at = (size_t) (t0 + r) * kvw + (size_t) kv_head * D + c;
-            cp_async16(tk + r * D + c, a.k_cache + at);
-            cp_async16(tv + r * D + c, a.v_cache + at);
+            cp_async16(tk + r * D + c, k_cache + at);
+            cp_async16(tv + r * D + c, v_cache + at);
         }
         cp_async_wait_all();
         sync();

@@ -72,6 +72,9 @@ struct GemvArgs
     // step state
     unsigned* state;        // state[0]: position of x's first row, or null (= 0)
     unsigned* err;          // error word, or null
+    // QkvRope of a batched decode step: row m of x is sequence m, whose cache
+    // rows start at k_cache / v_cache + m * cache_seq_stride. 0: one sequence.
+    size_t cache_seq_stride;
 };
 
 __device__ __forceinline__ unsigned step_position(const GemvArgs& a)
@@ -102,14 +105,15 @@ __device__ __forceinline__ void qkv_pair_store(const GemvArgs& a, unsigned unit,
         }
         else
         {
-            float* k = a.k_cache + (size_t) position * kvw + (size_t) (block - a.heads) * D;
+            float* k = a.k_cache + m * a.cache_seq_stride + (size_t) position * kvw + (size_t) (block - a.heads) * D;
             k[pair] = r0;
             k[pair + half] = r1;
         }
     }
     else
     {
-        float* v = a.v_cache + (size_t) position * kvw + (size_t) (block - a.heads - a.kv_heads) * D;
+        float* v = a.v_cache + m * a.cache_seq_stride + (size_t) position * kvw
+                   + (size_t) (block - a.heads - a.kv_heads) * D;
         v[pair] = v0;
         v[pair + half] = v1;
     }

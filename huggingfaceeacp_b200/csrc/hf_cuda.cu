@@ -38,6 +38,8 @@ using namespace hfk;
 namespace
 {
 constexpr int kStages = 3; // shared-memory ring depth of the streaming products (3 x 34 KiB)
+constexpr int kBatchSplits = 8;       // most attention splits per sequence of a batched step
+constexpr int kBatchArgmaxParts = 64; // argmax candidates per sequence of a batched step
 
 // Dynamic shared memory of q8_gemv_stream<K>: the stage ring plus either the
 // x vector (K = 2048) or the per-slab row partials (K > 2048). Two CTAs fit on
@@ -66,7 +68,6 @@ struct Q8
     int rows = 0;
     int cols = 0;
     const __half* scales() const { return reinterpret_cast<const __half*>(base + (size_t) rows * cols); }
-    size_t bytes() const { return (size_t) rows * cols + (size_t) rows * cols / 16; }
 };
 
 struct Layer
@@ -260,7 +261,8 @@ struct hf_ctx
     float* vcache = nullptr;
     float* rope_cos = nullptr;
     float* rope_sin = nullptr;
-    unsigned* slots = nullptr;
+    unsigned* slots = nullptr;     // the selected sequence's P + 1 token slots (a view of slot_base)
+    unsigned* slot_base = nullptr; // [sequences][P + 1]
     unsigned* state = nullptr; // [0] position, [1] error word, [2] logits ticket
     float* cand_val = nullptr;
     unsigned* cand_idx = nullptr;
@@ -276,6 +278,13 @@ struct hf_ctx
 
     int position = 0;
     std::map<int, cudaGraphExec_t> graphs; // decode step by attention split count
+
+    // Batched decode: `sequences` independent sequences share the weights and
+    // the position; each has its own slots and caches. The single-sequence
+    // calls act on sequence `seq` (0 outside a batched prefill): the decode
+    // graphs and the whole-loop kernel hold sequence 0's buffers.
+    int sequences = 1;
+    int seq = 0;
 
     int fail(int code, const std::string& text)
     {
@@ -308,8 +317,17 @@ struct hf_ctx
     {
         return persistent_ok && decode_path != HF_DECODE_GRAPH;
     }
-    float* layer_k(int l) const { return kcache + (size_t) l * shape.max_positions * kv_width(); }
-    float* layer_v(int l) const { return vcache + (size_t) l * shape.max_positions * kv_width(); }
+    // Caches are [layer][sequence][position][kv width]: one layer's caches of
+    // every sequence are contiguous, sequence to sequence seq_cache_stride().
+    size_t seq_cache_stride() const { return (size_t) shape.max_positions * kv_width(); }
+    float* layer_k(int l) const { return kcache + ((size_t) l * sequences + seq) * seq_cache_stride(); }
+    float* layer_v(int l) const { return vcache + ((size_t) l * sequences + seq) * seq_cache_stride(); }
+
+    void select_sequence(int q)
+    {
+        seq = q;
+        slots = slot_base + (size_t) q * (shape.max_positions + 1);
+    }
 
     bool all_loaded() const
     {
@@ -343,7 +361,7 @@ struct hf_ctx
         const hf_shape& s = shape;
         return launch(false, embed_q8, dim3((s.width + 255) / 256, 1), dim3(256), 0, stream,
                       (const uint8_t*) embedding.base, embedding.scales(), s.width, s.vocab, s.embed_scale,
-                      (const unsigned*) slots, (const unsigned*) state, 1, hidden, err_word());
+                      (const unsigned*) slots, (const unsigned*) state, 1, hidden, err_word(), 0);
     }
 
     cudaError_t launch_qkv(int l)
@@ -623,6 +641,156 @@ struct hf_ctx
     }
 
     // ---------------------------------------------------------------------
+    // One batched decode step: every sequence's next token at the shared
+    // position, row r of each product being sequence r, on the multi-row
+    // int8 MMA products over the stage records (the weights stream once per
+    // eight sequences).
+    int enqueue_batch_step()
+    {
+        const hf_shape& s = shape;
+        const int S = sequences;
+        const int P1 = s.max_positions + 1;
+        const size_t stride = seq_cache_stride();
+        cudaError_t e = launch(false, embed_q8, dim3((s.width + 255) / 256, S), dim3(256), 0, stream,
+                               (const uint8_t*) embedding.base, embedding.scales(), s.width, s.vocab, s.embed_scale,
+                               (const unsigned*) slot_base, (const unsigned*) state, S, hidden, err_word(), P1);
+        if (e != cudaSuccess)
+            return cuda(e, "embed launch");
+        const int keys = position + 1;
+        int splits = 1;
+        while (splits < kBatchSplits && splits * 64 < keys)
+            splits *= 2;
+        for (int l = 0; l < s.layers; ++l)
+        {
+            const Layer& L = layers[l];
+            float* k0 = kcache + (size_t) l * S * stride; // sequence 0's rows of this layer
+            float* v0 = vcache + (size_t) l * S * stride;
+            e = launch(true, rms_norm_rows, dim3(S), dim3(256), 0, stream, (const float*) hidden,
+                       (const float*) L.in_norm, s.width, s.rms_eps, normed);
+            if (e != cudaSuccess)
+                return cuda(e, "norm launch");
+
+            GemvArgs qkv = {};
+            qkv.w = L.qkv.base;
+            qkv.scales = L.qkv.scales();
+            qkv.N = L.qkv.rows;
+            qkv.K = s.width;
+            qkv.M = S;
+            qkv.x = normed;
+            qkv.out = qbuf;
+            qkv.k_cache = k0;
+            qkv.v_cache = v0;
+            qkv.cache_seq_stride = stride;
+            qkv.rope_cos = rope_cos;
+            qkv.rope_sin = rope_sin;
+            qkv.heads = s.heads;
+            qkv.kv_heads = s.kv_heads;
+            qkv.head_dim = s.head_width;
+            qkv.state = state;
+            qkv.err = err_word();
+            e = rows_mma_product<Epi::QkvRope, 2048>(true, L.qkv.records, stream, qkv, sms);
+            if (e != cudaSuccess)
+                return cuda(e, "q/k/v launch");
+
+            AttnArgs at = {};
+            at.q = qbuf;
+            at.k_cache = k0;
+            at.v_cache = v0;
+            at.cache_seq_stride = stride;
+            at.out = attended;
+            at.part_acc = attn_acc;
+            at.part_ml = attn_ml;
+            at.heads = s.heads;
+            at.kv_heads = s.kv_heads;
+            at.head_dim = s.head_width;
+            at.scale = 1.f / std::sqrt((float) s.head_width);
+            at.nsplit = splits;
+            at.state = state;
+            at.err = err_word();
+            e = launch_attention(s.heads / s.kv_heads, dim3(splits, s.kv_heads, S), stream, at);
+            if (e == cudaSuccess && splits > 1)
+                e = launch(true, mqa_merge, dim3((query_width() + 255) / 256, S), dim3(256), 0, stream, at);
+            if (e != cudaSuccess)
+                return cuda(e, "attention launch");
+
+            GemvArgs o = {};
+            o.w = L.o.base;
+            o.scales = L.o.scales();
+            o.N = s.width;
+            o.K = query_width();
+            o.M = S;
+            o.x = attended;
+            o.out = hidden;
+            o.state = state;
+            o.err = err_word();
+            e = rows_mma_product<Epi::Residual, 2048>(true, L.o.records, stream, o, sms);
+            if (e != cudaSuccess)
+                return cuda(e, "o_proj launch");
+
+            e = launch(true, rms_norm_rows, dim3(S), dim3(256), 0, stream, (const float*) hidden,
+                       (const float*) L.post_norm, s.width, s.rms_eps, normed);
+            if (e != cudaSuccess)
+                return cuda(e, "norm launch");
+
+            GemvArgs gu = {};
+            gu.w = L.gu.base;
+            gu.scales = L.gu.scales();
+            gu.N = L.gu.rows;
+            gu.K = s.width;
+            gu.M = S;
+            gu.x = normed;
+            gu.out = act;
+            gu.state = state;
+            gu.err = err_word();
+            e = rows_mma_product<Epi::GeGLU, 2048>(true, L.gu.records, stream, gu, sms);
+            if (e != cudaSuccess)
+                return cuda(e, "gate/up launch");
+
+            GemvArgs dn = {};
+            dn.w = L.down.base;
+            dn.scales = L.down.scales();
+            dn.N = s.width;
+            dn.K = s.intermediate;
+            dn.M = S;
+            dn.x = act;
+            dn.out = hidden;
+            dn.state = state;
+            dn.err = err_word();
+            e = rows_mma_product<Epi::Residual, 16384>(true, L.down.records, stream, dn, sms);
+            if (e != cudaSuccess)
+                return cuda(e, "down launch");
+        }
+
+        e = launch(true, rms_norm_rows, dim3(S), dim3(256), 0, stream, (const float*) hidden,
+                   (const float*) final_norm, s.width, s.rms_eps, normed);
+        if (e != cudaSuccess)
+            return cuda(e, "final norm launch");
+        GemvArgs lg = {};
+        lg.w = embedding.base;
+        lg.scales = embedding.scales();
+        lg.N = s.vocab;
+        lg.K = s.width;
+        lg.M = S;
+        lg.x = normed;
+        lg.out = logits;
+        lg.state = state;
+        lg.err = err_word();
+        e = rows_mma_product<Epi::Logits, 2048>(true, embedding.records, stream, lg, sms);
+        if (e != cudaSuccess)
+            return cuda(e, "logits launch");
+        e = launch(true, argmax_partial, dim3(kBatchArgmaxParts, S), dim3(256), 0, stream, (const float*) logits, s.vocab,
+                   (const float*) nullptr, kBatchArgmaxParts, cand_val, cand_idx);
+        if (e != cudaSuccess)
+            return cuda(e, "argmax launch");
+        e = launch(true, argmax_final_batch, dim3(S), dim3(32), 0, stream, (const float*) cand_val,
+                   (const unsigned*) cand_idx, kBatchArgmaxParts, slot_base, P1, (unsigned) position, state);
+        if (e != cudaSuccess)
+            return cuda(e, "argmax launch");
+        ++position;
+        return HF_OK;
+    }
+
+    // ---------------------------------------------------------------------
     // `rows` rows (prefill blocks, and every step on the generic path), with
     // the token ids already in slots[position ...]. all_logits: write every
     // row's logits (Decoder::step), else only the last row's (generation).
@@ -636,7 +804,7 @@ struct hf_ctx
         const hf_shape& s = shape;
         cudaError_t e = launch(false, embed_q8, dim3((s.width + 255) / 256, rows), dim3(256), 0, stream,
                                (const uint8_t*) embedding.base, embedding.scales(), s.width, s.vocab, s.embed_scale,
-                               (const unsigned*) slots, (const unsigned*) state, rows, hidden, err_word());
+                               (const unsigned*) slots, (const unsigned*) state, rows, hidden, err_word(), 0);
         if (e != cudaSuccess)
             return cuda(e, "embed launch");
         const int QH = s.heads / s.kv_heads;
@@ -825,7 +993,7 @@ struct hf_ctx
             const int rows = std::min(capacity, count - first);
             const bool last = first + rows == count;
             int rc;
-            if (rows == 1 && last && fast && !all_logits)
+            if (rows == 1 && last && fast && !all_logits && seq == 0)
                 rc = enqueue_decode_steps(1);
             else
                 rc = enqueue_rows(rows, all_logits, last);
@@ -867,20 +1035,19 @@ int hf_cuda_device_count(int* count)
     return HF_OK;
 }
 
-int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
+namespace
 {
-    if (!shape || !out)
-        return HF_E_INVALID;
+// A context of `sequences` sequences (1 for hf_cuda_create); the shape is
+// already checked.
+int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** out)
+{
     *out = nullptr;
-    const std::string refusal = shape_refusal(*shape);
-    if (!refusal.empty())
-        return HF_E_SHAPE;
-
     auto* ctx = new hf_ctx();
     ctx->device = device;
     ctx->shape = *shape;
     const hf_shape& s = ctx->shape;
     ctx->capacity = s.max_step_rows > 0 ? s.max_step_rows : s.max_positions;
+    ctx->sequences = sequences;
     auto bail = [&](int rc) {
         hf_cuda_destroy(ctx);
         return rc;
@@ -938,23 +1105,27 @@ int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
     }
 
     const size_t cap = ctx->capacity, P = s.max_positions;
+    const size_t cand = std::max<size_t>(1024, (size_t) sequences * kBatchArgmaxParts);
+    const size_t partials = std::max<size_t>(ctx->max_splits, (size_t) sequences * kBatchSplits);
     if (device_alloc(ctx, &ctx->hidden, cap * W, "hidden") || device_alloc(ctx, &ctx->normed, cap * W, "normed")
         || device_alloc(ctx, &ctx->qbuf, cap * QW, "queries") || device_alloc(ctx, &ctx->attended, cap * QW, "attended")
         || device_alloc(ctx, &ctx->act, cap * I, "activated") || device_alloc(ctx, &ctx->logits, cap * V, "logits")
-        || device_alloc(ctx, &ctx->kcache, (size_t) s.layers * P * KVW, "key cache")
-        || device_alloc(ctx, &ctx->vcache, (size_t) s.layers * P * KVW, "value cache")
+        || device_alloc(ctx, &ctx->kcache, (size_t) s.layers * sequences * P * KVW, "key cache")
+        || device_alloc(ctx, &ctx->vcache, (size_t) s.layers * sequences * P * KVW, "value cache")
         || device_alloc(ctx, &ctx->rope_cos, P * (s.head_width / 2), "rotary cosines")
         || device_alloc(ctx, &ctx->rope_sin, P * (s.head_width / 2), "rotary sines")
-        || device_alloc(ctx, &ctx->slots, P + 1, "sequence slots") || device_alloc(ctx, &ctx->state, 8, "step state")
-        || device_alloc(ctx, &ctx->cand_val, 1024, "argmax candidates")
-        || device_alloc(ctx, &ctx->cand_idx, 1024, "argmax candidates")
-        || device_alloc(ctx, &ctx->attn_acc, (size_t) ctx->max_splits * QW, "attention partials")
-        || device_alloc(ctx, &ctx->attn_ml, (size_t) ctx->max_splits * s.heads * 2, "attention partials"))
+        || device_alloc(ctx, &ctx->slot_base, sequences * (P + 1), "sequence slots")
+        || device_alloc(ctx, &ctx->state, 8, "step state")
+        || device_alloc(ctx, &ctx->cand_val, cand, "argmax candidates")
+        || device_alloc(ctx, &ctx->cand_idx, cand, "argmax candidates")
+        || device_alloc(ctx, &ctx->attn_acc, partials * QW, "attention partials")
+        || device_alloc(ctx, &ctx->attn_ml, partials * s.heads * 2, "attention partials"))
         return bail(HF_E_CUDA);
+    ctx->select_sequence(0);
     cudaMemset(ctx->state, 0, 8 * sizeof(unsigned));
-    cudaMemset(ctx->slots, 0, (P + 1) * sizeof(unsigned));
-    cudaMemset(ctx->kcache, 0, (size_t) s.layers * P * KVW * sizeof(float));
-    cudaMemset(ctx->vcache, 0, (size_t) s.layers * P * KVW * sizeof(float));
+    cudaMemset(ctx->slot_base, 0, sequences * (P + 1) * sizeof(unsigned));
+    cudaMemset(ctx->kcache, 0, (size_t) s.layers * sequences * P * KVW * sizeof(float));
+    cudaMemset(ctx->vcache, 0, (size_t) s.layers * sequences * P * KVW * sizeof(float));
 
     // Kernels/RoPE.cpp:7-34: angle = pos * theta^(-2i/D) in double, stored as float.
     const int half = s.head_width / 2;
@@ -1012,6 +1183,45 @@ int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
     *out = ctx;
     return HF_OK;
 }
+} // namespace
+
+int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
+{
+    if (!shape || !out)
+        return HF_E_INVALID;
+    *out = nullptr;
+    if (!shape_refusal(*shape).empty())
+        return HF_E_SHAPE;
+    return create_context(device, shape, 1, out);
+}
+
+int hf_cuda_create_batch(int device, const hf_shape* shape, int sequences, hf_ctx** out)
+{
+    if (!shape || !out || sequences < 1)
+        return HF_E_INVALID;
+    *out = nullptr;
+    if (!shape_refusal(*shape).empty())
+        return HF_E_SHAPE;
+    const int capacity = shape->max_step_rows > 0 ? shape->max_step_rows : shape->max_positions;
+    if (sequences > capacity)
+        return HF_E_CAPACITY; // a batched step carries one row per sequence
+    hf_ctx* ctx = nullptr;
+    const int rc = create_context(device, shape, sequences, &ctx);
+    if (rc)
+        return rc;
+    if (!ctx->record_pool) // the batched products run on the stage records only
+    {
+        hf_cuda_destroy(ctx);
+        return HF_E_SHAPE;
+    }
+    *out = ctx;
+    return HF_OK;
+}
+
+int hf_cuda_sequences(const hf_ctx* ctx)
+{
+    return ctx ? ctx->sequences : HF_E_INVALID;
+}
 
 void hf_cuda_destroy(hf_ctx* ctx)
 {
@@ -1023,7 +1233,7 @@ void hf_cuda_destroy(hf_ctx* ctx)
     for (auto& g: ctx->graphs)
         cudaGraphExecDestroy(g.second);
     void* buffers[] = {ctx->pool, ctx->record_pool, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
-                       ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slots, ctx->state,
+                       ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slot_base, ctx->state,
                        ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev};
     for (void* b: buffers)
         if (b)
@@ -1174,7 +1384,6 @@ int hf_cuda_step(hf_ctx* ctx, const uint32_t* tokens, int count, float* logits, 
                    "token upload");
     if (rc)
         return rc;
-    const int first = ctx->position;
     if (count == 1 && ctx->fast)
         rc = ctx->enqueue_decode_steps(1);
     else
@@ -1427,6 +1636,80 @@ int hf_cuda_generate_greedy(hf_ctx* ctx, const uint32_t* prompt, int prompt_leng
     }
     *count_out = emitted;
     return HF_OK;
+}
+
+int hf_cuda_prefill_batch_async(hf_ctx* ctx, const uint32_t* prompts, int prompt_length)
+{
+    if (!ctx || !prompts)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    for (int q = 0; q < ctx->sequences; ++q)
+        if (const int rc = check_tokens(ctx, prompts + (size_t) q * prompt_length, std::max(prompt_length, 0)))
+            return rc;
+    for (int q = 0; q < ctx->sequences; ++q)
+    {
+        ctx->select_sequence(q);
+        const int rc = hf_cuda_prefill_async(ctx, prompts + (size_t) q * prompt_length, prompt_length);
+        if (rc)
+        {
+            ctx->select_sequence(0);
+            return rc;
+        }
+    }
+    ctx->select_sequence(0);
+    return HF_OK;
+}
+
+int hf_cuda_decode_batch_async(hf_ctx* ctx, int steps)
+{
+    if (!ctx || steps < 0)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    if (!ctx->all_loaded())
+        return ctx->fail(HF_E_NOT_READY, "this decoder has not been prepared: every weight must be uploaded");
+    if (!ctx->record_pool)
+        return ctx->fail(HF_E_SHAPE, "batched steps run on the stage records, which this shape has none of");
+    if (ctx->position + steps > ctx->shape.max_positions)
+        return ctx->fail(HF_E_WINDOW, "these steps would carry the sequences past the window");
+    if (ctx->position == 0 && steps > 0)
+        return ctx->fail(HF_E_INVALID, "a decode step follows a prefill: the sequences are empty");
+    for (int i = 0; i < steps; ++i)
+    {
+        const int rc = ctx->enqueue_batch_step();
+        if (rc)
+            return rc;
+    }
+    return HF_OK;
+}
+
+int hf_cuda_read_batch_slots(hf_ctx* ctx, int first, int count, uint32_t* out)
+{
+    if (!ctx || !out || first < 0 || count < 0 || first + count > ctx->shape.max_positions + 1)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    if (count == 0)
+        return ctx->sync();
+    const size_t pitch = (size_t) (ctx->shape.max_positions + 1) * 4;
+    int rc = ctx->cuda(cudaMemcpy2DAsync(out, (size_t) count * 4, ctx->slot_base + first, pitch, (size_t) count * 4,
+                                         (size_t) ctx->sequences, cudaMemcpyDeviceToHost, ctx->stream),
+                       "slot readback");
+    if (rc)
+        return rc;
+    return ctx->sync();
+}
+
+int hf_cuda_generate_batch(hf_ctx* ctx, const uint32_t* prompts, int prompt_length, int tokens, uint32_t* out)
+{
+    if (!ctx || !prompts || tokens < 0 || (tokens > 0 && !out))
+        return HF_E_INVALID;
+    if (prompt_length + tokens - 1 > ctx->shape.max_positions)
+        return ctx->fail(HF_E_WINDOW, "these tokens would carry the sequences past the window");
+    int rc = hf_cuda_prefill_batch_async(ctx, prompts, prompt_length);
+    if (!rc && tokens > 1)
+        rc = hf_cuda_decode_batch_async(ctx, tokens - 1);
+    if (!rc)
+        rc = hf_cuda_read_batch_slots(ctx, prompt_length, tokens, out);
+    return rc;
 }
 
 void* hf_cuda_stream(const hf_ctx* ctx)

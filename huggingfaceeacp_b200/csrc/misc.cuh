@@ -8,10 +8,12 @@
 namespace hfk
 {
 // Kernels/Embed.h:45-77 over the Q8_0 tied table: h = scale * (q * s), with
-// token ids read from the sequence slots at the step's position.
+// token ids read from the sequence slots at the step's position. slot_stride 0:
+// row r is position + r of one sequence; otherwise row r is sequence r, whose
+// slots start at slots + r * slot_stride, every row at `position`.
 __global__ void __launch_bounds__(256) embed_q8(const uint8_t* table, const __half* scales, int width, int vocab,
                                                  float scale, const unsigned* slots, const unsigned* state, int rows,
-                                                 float* out, unsigned* err)
+                                                 float* out, unsigned* err, int slot_stride)
 {
     pdl_wait();
     const unsigned position = state ? *(volatile const unsigned*) state : 0u;
@@ -20,7 +22,7 @@ __global__ void __launch_bounds__(256) embed_q8(const uint8_t* table, const __ha
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= rows || c >= width)
         return;
-    unsigned token = slots[position + row];
+    unsigned token = slot_stride ? slots[(size_t) row * slot_stride + position] : slots[position + row];
     if (token >= (unsigned) vocab)
     {
         if (c == 0)
@@ -110,16 +112,11 @@ __global__ void __launch_bounds__(256) argmax_partial(const float* logits, int r
     }
 }
 
-// Kernels/Argmax.h:144-200: one warp folds a row's candidates; 0 when nothing
-// was allowed. With `slots`, also writes the token into the sequence slot
-// after the step and advances the position by `advance` rows (one row only).
-__global__ void argmax_final(const float* cand_val, const unsigned* cand_idx, int parts, int rows,
-                             unsigned* indices, unsigned* slots, unsigned* state, int advance)
+// One warp's fold of row `row`'s candidates (Kernels/Argmax.h:144-200): the
+// best index on every lane, 0xFFFFFFFF when nothing was allowed.
+__device__ __forceinline__ unsigned fold_candidates(const float* cand_val, const unsigned* cand_idx, int parts,
+                                                    int row, int lane)
 {
-    pdl_wait();
-    pdl_trigger();
-    const int row = blockIdx.x;
-    const int lane = threadIdx.x;
     float best = -INFINITY;
     unsigned best_i = 0xFFFFFFFFu;
     for (int c = lane; c < parts; c += 32)
@@ -143,6 +140,20 @@ __global__ void argmax_final(const float* cand_val, const unsigned* cand_idx, in
             best_i = i;
         }
     }
+    return best_i;
+}
+
+// Kernels/Argmax.h:144-200: one warp folds a row's candidates; 0 when nothing
+// was allowed. With `slots`, also writes the token into the sequence slot
+// after the step and advances the position by `advance` rows (one row only).
+__global__ void argmax_final(const float* cand_val, const unsigned* cand_idx, int parts, int rows,
+                             unsigned* indices, unsigned* slots, unsigned* state, int advance)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.x;
+    const int lane = threadIdx.x;
+    const unsigned best_i = fold_candidates(cand_val, cand_idx, parts, row, lane);
     if (lane == 0)
     {
         const unsigned token = best_i == 0xFFFFFFFFu ? 0u : best_i;
@@ -154,6 +165,26 @@ __global__ void argmax_final(const float* cand_val, const unsigned* cand_idx, in
             slots[position + (unsigned) advance] = token;
             *state = position + (unsigned) advance;
         }
+    }
+}
+
+// The batched decode's last fold: row r's token (argmax_final's rule) into
+// sequence r's slot after `position` (slots[r * slot_stride + position + 1]);
+// row 0 advances the shared position. `position` is the step's, from the host:
+// the rows may not read the state that row 0 writes.
+__global__ void argmax_final_batch(const float* cand_val, const unsigned* cand_idx, int parts, unsigned* slots,
+                                   int slot_stride, unsigned position, unsigned* state)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.x;
+    const int lane = threadIdx.x;
+    const unsigned best_i = fold_candidates(cand_val, cand_idx, parts, row, lane);
+    if (lane == 0)
+    {
+        slots[(size_t) row * slot_stride + position + 1] = best_i == 0xFFFFFFFFu ? 0u : best_i;
+        if (row == 0)
+            *state = position + 1;
     }
 }
 

@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) q8_rows_mma(const GemvArgs 
                         const int m = m0 + xm;
                         const unsigned unit = (unsigned) (row0 / 2 + j);
                         if constexpr (E == Epi::QkvRope)
-                            qkv_pair_store(a, unit, v0, v1, position + (unsigned) m, m);
+                            qkv_pair_store(a, unit, v0, v1, position + (a.cache_seq_stride ? 0u : (unsigned) m), m);
                         else
                             a.out[(size_t) m * (a.N / 2) + unit] = tanh_gelu(v0) * v1;
                     }

@@ -187,6 +187,13 @@ def cuda() -> ctypes.CDLL:
         lib = _load("libhf_cuda.so")
         lib.hf_cuda_device_count.argtypes = [ctypes.POINTER(ctypes.c_int)]
         lib.hf_cuda_create.argtypes = [ctypes.c_int, ctypes.POINTER(ShapeStruct), ctypes.POINTER(_vp)]
+        lib.hf_cuda_create_batch.argtypes = [ctypes.c_int, ctypes.POINTER(ShapeStruct), ctypes.c_int,
+                                             ctypes.POINTER(_vp)]
+        lib.hf_cuda_sequences.argtypes = [_vp]
+        lib.hf_cuda_prefill_batch_async.argtypes = [_vp, _vp, ctypes.c_int]
+        lib.hf_cuda_decode_batch_async.argtypes = [_vp, ctypes.c_int]
+        lib.hf_cuda_read_batch_slots.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp]
+        lib.hf_cuda_generate_batch.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]
         lib.hf_cuda_destroy.argtypes = [_vp]
         lib.hf_cuda_destroy.restype = None
         lib.hf_cuda_last_error.argtypes = [_vp]
@@ -305,16 +312,24 @@ def model_tensors(shape: DecoderShape):
 # ---------------------------------------------------------------------------
 
 class Context:
-    """One hf_ctx: a prepared decoder on one device (HF::Decoder + DecoderWeights)."""
+    """One hf_ctx: a prepared decoder on one device (HF::Decoder + DecoderWeights).
 
-    def __init__(self, shape: DecoderShape, device: int = 0):
+    sequences > 1 makes a batch context (hf_cuda_create_batch): that many
+    independent sequences decoded together by the *_batch methods; the other
+    methods act on sequence 0."""
+
+    def __init__(self, shape: DecoderShape, device: int = 0, sequences: int = 1):
         self.lib = cuda()
         self.shape = shape
+        self.sequences = sequences
         handle = _vp()
         struct = shape.struct()
-        rc = self.lib.hf_cuda_create(device, ctypes.byref(struct), ctypes.byref(handle))
+        if sequences == 1:
+            rc = self.lib.hf_cuda_create(device, ctypes.byref(struct), ctypes.byref(handle))
+        else:
+            rc = self.lib.hf_cuda_create_batch(device, ctypes.byref(struct), sequences, ctypes.byref(handle))
         if rc:
-            raise HFError(rc, "hf_cuda_create refused the shape or the device")
+            raise HFError(rc, "the engine refused the shape, the sequence count or the device")
         self.handle = handle
 
     def close(self):
@@ -410,6 +425,32 @@ class Context:
 
     def sync(self):
         self.check(self.lib.hf_cuda_sync(self.handle))
+
+    # ---- batched decode (hf_cuda_*_batch) ----------------------------------
+    def _prompts(self, prompts) -> np.ndarray:
+        prompts = np.ascontiguousarray(prompts, dtype=np.uint32)
+        if prompts.ndim != 2 or prompts.shape[0] != self.sequences:
+            raise ValueError(f"prompts must be [{self.sequences}, length]")
+        return prompts
+
+    def prefill_batch_async(self, prompts):
+        prompts = self._prompts(prompts)
+        self.check(self.lib.hf_cuda_prefill_batch_async(self.handle, _ptr(prompts), prompts.shape[1]))
+
+    def decode_batch_async(self, steps: int):
+        self.check(self.lib.hf_cuda_decode_batch_async(self.handle, steps))
+
+    def read_batch_slots(self, first: int, count: int) -> np.ndarray:
+        out = np.empty((self.sequences, count), dtype=np.uint32)
+        self.check(self.lib.hf_cuda_read_batch_slots(self.handle, first, count, _ptr(out)))
+        return out
+
+    def generate_batch(self, prompts, tokens: int) -> np.ndarray:
+        """[sequences, tokens]: each sequence's first `tokens` greedy ids."""
+        prompts = self._prompts(prompts)
+        out = np.empty((self.sequences, max(tokens, 1)), dtype=np.uint32)
+        self.check(self.lib.hf_cuda_generate_batch(self.handle, _ptr(prompts), prompts.shape[1], tokens, _ptr(out)))
+        return out[:, :tokens].copy()
 
     @property
     def stream(self) -> int:

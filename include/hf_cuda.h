@@ -161,6 +161,37 @@ enum { HF_DECODE_AUTO = 0, HF_DECODE_GRAPH = 1, HF_DECODE_PERSISTENT = 2 };
 int hf_cuda_set_decode_path(hf_ctx* ctx, int path);
 int hf_cuda_decode_path(const hf_ctx* ctx);
 
+/* ---- batched greedy decode of independent sequences ----------------------
+ * No counterpart in the reference, whose Decoder holds one sequence
+ * (Decoder.h:69-136) and runs several rows only for a prefill block
+ * (Decoder.cpp:400). A batch context holds `sequences` sequences that share
+ * the weights and one position: each has its own token slots and K/V caches
+ * ([layer][sequence][position][kv width] fp32). A batched step runs one row
+ * per sequence through the multi-row int8 tensor-core products, so the
+ * weights stream from HBM once per eight sequences, and every sequence's
+ * tokens equal what hf_cuda_generate_greedy produces for that sequence alone.
+ * Refusals: sequences > the step capacity (HF_E_CAPACITY), and shapes the
+ * stage records do not serve (HF_E_SHAPE; they need width 2048, 8 query
+ * heads of 256 over 1 KV head, a 16384-wide feed-forward and a vocabulary of
+ * whole 16-row tiles: Gemma-2B's). The single-sequence calls of a batch
+ * context act on sequence 0. */
+int hf_cuda_create_batch(int device, const hf_shape* shape, int sequences, hf_ctx** out);
+/* The sequences a context holds (1 for hf_cuda_create). */
+int hf_cuda_sequences(const hf_ctx* ctx);
+/* Begins every sequence and enqueues its prompt's prefill: prompts is
+ * [sequences, prompt_length] host token ids; each sequence's first generated
+ * token lands in its slot prompt_length. */
+int hf_cuda_prefill_batch_async(hf_ctx* ctx, const uint32_t* prompts, int prompt_length);
+/* Enqueues `steps` batched greedy steps, each embedding every sequence's slot
+ * `position` and writing its argmax into slot position + 1. */
+int hf_cuda_decode_batch_async(hf_ctx* ctx, int steps);
+/* Synchronises and copies slots [first, first + count) of every sequence into
+ * out [sequences, count]. */
+int hf_cuda_read_batch_slots(hf_ctx* ctx, int first, int count, uint32_t* out);
+/* Prefill, tokens - 1 batched steps, and the readback: out [sequences,
+ * tokens] receives every sequence's first `tokens` generated ids. */
+int hf_cuda_generate_batch(hf_ctx* ctx, const uint32_t* prompts, int prompt_length, int tokens, uint32_t* out);
+
 /* Phase tracing of the whole-loop kernel (the reference has wall-clock
  * timings only, Gemma.h:205-224): decodes `steps` tokens like
  * hf_cuda_decode_async, synchronously, and writes the first step's
