@@ -22,6 +22,7 @@
 #include "misc.cuh"
 #include "persistent.cuh"
 #include "rows_mma.cuh"
+#include "tc_gemm.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -65,6 +66,7 @@ struct Q8
 {
     uint8_t* base = nullptr;
     uint8_t* records = nullptr; // the stage-record copy the whole-loop kernel streams, or null
+    uint8_t* tc = nullptr;      // the tensor-core product's weight blocks (build_tc_blocks), or null
     int rows = 0;
     int cols = 0;
     const __half* scales() const { return reinterpret_cast<const __half*>(base + (size_t) rows * cols); }
@@ -130,6 +132,8 @@ void configure_kernels()
     cudaFuncSetAttribute(mqa_generic, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(decode_persistent<kPersistentStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int) persistent_smem<kPersistentStages>());
+    cudaFuncSetAttribute(q8_tc_gemm<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) tc_smem(64));
+    cudaFuncSetAttribute(q8_tc_gemm<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) tc_smem(128));
 }
 
 void configure_once(int device)
@@ -187,6 +191,37 @@ cudaError_t launch_attention(int QH, dim3 grid, cudaStream_t stream, const AttnA
 
 // A product of a.M rows of x on the int8 tensor cores over the weight's stage
 // records, in blocks of kRowsBlock rows.
+// How the tensor-core product tiles M rows of x against an [N, K] weight: the
+// x tile width (64 or 128 rows, the MMA's N), and a split of K when the
+// output tiles alone would leave SMs idle (each split keeps >= 4 chunks).
+struct TcPlan
+{
+    int nx, tiles_m, tiles_n, splits, cps;
+    size_t m_pad;
+};
+
+TcPlan tc_plan(int M, int N, int K, int sms)
+{
+    TcPlan p;
+    p.nx = M <= 64 ? 64 : 128;
+    p.tiles_m = (M + p.nx - 1) / p.nx;
+    p.tiles_n = N / kTcRows;
+    p.m_pad = (size_t) p.tiles_m * p.nx;
+    const int chunks = K / kTcChunk;
+    const int base = p.tiles_m * p.tiles_n;
+    const int splits = base >= sms ? 1 : std::min((sms + base - 1) / base, std::max(1, chunks / 4));
+    p.cps = (chunks + splits - 1) / splits;
+    p.splits = (chunks + p.cps - 1) / p.cps;
+    return p;
+}
+
+// Whether the product's tiles store straight into the destination (no split
+// sum, no epilogue beyond a plain store).
+constexpr bool tc_direct(Epi e, int splits)
+{
+    return splits == 1 && (e == Epi::Store || e == Epi::Logits);
+}
+
 template <Epi E, int K>
 cudaError_t rows_mma_product(bool pdl, const uint8_t* records, cudaStream_t stream, const GemvArgs& a, int sms)
 {
@@ -246,6 +281,10 @@ struct hf_ctx
 
     uint8_t* pool = nullptr;
     uint8_t* record_pool = nullptr; // stage records of every Q8 weight (the whole-loop kernel's copy)
+    uint8_t* tc_pool = nullptr;     // tensor-core weight blocks of every Q8 weight
+    __half* tc_x = nullptr;         // a product input's fp16 pieces
+    float* tc_xunscale = nullptr;   // their per-row powers of two
+    float* tc_ws = nullptr;         // split partial sums / unfused outputs of the tensor-core product
     Q8 embedding;
     float* final_norm = nullptr;
     std::vector<Layer> layers;
@@ -273,6 +312,7 @@ struct hf_ctx
     int max_splits = 1;
     bool persistent_ok = false; // the cooperative whole-loop kernel serves this shape on this device
     int gate_point = 1; // HF_GATE overrides (a tuning knob of the whole-loop kernel)
+    bool tc_off = false; // HF_TC=0 keeps multi-row products on the int8 MMA (for comparisons)
     int decode_path = HF_DECODE_AUTO;
     LayerDev* layer_dev = nullptr;
 
@@ -641,6 +681,56 @@ struct hf_ctx
     }
 
     // ---------------------------------------------------------------------
+    // A product of a.M > 8 rows of x on the tensor cores (tc_gemm.cuh): the
+    // input's fp16 pieces, the tiles (into the destination, or the split
+    // workspace), then the split sum with the epilogue.
+    template <Epi E>
+    cudaError_t tc_product(const Q8& w, const GemvArgs& a)
+    {
+        const TcPlan p = tc_plan(a.M, a.N, a.K, sms);
+        const bool direct = tc_direct(E, p.splits);
+        float* out = direct ? a.out : tc_ws;
+        const size_t split_stride = p.m_pad * (size_t) a.N;
+        const dim3 grid(p.tiles_n, p.tiles_m, p.splits);
+        cudaError_t e;
+        switch (p.nx)
+        {
+        case 64:
+            e = launch(true, prep_x_pieces<64>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x, a.M, a.K, tc_x,
+                       tc_xunscale);
+            if (e == cudaSuccess)
+                e = launch(true, q8_tc_gemm<64>, grid, dim3(kTcThreads), tc_smem(64), stream, (const uint8_t*) w.tc,
+                           (const __half*) tc_x, (const float*) tc_xunscale, out, split_stride, a.M, a.N, a.K, p.cps,
+                           a.err);
+            break;
+        default:
+            e = launch(true, prep_x_pieces<128>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x, a.M, a.K, tc_x,
+                       tc_xunscale);
+            if (e == cudaSuccess)
+                e = launch(true, q8_tc_gemm<128>, grid, dim3(kTcThreads), tc_smem(128), stream, (const uint8_t*) w.tc,
+                           (const __half*) tc_x, (const float*) tc_xunscale, out, split_stride, a.M, a.N, a.K, p.cps,
+                           a.err);
+            break;
+        }
+        if (e != cudaSuccess || direct)
+            return e;
+        const int units = (E == Epi::QkvRope || E == Epi::GeGLU) ? a.N / 2 : a.N;
+        const size_t threads = (size_t) a.M * units;
+        return launch(true, tc_finish<E>, dim3((unsigned) ((threads + 255) / 256)), dim3(256), 0, stream, a,
+                      (const float*) tc_ws, p.splits, split_stride);
+    }
+
+    // A product of a.M rows: the tensor cores above one 8-row block, the
+    // int8 MMA over the stage records up to it.
+    template <Epi E, int K>
+    cudaError_t multi_row(const Q8& w, const GemvArgs& a)
+    {
+        if (w.tc && a.M > kRowsBlock && !tc_off)
+            return tc_product<E>(w, a);
+        return rows_mma_product<E, K>(true, w.records, stream, a, sms);
+    }
+
+    // ---------------------------------------------------------------------
     // One batched decode step: every sequence's next token at the shared
     // position, row r of each product being sequence r, on the multi-row
     // int8 MMA products over the stage records (the weights stream once per
@@ -688,7 +778,7 @@ struct hf_ctx
             qkv.head_dim = s.head_width;
             qkv.state = state;
             qkv.err = err_word();
-            e = rows_mma_product<Epi::QkvRope, 2048>(true, L.qkv.records, stream, qkv, sms);
+            e = multi_row<Epi::QkvRope, 2048>(L.qkv, qkv);
             if (e != cudaSuccess)
                 return cuda(e, "q/k/v launch");
 
@@ -723,7 +813,7 @@ struct hf_ctx
             o.out = hidden;
             o.state = state;
             o.err = err_word();
-            e = rows_mma_product<Epi::Residual, 2048>(true, L.o.records, stream, o, sms);
+            e = multi_row<Epi::Residual, 2048>(L.o, o);
             if (e != cudaSuccess)
                 return cuda(e, "o_proj launch");
 
@@ -742,7 +832,7 @@ struct hf_ctx
             gu.out = act;
             gu.state = state;
             gu.err = err_word();
-            e = rows_mma_product<Epi::GeGLU, 2048>(true, L.gu.records, stream, gu, sms);
+            e = multi_row<Epi::GeGLU, 2048>(L.gu, gu);
             if (e != cudaSuccess)
                 return cuda(e, "gate/up launch");
 
@@ -756,7 +846,7 @@ struct hf_ctx
             dn.out = hidden;
             dn.state = state;
             dn.err = err_word();
-            e = rows_mma_product<Epi::Residual, 16384>(true, L.down.records, stream, dn, sms);
+            e = multi_row<Epi::Residual, 16384>(L.down, dn);
             if (e != cudaSuccess)
                 return cuda(e, "down launch");
         }
@@ -775,7 +865,7 @@ struct hf_ctx
         lg.out = logits;
         lg.state = state;
         lg.err = err_word();
-        e = rows_mma_product<Epi::Logits, 2048>(true, embedding.records, stream, lg, sms);
+        e = multi_row<Epi::Logits, 2048>(embedding, lg);
         if (e != cudaSuccess)
             return cuda(e, "logits launch");
         e = launch(true, argmax_partial, dim3(kBatchArgmaxParts, S), dim3(256), 0, stream, (const float*) logits, s.vocab,
@@ -833,7 +923,7 @@ struct hf_ctx
             qkv.head_dim = s.head_width;
             qkv.state = state;
             qkv.err = err_word();
-            e = L.qkv.records ? rows_mma_product<Epi::QkvRope, 2048>(true, L.qkv.records, stream, qkv, sms)
+            e = L.qkv.records ? multi_row<Epi::QkvRope, 2048>(L.qkv, qkv)
                               : generic_product<Epi::QkvRope>(true, L.qkv.rows / 2, stream, qkv, sms);
             if (e != cudaSuccess)
                 return cuda(e, "q/k/v launch");
@@ -870,7 +960,7 @@ struct hf_ctx
             o.out = hidden;
             o.state = state;
             o.err = err_word();
-            e = L.o.records ? rows_mma_product<Epi::Residual, 2048>(true, L.o.records, stream, o, sms)
+            e = L.o.records ? multi_row<Epi::Residual, 2048>(L.o, o)
                             : generic_product<Epi::Residual>(true, s.width, stream, o, sms);
             if (e != cudaSuccess)
                 return cuda(e, "o_proj launch");
@@ -890,7 +980,7 @@ struct hf_ctx
             gu.out = act;
             gu.state = state;
             gu.err = err_word();
-            e = L.gu.records ? rows_mma_product<Epi::GeGLU, 2048>(true, L.gu.records, stream, gu, sms)
+            e = L.gu.records ? multi_row<Epi::GeGLU, 2048>(L.gu, gu)
                              : generic_product<Epi::GeGLU>(true, L.gu.rows / 2, stream, gu, sms);
             if (e != cudaSuccess)
                 return cuda(e, "gate/up launch");
@@ -905,7 +995,7 @@ struct hf_ctx
             dn.out = hidden;
             dn.state = state;
             dn.err = err_word();
-            e = L.down.records ? rows_mma_product<Epi::Residual, 16384>(true, L.down.records, stream, dn, sms)
+            e = L.down.records ? multi_row<Epi::Residual, 16384>(L.down, dn)
                                : generic_product<Epi::Residual>(true, s.width, stream, dn, sms);
             if (e != cudaSuccess)
                 return cuda(e, "down launch");
@@ -932,7 +1022,7 @@ struct hf_ctx
         lg.out = logits + (size_t) (all_logits ? 0 : rows - 1) * s.vocab;
         lg.state = state;
         lg.err = err_word();
-        e = embedding.records ? rows_mma_product<Epi::Logits, 2048>(true, embedding.records, stream, lg, sms)
+        e = embedding.records ? multi_row<Epi::Logits, 2048>(embedding, lg)
                               : generic_product<Epi::Logits>(true, s.vocab, stream, lg, sms);
         if (e != cudaSuccess)
             return cuda(e, "logits launch");
@@ -1058,6 +1148,8 @@ int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** ou
     ctx->sms = sm_count(device);
     if (const char* knob = std::getenv("HF_GATE"))
         ctx->gate_point = std::max(0, std::min(2, std::atoi(knob)));
+    if (const char* knob = std::getenv("HF_TC"))
+        ctx->tc_off = std::atoi(knob) == 0;
     ctx->max_splits = 128;
     const int QH = s.heads / s.kv_heads;
     ctx->fast = s.width == 2048 && s.heads * s.head_width == 2048 && s.head_width == 256 && QH <= 8
@@ -1161,6 +1253,45 @@ int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** ou
             mirror(L.gu);
             mirror(L.down);
         }
+        // The tensor-core product's weight blocks, and its input and split
+        // buffers sized for every row count a step or a batch can carry.
+        if ((QW + 2 * KVW) % kTcRows == 0 && W % kTcRows == 0 && V % kTcRows == 0 && (2 * I) % kTcRows == 0)
+        {
+            auto tcbytes = [&](size_t rows, size_t cols) { return round256(tc_weight_bytes(rows, cols)); };
+            const size_t tc_bytes = tcbytes(V, W)
+                                    + (size_t) s.layers
+                                          * (tcbytes(QW + 2 * KVW, W) + tcbytes(W, QW) + tcbytes(2 * I, W) + tcbytes(W, I));
+            const int most_rows = std::max(ctx->capacity, sequences);
+            size_t ws = 1;
+            struct Product { size_t n, k; bool finish; };
+            const Product products[] = {{QW + 2 * KVW, W, true}, {W, QW, true}, {2 * I, W, true}, {W, I, true}, {V, W, false}};
+            for (int m = kRowsBlock + 1; m <= most_rows; ++m)
+                for (const Product& pr: products)
+                {
+                    const TcPlan plan = tc_plan(m, (int) pr.n, (int) pr.k, ctx->sms);
+                    if (pr.finish || plan.splits > 1)
+                        ws = std::max(ws, (size_t) plan.splits * plan.m_pad * pr.n);
+                }
+            const size_t m_pad = tc_plan(most_rows, (int) W, (int) W, ctx->sms).m_pad;
+            if (ctx->cuda(cudaMalloc(&ctx->tc_pool, tc_bytes), "tensor-core weight blocks")
+                || device_alloc(ctx, &ctx->tc_x, tc_x_bytes(m_pad, std::max({W, QW, I})) / sizeof(__half), "product input pieces")
+                || device_alloc(ctx, &ctx->tc_xunscale, m_pad, "product input scales")
+                || device_alloc(ctx, &ctx->tc_ws, ws, "product workspace"))
+                return bail(HF_E_CUDA);
+            uint8_t* at_tc = ctx->tc_pool;
+            auto place = [&](Q8& t) {
+                t.tc = at_tc;
+                at_tc += tcbytes(t.rows, t.cols);
+            };
+            place(ctx->embedding);
+            for (auto& L: ctx->layers)
+            {
+                place(L.qkv);
+                place(L.o);
+                place(L.gu);
+                place(L.down);
+            }
+        }
         std::vector<LayerDev> table(s.layers);
         for (int l = 0; l < s.layers; ++l)
         {
@@ -1232,7 +1363,7 @@ void hf_cuda_destroy(hf_ctx* ctx)
         cudaStreamSynchronize(ctx->stream);
     for (auto& g: ctx->graphs)
         cudaGraphExecDestroy(g.second);
-    void* buffers[] = {ctx->pool, ctx->record_pool, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
+    void* buffers[] = {ctx->pool, ctx->record_pool, ctx->tc_pool, ctx->tc_x, ctx->tc_xunscale, ctx->tc_ws, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
                        ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slot_base, ctx->state,
                        ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev};
     for (void* b: buffers)
@@ -1307,6 +1438,11 @@ int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, 
         build_records<<<(target->rows / 16) * (target->cols / 2048), 256>>>(target->base, target->rows,
                                                                             target->cols, target->records);
         rc = ctx->cuda(cudaDeviceSynchronize(), "record build");
+    }
+    if (!rc && target->tc)
+    {
+        build_tc_blocks<<<target->rows / kTcRows, kTcRows>>>(target->base, target->scales(), target->cols, target->tc);
+        rc = ctx->cuda(cudaDeviceSynchronize(), "tensor-core block build");
     }
     if (rc)
         return rc;

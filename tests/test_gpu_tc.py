@@ -1,0 +1,49 @@
+"""Multi-row Q8_0 products on the tcgen05 tensor cores (csrc/tc_gemm.cuh):
+prefill blocks and batched decode steps of more than eight rows.
+
+The reference runs these through its tiled product (TiledMatMul.h:171-652,
+chosen for rows > 3 at Decoder.cpp:400) in fp32; here each product is three
+fp16 MMAs over exact splits of the weights and of x, and every step is checked
+against the double-precision oracle at the decoder tolerance
+(DecoderTests.cpp:41, 61-75), across the tile shapes the host picks: 256-row x
+tiles (two of them), 128 and 64 (the latter with K split across CTAs).
+"""
+import numpy as np
+import pytest
+
+import oracle_bindings as ob
+from huggingfaceeacp_b200 import native
+
+pytestmark = pytest.mark.gpu
+
+TOLERANCE = 5e-6
+SHAPE = native.DecoderShape(width=2048, heads=8, kv_heads=1, head_width=256, layers=2, intermediate=16384,
+                            vocab=8192, max_positions=640, max_step_rows=512, embed_scale=1.0)
+
+
+def test_tensor_core_prefill_blocks_match_reference():
+    with native.Context(SHAPE) as ctx:
+        tensors = ctx.load_synthetic(seed=17, keep=True)
+        oracle = ob.OracleModel(SHAPE, tensors)
+        prompt = native.synthetic_tokens(17, 429, SHAPE.vocab)
+        first = 0
+        try:
+            for rows in (300, 100, 20, 9):  # x tiles: 3 x 128, 128, 64 (split K), 64
+                block = prompt[first:first + rows]
+                first += rows
+                logits, hidden = ctx.step(block)
+                ref_hidden, ref_logits = oracle.step(block)
+                assert ob.worst_error(logits, ref_logits) <= TOLERANCE, rows
+                assert ob.worst_error(hidden, ref_hidden) <= TOLERANCE, rows
+        finally:
+            oracle.close()
+
+
+def test_tensor_core_batched_decode_matches_reference_per_sequence():
+    sequences, length, tokens = 12, 20, 8
+    with native.Context(SHAPE, sequences=sequences) as ctx:
+        tensors = ctx.load_synthetic(seed=23, keep=True)
+        prompts = np.stack([native.synthetic_tokens(200 + q, length, SHAPE.vocab) for q in range(sequences)])
+        out = ctx.generate_batch(prompts, tokens)
+        for q in range(sequences):
+            assert list(out[q]) == ob.greedy_reference(SHAPE, tensors, prompts[q], tokens), q
