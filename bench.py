@@ -9,6 +9,12 @@ Every rank decodes its own sequence on its own GPU (independent replicas, no
 collective on the data path; weak scaling), and `value` is the whole-job
 tok/s: the tokens all ranks decoded over the max-over-ranks device time.
 
+The metric's second half, b=64/GPU, is the `batched` object of
+the same line: each rank decodes 64 independent sequences (512-token seeded
+prompts, seed 3) with batched greedy steps on the tensor cores; its value is
+the whole-job tok/s over the max-over-ranks device time of `--batched-steps`
+steps (256 by default, the config's length).
+
 `value` is device-timed (CUDA events on the engine's stream around K decode
 steps, weights resident in HBM). `e2e` is the same metric through the public
 generate call (HF::Gemma::generate's C-ABI, hf_cuda_generate_greedy) with the
@@ -41,6 +47,10 @@ WORKLOAD = "config0: Gemma-2B Q8_0 batch-1 greedy decode, BOS + 15 seeded prompt
 PUBLISHED_TOK_S = 161.6  # the reference's int8-blocks decode, 16 tokens (Apple M4 Max, Metal)
 PROMPT_LENGTH = 16
 SEED = 0
+BATCH_SEQUENCES = 64      # configs[3]: sequences per GPU
+BATCH_PROMPT = 512        # configs[3]: prompt tokens per sequence
+BATCH_SEED = 3
+BATCH_WORKLOAD = "config3: 64 independent sequences per GPU, 512-token seeded prompts (seed 3), greedy steps"
 
 
 def measured_peaks():
@@ -127,8 +137,8 @@ def physical_index(local_rank: int) -> int:
     return local_rank
 
 
-def build_model(native, shape, keep: bool):
-    ctx = native.Context(shape, device=int(os.environ.get("LOCAL_RANK", "0")))
+def build_model(native, shape, keep: bool, sequences: int = 1):
+    ctx = native.Context(shape, device=int(os.environ.get("LOCAL_RANK", "0")), sequences=sequences)
     tensors = ctx.load_synthetic(seed=SEED, keep=keep)
     return ctx, tensors
 
@@ -202,9 +212,12 @@ def run_ours(args):
         if dist:
             dist.barrier()
 
-    shape = native.GEMMA_2B.replace(max_step_rows=512)
+    # One context of 64 sequences: sequence 0 runs the batch-1 decode, all 64
+    # the batched steps (the weights are uploaded once).
+    window = max(BATCH_PROMPT + args.batched_steps + args.warmup, PROMPT_LENGTH + 2 * (args.warmup + args.steps)) + 8
+    shape = native.GEMMA_2B.replace(max_step_rows=BATCH_PROMPT, max_positions=window)
     keep = rank == 0 and world == 1 and not args.no_cpu_baseline
-    ctx, tensors = build_model(native, shape, keep)
+    ctx, tensors = build_model(native, shape, keep, BATCH_SEQUENCES)
     prompt = native.synthetic_tokens(SEED, PROMPT_LENGTH, shape.vocab)
 
     # ---- device-timed decode: K steps with the weights resident
@@ -251,6 +264,51 @@ def run_ours(args):
            "h2d_bytes_per_step": 4.0 * PROMPT_LENGTH / max(1, len(generated)), "d2h_bytes_per_step": 4,
            "call": "hf_cuda_generate_greedy (prefill + decode, wall clock)"}
 
+    # ---- batched decode: 64 sequences, device-timed batched steps
+    prompts = np.stack([native.synthetic_tokens(BATCH_SEED + q, BATCH_PROMPT, shape.vocab)
+                        for q in range(BATCH_SEQUENCES)])
+    barrier()
+    torch.cuda.synchronize()
+    p_start, p_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p_start.record(stream)
+    ctx.prefill_batch_async(prompts)
+    p_stop.record(stream)
+    ctx.decode_batch_async(args.warmup)
+    ctx.sync()
+    batch_first = ctx.position
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(physical_index(local_rank)) as batch_clocks:
+        b_start, b_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b_start.record(stream)
+        ctx.decode_batch_async(args.batched_steps)
+        b_stop.record(stream)
+        ctx.sync()
+        torch.cuda.synchronize()
+    batch_ms = b_start.elapsed_time(b_stop)
+    prefill_ms = p_start.elapsed_time(p_stop)
+    barrier()
+    if dist:
+        t = torch.tensor([batch_ms, prefill_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        batch_ms, prefill_ms = float(t[0].item()), float(t[1].item())
+    batch_tokens = ctx.read_batch_slots(batch_first + 1, min(4, args.batched_steps))
+    batch_step_ms = batch_ms / args.batched_steps
+    batch_keys = batch_first + args.batched_steps // 2
+    batch_step_bytes = native.batched_decode_bytes(shape, BATCH_SEQUENCES, batch_keys)
+    batch_gbs = batch_step_bytes / (batch_step_ms * 1e6)
+    batched = {
+        "workload": BATCH_WORKLOAD, "value": world * BATCH_SEQUENCES * args.batched_steps / (batch_ms / 1000.0),
+        "unit": "tok/s", "n_gpus": world, "sequences_per_gpu": BATCH_SEQUENCES, "steps": args.batched_steps,
+        "warmup": args.warmup, "ms_per_step": batch_step_ms, "scaling": "weak",
+        "prefill_tok_s": world * BATCH_SEQUENCES * BATCH_PROMPT / (prefill_ms / 1000.0),
+        "roofline": {"bound": "hbm", "achieved": batch_gbs, "peak": peak, "unit": "GB/s", "frac": batch_gbs / peak,
+                     "peak_kind": peak_kind, "algorithmic_bytes_per_step": batch_step_bytes,
+                     "note": "weights once per step + every sequence's K/V rows and logits"},
+        "clocks": batch_clocks.summary(),
+        "tokens_head": [[int(t) for t in row] for row in batch_tokens[:2]],
+    }
+
     # ---- roofline of every decode kernel, live (cycling layers: HBM, not L2)
     ctx.begin_sequence()
     ctx.prefill_async(prompt)
@@ -291,6 +349,7 @@ def run_ours(args):
                           "frac": step_bytes / (ms_per_step * 1e6) / peak},
         "roofline": roofline,
         "e2e": e2e,
+        "batched": batched,
         "gpu_launches": launches,
         "decode_path": {0: "generic", 1: "graph", 2: "persistent"}[path],
         "clocks": clocks.summary(),
@@ -344,6 +403,8 @@ def main():
     parser.add_argument("--warmup", type=int, default=4)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--cpu-steps", type=int, default=16)
+    parser.add_argument("--batched-steps", type=int, default=256,
+                        help="batched decode steps timed for the b=64/GPU half of the metric")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--profile-case", action="store_true",
                         help="run the small ncu capture case of the decode kernel instead of the bench")

@@ -500,3 +500,10 @@ def decode_bytes(shape: DecoderShape, keys: int) -> int:
     norms = 4 * shape.width * (2 * shape.layers + 1)
     kv = 4 * 2 * shape.kv_width * shape.layers
     return weight_bytes(shape) + norms + kv * keys + kv + 4 * shape.vocab
+
+
+def batched_decode_bytes(shape: DecoderShape, sequences: int, keys: int) -> int:
+    """Algorithmic bytes of one batched decode step: the weights once, and per
+    sequence its K/V rows read (`keys` positions) and written, and its logits."""
+    per_sequence = decode_bytes(shape, keys) - weight_bytes(shape) - 4 * shape.width * (2 * shape.layers + 1)
+    return decode_bytes(shape, keys) + (sequences - 1) * per_sequence
