@@ -132,8 +132,14 @@ void configure_kernels()
     cudaFuncSetAttribute(mqa_generic, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(decode_persistent<kPersistentStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int) persistent_smem<kPersistentStages>());
-    cudaFuncSetAttribute(q8_tc_gemm<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) tc_smem(64));
-    cudaFuncSetAttribute(q8_tc_gemm<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) tc_smem(128));
+#define HF_TC_SMEM(E)                                                                                          \
+    cudaFuncSetAttribute(q8_tc_gemm_ts<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kTsSmem);           \
+    cudaFuncSetAttribute(q8_tc_gemm<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kTcSmem);
+    HF_TC_SMEM(Epi::QkvRope)
+    HF_TC_SMEM(Epi::Residual)
+    HF_TC_SMEM(Epi::GeGLU)
+    HF_TC_SMEM(Epi::Logits)
+#undef HF_TC_SMEM
 }
 
 void configure_once(int device)
@@ -213,13 +219,6 @@ TcPlan tc_plan(int M, int N, int K, int sms)
     p.cps = (chunks + splits - 1) / splits;
     p.splits = (chunks + p.cps - 1) / p.cps;
     return p;
-}
-
-// Whether the product's tiles store straight into the destination (no split
-// sum, no epilogue beyond a plain store).
-constexpr bool tc_direct(Epi e, int splits)
-{
-    return splits == 1 && (e == Epi::Store || e == Epi::Logits);
 }
 
 template <Epi E, int K>
@@ -682,37 +681,35 @@ struct hf_ctx
 
     // ---------------------------------------------------------------------
     // A product of a.M > 8 rows of x on the tensor cores (tc_gemm.cuh): the
-    // input's fp16 pieces, the tiles (into the destination, or the split
-    // workspace), then the split sum with the epilogue.
+    // input's fp16 pieces (RMS-normalised on the way when a.norm_w is set),
+    // then the tiles with the epilogue, or, with K split across CTAs, the
+    // partial sums and tc_finish.
     template <Epi E>
     cudaError_t tc_product(const Q8& w, const GemvArgs& a)
     {
         const TcPlan p = tc_plan(a.M, a.N, a.K, sms);
-        const bool direct = tc_direct(E, p.splits);
-        float* out = direct ? a.out : tc_ws;
         const size_t split_stride = p.m_pad * (size_t) a.N;
         const dim3 grid(p.tiles_n, p.tiles_m, p.splits);
         cudaError_t e;
-        switch (p.nx)
+        if (p.nx == 64)
         {
-        case 64:
-            e = launch(true, prep_x_pieces<64>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x, a.M, a.K, tc_x,
-                       tc_xunscale);
+            e = launch(true, prep_x_pieces<64>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x, a.norm_w, a.eps,
+                       a.M, a.K, tc_x, tc_xunscale);
             if (e == cudaSuccess)
-                e = launch(true, q8_tc_gemm<64>, grid, dim3(kTcThreads), tc_smem(64), stream, (const uint8_t*) w.tc,
-                           (const __half*) tc_x, (const float*) tc_xunscale, out, split_stride, a.M, a.N, a.K, p.cps,
-                           a.err);
-            break;
-        default:
-            e = launch(true, prep_x_pieces<128>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x, a.M, a.K, tc_x,
-                       tc_xunscale);
-            if (e == cudaSuccess)
-                e = launch(true, q8_tc_gemm<128>, grid, dim3(kTcThreads), tc_smem(128), stream, (const uint8_t*) w.tc,
-                           (const __half*) tc_x, (const float*) tc_xunscale, out, split_stride, a.M, a.N, a.K, p.cps,
-                           a.err);
-            break;
+                e = launch(true, q8_tc_gemm_ts<E>, grid, dim3(kTsThreads), kTsSmem, stream, a,
+                           (const uint8_t*) w.tc, (const __half*) tc_x, (const float*) tc_xunscale, tc_ws,
+                           split_stride, p.cps);
         }
-        if (e != cudaSuccess || direct)
+        else
+        {
+            e = launch(true, prep_x_pieces<128>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x, a.norm_w, a.eps,
+                       a.M, a.K, tc_x, tc_xunscale);
+            if (e == cudaSuccess)
+                e = launch(true, q8_tc_gemm<E>, grid, dim3(kTcThreads), kTcSmem, stream, a,
+                           (const uint8_t*) w.tc, (const __half*) tc_x, (const float*) tc_xunscale, tc_ws,
+                           split_stride, p.cps);
+        }
+        if (e != cudaSuccess || p.splits == 1)
             return e;
         const int units = (E == Epi::QkvRope || E == Epi::GeGLU) ? a.N / 2 : a.N;
         const size_t threads = (size_t) a.M * units;
@@ -720,13 +717,41 @@ struct hf_ctx
                       (const float*) tc_ws, p.splits, split_stride);
     }
 
+    // The generic product (any shape), RMS-normalising x into `normed` first
+    // when a.norm_w is set.
+    template <Epi E>
+    cudaError_t normed_generic(int units, GemvArgs a)
+    {
+        if (a.norm_w)
+        {
+            const cudaError_t e = launch(true, rms_norm_rows, dim3(a.M), dim3(256), 0, stream, a.x,
+                                         (const float*) a.norm_w, a.K, a.eps, normed);
+            if (e != cudaSuccess)
+                return e;
+            a.x = normed;
+            a.norm_w = nullptr;
+        }
+        return generic_product<E>(true, units, stream, a, sms);
+    }
+
     // A product of a.M rows: the tensor cores above one 8-row block, the
-    // int8 MMA over the stage records up to it.
+    // int8 MMA over the stage records up to it. With a.norm_w, x is first
+    // RMS-normalised (fused into the tensor-core path's input split; into
+    // `normed` by rms_norm_rows before the int8 MMA).
     template <Epi E, int K>
-    cudaError_t multi_row(const Q8& w, const GemvArgs& a)
+    cudaError_t multi_row(const Q8& w, GemvArgs a)
     {
         if (w.tc && a.M > kRowsBlock && !tc_off)
             return tc_product<E>(w, a);
+        if (a.norm_w)
+        {
+            const cudaError_t e = launch(true, rms_norm_rows, dim3(a.M), dim3(256), 0, stream, a.x,
+                                         (const float*) a.norm_w, a.K, a.eps, normed);
+            if (e != cudaSuccess)
+                return e;
+            a.x = normed;
+            a.norm_w = nullptr;
+        }
         return rows_mma_product<E, K>(true, w.records, stream, a, sms);
     }
 
@@ -755,10 +780,6 @@ struct hf_ctx
             const Layer& L = layers[l];
             float* k0 = kcache + (size_t) l * S * stride; // sequence 0's rows of this layer
             float* v0 = vcache + (size_t) l * S * stride;
-            e = launch(true, rms_norm_rows, dim3(S), dim3(256), 0, stream, (const float*) hidden,
-                       (const float*) L.in_norm, s.width, s.rms_eps, normed);
-            if (e != cudaSuccess)
-                return cuda(e, "norm launch");
 
             GemvArgs qkv = {};
             qkv.w = L.qkv.base;
@@ -766,7 +787,9 @@ struct hf_ctx
             qkv.N = L.qkv.rows;
             qkv.K = s.width;
             qkv.M = S;
-            qkv.x = normed;
+            qkv.x = hidden;
+            qkv.norm_w = L.in_norm;
+            qkv.eps = s.rms_eps;
             qkv.out = qbuf;
             qkv.k_cache = k0;
             qkv.v_cache = v0;
@@ -817,10 +840,6 @@ struct hf_ctx
             if (e != cudaSuccess)
                 return cuda(e, "o_proj launch");
 
-            e = launch(true, rms_norm_rows, dim3(S), dim3(256), 0, stream, (const float*) hidden,
-                       (const float*) L.post_norm, s.width, s.rms_eps, normed);
-            if (e != cudaSuccess)
-                return cuda(e, "norm launch");
 
             GemvArgs gu = {};
             gu.w = L.gu.base;
@@ -828,7 +847,9 @@ struct hf_ctx
             gu.N = L.gu.rows;
             gu.K = s.width;
             gu.M = S;
-            gu.x = normed;
+            gu.x = hidden;
+            gu.norm_w = L.post_norm;
+            gu.eps = s.rms_eps;
             gu.out = act;
             gu.state = state;
             gu.err = err_word();
@@ -901,10 +922,6 @@ struct hf_ctx
         for (int l = 0; l < s.layers; ++l)
         {
             const Layer& L = layers[l];
-            e = launch(true, rms_norm_rows, dim3(rows), dim3(256), 0, stream, (const float*) hidden,
-                       (const float*) L.in_norm, s.width, s.rms_eps, normed);
-            if (e != cudaSuccess)
-                return cuda(e, "norm launch");
 
             GemvArgs qkv = {};
             qkv.w = L.qkv.base;
@@ -912,7 +929,9 @@ struct hf_ctx
             qkv.N = L.qkv.rows;
             qkv.K = s.width;
             qkv.M = rows;
-            qkv.x = normed;
+            qkv.x = hidden;
+            qkv.norm_w = L.in_norm;
+            qkv.eps = s.rms_eps;
             qkv.out = qbuf;
             qkv.k_cache = layer_k(l);
             qkv.v_cache = layer_v(l);
@@ -923,8 +942,7 @@ struct hf_ctx
             qkv.head_dim = s.head_width;
             qkv.state = state;
             qkv.err = err_word();
-            e = L.qkv.records ? multi_row<Epi::QkvRope, 2048>(L.qkv, qkv)
-                              : generic_product<Epi::QkvRope>(true, L.qkv.rows / 2, stream, qkv, sms);
+            e = L.qkv.records ? multi_row<Epi::QkvRope, 2048>(L.qkv, qkv) : normed_generic<Epi::QkvRope>(L.qkv.rows / 2, qkv);
             if (e != cudaSuccess)
                 return cuda(e, "q/k/v launch");
 
@@ -965,10 +983,6 @@ struct hf_ctx
             if (e != cudaSuccess)
                 return cuda(e, "o_proj launch");
 
-            e = launch(true, rms_norm_rows, dim3(rows), dim3(256), 0, stream, (const float*) hidden,
-                       (const float*) L.post_norm, s.width, s.rms_eps, normed);
-            if (e != cudaSuccess)
-                return cuda(e, "norm launch");
 
             GemvArgs gu = {};
             gu.w = L.gu.base;
@@ -976,12 +990,13 @@ struct hf_ctx
             gu.N = L.gu.rows;
             gu.K = s.width;
             gu.M = rows;
-            gu.x = normed;
+            gu.x = hidden;
+            gu.norm_w = L.post_norm;
+            gu.eps = s.rms_eps;
             gu.out = act;
             gu.state = state;
             gu.err = err_word();
-            e = L.gu.records ? multi_row<Epi::GeGLU, 2048>(L.gu, gu)
-                             : generic_product<Epi::GeGLU>(true, L.gu.rows / 2, stream, gu, sms);
+            e = L.gu.records ? multi_row<Epi::GeGLU, 2048>(L.gu, gu) : normed_generic<Epi::GeGLU>(L.gu.rows / 2, gu);
             if (e != cudaSuccess)
                 return cuda(e, "gate/up launch");
 
@@ -1263,13 +1278,13 @@ int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** ou
                                           * (tcbytes(QW + 2 * KVW, W) + tcbytes(W, QW) + tcbytes(2 * I, W) + tcbytes(W, I));
             const int most_rows = std::max(ctx->capacity, sequences);
             size_t ws = 1;
-            struct Product { size_t n, k; bool finish; };
-            const Product products[] = {{QW + 2 * KVW, W, true}, {W, QW, true}, {2 * I, W, true}, {W, I, true}, {V, W, false}};
+            struct Product { size_t n, k; };
+            const Product products[] = {{QW + 2 * KVW, W}, {W, QW}, {2 * I, W}, {W, I}, {V, W}};
             for (int m = kRowsBlock + 1; m <= most_rows; ++m)
                 for (const Product& pr: products)
                 {
                     const TcPlan plan = tc_plan(m, (int) pr.n, (int) pr.k, ctx->sms);
-                    if (pr.finish || plan.splits > 1)
+                    if (plan.splits > 1)
                         ws = std::max(ws, (size_t) plan.splits * plan.m_pad * pr.n);
                 }
             const size_t m_pad = tc_plan(most_rows, (int) W, (int) W, ctx->sms).m_pad;

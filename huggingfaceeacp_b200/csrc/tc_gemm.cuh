@@ -22,23 +22,40 @@
 // r of an 8-row x 128-byte atom is stored at chunk c ^ (r & 7)):
 //  - weights, built once at upload (build_tc_blocks): per 128-row tile t and
 //    64-column chunk c, one contiguous block of 8,704 bytes: the int8 quants
-//    [128][64] row-major, then the rows' two fp16 scales each pre-multiplied
-//    by the row's power of two; after all blocks, a float per row undoing it.
+//    as [4 16-column groups][128 rows][16 bytes] (so 32 threads reading 32
+//    rows' same group touch consecutive words), then the rows' two fp16
+//    scales [128][2], each pre-multiplied by the row's power of two; after
+//    all blocks, a float per row undoing it.
 //  - x, per product (prep_x_pieces): per NX-row tile and 64-column chunk, the
 //    hi then the mid pieces, [NX][64] fp16 each, already swizzled; a float
 //    per row undoing its power of two.
 //
-// The kernel (one output tile of 128 weight rows x NX rows of x, one K range):
+// The kernels (one output tile of 128 weight rows x NX rows of x, one K range):
+//  q8_tc_gemm_ts  NX = 64 (batched decode steps): the converted weight tiles
+//                 live in TMEM and are the MMA's A operand there
+//                 (tcgen05.mma ... [a-tmem]), so shared memory carries only
+//                 the bulk copies and the x operand;
+//  q8_tc_gemm     NX = 128 (prefill blocks): the converted tiles are in shared
+//                 memory (TMEM holds the 512 columns of accumulators).
+// Roles in both:
 //  warp 0 lane 0  producer: one bulk copy of the weight block and one of the
-//                 x block per stage;
-//  warp 1         allocates TMEM (two sets of two NX-column accumulators);
-//                 lane 0 issues the 12 MMAs of a stage (4 k-steps x 3
-//                 products) into one set and commits them to the stage's
-//                 empty barrier and to that set's full barrier;
-//  warps 2-5      convert the stage's int8 weights to the fp16 hi/lo tiles
-//                 (generic-proxy stores, fenced for the tensor core);
-//  warps 6-9      drain each finished accumulator from TMEM into fp32
-//                 register sums, then store the tile.
+//                 x block per load stage;
+//  MMA issuers   warp 1 (which also allocates TMEM) for even chunks, the last
+//                 warp for odd ones: lane 0 issues the chunk's 12 MMAs (4
+//                 k-steps x 3 products) into an accumulator set and commits
+//                 them to the load stage's, the weight tile's and the set's
+//                 barriers. Two issuers, because a barrier wait by a thread
+//                 with MMAs in flight stalls it for about 400 cycles: each
+//                 waits while the other's MMAs keep the tensor core busy;
+//  warps 2-9      convert chunk i's int8 weights into one of two fp16 hi/lo
+//                 tile buffers while the tensor core runs chunk i - 1;
+//  drain          read each chunk's finished accumulators from TMEM into fp32
+//                 register sums, then apply the product's epilogue (or, when
+//                 K is split across CTAs, store the partial sums): warps
+//                 10-13 in q8_tc_gemm_ts (one per TMEM lane quarter, all 64
+//                 columns), warps 2-9 themselves in q8_tc_gemm (after
+//                 converting chunk i they drain chunk i - 1, each half of its
+//                 quarter's 128 columns).
 #pragma once
 
 #include "common.cuh"
@@ -50,25 +67,22 @@ constexpr int kTcRows = 128;                             // weight rows per tile
 constexpr int kTcChunk = 64;                             // columns per stage (one 128-byte swizzle atom of fp16)
 constexpr int kTcQuantBytes = kTcRows * kTcChunk;        // 8 KiB
 constexpr int kTcBlockBytes = kTcQuantBytes + kTcRows * 2 * 2; // + two fp16 scales per row
-constexpr int kTcThreads = 320;
+
 constexpr int kTcTileBytes = kTcRows * kTcChunk * 2;    // one fp16 A tile: 16 KiB
 
-__host__ __device__ constexpr int tc_stages(int)
-{
-    return 3;
-}
+// q8_tc_gemm's shared memory: two buffers of the converted fp16 weight tiles
+// (hi, lo), then a ring of 3 load stages, each the x block (hi, mid) and the
+// raw weight block, rounded to 1 KiB so every swizzle atom stays 1 KiB-aligned.
+constexpr int kTcStages = 3;
+constexpr size_t kTcStageBytes = ((size_t) 2 * 128 * 128 + kTcBlockBytes + 1023) / 1024 * 1024;
+constexpr size_t kTcSmem = (size_t) 4 * kTcTileBytes + kTcStageBytes * kTcStages + 1024; // + alignment slack
+constexpr int kTcThreads = 352; // producer, 2 MMA issuers, 8 convert-and-drain warps
 
-// Bytes of one stage: A hi, A lo, the x block (hi, mid), the raw weight block;
-// rounded to 1 KiB so every swizzle atom stays 1 KiB-aligned.
-__host__ __device__ constexpr size_t tc_stage_bytes(int nx)
-{
-    return ((size_t) 2 * kTcTileBytes + (size_t) 2 * nx * 128 + kTcBlockBytes + 1023) / 1024 * 1024;
-}
-
-__host__ __device__ constexpr size_t tc_smem(int nx)
-{
-    return tc_stage_bytes(nx) * tc_stages(nx) + 1024; // + alignment slack
-}
+// q8_tc_gemm_ts's shared memory: a ring of 8 load stages (x block, raw block).
+constexpr int kTsStages = 8;
+constexpr size_t kTsStageBytes = ((size_t) 2 * 64 * 128 + kTcBlockBytes + 1023) / 1024 * 1024;
+constexpr size_t kTsSmem = kTsStageBytes * kTsStages + 1024;
+constexpr int kTsThreads = 480; // producer, 2 MMA issuers, 8 converters, 4 drain warps
 
 // The weight blocks of an [N, K] tensor (N % 128 == 0, K % 64 == 0).
 __host__ __device__ constexpr size_t tc_weight_bytes(size_t N, size_t K)
@@ -125,6 +139,34 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a, uint64_t b, 
         : "memory");
 }
 
+// The same with the A operand in TMEM (K-major: lane = row, two fp16 per
+// 32-bit column, the lower k in the low half).
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns from registers (thread t: lane
+// taddr's lane + t), then the wait for this thread's TMEM stores.
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t (&r)[16])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+                 "%13, %14, %15, %16};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+                 "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_wait_st()
+{
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Arrives on `bar` once every MMA this thread issued so far has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar)
 {
@@ -133,7 +175,7 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar)
 }
 
 // 32 lanes x 16 consecutive 32-bit columns: thread t gets lane (taddr's lane
-// + t), columns col .. col + 15.
+// + t), columns col .. col + 15. The values are usable after tc_wait_ld(r).
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16])
 {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
@@ -142,7 +184,18 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16])
                    "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
                    "=r"(r[15])
                  : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Waits for this thread's TMEM loads; naming r as read and written keeps the
+// compiler from using r before the wait.
+__device__ __forceinline__ void tc_wait_ld(uint32_t (&r)[16])
+{
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15])
+                 :
+                 : "memory");
 }
 
 // ---- weight blocks (once per upload) --------------------------------------
@@ -170,10 +223,9 @@ __global__ void __launch_bounds__(kTcRows) build_tc_blocks(const uint8_t* quants
     {
         uint8_t* block = blocks + ((size_t) t * chunks + c) * kTcBlockBytes;
         const uint4* src = reinterpret_cast<const uint4*>(qrow + (size_t) c * kTcChunk);
-        uint4* dst = reinterpret_cast<uint4*>(block + r * kTcChunk);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-            dst[j] = src[j];
+            reinterpret_cast<uint4*>(block + j * kTcRows * 16)[r] = src[j];
         __half* bs = reinterpret_cast<__half*>(block + kTcQuantBytes) + r * 2;
         bs[0] = __float2half_rn(ldexpf(__half2float(srow[2 * c]), shift));
         bs[1] = __float2half_rn(ldexpf(__half2float(srow[2 * c + 1]), shift));
@@ -181,11 +233,15 @@ __global__ void __launch_bounds__(kTcRows) build_tc_blocks(const uint8_t* quants
 }
 
 // ---- x pieces (once per product input) --------------------------------------
-// One CTA of 256 threads per row of the padded tile set: the row's power of
-// two (max |x| = f 2^e is scaled to f 2^14), then the hi and mid fp16 pieces
-// of every 8-column group in their swizzled places. Rows >= M are zeros.
+// One CTA of 256 threads per row of the padded tile set. With `norm_w`, the
+// row is first RMS-normalised exactly as rms_norm_rows does it (same fold
+// order, same expression: x * (1 / sqrt(mean(x^2) + eps)) * (1 + w)). Then the
+// row's power of two (max |x| = f 2^e is scaled to f 2^14), and the hi and mid
+// fp16 pieces of every 8-column group in their swizzled places. Rows >= M are
+// zeros.
 template <int NX>
-__global__ void __launch_bounds__(256) prep_x_pieces(const float* x, int M, int K, __half* pieces, float* unscale)
+__global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float* norm_w, float eps, int M, int K,
+                                                     __half* pieces, float* unscale)
 {
     __shared__ float red[8];
     pdl_wait();
@@ -193,12 +249,31 @@ __global__ void __launch_bounds__(256) prep_x_pieces(const float* x, int M, int 
     const int m = blockIdx.x, tid = threadIdx.x;
     const bool live = m < M;
     const float* row = x + (size_t) m * K;
+    float scale = 1.f;
+    if (norm_w && live)
+    {
+        float s = 0.f;
+        for (int c = tid; c < K; c += 256)
+            s += row[c] * row[c];
+        s = warp_sum(s);
+        if ((tid & 31) == 0)
+            red[tid >> 5] = s;
+        __syncthreads();
+        float total = 0.f;
+        for (int w = 0; w < 8; ++w)
+            total += red[w];
+        scale = 1.f / sqrtf(total / (float) K + eps);
+        __syncthreads();
+    }
+    auto value = [&](int c, float v) { return norm_w ? v * scale * (1.f + norm_w[c]) : v; };
+
     float mx = 0.f;
     if (live)
         for (int k = tid * 4; k < K; k += 1024)
         {
             const float4 v = __ldcg(reinterpret_cast<const float4*>(row + k));
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(value(k, v.x)), fabsf(value(k + 1, v.y))),
+                                 fmaxf(fabsf(value(k + 2, v.z)), fabsf(value(k + 3, v.w)))));
         }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
@@ -228,6 +303,9 @@ __global__ void __launch_bounds__(256) prep_x_pieces(const float* x, int M, int 
             const float4 a = __ldcg(reinterpret_cast<const float4*>(row + k));
             const float4 b = __ldcg(reinterpret_cast<const float4*>(row + k + 4));
             v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                v[i] = value(k + i, v[i]);
         }
         else
         {
@@ -280,52 +358,183 @@ __device__ __forceinline__ void tc_split16(uint4 q, __half2 s2, uint4& hi0, uint
     lo1 = make_uint4(l[4], l[5], l[6], l[7]);
 }
 
-// out[m, n] (+ split * split_stride) = sum over this CTA's K range of
-// x[m, k] w[n, k], for the tile (blockIdx.x: 128 weight rows, blockIdx.y: NX
-// rows of x) and the K range blockIdx.z of `chunks_per_split` 64-column
-// chunks. Rows m >= M are not stored.
+// The end of a tile: DN accumulated columns (x rows m0 .. m0 + DN - 1) of
+// weight row n, times the row powers of two, through the product's epilogue
+// E, or, when K is split across CTAs (gridDim.z > 1), as partial sums into
+// ws + split * split_stride ([m][n]) for tc_finish. Rows m >= a.M are not
+// stored. Called by all 32 lanes of a warp (the paired epilogues exchange
+// values between lanes l and l ^ 1, weight rows 2u and 2u + 1).
+//
+// The rows' powers of two are read 16 at a time ahead of the group's stores:
+// the stores may alias them as far as the compiler knows, so read one by one
+// each would wait a full L2 round trip.
+template <Epi E, int DN>
+__device__ __forceinline__ void tc_store_tile(const GemvArgs& a, const float (&sum)[DN], int n, int m0, float wu,
+                                              const float* xunscale, float* ws, size_t split_stride)
+{
+    const int lane = threadIdx.x & 31;
+    constexpr bool PAIRS = E == Epi::QkvRope || E == Epi::GeGLU;
+    const bool partial = gridDim.z > 1;
+    unsigned position = 0;
+    if constexpr (E == Epi::QkvRope)
+        position = step_position(a);
+#pragma unroll
+    for (int g = 0; g < DN; g += 16)
+    {
+        if (m0 + g >= a.M) // the same on every lane
+            break;
+        float f[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            f[j] = wu * xunscale[min(m0 + g + j, a.M - 1)];
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+        {
+            const int m = m0 + g + j;
+            if (m >= a.M)
+                break;
+            const float v = sum[g + j] * f[j];
+            if (partial)
+            {
+                ws[(size_t) blockIdx.z * split_stride + (size_t) m * a.N + n] = v;
+                continue;
+            }
+            if constexpr (PAIRS)
+            {
+                const float v1 = __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+                if ((lane & 1) == 0)
+                {
+                    if constexpr (E == Epi::QkvRope)
+                        qkv_pair_store(a, (unsigned) (n >> 1), v, v1,
+                                       position + (a.cache_seq_stride ? 0u : (unsigned) m), m);
+                    else
+                        a.out[(size_t) m * (a.N / 2) + (n >> 1)] = tanh_gelu(v) * v1;
+                }
+            }
+            else
+                plain_epilogue(E == Epi::Logits ? Epi::Store : E, v, a.bias, n, a.out + (size_t) m * a.N + n);
+        }
+    }
+}
+
+// Drains accumulator set b (large at `large`, small at `large + small_off`
+// columns) of one TMEM lane quarter, DN columns from col0, into sum.
+template <int DN>
+__device__ __forceinline__ void tc_drain(uint32_t large, uint32_t small_off, float (&sum)[DN])
+{
+#pragma unroll
+    for (int j0 = 0; j0 < DN; j0 += 16)
+    {
+        uint32_t v[16], w[16];
+        tc_ld16(large + (uint32_t) j0, v);
+        tc_ld16(large + small_off + (uint32_t) j0, w);
+        tc_wait_ld(v);
+        tc_wait_ld(w);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj)
+            sum[j0 + jj] += __uint_as_float(v[jj]) + __uint_as_float(w[jj]);
+    }
+}
+
+// The 12 MMAs of one 64-column chunk: per k-step of 16, x_hi.w_hi into the
+// large accumulator, x_hi.w_lo and x_mid.w_hi into the small one; the first
+// k-step starts both afresh.
+template <bool A_IN_TMEM>
+__device__ __forceinline__ void tc_chunk_mmas(uint32_t large, uint32_t small, uint64_t a_hi_desc, uint64_t a_lo_desc,
+                                              uint32_t a_hi_tmem, uint32_t a_lo_tmem, uint64_t b_hi, uint64_t b_mid,
+                                              uint32_t idesc)
+{
+#pragma unroll
+    for (int k = 0; k < kTcChunk / 16; ++k)
+    {
+        const uint64_t o = 2 * k; // 32 bytes of each swizzled row = 2 descriptor units
+        if constexpr (A_IN_TMEM)
+        {
+            const uint32_t c = 8 * k; // 16 fp16 = 8 TMEM columns
+            tc_mma_ts(large, a_hi_tmem + c, b_hi + o, idesc, k > 0 ? 1u : 0u);
+            tc_mma_ts(small, a_lo_tmem + c, b_hi + o, idesc, k > 0 ? 1u : 0u);
+            tc_mma_ts(small, a_hi_tmem + c, b_mid + o, idesc, 1u);
+        }
+        else
+        {
+            tc_mma(large, a_hi_desc + o, b_hi + o, idesc, k > 0 ? 1u : 0u);
+            tc_mma(small, a_lo_desc + o, b_hi + o, idesc, k > 0 ? 1u : 0u);
+            tc_mma(small, a_hi_desc + o, b_mid + o, idesc, 1u);
+        }
+    }
+}
+
+// The producer lane: one bulk copy of the weight block and one of the x block
+// per load stage, each stage reused once the MMAs that read it are done.
+template <int NX, int LS>
+__device__ __forceinline__ void tc_produce(uint8_t* loads, size_t lsb, const uint8_t* wblocks, const __half* xpieces,
+                                           int t, int xt, int chunks, int c0, int count, uint64_t* full,
+                                           uint64_t* empty, unsigned* err)
+{
+    constexpr int XB = 2 * NX * 128;
+    const uint64_t policy = evict_first_policy();
+    for (int i = 0; i < count; ++i)
+    {
+        const int s = i % LS;
+        if (i >= LS && !mbar_wait(&empty[s], ((i / LS) - 1) & 1u))
+        {
+            flag_error(err, kErrWaitTimeout);
+            break;
+        }
+        uint8_t* st = loads + s * lsb;
+        mbar_expect_tx(&full[s], kTcBlockBytes + XB);
+        bulk_load(st + XB, wblocks + ((size_t) t * chunks + c0 + i) * kTcBlockBytes, kTcBlockBytes, &full[s], policy);
+        bulk_load(st, xpieces + ((size_t) xt * chunks + c0 + i) * (XB / 2), XB, &full[s], policy);
+    }
+}
+
+// y = x w^T for the tile (blockIdx.x: 128 weight rows, blockIdx.y: 128 rows of
+// x) over the K range blockIdx.z of `chunks_per_split` 64-column chunks, then
+// tc_store_tile. Converted weight tiles in shared memory.
 //
 // The tensor core adds into its fp32 accumulator without rounding to nearest,
 // and over thousands of additions that drifts well past an fp32 sum's error.
 // So every 64-column chunk starts fresh accumulators (two sets, in turn), and
-// the drain warps add each finished set into fp32 registers, rounding to
-// nearest, while the tensor core fills the other. Within a set, the large
-// products x_hi.w_hi and the small ones (x_hi.w_lo, x_mid.w_hi, 2^-11 of
-// them) have separate accumulators, so the small ones do not truncate at the
-// large one's magnitude: each chunk's large sum sees 4 additions, not 12.
-template <int NX>
+// the drain adds each finished set into fp32 registers, rounding to nearest,
+// while the tensor core fills the other. Within a set, the large products
+// x_hi.w_hi and the small ones (x_hi.w_lo, x_mid.w_hi, 2^-11 of them) have
+// separate accumulators, so the small ones do not truncate at the large
+// one's magnitude: each chunk's large sum sees 4 additions, not 12.
+template <Epi E>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    q8_tc_gemm(const uint8_t* wblocks, const __half* xpieces, const float* xunscale, float* out, size_t split_stride,
-               int M, int N, int K, int chunks_per_split, unsigned* err)
+    q8_tc_gemm(const GemvArgs a, const uint8_t* wblocks, const __half* xpieces, const float* xunscale, float* ws,
+               size_t split_stride, int chunks_per_split)
 {
-    static_assert(NX == 64 || NX == 128, "the drain keeps NX sums per thread in registers");
-    constexpr int ST = tc_stages(NX);
-    constexpr size_t SB = tc_stage_bytes(NX);
+    constexpr int NX = 128, LS = kTcStages;
+    constexpr size_t LSB = kTcStageBytes;
     constexpr int XB = 2 * NX * 128; // bytes of one x block (hi + mid)
+    constexpr int DN = NX / 2;       // accumulator columns one drain thread keeps
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t full[ST], converted[ST], empty[ST], acc_full[2], acc_empty[2];
+    __shared__ uint64_t full[LS], empty[LS], converted[2], a_free[2], acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
 
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    uint8_t* loads = smem + 4 * kTcTileBytes;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int t = blockIdx.x, xt = blockIdx.y, split = blockIdx.z;
-    const int chunks = K / kTcChunk;
-    const int c0 = split * chunks_per_split;
-    const int c1 = min(chunks, c0 + chunks_per_split);
-    const int count = c1 - c0;
+    const int t = blockIdx.x, xt = blockIdx.y;
+    const int chunks = a.K / kTcChunk;
+    const int c0 = blockIdx.z * chunks_per_split;
+    const int count = min(chunks, c0 + chunks_per_split) - c0;
+    unsigned* err = a.err;
 
     if (tid == 0)
     {
-        for (int s = 0; s < ST; ++s)
+        for (int s = 0; s < LS; ++s)
         {
             mbar_init(&full[s], 1);
-            mbar_init(&converted[s], 128);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b)
         {
+            mbar_init(&converted[b], 256);
+            mbar_init(&a_free[b], 1);
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 128);
+            mbar_init(&acc_empty[b], 256);
         }
         mbar_fence_init();
     }
@@ -345,98 +554,245 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 0)
     {
         if (lane == 0)
-        {
-            const uint64_t policy = evict_first_policy();
-            for (int i = 0; i < count; ++i)
-            {
-                const int s = i % ST;
-                if (i >= ST && !mbar_wait(&empty[s], ((i / ST) - 1) & 1u))
-                {
-                    flag_error(err, kErrWaitTimeout);
-                    break;
-                }
-                uint8_t* st = smem + s * SB;
-                mbar_expect_tx(&full[s], kTcBlockBytes + XB);
-                bulk_load(st + 2 * kTcTileBytes + XB, wblocks + ((size_t) t * chunks + c0 + i) * kTcBlockBytes,
-                          kTcBlockBytes, &full[s], policy);
-                bulk_load(st + 2 * kTcTileBytes, xpieces + ((size_t) xt * chunks + c0 + i) * (XB / 2), XB, &full[s],
-                          policy);
-            }
-        }
+            tc_produce<NX, LS>(loads, LSB, wblocks, xpieces, t, xt, chunks, c0, count, full, empty, err);
         __syncwarp();
     }
-    else if (warp == 1)
+    else if (warp == 1 || warp == 10) // even chunks, odd chunks
     {
         if (lane == 0)
         {
             const uint32_t idesc = tc_idesc(NX);
-            for (int i = 0; i < count; ++i)
+            for (int i = warp == 1 ? 0 : 1; i < count; i += 2)
             {
-                const int s = i % ST, b = i & 1;
-                if (!mbar_wait(&converted[s], (i / ST) & 1u)
+                const int s = i % LS, b = i & 1;
+                if (!mbar_wait(&converted[b], (i >> 1) & 1u)
                     || (i >= 2 && !mbar_wait(&acc_empty[b], ((i >> 1) - 1) & 1u)))
                 {
                     flag_error(err, kErrWaitTimeout);
                     break;
                 }
                 tc_fence_after();
-                const uint32_t base = smem_addr(smem + s * SB);
-                const uint64_t a_hi = tc_desc(base), a_lo = tc_desc(base + kTcTileBytes);
-                const uint64_t b_hi = tc_desc(base + 2 * kTcTileBytes), b_mid = tc_desc(base + 2 * kTcTileBytes + XB / 2);
-                const uint32_t large = tmem + (uint32_t) (2 * b * NX), small = large + NX;
-#pragma unroll
-                for (int k = 0; k < kTcChunk / 16; ++k) // k-steps of 16 fp16 = 32 bytes = 2 descriptor units
-                {
-                    const uint64_t o = 2 * k;
-                    tc_mma(large, a_hi + o, b_hi + o, idesc, k > 0 ? 1u : 0u);
-                    tc_mma(small, a_lo + o, b_hi + o, idesc, k > 0 ? 1u : 0u);
-                    tc_mma(small, a_hi + o, b_mid + o, idesc, 1u);
-                }
+                const uint32_t abase = smem_addr(smem + b * 2 * kTcTileBytes);
+                const uint32_t xbase = smem_addr(loads + s * LSB);
+                const uint32_t large = tmem + (uint32_t) (2 * b * NX);
+                tc_chunk_mmas<false>(large, large + NX, tc_desc(abase), tc_desc(abase + kTcTileBytes), 0, 0,
+                                     tc_desc(xbase), tc_desc(xbase + XB / 2), idesc);
                 tc_commit(&empty[s]);
+                tc_commit(&a_free[b]);
                 tc_commit(&acc_full[b]);
             }
         }
         __syncwarp();
     }
-    else if (warp < 6)
+    else
     {
-        // ---- converters: warps 2-5, 128 threads, 4 (row, 16-byte chunk) items each
-        const int ct = tid - 64;
-        for (int i = 0; i < count; ++i)
-        {
-            const int s = i % ST;
-            if (!mbar_wait(&full[s], (i / ST) & 1u))
-            {
-                flag_error(err, kErrWaitTimeout);
-                break;
-            }
-            uint8_t* st = smem + s * SB;
-            const uint8_t* raw = st + 2 * kTcTileBytes + XB;
+        // ---- warps 2-9: convert chunk i into tile buffer i & 1, then drain
+        // chunk i - 1. TMEM lane block (warp % 4) * 32 is weight rows
+        // t * 128 + that block; warps 2-5 keep x columns [0, 64), 6-9 [64, 128).
+        const int ct = tid - 64; // 0 .. 255
+        const int quarter = warp & 3;
+        const int col0 = ((warp - 2) >> 2) * DN;
+        const uint32_t lanes = (uint32_t) (quarter * 32) << 16;
+        float sum[DN];
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
+        for (int j = 0; j < DN; ++j)
+            sum[j] = 0.f;
+        auto drain = [&](int i) -> bool {
+            const int b = i & 1;
+            // warp-uniform: the TMEM loads are warp-collective
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[b], (i >> 1) & 1u)))
+                return false;
+            tc_fence_after();
+            tc_drain<DN>(tmem + lanes + (uint32_t) (2 * b * NX + col0), NX, sum);
+            tc_fence_before();
+            mbar_arrive(&acc_empty[b]);
+            return true;
+        };
+        auto convert = [&](int i) -> bool {
+            const int s = i % LS, b = i & 1;
+            const bool ready =
+                mbar_wait(&full[s], (i / LS) & 1u) && (i < 2 || mbar_wait(&a_free[b], ((i >> 1) - 1) & 1u));
+            if (!__all_sync(0xFFFFFFFFu, ready))
+                return false;
+            const uint8_t* raw = loads + s * LSB + XB;
+            uint8_t* atile = smem + b * 2 * kTcTileBytes;
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
             {
-                const int item = ct + 128 * q;
-                const int r = item >> 2, ch = item & 3;
-                const uint4 quant = *reinterpret_cast<const uint4*>(raw + r * kTcChunk + ch * 16);
+                const int item = ct + 256 * q;
+                const int ch = item >> 7, r = item & 127; // consecutive threads: consecutive rows
+                const uint4 quant = *reinterpret_cast<const uint4*>(raw + ch * kTcRows * 16 + r * 16);
                 const __half scale = reinterpret_cast<const __half*>(raw + kTcQuantBytes)[r * 2 + (ch >> 1)];
                 uint4 h0, h1, l0, l1;
                 tc_split16(quant, __half2half2(scale), h0, h1, l0, l1);
                 const int sw = r & 7;
-                uint8_t* arow = st + r * 128;
+                uint8_t* arow = atile + r * 128;
                 *reinterpret_cast<uint4*>(arow + (((2 * ch) ^ sw) << 4)) = h0;
                 *reinterpret_cast<uint4*>(arow + (((2 * ch + 1) ^ sw) << 4)) = h1;
                 *reinterpret_cast<uint4*>(arow + kTcTileBytes + (((2 * ch) ^ sw) << 4)) = l0;
                 *reinterpret_cast<uint4*>(arow + kTcTileBytes + (((2 * ch + 1) ^ sw) << 4)) = l1;
             }
             fence_proxy_async();
-            mbar_arrive(&converted[s]);
+            mbar_arrive(&converted[b]);
+            return true;
+        };
+        bool ok = true;
+        for (int i = 0; i < count && ok; ++i)
+            ok = convert(i) && (i == 0 || drain(i - 1));
+        if (ok && count > 0)
+            ok = drain(count - 1);
+        if (!ok)
+            flag_error(err, kErrWaitTimeout);
+        __syncwarp();
+        if (ok)
+        {
+            const int n = t * kTcRows + quarter * 32 + lane;
+            const float wu = reinterpret_cast<const float*>(wblocks + (size_t) (a.N / kTcRows) * chunks * kTcBlockBytes)[n];
+            tc_store_tile<E, DN>(a, sum, n, xt * NX + col0, wu, xunscale, ws, split_stride);
+        }
+    }
+    __syncthreads();
+    if (warp == 1)
+    {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(4 * NX) : "memory");
+    }
+    pdl_trigger();
+}
+
+// The same product for a 64-row x tile, with the converted weight tiles in
+// TMEM as the MMA's A operand. TMEM columns: tile buffer b (chunk i: b = i % 2)
+// hi at 64 b, lo at 64 b + 32 (a 64-column chunk of fp16 is 32 columns);
+// accumulator set c (chunk i: c = i % 3) large at 128 + 128 c, small 64
+// further. Three sets give the drain two chunks of slack before the tensor
+// core needs its set again.
+template <Epi E>
+__global__ void __launch_bounds__(kTsThreads, 1)
+    q8_tc_gemm_ts(const GemvArgs a, const uint8_t* wblocks, const __half* xpieces, const float* xunscale, float* ws,
+                  size_t split_stride, int chunks_per_split)
+{
+    constexpr int NX = 64, LS = kTsStages;
+    constexpr size_t LSB = kTsStageBytes;
+    constexpr int XB = 2 * NX * 128;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t full[LS], empty[LS], converted[2], a_free[2], acc_full[3], acc_empty[3];
+    __shared__ uint32_t tmem_slot;
+
+    uint8_t* loads = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t = blockIdx.x, xt = blockIdx.y;
+    const int chunks = a.K / kTcChunk;
+    const int c0 = blockIdx.z * chunks_per_split;
+    const int count = min(chunks, c0 + chunks_per_split) - c0;
+    unsigned* err = a.err;
+
+    if (tid == 0)
+    {
+        for (int s = 0; s < LS; ++s)
+        {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b)
+        {
+            mbar_init(&converted[b], 256);
+            mbar_init(&a_free[b], 1);
+        }
+        for (int c = 0; c < 3; ++c)
+        {
+            mbar_init(&acc_full[c], 1);
+            mbar_init(&acc_empty[c], 128);
+        }
+        mbar_fence_init();
+    }
+    if (warp == 1)
+    {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    pdl_wait();
+
+    if (warp == 0)
+    {
+        if (lane == 0)
+            tc_produce<NX, LS>(loads, LSB, wblocks, xpieces, t, xt, chunks, c0, count, full, empty, err);
+        __syncwarp();
+    }
+    else if (warp == 1 || warp == 14) // even chunks, odd chunks
+    {
+        if (lane == 0)
+        {
+            const uint32_t idesc = tc_idesc(NX);
+            for (int i = warp == 1 ? 0 : 1; i < count; i += 2)
+            {
+                const int s = i % LS, b = i & 1, c = i % 3;
+                if (!mbar_wait(&converted[b], (i >> 1) & 1u)
+                    || (i >= 3 && !mbar_wait(&acc_empty[c], ((i / 3) - 1) & 1u)))
+                {
+                    flag_error(err, kErrWaitTimeout);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t xbase = smem_addr(loads + s * LSB);
+                const uint32_t a_hi = tmem + (uint32_t) (64 * b);
+                const uint32_t large = tmem + 128u + (uint32_t) (128 * c);
+                tc_chunk_mmas<true>(large, large + 64u, 0, 0, a_hi, a_hi + 32u, tc_desc(xbase),
+                                    tc_desc(xbase + XB / 2), idesc);
+                tc_commit(&empty[s]);
+                tc_commit(&a_free[b]);
+                tc_commit(&acc_full[c]);
+            }
+        }
+        __syncwarp();
+    }
+    else if (warp < 10)
+    {
+        // ---- converters, warps 2-9: lane quarter (warp % 4), x columns half
+        // h = (warp - 2) / 4 of the chunk: row r's 32 weights 32 h .. 32 h + 31
+        // (one Q8_0 block, one scale) -> 16 TMEM columns of hi, 16 of lo.
+        const int quarter = warp & 3, h = (warp - 2) >> 2;
+        const int r = quarter * 32 + lane;
+        const uint32_t lanes = (uint32_t) (quarter * 32) << 16;
+        for (int i = 0; i < count; ++i)
+        {
+            const int s = i % LS, b = i & 1;
+            const bool ready =
+                mbar_wait(&full[s], (i / LS) & 1u) && (i < 2 || mbar_wait(&a_free[b], ((i >> 1) - 1) & 1u));
+            if (!__all_sync(0xFFFFFFFFu, ready)) // warp-uniform: the TMEM stores are warp-collective
+            {
+                flag_error(err, kErrWaitTimeout);
+                break;
+            }
+            tc_fence_after();
+            const uint8_t* raw = loads + s * LSB + XB;
+            const uint4 q0 = *reinterpret_cast<const uint4*>(raw + (2 * h) * kTcRows * 16 + r * 16);
+            const uint4 q1 = *reinterpret_cast<const uint4*>(raw + (2 * h + 1) * kTcRows * 16 + r * 16);
+            const __half2 s2 = __half2half2(reinterpret_cast<const __half*>(raw + kTcQuantBytes)[r * 2 + h]);
+            uint4 h0, h1, h2, h3, l0, l1, l2, l3;
+            tc_split16(q0, s2, h0, h1, l0, l1);
+            tc_split16(q1, s2, h2, h3, l2, l3);
+            const uint32_t hi[16] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w,
+                                     h2.x, h2.y, h2.z, h2.w, h3.x, h3.y, h3.z, h3.w};
+            const uint32_t lo[16] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w,
+                                     l2.x, l2.y, l2.z, l2.w, l3.x, l3.y, l3.z, l3.w};
+            const uint32_t col = tmem + lanes + (uint32_t) (64 * b + 16 * h);
+            tc_st16(col, hi);
+            tc_st16(col + 32u, lo);
+            tc_wait_st();
+            tc_fence_before();
+            mbar_arrive(&converted[b]);
         }
         __syncwarp();
     }
     else
     {
-        // ---- drain warps 6-9: TMEM lane block (warp % 4) * 32 is weight rows
-        // t * 128 + that block; each thread keeps its row's NX sums.
+        // ---- drain warps 10-13: lane quarter (warp % 4), all 64 x columns
         const int quarter = warp & 3;
         const uint32_t lanes = (uint32_t) (quarter * 32) << 16;
         float sum[NX];
@@ -446,49 +802,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bool ok = true;
         for (int i = 0; i < count; ++i)
         {
-            const int b = i & 1;
-            if (!mbar_wait(&acc_full[b], (i >> 1) & 1u))
+            const int c = i % 3;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[c], (i / 3) & 1u)))
             {
-                flag_error(err, kErrWaitTimeout);
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t taddr = tmem + lanes + (uint32_t) (2 * b * NX);
-#pragma unroll
-            for (int j0 = 0; j0 < NX; j0 += 16)
-            {
-                uint32_t v[16], w[16];
-                tc_ld16(taddr + (uint32_t) j0, v);
-                tc_ld16(taddr + (uint32_t) (NX + j0), w);
-#pragma unroll
-                for (int jj = 0; jj < 16; ++jj)
-                    sum[j0 + jj] += __uint_as_float(v[jj]) + __uint_as_float(w[jj]);
-            }
+            tc_drain<NX>(tmem + lanes + 128u + (uint32_t) (128 * c), 64u, sum);
             tc_fence_before();
-            mbar_arrive(&acc_empty[b]);
+            mbar_arrive(&acc_empty[c]);
         }
+        if (!ok)
+            flag_error(err, kErrWaitTimeout);
         __syncwarp();
         if (ok)
         {
             const int n = t * kTcRows + quarter * 32 + lane;
-            const float wu =
-                reinterpret_cast<const float*>(wblocks + (size_t) (N / kTcRows) * chunks * kTcBlockBytes)[n];
-            float* o = out + (size_t) split * split_stride + n;
-#pragma unroll
-            for (int j = 0; j < NX; ++j)
-            {
-                const int m = xt * NX + j;
-                if (m < M)
-                    o[(size_t) m * N] = sum[j] * wu * xunscale[m];
-            }
+            const float wu = reinterpret_cast<const float*>(wblocks + (size_t) (a.N / kTcRows) * chunks * kTcBlockBytes)[n];
+            tc_store_tile<E, NX>(a, sum, n, xt * NX, wu, xunscale, ws, split_stride);
         }
     }
     __syncthreads();
     if (warp == 1)
     {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(4 * NX) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
     }
     pdl_trigger();
 }
