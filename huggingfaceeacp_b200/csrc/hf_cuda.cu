@@ -199,7 +199,9 @@ cudaError_t launch_attention(int QH, dim3 grid, cudaStream_t stream, const AttnA
 // records, in blocks of kRowsBlock rows.
 // How the tensor-core product tiles M rows of x against an [N, K] weight: the
 // x tile width (64 or 128 rows, the MMA's N), and a split of K when the
-// output tiles alone would leave SMs idle (each split keeps >= 4 chunks).
+// output tiles alone would leave SMs idle: the most splits that still fit in
+// one wave of CTAs (a second, nearly empty wave would double the time), each
+// keeping >= 4 chunks.
 struct TcPlan
 {
     int nx, tiles_m, tiles_n, splits, cps;
@@ -215,7 +217,7 @@ TcPlan tc_plan(int M, int N, int K, int sms)
     p.m_pad = (size_t) p.tiles_m * p.nx;
     const int chunks = K / kTcChunk;
     const int base = p.tiles_m * p.tiles_n;
-    const int splits = base >= sms ? 1 : std::min((sms + base - 1) / base, std::max(1, chunks / 4));
+    const int splits = base >= sms ? 1 : std::max(1, std::min(sms / base, chunks / 4));
     p.cps = (chunks + splits - 1) / splits;
     p.splits = (chunks + p.cps - 1) / p.cps;
     return p;

@@ -358,61 +358,62 @@ __device__ __forceinline__ void tc_split16(uint4 q, __half2 s2, uint4& hi0, uint
     lo1 = make_uint4(l[4], l[5], l[6], l[7]);
 }
 
-// The end of a tile: DN accumulated columns (x rows m0 .. m0 + DN - 1) of
-// weight row n, times the row powers of two, through the product's epilogue
-// E, or, when K is split across CTAs (gridDim.z > 1), as partial sums into
-// ws + split * split_stride ([m][n]) for tc_finish. Rows m >= a.M are not
-// stored. Called by all 32 lanes of a warp (the paired epilogues exchange
-// values between lanes l and l ^ 1, weight rows 2u and 2u + 1).
-//
-// The rows' powers of two are read 16 at a time ahead of the group's stores:
-// the stores may alias them as far as the compiler knows, so read one by one
-// each would wait a full L2 round trip.
-template <Epi E, int DN>
-__device__ __forceinline__ void tc_store_tile(const GemvArgs& a, const float (&sum)[DN], int n, int m0, float wu,
-                                              const float* xunscale, float* ws, size_t split_stride)
+// The end of a tile. The drain threads put their sums (times the weight row's
+// power of two) into shared memory as tile[j][n_local] (j: x row within the
+// tile, n_local: weight row within it), no longer needed for loads by then;
+// then every thread of the CTA takes outputs in turn, consecutive threads
+// consecutive weight rows, through the product's epilogue E (or, when K is
+// split across CTAs, into ws + split * split_stride as partial sums for
+// tc_finish). Rows m >= a.M are not stored.
+template <int DN>
+__device__ __forceinline__ void tc_sums_to_smem(float* tile, const float (&sum)[DN], int n_local, int j0, float wu)
 {
-    const int lane = threadIdx.x & 31;
-    constexpr bool PAIRS = E == Epi::QkvRope || E == Epi::GeGLU;
-    const bool partial = gridDim.z > 1;
-    unsigned position = 0;
-    if constexpr (E == Epi::QkvRope)
-        position = step_position(a);
 #pragma unroll
-    for (int g = 0; g < DN; g += 16)
+    for (int j = 0; j < DN; ++j)
+        tile[(j0 + j) * kTcRows + n_local] = sum[j] * wu;
+}
+
+// xu: the tile rows' powers of two, staged in shared memory.
+template <Epi E>
+__device__ __forceinline__ void tc_epilogue(const GemvArgs& a, const float* tile, const float* xu, int rows, int n0,
+                                            int m0, float* ws, size_t split_stride)
+{
+    const int threads = blockDim.x;
+    if (gridDim.z > 1)
     {
-        if (m0 + g >= a.M) // the same on every lane
-            break;
-        float f[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-            f[j] = wu * xunscale[min(m0 + g + j, a.M - 1)];
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
+        float* o = ws + (size_t) blockIdx.z * split_stride;
+        for (int i = threadIdx.x; i < rows * kTcRows; i += threads)
         {
-            const int m = m0 + g + j;
-            if (m >= a.M)
-                break;
-            const float v = sum[g + j] * f[j];
-            if (partial)
-            {
-                ws[(size_t) blockIdx.z * split_stride + (size_t) m * a.N + n] = v;
-                continue;
-            }
-            if constexpr (PAIRS)
-            {
-                const float v1 = __shfl_xor_sync(0xFFFFFFFFu, v, 1);
-                if ((lane & 1) == 0)
-                {
-                    if constexpr (E == Epi::QkvRope)
-                        qkv_pair_store(a, (unsigned) (n >> 1), v, v1,
-                                       position + (a.cache_seq_stride ? 0u : (unsigned) m), m);
-                    else
-                        a.out[(size_t) m * (a.N / 2) + (n >> 1)] = tanh_gelu(v) * v1;
-                }
-            }
+            const int j = i / kTcRows, nl = i % kTcRows;
+            o[(size_t) (m0 + j) * a.N + n0 + nl] = tile[i] * xu[j];
+        }
+        return;
+    }
+    if constexpr (E == Epi::QkvRope || E == Epi::GeGLU)
+    {
+        unsigned position = 0;
+        if constexpr (E == Epi::QkvRope)
+            position = step_position(a);
+        for (int i = threadIdx.x; i < rows * (kTcRows / 2); i += threads)
+        {
+            const int j = i / (kTcRows / 2), u = i % (kTcRows / 2);
+            const float2 p = *reinterpret_cast<const float2*>(tile + j * kTcRows + 2 * u);
+            const int m = m0 + j;
+            const unsigned unit = (unsigned) (n0 / 2 + u);
+            if constexpr (E == Epi::QkvRope)
+                qkv_pair_store(a, unit, p.x * xu[j], p.y * xu[j], position + (a.cache_seq_stride ? 0u : (unsigned) m),
+                               m);
             else
-                plain_epilogue(E == Epi::Logits ? Epi::Store : E, v, a.bias, n, a.out + (size_t) m * a.N + n);
+                a.out[(size_t) m * (a.N / 2) + unit] = tanh_gelu(p.x * xu[j]) * (p.y * xu[j]);
+        }
+    }
+    else
+    {
+        for (int i = threadIdx.x; i < rows * kTcRows; i += threads)
+        {
+            const int j = i / kTcRows, nl = i % kTcRows;
+            plain_epilogue(E == Epi::Logits ? Epi::Store : E, tile[i] * xu[j], a.bias, n0 + nl,
+                           a.out + (size_t) (m0 + j) * a.N + n0 + nl);
         }
     }
 }
@@ -490,7 +491,7 @@ __device__ __forceinline__ void tc_produce(uint8_t* loads, size_t lsb, const uin
 
 // y = x w^T for the tile (blockIdx.x: 128 weight rows, blockIdx.y: 128 rows of
 // x) over the K range blockIdx.z of `chunks_per_split` 64-column chunks, then
-// tc_store_tile. Converted weight tiles in shared memory.
+// tc_epilogue. Converted weight tiles in shared memory.
 //
 // The tensor core adds into its fp32 accumulator without rounding to nearest,
 // and over thousands of additions that drifts well past an fp32 sum's error.
@@ -512,6 +513,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t full[LS], empty[LS], converted[2], a_free[2], acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
+    __shared__ int tile_ok;
 
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     uint8_t* loads = smem + 4 * kTcTileBytes;
@@ -524,6 +526,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (tid == 0)
     {
+        tile_ok = 1;
         for (int s = 0; s < LS; ++s)
         {
             mbar_init(&full[s], 1);
@@ -642,16 +645,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (ok && count > 0)
             ok = drain(count - 1);
         if (!ok)
-            flag_error(err, kErrWaitTimeout);
-        __syncwarp();
-        if (ok)
         {
-            const int n = t * kTcRows + quarter * 32 + lane;
-            const float wu = reinterpret_cast<const float*>(wblocks + (size_t) (a.N / kTcRows) * chunks * kTcBlockBytes)[n];
-            tc_store_tile<E, DN>(a, sum, n, xt * NX + col0, wu, xunscale, ws, split_stride);
+            flag_error(err, kErrWaitTimeout);
+            tile_ok = 0;
+        }
+        else
+        {
+            const int nl = quarter * 32 + lane;
+            const float wu =
+                reinterpret_cast<const float*>(wblocks + (size_t) (a.N / kTcRows) * chunks * kTcBlockBytes)[t * kTcRows + nl];
+            tc_sums_to_smem<DN>(reinterpret_cast<float*>(loads), sum, nl, col0, wu);
         }
     }
+    __syncthreads(); // every role done: the load ring is free and holds the tile's sums
+    const int rows = min(NX, a.M - xt * NX);
+    if (tid < rows)
+        reinterpret_cast<float*>(loads)[NX * kTcRows + tid] = xunscale[xt * NX + tid];
     __syncthreads();
+    if (tile_ok)
+        tc_epilogue<E>(a, reinterpret_cast<const float*>(loads), reinterpret_cast<const float*>(loads) + NX * kTcRows,
+                       rows, t * kTcRows, xt * NX, ws, split_stride);
     if (warp == 1)
     {
         tc_fence_after();
@@ -677,6 +690,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t full[LS], empty[LS], converted[2], a_free[2], acc_full[3], acc_empty[3];
     __shared__ uint32_t tmem_slot;
+    __shared__ int tile_ok;
 
     uint8_t* loads = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -688,6 +702,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
 
     if (tid == 0)
     {
+        tile_ok = 1;
         for (int s = 0; s < LS; ++s)
         {
             mbar_init(&full[s], 1);
@@ -814,16 +829,26 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             mbar_arrive(&acc_empty[c]);
         }
         if (!ok)
-            flag_error(err, kErrWaitTimeout);
-        __syncwarp();
-        if (ok)
         {
-            const int n = t * kTcRows + quarter * 32 + lane;
-            const float wu = reinterpret_cast<const float*>(wblocks + (size_t) (a.N / kTcRows) * chunks * kTcBlockBytes)[n];
-            tc_store_tile<E, NX>(a, sum, n, xt * NX, wu, xunscale, ws, split_stride);
+            flag_error(err, kErrWaitTimeout);
+            tile_ok = 0;
+        }
+        else
+        {
+            const int nl = quarter * 32 + lane;
+            const float wu =
+                reinterpret_cast<const float*>(wblocks + (size_t) (a.N / kTcRows) * chunks * kTcBlockBytes)[t * kTcRows + nl];
+            tc_sums_to_smem<NX>(reinterpret_cast<float*>(loads), sum, nl, 0, wu);
         }
     }
+    __syncthreads(); // every role done: the load ring is free and holds the tile's sums
+    const int rows = min(NX, a.M - xt * NX);
+    if (tid < rows)
+        reinterpret_cast<float*>(loads)[NX * kTcRows + tid] = xunscale[xt * NX + tid];
     __syncthreads();
+    if (tile_ok)
+        tc_epilogue<E>(a, reinterpret_cast<const float*>(loads), reinterpret_cast<const float*>(loads) + NX * kTcRows,
+                       rows, t * kTcRows, xt * NX, ws, split_stride);
     if (warp == 1)
     {
         tc_fence_after();
