@@ -430,6 +430,30 @@ def run_profile_case(args):
     return 0
 
 
+def run_profile_batched(args):
+    """A small case of the batched decode step for ncu captures (not a bench
+    line): Gemma-2B's layer and head shapes with 2 layers and a 64,000-token
+    vocabulary, 64 sequences (one 64-row x tile) of 8-token prompts, then
+    `--steps` batched steps. The prompts' prefill runs the int8 MMA (8 rows), so
+    the first q8_tc_gemm_ts launch is step 1's q/k/v; per step the launches are
+    q/k/v, o, gate/up, down per layer, then the logits (139 MB of weights, above
+    L2): `-k regex:q8_tc_gemm_ts -s 8 -c 1` captures step 1's logits product."""
+    from huggingfaceeacp_b200 import native
+
+    shape = native.GEMMA_2B.replace(layers=2, vocab=64000, max_positions=64, max_step_rows=64)
+    sequences = 64
+    with native.Context(shape, sequences=sequences) as ctx:
+        ctx.load_synthetic(seed=SEED)
+        prompts = np.stack([native.synthetic_tokens(BATCH_SEED + q, 8, shape.vocab) for q in range(sequences)])
+        ctx.prefill_batch_async(prompts)
+        ctx.decode_batch_async(args.steps)
+        ctx.sync()
+    logits_bytes = 64000 * 2048 * 17 // 16
+    print(json.dumps({"profile_case": "Gemma-2B shapes, 2 layers, vocab 64000, 64 sequences, batched steps",
+                      "steps": args.steps, "logits_weight_bytes": logits_bytes}), flush=True)
+    return 0
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -440,10 +464,13 @@ def main():
     parser.add_argument("--batched-steps", type=int, default=256,
                         help="batched decode steps timed for the b=64/GPU half of the metric")
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--profile-case", action="store_true",
-                        help="run the small ncu capture case of the decode kernel instead of the bench")
+    parser.add_argument("--profile-case", nargs="?", const="decode", choices=["decode", "batched"],
+                        help="run a small ncu capture case instead of the bench: the decode kernel (default) or "
+                             "a batched step's tensor-core products")
     args = parser.parse_args()
     args.warmup = max(3, args.warmup)
+    if args.profile_case == "batched":
+        return run_profile_batched(args)
     if args.profile_case:
         return run_profile_case(args)
     if args.impl == "reference":
