@@ -437,6 +437,27 @@ __device__ __forceinline__ void tc_drain(uint32_t large, uint32_t small_off, flo
     }
 }
 
+// Drains q8_tc_gemm_ts's accumulator set at `d1` (x_hi.w_hi at d1, x_mid.w_hi
+// 64 columns on, x_hi.w_lo 128 on) of one TMEM lane quarter into sum.
+template <int DN>
+__device__ __forceinline__ void tc_drain3(uint32_t d1, float (&sum)[DN])
+{
+#pragma unroll
+    for (int j0 = 0; j0 < DN; j0 += 16)
+    {
+        uint32_t u[16], v[16], w[16];
+        tc_ld16(d1 + (uint32_t) j0, u);
+        tc_ld16(d1 + 64u + (uint32_t) j0, v);
+        tc_ld16(d1 + 128u + (uint32_t) j0, w);
+        tc_wait_ld(u);
+        tc_wait_ld(v);
+        tc_wait_ld(w);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj)
+            sum[j0 + jj] += __uint_as_float(u[jj]) + (__uint_as_float(v[jj]) + __uint_as_float(w[jj]));
+    }
+}
+
 // The 12 MMAs of one 64-column chunk: per k-step of 16, x_hi.w_hi into the
 // large accumulator, x_hi.w_lo and x_mid.w_hi into the small one; the first
 // k-step starts both afresh.
@@ -674,11 +695,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // The same product for a 64-row x tile, with the converted weight tiles in
-// TMEM as the MMA's A operand. TMEM columns: tile buffer b (chunk i: b = i % 2)
-// hi at 64 b, lo at 64 b + 32 (a 64-column chunk of fp16 is 32 columns);
-// accumulator set c (chunk i: c = i % 3) large at 128 + 128 c, small 64
-// further. Three sets give the drain two chunks of slack before the tensor
-// core needs its set again.
+// TMEM as the MMA's A operand, and two MMAs per k-step instead of three: the
+// x block's hi and mid pieces are consecutive in shared memory, so one N = 128
+// MMA multiplies w_hi by both (the tensor core's full rate; N = 64 runs at
+// two thirds of it), and one N = 64 MMA multiplies w_lo by x_hi. TMEM columns:
+// tile buffer b (chunk i: b = i % 2) hi at 64 b, lo at 64 b + 32 (a 64-column
+// chunk of fp16 is 32 columns); accumulator set c (chunk i: c = i % 2) at
+// 128 + 192 c: [x_hi.w_hi | x_mid.w_hi] (128 columns), then x_hi.w_lo (64).
+// Each of the three terms has its own accumulator.
 template <Epi E>
 __global__ void __launch_bounds__(kTsThreads, 1)
     q8_tc_gemm_ts(const GemvArgs a, const uint8_t* wblocks, const __half* xpieces, const float* xunscale, float* ws,
@@ -688,7 +712,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     constexpr size_t LSB = kTsStageBytes;
     constexpr int XB = 2 * NX * 128;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t full[LS], empty[LS], converted[2], a_free[2], acc_full[3], acc_empty[3];
+    __shared__ uint64_t full[LS], empty[LS], converted[2], a_free[2], acc_full[2], acc_empty[2];
     __shared__ uint32_t tmem_slot;
     __shared__ int tile_ok;
 
@@ -713,7 +737,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             mbar_init(&converted[b], 256);
             mbar_init(&a_free[b], 1);
         }
-        for (int c = 0; c < 3; ++c)
+        for (int c = 0; c < 2; ++c)
         {
             mbar_init(&acc_full[c], 1);
             mbar_init(&acc_empty[c], 128);
@@ -743,12 +767,12 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     {
         if (lane == 0)
         {
-            const uint32_t idesc = tc_idesc(NX);
+            const uint32_t idesc = tc_idesc(NX), idesc128 = tc_idesc(2 * NX);
             for (int i = warp == 1 ? 0 : 1; i < count; i += 2)
             {
-                const int s = i % LS, b = i & 1, c = i % 3;
+                const int s = i % LS, b = i & 1, c = i & 1;
                 if (!mbar_wait(&converted[b], (i >> 1) & 1u)
-                    || (i >= 3 && !mbar_wait(&acc_empty[c], ((i / 3) - 1) & 1u)))
+                    || (i >= 2 && !mbar_wait(&acc_empty[c], ((i >> 1) - 1) & 1u)))
                 {
                     flag_error(err, kErrWaitTimeout);
                     break;
@@ -756,9 +780,14 @@ __global__ void __launch_bounds__(kTsThreads, 1)
                 tc_fence_after();
                 const uint32_t xbase = smem_addr(loads + s * LSB);
                 const uint32_t a_hi = tmem + (uint32_t) (64 * b);
-                const uint32_t large = tmem + 128u + (uint32_t) (128 * c);
-                tc_chunk_mmas<true>(large, large + 64u, 0, 0, a_hi, a_hi + 32u, tc_desc(xbase),
-                                    tc_desc(xbase + XB / 2), idesc);
+                const uint32_t d1 = tmem + 128u + (uint32_t) (192 * c), d2 = d1 + 128u;
+                const uint64_t b_both = tc_desc(xbase); // x_hi rows 0-63, x_mid rows 64-127
+#pragma unroll
+                for (int k = 0; k < kTcChunk / 16; ++k)
+                {
+                    tc_mma_ts(d1, a_hi + 8u * k, b_both + 2 * k, idesc128, k > 0 ? 1u : 0u);
+                    tc_mma_ts(d2, a_hi + 32u + 8u * k, b_both + 2 * k, idesc, k > 0 ? 1u : 0u);
+                }
                 tc_commit(&empty[s]);
                 tc_commit(&a_free[b]);
                 tc_commit(&acc_full[c]);
@@ -817,14 +846,14 @@ __global__ void __launch_bounds__(kTsThreads, 1)
         bool ok = true;
         for (int i = 0; i < count; ++i)
         {
-            const int c = i % 3;
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[c], (i / 3) & 1u)))
+            const int c = i & 1;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[c], (i >> 1) & 1u)))
             {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            tc_drain<NX>(tmem + lanes + 128u + (uint32_t) (128 * c), 64u, sum);
+            tc_drain3<NX>(tmem + lanes + 128u + (uint32_t) (192 * c), sum);
             tc_fence_before();
             mbar_arrive(&acc_empty[c]);
         }
