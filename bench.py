@@ -364,7 +364,10 @@ def run_ours(args):
         dominant = max(per_step_us, key=per_step_us.get)
         launch_bytes, launch_us = kernels[dominant]["bytes"], kernels[dominant]["us"]
         achieved = kernels[dominant]["gbs"]
-    traffic = committed_traffic().get(dominant)
+    # DRAM bytes per launch: the ncu capture's traffic per algorithmic byte
+    # (profiles/traffic.json) times this launch's algorithmic bytes.
+    ratio = committed_traffic().get(dominant, {}).get("dram_bytes_per_algorithmic_byte")
+    traffic = ratio * launch_bytes if ratio else None
     roofline = {"kernel": dominant, "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                 "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                 "algorithmic_bytes_per_launch": launch_bytes, "mean_launch_us": launch_us,
