@@ -67,7 +67,7 @@ def measured_peaks():
 
 
 def committed_traffic():
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    """DRAM bytes per algorithmic byte of the dominant kernel, from the committed ncu summary."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(path):
         with open(path) as f:
