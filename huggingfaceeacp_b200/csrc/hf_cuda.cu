@@ -695,8 +695,10 @@ struct hf_ctx
         cudaError_t e;
         if (p.nx == 64)
         {
-            e = launch(true, prep_x_pieces<64>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x, a.norm_w, a.eps,
-                       a.M, a.K, tc_x, tc_xunscale);
+            e = a.K == 16384 ? launch(true, prep_x_pieces<64, 16384>, dim3((unsigned) p.m_pad), dim3(256), 0, stream,
+                                      a.x, a.norm_w, a.eps, a.M, tc_x, tc_xunscale)
+                             : launch(true, prep_x_pieces<64, 2048>, dim3((unsigned) p.m_pad), dim3(256), 0, stream,
+                                      a.x, a.norm_w, a.eps, a.M, tc_x, tc_xunscale);
             if (e == cudaSuccess)
                 e = launch(true, q8_tc_gemm_ts<E>, grid, dim3(kTsThreads), kTsSmem, stream, a,
                            (const uint8_t*) w.tc, (const __half*) tc_x, (const float*) tc_xunscale, tc_ws,
@@ -704,8 +706,10 @@ struct hf_ctx
         }
         else
         {
-            e = launch(true, prep_x_pieces<128>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x, a.norm_w, a.eps,
-                       a.M, a.K, tc_x, tc_xunscale);
+            e = a.K == 16384 ? launch(true, prep_x_pieces<128, 16384>, dim3((unsigned) p.m_pad), dim3(256), 0, stream,
+                                      a.x, a.norm_w, a.eps, a.M, tc_x, tc_xunscale)
+                             : launch(true, prep_x_pieces<128, 2048>, dim3((unsigned) p.m_pad), dim3(256), 0, stream,
+                                      a.x, a.norm_w, a.eps, a.M, tc_x, tc_xunscale);
             if (e == cudaSuccess)
                 e = launch(true, q8_tc_gemm<E>, grid, dim3(kTcThreads), kTcSmem, stream, a,
                            (const uint8_t*) w.tc, (const __half*) tc_x, (const float*) tc_xunscale, tc_ws,
@@ -743,7 +747,7 @@ struct hf_ctx
     template <Epi E, int K>
     cudaError_t multi_row(const Q8& w, GemvArgs a)
     {
-        if (w.tc && a.M > kRowsBlock && !tc_off)
+        if (w.tc && a.M > kRowsBlock && !tc_off && (a.K == 2048 || a.K == 16384))
             return tc_product<E>(w, a);
         if (a.norm_w)
         {

@@ -233,16 +233,18 @@ __global__ void __launch_bounds__(kTcRows) build_tc_blocks(const uint8_t* quants
 }
 
 // ---- x pieces (once per product input) --------------------------------------
-// One CTA of 256 threads per row of the padded tile set. With `norm_w`, the
-// row is first RMS-normalised exactly as rms_norm_rows does it (same fold
-// order, same expression: x * (1 / sqrt(mean(x^2) + eps)) * (1 + w)). Then the
+// One CTA of 256 threads per row of the padded tile set; thread t holds the
+// row's 8-column groups t, t + 256, ... (K / 2048 of them) in registers, so
+// the row is read once (twice with a norm). With `norm_w`, the row is first
+// RMS-normalised exactly as rms_norm_rows does it (the sum of squares in its
+// strided order, then x * (1 / sqrt(mean(x^2) + eps)) * (1 + w)). Then the
 // row's power of two (max |x| = f 2^e is scaled to f 2^14), and the hi and mid
-// fp16 pieces of every 8-column group in their swizzled places. Rows >= M are
-// zeros.
-template <int NX>
-__global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float* norm_w, float eps, int M, int K,
+// fp16 pieces of every group in their swizzled places. Rows >= M are zeros.
+template <int NX, int K>
+__global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float* norm_w, float eps, int M,
                                                      __half* pieces, float* unscale)
 {
+    constexpr int G = K / 2048; // 8-column groups per thread
     __shared__ float red[8];
     pdl_wait();
     pdl_trigger();
@@ -265,16 +267,38 @@ __global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float
         scale = 1.f / sqrtf(total / (float) K + eps);
         __syncthreads();
     }
-    auto value = [&](int c, float v) { return norm_w ? v * scale * (1.f + norm_w[c]) : v; };
-
-    float mx = 0.f;
-    if (live)
-        for (int k = tid * 4; k < K; k += 1024)
+    float v[G][8];
+#pragma unroll
+    for (int q = 0; q < G; ++q)
+    {
+        const int k = (tid + 256 * q) * 8;
+        if (live)
         {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(row + k));
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(value(k, v.x)), fabsf(value(k + 1, v.y))),
-                                 fmaxf(fabsf(value(k + 2, v.z)), fabsf(value(k + 3, v.w)))));
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(row + k));
+            const float4 b = __ldcg(reinterpret_cast<const float4*>(row + k + 4));
+            v[q][0] = a.x; v[q][1] = a.y; v[q][2] = a.z; v[q][3] = a.w;
+            v[q][4] = b.x; v[q][5] = b.y; v[q][6] = b.z; v[q][7] = b.w;
         }
+        else
+        {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                v[q][i] = 0.f;
+        }
+    }
+    float mx = 0.f;
+#pragma unroll
+    for (int q = 0; q < G; ++q)
+    {
+        const int k = (tid + 256 * q) * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+        {
+            if (norm_w && live)
+                v[q][i] = v[q][i] * scale * (1.f + norm_w[k + i]);
+            mx = fmaxf(mx, fabsf(v[q][i]));
+        }
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
         mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
@@ -293,32 +317,17 @@ __global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float
         unscale[m] = ldexpf(1.f, -shift);
 
     const int tile = m / NX, j = m % NX;
-    const int chunks = K / kTcChunk;
-    for (int g = tid; g < K / 8; g += 256) // one 8-column group (16 bytes of each piece)
+    constexpr int chunks = K / kTcChunk;
+#pragma unroll
+    for (int q = 0; q < G; ++q)
     {
-        const int k = g * 8, c = k / kTcChunk, cc = (k % kTcChunk) / 8;
-        float v[8];
-        if (live)
-        {
-            const float4 a = __ldcg(reinterpret_cast<const float4*>(row + k));
-            const float4 b = __ldcg(reinterpret_cast<const float4*>(row + k + 4));
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                v[i] = value(k + i, v[i]);
-        }
-        else
-        {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                v[i] = 0.f;
-        }
+        const int k = (tid + 256 * q) * 8, c = k / kTcChunk, cc = (k % kTcChunk) / 8;
         __align__(16) __half hi[8];
         __align__(16) __half mid[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
         {
-            const float s = ldexpf(v[i], shift);
+            const float s = ldexpf(v[q][i], shift);
             hi[i] = __float2half_rn(s);
             mid[i] = __float2half_rn(s - __half2float(hi[i]));
         }
