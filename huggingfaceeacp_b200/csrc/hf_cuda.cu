@@ -22,6 +22,7 @@
 #include "misc.cuh"
 #include "persistent.cuh"
 #include "rows_mma.cuh"
+#include "sampling.cuh"
 #include "tc_gemm.cuh"
 
 #include <algorithm>
@@ -31,6 +32,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <random>
 #include <string>
 #include <vector>
 
@@ -308,6 +310,8 @@ struct hf_ctx
     unsigned* cand_idx = nullptr;
     float* attn_acc = nullptr;
     float* attn_ml = nullptr;
+    double* sample_uniforms = nullptr; // [max_positions + 1] a sampled run's uniforms
+    float* sample_mask = nullptr;      // [vocab] hf_cuda_sample's mask row
     uint8_t* staging = nullptr;
     size_t staging_bytes = 0;
     int max_splits = 1;
@@ -1078,6 +1082,8 @@ struct hf_ctx
             text += " a token id outside the vocabulary reached the embedding gather;";
         if (word & kErrPosition)
             text += " a step ran past the window;";
+        if (word & kErrSampleSet)
+            text += " a top-p set needed more than the device sampler's 1024 candidates;";
         return fail(HF_E_DEVICE, text);
     }
 
@@ -1232,7 +1238,9 @@ int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** ou
         || device_alloc(ctx, &ctx->cand_val, cand, "argmax candidates")
         || device_alloc(ctx, &ctx->cand_idx, cand, "argmax candidates")
         || device_alloc(ctx, &ctx->attn_acc, partials * QW, "attention partials")
-        || device_alloc(ctx, &ctx->attn_ml, partials * s.heads * 2, "attention partials"))
+        || device_alloc(ctx, &ctx->attn_ml, partials * s.heads * 2, "attention partials")
+        || device_alloc(ctx, &ctx->sample_uniforms, P + 1, "sampling uniforms")
+        || device_alloc(ctx, &ctx->sample_mask, V, "sampling mask"))
         return bail(HF_E_CUDA);
     ctx->select_sequence(0);
     cudaMemset(ctx->state, 0, 8 * sizeof(unsigned));
@@ -1386,7 +1394,8 @@ void hf_cuda_destroy(hf_ctx* ctx)
         cudaGraphExecDestroy(g.second);
     void* buffers[] = {ctx->pool, ctx->record_pool, ctx->tc_pool, ctx->tc_x, ctx->tc_xunscale, ctx->tc_ws, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
                        ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slot_base, ctx->state,
-                       ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev};
+                       ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev,
+                       ctx->sample_uniforms, ctx->sample_mask};
     for (void* b: buffers)
         if (b)
             cudaFree(b);
@@ -1866,6 +1875,171 @@ int hf_cuda_generate_batch(hf_ctx* ctx, const uint32_t* prompts, int prompt_leng
         rc = hf_cuda_decode_batch_async(ctx, tokens - 1);
     if (!rc)
         rc = hf_cuda_read_batch_slots(ctx, prompt_length, tokens, out);
+    return rc;
+}
+
+namespace
+{
+// Sampler::validated (Sampler.cpp:27-40), plus the device sampler's top-k limit.
+int sampling_refusal(hf_ctx* ctx, const hf_sampling* o)
+{
+    if (!(o->temperature >= 0.f))
+        return ctx->fail(HF_E_INVALID, "a sampling temperature must be zero or positive");
+    if (o->top_k < 0)
+        return ctx->fail(HF_E_INVALID, "a top-k count cannot be negative");
+    if (!(o->top_p > 0.f && o->top_p <= 1.f))
+        return ctx->fail(HF_E_INVALID, "a top-p mass must lie inside (0, 1]");
+    if (o->top_k > kSampleMaxK && o->top_k < ctx->shape.vocab)
+        return ctx->fail(HF_E_INVALID, "the device sampler keeps at most 1024 top-k candidates");
+    return HF_OK;
+}
+
+// The reference's uniforms (Sampler.cpp:211-214): the top 53 bits of
+// std::mt19937_64 draws, seeded once per sampled run.
+std::vector<double> sampling_uniforms(uint64_t seed, int count)
+{
+    std::mt19937_64 generator(seed);
+    std::vector<double> u((size_t) std::max(count, 0));
+    for (double& v: u)
+        v = (double) (generator() >> 11) * 0x1.0p-53;
+    return u;
+}
+
+SampleArgs sample_args(hf_ctx* ctx, const float* row, const float* mask, int length, const hf_sampling* o,
+                       unsigned* slots, unsigned* state)
+{
+    SampleArgs a = {};
+    a.logits = row;
+    a.mask = mask;
+    a.V = length;
+    a.temperature = o->temperature;
+    a.top_k = o->top_k >= length ? 0 : o->top_k; // keep >= candidates: no cut (Sampler.cpp:125-130)
+    a.top_p = o->top_p;
+    a.uniforms = ctx->sample_uniforms;
+    a.draws = ctx->state + 5;
+    a.slots = slots;
+    a.state = state;
+    a.err = ctx->err_word();
+    return a;
+}
+} // namespace
+
+int hf_cuda_sample(hf_ctx* ctx, const float* logits, const float* mask, int length, const hf_sampling* options,
+                   int draws, uint32_t* tokens_out)
+{
+    if (!ctx || !logits || !options || draws < 0 || (draws > 0 && !tokens_out))
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    if (length != ctx->shape.vocab)
+        return ctx->fail(HF_E_INVALID, "a sampled row holds one logit per vocabulary token");
+    if (int rc = sampling_refusal(ctx, options))
+        return rc;
+    if (draws > ctx->shape.max_positions + 1)
+        return ctx->fail(HF_E_CAPACITY, "more draws than this decoder holds uniforms for");
+    if (options->temperature == 0.f) // greedy: Sampler::argmax, no draws consumed
+    {
+        std::vector<uint32_t> one(1);
+        int rc = hf_cuda_argmax(ctx, logits, mask, 1, length, one.data());
+        for (int i = 0; i < draws && !rc; ++i)
+            tokens_out[i] = one[0];
+        return rc;
+    }
+    const std::vector<double> u = sampling_uniforms(options->seed, draws);
+    const unsigned zero = 0;
+    int rc = ctx->cuda(cudaMemcpyAsync(ctx->logits, logits, (size_t) length * 4, cudaMemcpyHostToDevice, ctx->stream),
+                       "row upload");
+    if (!rc && mask)
+        rc = ctx->cuda(cudaMemcpyAsync(ctx->sample_mask, mask, (size_t) length * 4, cudaMemcpyHostToDevice, ctx->stream),
+                       "mask upload");
+    if (!rc && draws > 0)
+        rc = ctx->cuda(cudaMemcpyAsync(ctx->sample_uniforms, u.data(), u.size() * 8, cudaMemcpyHostToDevice, ctx->stream),
+                       "uniforms upload");
+    if (!rc)
+        rc = ctx->cuda(cudaMemcpyAsync(ctx->state + 5, &zero, 4, cudaMemcpyHostToDevice, ctx->stream), "draw reset");
+    // each draw lands in the scratch slot row slots[i] (the sequence is not touched: a copy of its head first)
+    std::vector<uint32_t> saved((size_t) draws);
+    if (!rc && draws > 0)
+        rc = ctx->cuda(cudaMemcpyAsync(saved.data(), ctx->slots, (size_t) draws * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                       "slot save");
+    for (int i = 0; i < draws && !rc; ++i)
+    {
+        const SampleArgs a = sample_args(ctx, ctx->logits, mask ? ctx->sample_mask : nullptr, length, options,
+                                         ctx->slots + i, nullptr);
+        rc = ctx->cuda(launch(false, sample_row, dim3(1), dim3(kSampleThreads), 0, ctx->stream, a), "sampler launch");
+    }
+    if (!rc && draws > 0)
+        rc = ctx->cuda(cudaMemcpyAsync(tokens_out, ctx->slots, (size_t) draws * 4, cudaMemcpyDeviceToHost, ctx->stream),
+                       "token readback");
+    if (!rc && draws > 0)
+        rc = ctx->cuda(cudaMemcpyAsync(ctx->slots, saved.data(), (size_t) draws * 4, cudaMemcpyHostToDevice, ctx->stream),
+                       "slot restore");
+    if (!rc)
+        rc = ctx->sync();
+    return rc;
+}
+
+int hf_cuda_generate_sampled(hf_ctx* ctx, const uint32_t* prompt, int prompt_length, int max_tokens, int eos,
+                             const hf_sampling* options, uint32_t* tokens_out, int* count_out)
+{
+    if (!ctx || !prompt || !options || !count_out || (max_tokens > 0 && !tokens_out))
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    if (int rc = sampling_refusal(ctx, options))
+        return rc;
+    if (options->temperature == 0.f)
+        return hf_cuda_generate_greedy(ctx, prompt, prompt_length, max_tokens, eos, tokens_out, count_out);
+    *count_out = 0;
+    int rc = hf_cuda_prefill_async(ctx, prompt, prompt_length);
+    if (rc)
+        return rc;
+    const int window = ctx->shape.max_positions - prompt_length;
+    const int limit = max_tokens > 0 ? std::min(max_tokens, window) : window;
+    if (limit <= 0)
+        return ctx->sync();
+    // Gemma::generateBySampling (Gemma.cpp:545-592): the prefill's last row is
+    // the first draw's; then one step per token, each draw replacing the
+    // step's argmax in the slot the next step embeds.
+    const std::vector<double> u = sampling_uniforms(options->seed, limit);
+    const unsigned zero = 0;
+    rc = ctx->cuda(cudaMemcpyAsync(ctx->sample_uniforms, u.data(), u.size() * 8, cudaMemcpyHostToDevice, ctx->stream),
+                   "uniforms upload");
+    if (!rc)
+        rc = ctx->cuda(cudaMemcpyAsync(ctx->state + 5, &zero, 4, cudaMemcpyHostToDevice, ctx->stream), "draw reset");
+    const int V = ctx->shape.vocab;
+    const int last_row = (prompt_length - 1) % ctx->capacity; // the prefill's last block keeps its last row's logits
+    const float* row = ctx->logits + (size_t) last_row * V;
+    int emitted = 0;
+    std::vector<uint32_t> chunk;
+    for (int t = 0; t < limit && !rc; ++t)
+    {
+        if (t > 0)
+        {
+            rc = hf_cuda_decode_async(ctx, 1);
+            row = ctx->logits; // a decode step's row
+        }
+        if (!rc)
+            rc = ctx->cuda(launch(true, sample_row, dim3(1), dim3(kSampleThreads), 0, ctx->stream,
+                                  sample_args(ctx, row, nullptr, V, options, ctx->slots, ctx->state)),
+                           "sampler launch");
+        const bool flush = t + 1 == limit || (t + 1) % 16 == 0;
+        if (!rc && flush)
+        {
+            const int ready = t + 1;
+            chunk.resize((size_t) (ready - emitted));
+            rc = hf_cuda_read_slots(ctx, prompt_length + emitted, ready - emitted, chunk.data());
+            for (int j = 0; j < ready - emitted && !rc; ++j)
+            {
+                if (eos >= 0 && chunk[j] == (uint32_t) eos)
+                {
+                    *count_out = emitted + j;
+                    return HF_OK;
+                }
+                tokens_out[emitted + j] = chunk[j];
+            }
+            emitted = ready;
+        }
+    }
+    *count_out = emitted;
     return rc;
 }
 

@@ -181,6 +181,12 @@ def host() -> ctypes.CDLL:
     return _host
 
 
+class SamplingStruct(ctypes.Structure):
+    """hf_sampling (include/hf_cuda.h): HF::SamplingOptions."""
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_int32), ("top_p", ctypes.c_float),
+                ("seed", ctypes.c_uint64)]
+
+
 def cuda() -> ctypes.CDLL:
     global _cuda
     if _cuda is None:
@@ -194,6 +200,9 @@ def cuda() -> ctypes.CDLL:
         lib.hf_cuda_decode_batch_async.argtypes = [_vp, ctypes.c_int]
         lib.hf_cuda_read_batch_slots.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp]
         lib.hf_cuda_generate_batch.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]
+        lib.hf_cuda_sample.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.POINTER(SamplingStruct), ctypes.c_int, _vp]
+        lib.hf_cuda_generate_sampled.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.POINTER(SamplingStruct), _vp, ctypes.POINTER(ctypes.c_int)]
         lib.hf_cuda_destroy.argtypes = [_vp]
         lib.hf_cuda_destroy.restype = None
         lib.hf_cuda_last_error.argtypes = [_vp]
@@ -425,6 +434,27 @@ class Context:
 
     def sync(self):
         self.check(self.lib.hf_cuda_sync(self.handle))
+
+    # ---- sampling on the device (hf_cuda_sample, hf_cuda_generate_sampled) --
+    def sample(self, logits, temperature: float, top_k: int = 0, top_p: float = 1.0, seed: int = 0, draws: int = 1,
+               mask=None) -> np.ndarray:
+        logits = np.ascontiguousarray(logits, dtype=np.float32)
+        mask = None if mask is None else np.ascontiguousarray(mask, dtype=np.float32)
+        out = np.empty(max(draws, 1), dtype=np.uint32)
+        options = SamplingStruct(temperature, top_k, top_p, seed)
+        self.check(self.lib.hf_cuda_sample(self.handle, _ptr(logits), _ptr(mask), logits.size, ctypes.byref(options),
+                                           draws, _ptr(out)))
+        return out[:draws].copy()
+
+    def generate_sampled(self, prompt, max_tokens: int, temperature: float, top_k: int = 0, top_p: float = 1.0,
+                         seed: int = 0, eos: int = -1) -> np.ndarray:
+        prompt = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.empty(max(max_tokens, 1), dtype=np.uint32)
+        count = ctypes.c_int(0)
+        options = SamplingStruct(temperature, top_k, top_p, seed)
+        self.check(self.lib.hf_cuda_generate_sampled(self.handle, _ptr(prompt), prompt.size, max_tokens, eos,
+                                                     ctypes.byref(options), _ptr(out), ctypes.byref(count)))
+        return out[: count.value].copy()
 
     # ---- batched decode (hf_cuda_*_batch) ----------------------------------
     def _prompts(self, prompts) -> np.ndarray:

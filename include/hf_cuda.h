@@ -132,6 +132,39 @@ int hf_cuda_argmax_noalloc(const float* logits, const float* mask, int rows, int
 int hf_cuda_generate_greedy(hf_ctx* ctx, const uint32_t* prompt, int prompt_length, int max_tokens, int eos,
                             uint32_t* tokens_out, int* count_out);
 
+/* ---- sampling on the device ----------------------------------------------
+ * Replaces HF::SamplingOptions / Sampler::sample (Sampling/Sampler.h:33-107,
+ * Sampler.cpp:78-215) with the draw made on the device, so a sampled run reads
+ * back a token per step instead of a 1 MB logits row (Gemma.cpp:536-545).
+ * Same rules and order: temperature (0 = greedy), then top-k (0 = off), then
+ * top-p (1 = off; the boundary token kept), a softmax over what is left, and
+ * one uniform per draw: the top 53 bits of std::mt19937_64(seed) draws. The
+ * device keeps at most 1024 ranked candidates: top_k above 1024 (and below
+ * the vocabulary) is refused with HF_E_INVALID, and a top-p set without a
+ * top-k that needs more than 1024 candidates is reported by hf_cuda_sync as
+ * HF_E_DEVICE. Tokens equal the reference's; with neither cut, the walk over
+ * the whole vocabulary sums in parallel, which can only differ when the
+ * uniform lands within ~1e-16 of a cumulative boundary. */
+typedef struct hf_sampling
+{
+    float temperature;
+    int32_t top_k;
+    float top_p;
+    uint64_t seed;
+} hf_sampling;
+/* `draws` tokens from one host row of `length` (= vocab) logits, the
+ * generator advancing by one per draw (repeated Sampler::sample calls on one
+ * row); mask as hf_cuda_argmax's, may be null. Synchronous. */
+int hf_cuda_sample(hf_ctx* ctx, const float* logits, const float* mask, int length, const hf_sampling* options,
+                   int draws, uint32_t* tokens_out);
+/* Replaces HF::Gemma::generate with SamplingOptions (Gemma::generateBySampling,
+ * Gemma.cpp:545-592): begins a sequence, prefills the prompt, then per token
+ * samples the last logits row on the device into the slot the next step
+ * embeds; stops at max_tokens, the window or `eos` (not included). A zero
+ * temperature is hf_cuda_generate_greedy. */
+int hf_cuda_generate_sampled(hf_ctx* ctx, const uint32_t* prompt, int prompt_length, int max_tokens, int eos,
+                             const hf_sampling* options, uint32_t* tokens_out, int* count_out);
+
 /* ---- asynchronous hooks (bench and the C++ HF::Gemma loop) -------------- */
 /* Begins a sequence and enqueues the prompt's prefill plus the argmax that
  * writes the first generated token into slot prompt_length. */

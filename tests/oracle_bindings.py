@@ -85,6 +85,10 @@ def ref() -> ctypes.CDLL:
         lib.ref_dequantize_int8_blocks.argtypes = [_vp, ctypes.c_longlong, _vp]
         lib.ref_sampler_argmax.argtypes = [_vp, _vp, ctypes.c_longlong]
         lib.ref_mt19937_raw.argtypes = [ctypes.c_uint, ctypes.c_int, _vp]
+        lib.ref_sampler_sample.argtypes = [_vp, _vp, ctypes.c_longlong, ctypes.c_float, ctypes.c_int, ctypes.c_float,
+                                           ctypes.c_ulonglong, ctypes.c_int, _vp]
+        lib.ref_sampler_sample_at.argtypes = [_vp, ctypes.c_longlong, ctypes.c_float, ctypes.c_int, ctypes.c_float,
+                                              ctypes.c_ulonglong, ctypes.c_int, _vp]
         _ref = lib
     return _ref
 
@@ -218,3 +222,23 @@ def greedy_reference(shape, tensors, prompt, count, precision="double", eos=-1, 
             break
     model.close()
     return (tokens, margins) if with_margins else tokens
+
+
+def ref_sample(logits, mask, temperature, top_k, top_p, seed, draws):
+    """The reference's own Sampler (Sampler.cpp:78-215): `draws` tokens from one row."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    mask = None if mask is None else np.ascontiguousarray(mask, dtype=np.float32)
+    out = np.zeros(draws, dtype=np.int32)
+    rc = ref().ref_sampler_sample(p(logits), p(mask) if mask is not None else None, logits.size, temperature, top_k,
+                                  top_p, seed, draws, p(out))
+    assert rc == 0, "the reference refused the sampling options"
+    return out.astype(np.uint32)
+
+
+def ref_sample_at(logits, temperature, top_k, top_p, seed, skip):
+    """The reference Sampler's draw from `logits` after `skip` earlier draws."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    out = np.zeros(1, dtype=np.int32)
+    rc = ref().ref_sampler_sample_at(p(logits), logits.size, temperature, top_k, top_p, seed, skip, p(out))
+    assert rc == 0
+    return int(out[0])
