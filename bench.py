@@ -9,6 +9,8 @@ Every rank decodes its own sequence on its own GPU (independent replicas, no
 collective on the data path; weak scaling), and `value` is the whole-job
 tok/s: the tokens all ranks decoded over the max-over-ranks device time.
 
+The `prefill` object is configs[4]: eight 2048-token seeded prompts (seed 4)
+prefilled one after another, device-timed, against the tensor-core roofline.
 The `long_context` object is configs[2]: an 8,064-token seeded prompt, then
 the 128 decode steps to an 8,192-position window, device-timed. The metric's
 second half, b=64/GPU, is the `batched` object of the same line: each rank decodes 64 independent sequences (512-token seeded
@@ -55,6 +57,11 @@ BATCH_WORKLOAD = "config3: 64 independent sequences per GPU, 512-token seeded pr
 LONG_PROMPT = 8064        # configs[2]: prompt tokens, then decode to an 8,192-position window
 LONG_SEED = 2
 LONG_WORKLOAD = "config2: Gemma-2B batch-1 prefill of 8064 seeded ids (seed 2), greedy decode to 8192 positions"
+PREFILL_SEQUENCES = 8     # configs[4]: 8 x 2048-token prompts
+PREFILL_PROMPT = 2048
+PREFILL_SEED = 4
+PREFILL_WORKLOAD = ("config4: Gemma-2B prefill of 8 independent 2048-token seeded prompts (seed 4), one after another "
+                    "through one context on the tcgen05 products")
 
 
 def measured_peaks():
@@ -64,6 +71,24 @@ def measured_peaks():
             peaks = json.load(f)
         return float(peaks["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def prefill_flops(shape, prompt: int) -> float:
+    """Algorithmic FLOPs of one prompt's prefill: 2 per multiply-add of every
+    linear weight for every row, causal attention (q.k and p.v over the
+    prefix), and the last row's logits (only the last row is sampled)."""
+    q, kv = shape.heads * shape.head_width, shape.kv_heads * shape.head_width
+    linear = shape.width * (q + 2 * kv) + q * shape.width + 3 * shape.width * shape.intermediate
+    attention = 2 * 2 * shape.heads * shape.head_width * prompt * (prompt + 1) / 2
+    return shape.layers * (2.0 * prompt * linear + attention) + 2.0 * shape.width * shape.vocab
+
+
+def measured_tensor_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (cuBLAS bf16, burst)"
+    return 1590.0, "fallback"
 
 
 def committed_traffic():
@@ -342,6 +367,37 @@ def run_ours(args):
                      "peak_kind": peak_kind, "note": "weights + the step's K/V reads at 8065..8191 keys"},
     }
 
+    # ---- prefill throughput: 8 x 2048-token prompts, device-timed
+    prefill_prompts = [native.synthetic_tokens(PREFILL_SEED + q, PREFILL_PROMPT, shape.vocab)
+                       for q in range(PREFILL_SEQUENCES)]
+    barrier()
+    torch.cuda.synchronize()
+    f_start, f_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f_start.record(stream)
+    for prompt_q in prefill_prompts:
+        ctx.begin_sequence()
+        ctx.prefill_async(prompt_q)
+    f_stop.record(stream)
+    ctx.sync()
+    prefill_run_ms = f_start.elapsed_time(f_stop)
+    barrier()
+    if dist:
+        t = torch.tensor([prefill_run_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        prefill_run_ms = float(t[0].item())
+    tensor_peak, tensor_peak_kind = measured_tensor_peak()
+    flops = PREFILL_SEQUENCES * prefill_flops(shape, PREFILL_PROMPT)
+    tflops = world * flops / (prefill_run_ms * 1e9)
+    prefill = {
+        "workload": PREFILL_WORKLOAD, "value": world * PREFILL_SEQUENCES * PREFILL_PROMPT / (prefill_run_ms / 1000.0),
+        "unit": "tok/s", "n_gpus": world, "ms": prefill_run_ms, "scaling": "weak",
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": tensor_peak, "unit": "TFLOP/s",
+                     "frac": tflops / tensor_peak, "peak_kind": tensor_peak_kind,
+                     "algorithmic_flops_per_gpu": flops,
+                     "note": "2 FLOPs per weight multiply-add of every row, causal attention, last-row logits; each "
+                             "Q8_0 product runs as three exact f16 tensor-core products"},
+    }
+
     # ---- roofline of every decode kernel, live (cycling layers: HBM, not L2)
     ctx.begin_sequence()
     ctx.prefill_async(prompt)
@@ -387,6 +443,7 @@ def run_ours(args):
         "e2e": e2e,
         "batched": batched,
         "long_context": long_context,
+        "prefill": prefill,
         "gpu_launches": launches,
         "decode_path": {0: "generic", 1: "graph", 2: "persistent"}[path],
         "clocks": clocks.summary(),

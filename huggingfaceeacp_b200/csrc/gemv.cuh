@@ -75,6 +75,10 @@ struct GemvArgs
     // QkvRope of a batched decode step: row m of x is sequence m, whose cache
     // rows start at k_cache / v_cache + m * cache_seq_stride. 0: one sequence.
     size_t cache_seq_stride;
+    // GeGLU of the whole-loop kernel: the activation entries also land in
+    // act_local[unit - act_base] (shared memory), or act_local is null.
+    float* act_local;
+    int act_base;
 };
 
 __device__ __forceinline__ unsigned step_position(const GemvArgs& a)

@@ -69,6 +69,7 @@ struct Q8
     uint8_t* base = nullptr;
     uint8_t* records = nullptr; // the stage-record copy the whole-loop kernel streams, or null
     uint8_t* tc = nullptr;      // the tensor-core product's weight blocks (build_tc_blocks), or null
+    uint8_t* slices = nullptr;  // down only: the whole-loop kernel's K-split copy (build_down_slices), or null
     int rows = 0;
     int cols = 0;
     const __half* scales() const { return reinterpret_cast<const __half*>(base + (size_t) rows * cols); }
@@ -284,6 +285,8 @@ struct hf_ctx
 
     uint8_t* pool = nullptr;
     uint8_t* record_pool = nullptr; // stage records of every Q8 weight (the whole-loop kernel's copy)
+    uint8_t* slice_pool = nullptr;  // every layer's down matrix as K-split slices (the whole-loop kernel's)
+    unsigned long long* down_acc = nullptr; // [2][width] the whole-loop kernel's fixed-point down sums
     uint8_t* tc_pool = nullptr;     // tensor-core weight blocks of every Q8 weight
     __half* tc_x = nullptr;         // a product input's fp16 pieces
     float* tc_xunscale = nullptr;   // their per-row powers of two
@@ -606,6 +609,7 @@ struct hf_ctx
         p.exit_ticket = exit_ticket();
         p.steps = steps;
         p.gate_point = gate_point;
+        p.down_acc = down_acc;
         p.trace = trace;
         cudaLaunchConfig_t config = {};
         config.gridDim = dim3(persistent_grid());
@@ -1321,12 +1325,28 @@ int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** ou
                 place(L.down);
             }
         }
+        // The whole-loop kernel's down product runs split over K (each CTA on
+        // 3 or 4 of the activation's 32-entry blocks, build_down_slices): it
+        // needs the 2048-wide model and between I / 128 and I / 32 SMs.
+        const int act_blocks = (int) (I / kBlock);
+        const bool split_down = W == (size_t) kDownRows && ctx->sms <= act_blocks
+                                && (act_blocks + ctx->sms - 1) / ctx->sms <= kMaxActBlocks;
+        if (split_down)
+        {
+            const size_t slice_bytes = (size_t) (W / kSliceRows) * act_blocks * kSliceUnitBytes;
+            if (ctx->cuda(cudaMalloc(&ctx->slice_pool, slice_bytes * s.layers), "down slices")
+                || device_alloc(ctx, &ctx->down_acc, 2 * (size_t) W, "down sums")
+                || ctx->cuda(cudaMemset(ctx->down_acc, 0, 2 * (size_t) W * sizeof(unsigned long long)), "down sums"))
+                return bail(HF_E_CUDA);
+            for (int l = 0; l < s.layers; ++l)
+                ctx->layers[l].down.slices = ctx->slice_pool + (size_t) l * slice_bytes;
+        }
         std::vector<LayerDev> table(s.layers);
         for (int l = 0; l < s.layers; ++l)
         {
             const Layer& L = ctx->layers[l];
             table[l] = {L.qkv.records, L.o.records, L.gu.records, L.down.records, L.in_norm, L.post_norm,
-                        ctx->layer_k(l), ctx->layer_v(l)};
+                        ctx->layer_k(l), ctx->layer_v(l), L.down.slices};
         }
         if (device_alloc(ctx, &ctx->layer_dev, table.size(), "layer table")
             || ctx->cuda(cudaMemcpy(ctx->layer_dev, table.data(), table.size() * sizeof(LayerDev), cudaMemcpyHostToDevice),
@@ -1336,7 +1356,7 @@ int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** ou
         cudaDeviceGetAttribute(&cooperative, cudaDevAttrCooperativeLaunch, device);
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, decode_persistent<kPersistentStages>, kPThreads,
                                                       persistent_smem<kPersistentStages>());
-        ctx->persistent_ok = cooperative && resident >= 1;
+        ctx->persistent_ok = cooperative && resident >= 1 && split_down;
     }
     if (cudaDeviceSynchronize() != cudaSuccess)
         return bail(HF_E_CUDA);
@@ -1392,7 +1412,7 @@ void hf_cuda_destroy(hf_ctx* ctx)
         cudaStreamSynchronize(ctx->stream);
     for (auto& g: ctx->graphs)
         cudaGraphExecDestroy(g.second);
-    void* buffers[] = {ctx->pool, ctx->record_pool, ctx->tc_pool, ctx->tc_x, ctx->tc_xunscale, ctx->tc_ws, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
+    void* buffers[] = {ctx->pool, ctx->record_pool, ctx->slice_pool, ctx->down_acc, ctx->tc_pool, ctx->tc_x, ctx->tc_xunscale, ctx->tc_ws, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
                        ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slot_base, ctx->state,
                        ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev,
                        ctx->sample_uniforms, ctx->sample_mask};
@@ -1468,6 +1488,12 @@ int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, 
         build_records<<<(target->rows / 16) * (target->cols / 2048), 256>>>(target->base, target->rows,
                                                                             target->cols, target->records);
         rc = ctx->cuda(cudaDeviceSynchronize(), "record build");
+    }
+    if (!rc && target->slices)
+    {
+        build_down_slices<<<(target->rows / kSliceRows) * (target->cols / kBlock), 256>>>(target->base, target->rows,
+                                                                                          target->cols, target->slices);
+        rc = ctx->cuda(cudaDeviceSynchronize(), "down slice build");
     }
     if (!rc && target->tc)
     {

@@ -219,7 +219,12 @@ __device__ bool consume_tiles(const GemvArgs& a, Slab slab, const Ring& ring, un
                 if constexpr (E == Epi::QkvRope)
                     qkv_pair_store(a, unit, v0, v1, position, 0);
                 else
-                    a.out[unit] = tanh_gelu(v0) * v1;
+                {
+                    const float value = tanh_gelu(v0) * v1;
+                    a.out[unit] = value;
+                    if (a.act_local)
+                        a.act_local[unit - a.act_base] = value;
+                }
             }
         }
         else if (lane < kTileRows)

@@ -259,6 +259,35 @@ __global__ void __launch_bounds__(256) build_records(const uint8_t* src, int row
     }
 }
 
+// The persistent decode's down product is split over K: each CTA multiplies
+// the activation blocks it produced by the matching columns of every row
+// (persistent.cuh, consume_down_slices). This copy of the down matrix (rows x
+// K in device layout) is laid out for that as units (g, kb) of 8,704 bytes,
+// stored [g][kb], for each 256-row group g and 32-column k-block kb: the 16
+// row tiles' quants, tile t at t * 512 as the k-block's two 16-byte halves
+// (half h at h * 256, row r of the tile at r * 16), then the 256 fp16 scales
+// in row order. A CTA's blocks [b0, b1) of group g are one contiguous record.
+constexpr int kSliceRows = 256;
+constexpr int kSliceUnitBytes = kSliceRows * 32 + kSliceRows * 2; // 8,704
+__global__ void __launch_bounds__(256) build_down_slices(const uint8_t* src, int rows, int K, uint8_t* dst)
+{
+    const int kblocks = K / kBlock;
+    const int g = blockIdx.x / kblocks, kb = blockIdx.x % kblocks;
+    if ((g + 1) * kSliceRows > rows)
+        return;
+    uint8_t* unit = dst + (size_t) blockIdx.x * kSliceUnitBytes;
+    for (int i = threadIdx.x; i < kSliceRows * 2; i += blockDim.x)
+    {
+        const int rr = i >> 1, h = i & 1, t = rr >> 4, r = rr & 15;
+        *reinterpret_cast<uint4*>(unit + t * 512 + h * 256 + r * 16) =
+            *reinterpret_cast<const uint4*>(src + (size_t) (g * kSliceRows + rr) * K + kb * kBlock + h * 16);
+    }
+    const __half* ss = reinterpret_cast<const __half*>(src + (size_t) rows * K);
+    __half* ds = reinterpret_cast<__half*>(unit + kSliceRows * 32);
+    for (int i = threadIdx.x; i < kSliceRows; i += blockDim.x)
+        ds[i] = ss[(size_t) (g * kSliceRows + i) * kblocks + kb];
+}
+
 // Int8Blocks.cpp:114-136 on the device, one warp per block of 32: the same
 // fp16 round-to-nearest-even scale and the same double division with
 // ties-to-even rounding, so the bytes equal the host quantizer's.

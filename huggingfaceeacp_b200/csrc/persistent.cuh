@@ -15,8 +15,16 @@
 //   embed (every CTA, locally) | per layer: q/k/v + RoPE + cache write |
 //   attention (one CTA per 16-key context split, a group per four heads) |
 //   [split merge, long contexts only] | o_proj + residual (short contexts fold
-//   the splits while staging x) | gate/up + GeGLU | down + residual | then
-//   logits + argmax (ticket fold writes the next token's slot)
+//   the splits while staging x) | gate/up + GeGLU on the CTA's own activation
+//   blocks, then down over those blocks (split over K, summed in fixed point)
+//   | then logits + argmax (ticket fold writes the next token's slot)
+//
+// The down product needs no phase of its own: a CTA that produced activation
+// blocks [b0, b1) multiplies them by the same columns of every down row
+// (build_down_slices) and adds each row's partial, as an integer multiple of
+// 2^-32, into a fixed-point accumulator. Integer sums do not depend on the
+// order the CTAs' additions land in, so the result is deterministic; the next
+// phase adds the accumulator to the residual stream while staging its input.
 //
 // Every cross-CTA read goes through L2 (ld.global.cg / cp.async.cg): an SM's L1
 // may hold lines of an activation from an earlier phase. Small values that
@@ -52,8 +60,8 @@ enum : unsigned
 };
 constexpr unsigned kErrAbort = kErrWaitTimeout | kErrBarrierTimeout; // a wait gave up: every CTA leaves
 
-// A layer's weights as stage records (build_records): 16 rows x 2048 columns
-// each; the down matrix's tiles in eight column chunks.
+// A layer's weights as stage records (build_records: 16 rows x 2048 columns
+// each), and the down matrix as K-split slices (build_down_slices).
 struct LayerDev
 {
     const uint8_t* qkv;
@@ -64,6 +72,7 @@ struct LayerDev
     const float* post_norm;
     float* k_cache;
     float* v_cache;
+    const uint8_t* down_slices;
 };
 
 struct PersistentArgs
@@ -98,6 +107,7 @@ struct PersistentArgs
     int gate_point;            // where a layer's gate/up records are released: 0 never held, 1 after the
                                // attention phase, 2 after the o_proj staging
     unsigned long long* trace; // [gridDim.x][kTraceEvents] first-step phase stamps, or null
+    unsigned long long* down_acc; // [2][2048] the down sums in units of 2^-32, by layer parity
 };
 
 // Phase tracing: thread 0 of every CTA stamps %globaltimer (ns) into fixed
@@ -126,7 +136,7 @@ enum TraceEvent : int
     kTrGuStaged,
     kTrGuLimbs,
     kTrGuDone,
-    kTrGuLeft,
+    kTrGuLeft,        // (not stamped: no barrier between gate/up and down)
     kTrDownStaged,    // limb form of the activation, eight chunks
     kTrDownDone,
     kTrDownLeft,
@@ -557,92 +567,141 @@ __device__ void attend_split(const PersistentArgs& p, const LayerDev& L, unsigne
     }
 }
 
-// ---- down + residual ---------------------------------------------------------
-// The down matrix streams as (16-row tile, 2048-column chunk) records, a
-// tile's eight chunks consecutive, on the limb MMA like the other products. A
-// CTA owns whole tiles (one or none at Gemma's sizes); the activation (16384
-// values) is put into the limb form chunk by chunk: eight fragment sets
-// (64 KiB, in the attention area) and their k-block factors.
-constexpr int kDownChunks = 8;
-
-__device__ __forceinline__ void stage_down_limbs(const float* act, uint2* frags8, float* xexp8, int tid)
+// ---- gate/up + GeGLU + down, split over the activation ---------------------
+// CTA c owns the activation's 32-entry blocks [n c / ctas, n (c + 1) / ctas)
+// (n = intermediate / 32; 3 or 4 blocks on 148 SMs): the four 16-row gate/up
+// tiles that produce each block, and the down product over those blocks.
+struct Blocks
 {
-    float4 v[kDownChunks];
-#pragma unroll
-    for (int c = 0; c < kDownChunks; ++c)
-        v[c] = __ldcg(reinterpret_cast<const float4*>(act) + c * 512 + tid);
-#pragma unroll
-    for (int c = 0; c < kDownChunks; ++c)
-        limbs_from_regs(v[c], frags8 + c * 1024, xexp8 + c * 64, tid);
+    int b0, b1;
+};
+
+__device__ __forceinline__ Blocks act_blocks(int intermediate, int cta, int ctas)
+{
+    const int n = intermediate / kBlock;
+    return Blocks {n * cta / ctas, n * (cta + 1) / ctas};
+}
+
+constexpr int kDownRows = 2048;                        // down outputs (the model width)
+constexpr int kDownRecords = kDownRows / kSliceRows;   // 256-row slice records per CTA and layer
+constexpr int kMaxActBlocks = kRecordBytes / kSliceUnitBytes; // 4: a slice record fits a ring slot
+static_assert(kDownRecords % 2 == 0 && kSliceRows / kTileRows == 2 * 8, "two 16-row tiles per warp");
+
+// The CTA's nb activation blocks (shared memory, act_local) in the limb form:
+// the first warp's lanes 8u .. 8u + 7 take block u (zeros past nb).
+__device__ __forceinline__ void stage_slice_limbs(const float* act_local, int nb, uint2* frags, float* xexp, int tid)
+{
+    if (tid < 32)
+    {
+        const int u = tid >> 3;
+        const float4 v = u < nb ? reinterpret_cast<const float4*>(act_local)[tid] : make_float4(0.f, 0.f, 0.f, 0.f);
+        limbs_from_regs(v, frags, xexp, tid);
+    }
     consumers_sync();
 }
 
-// Drains the CTA's down tiles [r0, r1): the two groups take alternate chunk
-// records, each folds a record's 16 row sums over its warps (red, as
-// consume_tiles does) and adds them to its running sums (`rowsum`, [2][16],
-// zero on entry); at a tile's end the two groups' sums (group 0's first) are
-// added to the residual stream.
+// One row's partial down sum into the accumulator, as an integer multiple of
+// 2^-32 (|partial| < 2^31).
+__device__ __forceinline__ void red_add_fixed(unsigned long long* acc, float v)
+{
+    atomicAdd(acc, (unsigned long long) __float2ll_rn(v * 4294967296.f));
+}
+
+// The residual stream after a down product: hidden plus the accumulated
+// sums, for this thread's four entries.
+__device__ __forceinline__ float4 residual_after_down(const float* hidden, const unsigned long long* acc, int tid)
+{
+    constexpr float kUnit = 2.3283064365386963e-10f; // 2^-32
+    float4 h = __ldcg(reinterpret_cast<const float4*>(hidden) + tid);
+    const longlong2 s01 = __ldcg(reinterpret_cast<const longlong2*>(acc) + 2 * tid);
+    const longlong2 s23 = __ldcg(reinterpret_cast<const longlong2*>(acc) + 2 * tid + 1);
+    h.x += (float) s01.x * kUnit;
+    h.y += (float) s01.y * kUnit;
+    h.z += (float) s23.x * kUnit;
+    h.w += (float) s23.y * kUnit;
+    return h;
+}
+
+// Down, split over K: the CTA's nb activation blocks (their limb form in
+// frags / xexp) against the same columns of all 2,048 rows, streamed as eight
+// 256-row slice records; the two groups take alternate records, each warp two
+// 16-row tiles of a record, on the exact int8 limb MMA. Each row's partial is
+// added into `acc` (red_add_fixed).
 template <int NST>
-__device__ bool consume_down_tiles(const GemvArgs& a, Slab tiles, const Ring& ring, unsigned& seq,
-                                   const uint2* frags8, const float* xexp8, float* red, float* rowsum, int group)
+__device__ bool consume_down_slices(const Ring& ring, unsigned& seq, const uint2* frags, const float* xexp, int nb,
+                                    unsigned long long* acc, unsigned* err, int group)
 {
     const int tid = threadIdx.x, lane = tid & 31, warp = (tid >> 5) & 7;
-    float* gred = red + group * 2 * 8 * kTileRows;
-    bool ok = true;
-    int mine = 0;
-    for (int r0 = tiles.r0; r0 < tiles.r1; r0 += kTileRows)
-    {
-        for (int c = 0; c < kDownChunks; ++c, ++seq)
-        {
-            if ((int) (seq & 1u) != group)
-                continue;
-            const int buf = (int) (seq % NST);
-            if (ok && !mbar_wait(&ring.full[buf], (seq / NST) & 1u))
-            {
-                if (lane == 0)
-                    flag_error(a.err, kErrWaitTimeout);
-                ok = false;
-            }
-            float2 part = make_float2(0.f, 0.f);
-            if (ok)
-            {
-                uint32_t b[8][2];
-                float factor[8];
-                load_limb_frags(frags8 + c * 1024, xexp8 + c * 64, warp, lane, b, factor);
-                part = tile_partial(ring.quants + buf * ring.quant_stride,
-                                    reinterpret_cast<const __half*>(ring.scales + buf * ring.scale_stride), warp, lane,
-                                    b, factor);
-            }
-            __syncwarp();
-            if (lane == 0)
-                mbar_arrive(&ring.empty[buf], 2u);
-            float* r = gred + (mine & 1) * 8 * kTileRows;
-            if ((lane & 3) == 0)
-            {
-                r[warp * kTileRows + (lane >> 2)] = part.x;
-                r[warp * kTileRows + (lane >> 2) + 8] = part.y;
-            }
-            named_sync(2 + group, 256);
-            if (warp == (mine & 7) && lane < kTileRows)
-            {
-                float v = 0.f;
+    const int g = lane >> 2, t = lane & 3;
+    uint32_t b[kMaxActBlocks][2];
+    float factor[kMaxActBlocks];
 #pragma unroll
-                for (int w = 0; w < kConsumerWarps; ++w)
-                    v += r[w * kTileRows + lane];
-                rowsum[group * kTileRows + lane] += v;
-            }
-            ++mine;
-        }
-        consumers_sync(); // both groups' sums are in
-        if (tid < kTileRows)
+    for (int u = 0; u < kMaxActBlocks; ++u)
+    {
+        const uint2 f = g < 4 && u < nb ? frags[u * 16 + lane] : make_uint2(0u, 0u);
+        b[u][0] = f.x;
+        b[u][1] = f.y;
+        factor[u] = xexp[u] * (t == 0 ? 1.f : (t == 1 ? 65536.f : 0.f));
+    }
+    const int m = lane >> 3;                                 // the ldmatrix matrix this lane addresses
+    const int row = (lane & 7) + 8 * (m & 1), half = m >> 1; // its row and 16-byte half of the k-block
+    bool ok = true;
+    for (int r = 0; r < kDownRecords; ++r, ++seq)
+    {
+        if ((int) (seq & 1u) != group)
+            continue;
+        const int buf = (int) (seq % NST);
+        if (ok && !mbar_wait(&ring.full[buf], (seq / NST) & 1u))
         {
-            const float v = rowsum[tid] + rowsum[kTileRows + tid];
-            rowsum[tid] = 0.f;
-            rowsum[kTileRows + tid] = 0.f;
-            if (ok)
-                plain_epilogue(Epi::Residual, v, nullptr, r0 + tid, a.out + r0 + tid);
+            if (lane == 0)
+                flag_error(err, kErrWaitTimeout);
+            ok = false;
         }
-        consumers_sync(); // zeroed before the next tile's sums
+        float sums[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+        if (ok)
+        {
+            const uint8_t* record = ring.quants + buf * ring.quant_stride;
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+            {
+                const int tile = 2 * warp + h;
+                float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+                for (int u = 0; u < kMaxActBlocks; ++u)
+                {
+                    if (u < nb)
+                    {
+                        const uint8_t* unit = record + u * kSliceUnitBytes;
+                        uint32_t a[4];
+                        ldmatrix_x4(a, unit + tile * 512 + half * 256 + row * 16);
+                        int c[4];
+                        mma_s8(c, a, b[u][0], b[u][1]);
+                        const __half* sc = reinterpret_cast<const __half*>(unit + kSliceRows * 32) + tile * kTileRows;
+                        acc0 = fmaf((float) (c[0] + 256 * c[1]), factor[u] * __half2float(sc[g]), acc0);
+                        acc1 = fmaf((float) (c[2] + 256 * c[3]), factor[u] * __half2float(sc[g + 8]), acc1);
+                    }
+                }
+                acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
+                acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 1);
+                acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 2);
+                acc1 += __shfl_xor_sync(0xFFFFFFFFu, acc1, 2);
+                sums[h][0] = acc0;
+                sums[h][1] = acc1;
+            }
+        }
+        __syncwarp();
+        if (lane == 0)
+            mbar_arrive(&ring.empty[buf], 2u);
+        if (ok && t == 0)
+        {
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+            {
+                const int first = r * kSliceRows + (2 * warp + h) * kTileRows + g;
+                red_add_fixed(acc + first, sums[h][0]);
+                red_add_fixed(acc + first + 8, sums[h][1]);
+            }
+        }
     }
     return ok;
 }
@@ -652,10 +711,11 @@ __device__ bool consume_down_tiles(const GemvArgs& a, Slab tiles, const Ring& ri
 // of the schedule is a pure function of k.
 struct Plan
 {
-    Slab slab[5]; // rows of q/k/v, o, gate/up, down, logits
+    Slab slab[5]; // rows of q/k/v, o, gate/up, (down: unused), logits
     int stages[5];
     int per_layer;
     int per_step;
+    Blocks blocks; // the CTA's activation blocks
 };
 
 __device__ __forceinline__ Plan make_plan(const PersistentArgs& p, int cta, int ctas)
@@ -663,20 +723,21 @@ __device__ __forceinline__ Plan make_plan(const PersistentArgs& p, int cta, int 
     Plan plan;
     plan.slab[0] = cta_tiles(p.qkv_rows, cta, ctas);
     plan.slab[1] = cta_tiles(2048, cta, ctas);
-    plan.slab[2] = cta_tiles(2 * p.intermediate, cta, ctas);
-    plan.slab[3] = cta_tiles(2048, cta, ctas); // whole tiles, kDownChunks records each
+    plan.blocks = act_blocks(p.intermediate, cta, ctas);
+    plan.slab[2] = Slab {4 * kTileRows * plan.blocks.b0, 4 * kTileRows * plan.blocks.b1}; // a gate/up pair per row pair
+    plan.slab[3] = Slab {0, 0};
     plan.slab[4] = cta_tiles(p.vocab, cta, ctas);
     for (int i = 0; i < 5; ++i)
-        plan.stages[i] = (plan.slab[i].r1 - plan.slab[i].r0) / kTileRows * (i == 3 ? kDownChunks : 1);
+        plan.stages[i] = i == 3 ? kDownRecords : (plan.slab[i].r1 - plan.slab[i].r0) / kTileRows;
     plan.per_layer = plan.stages[0] + plan.stages[1] + plan.stages[2] + plan.stages[3];
     plan.per_step = p.n_layers * plan.per_layer + plan.stages[4];
     return plan;
 }
 
 // The record stage k of the schedule streams, with its product (0 q/k/v, 1 o,
-// 2 gate/up, 3 down, 4 logits) and its index within the CTA's slab.
+// 2 gate/up, 3 down, 4 logits), its index within the CTA's slab and its size.
 __device__ __forceinline__ const uint8_t* plan_stage(const PersistentArgs& p, const Plan& plan, long long k,
-                                                     int& product, int& index)
+                                                     int& product, int& index, unsigned& bytes)
 {
     int r = (int) (k % plan.per_step);
     product = 4;
@@ -688,13 +749,22 @@ __device__ __forceinline__ const uint8_t* plan_stage(const PersistentArgs& p, co
         product = 0;
         while (r >= plan.stages[product])
             r -= plan.stages[product++];
-        const uint8_t* rs[4] = {L.qkv, L.o, L.gu, L.down};
+        if (product == 3)
+        {
+            // slice record r: units (r, b0) .. (r, b1 - 1), contiguous
+            index = r;
+            const int nb = plan.blocks.b1 - plan.blocks.b0;
+            bytes = (unsigned) (nb * kSliceUnitBytes);
+            return L.down_slices + ((size_t) r * (p.intermediate / kBlock) + plan.blocks.b0) * kSliceUnitBytes;
+        }
+        const uint8_t* rs[3] = {L.qkv, L.o, L.gu};
         records = rs[product];
     }
     else
         r -= p.n_layers * plan.per_layer;
     index = r;
-    const int record = plan.slab[product].r0 / kTileRows * (product == 3 ? kDownChunks : 1) + r;
+    bytes = kRecordBytes;
+    const int record = plan.slab[product].r0 / kTileRows + r;
     return records + (size_t) record * kRecordBytes;
 }
 
@@ -721,7 +791,8 @@ __device__ void persistent_producer(const PersistentArgs& p, const Ring& ring, u
             return;
         }
         int product, index;
-        const uint8_t* record = plan_stage(p, plan, k, product, index);
+        unsigned bytes;
+        const uint8_t* record = plan_stage(p, plan, k, product, index, bytes);
         if (product == 2 && index == 0 && p.gate_point != 0)
         {
             if (!mbar_wait(gate, gates & 1u))
@@ -731,8 +802,8 @@ __device__ void persistent_producer(const PersistentArgs& p, const Ring& ring, u
             }
             ++gates;
         }
-        mbar_expect_tx(&ring.full[b], kRecordBytes);
-        bulk_load(ring.quants + b * kRecordBytes, record, kRecordBytes, &ring.full[b], policy);
+        mbar_expect_tx(&ring.full[b], bytes);
+        bulk_load(ring.quants + b * kRecordBytes, record, bytes, &ring.full[b], policy);
     }
 }
 
@@ -763,9 +834,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
     const Ring ring {smem, smem + kRecordQuants, full, empty, kRecordBytes, kRecordBytes}; // a record per slot
     float* sx = reinterpret_cast<float*>(smem + NST * kRecordBytes); // down: k-block factors, row sums
     uint2* frags = reinterpret_cast<uint2*>(sx + 2048);             // limb B fragments (8 KiB)
-    float* attn_area = sx + 4096; // attention K/V tile and folds; the merge's landing; the down fragments
-    float* down_xexp = sx;        // [kDownChunks][64]
-    float* down_rowsum = sx + kDownChunks * 64; // [2 groups][16]
+    float* attn_area = sx + 4096; // attention K/V tile and folds; the merge's landing; the CTA's activation blocks
 
     const int tid = threadIdx.x;
     if (tid == 0)
@@ -789,8 +858,14 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
         shared_word = *(volatile const unsigned*) p.state;
     consumers_sync();
     const unsigned position0 = shared_word;
-    if (tid < 2 * kTileRows)
-        down_rowsum[tid] = 0.f; // ordered before its first use by the barriers between
+    // The launch's first layer's down sums start from zero (ordered before them
+    // by the barriers between); each later buffer is cleared after its last
+    // read, below.
+    if (cta == ctas - 1)
+    {
+        reinterpret_cast<longlong2*>(p.down_acc)[2 * tid] = make_longlong2(0, 0);
+        reinterpret_cast<longlong2*>(p.down_acc)[2 * tid + 1] = make_longlong2(0, 0);
+    }
     unsigned seq = 0, epoch = 0;
     float4 nw;
 
@@ -801,6 +876,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
     };
     uint32_t bfrag[8][2];
     float bfactor[8];
+    float4 resid = make_float4(0.f, 0.f, 0.f, 0.f); // this thread's four residual-stream entries after a down product
     // x of a K = 2048 product (one float4 per thread) into the limb form, then
     // each warp's B fragments into registers; stamps both points.
     auto stage = [&](float4 v, bool norm, int slot) {
@@ -866,6 +942,9 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
             float best = -INFINITY;
             unsigned best_i = 0xFFFFFFFFu;
             const int ts = 2 + kTraceLayerSlots * l; // this layer's trace slots
+            // layers run so far in this launch: its parity picks the down-sum buffer,
+            // so consecutive layers alternate across step boundaries too
+            const int layer_run = step * p.n_layers + l;
 
             // ---- q/k/v with RMSNorm, RoPE and the cache write
             {
@@ -882,7 +961,11 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
                 a.kv_heads = 1;
                 a.head_dim = p.head_dim;
                 a.err = p.err;
-                stage(l == 0 ? embedded : __ldcg(hidden4 + tid), true, ts + kTrQkvStaged);
+                // the previous layer's down sums join the residual stream (CTA 0
+                // stores it after the barrier: every CTA reads the old one here)
+                if (l > 0)
+                    resid = residual_after_down(p.hidden, p.down_acc + ((layer_run - 1) & 1) * kDownRows, tid);
+                stage(l == 0 ? embedded : resid, true, ts + kTrQkvStaged);
                 consume_tiles<Epi::QkvRope, NST, kPGroups>(a, cta_tiles(p.qkv_rows, cta, ctas), ring, seq, bfrag,
                                                            bfactor, red, position, best, best_i, group, 2 + group);
             }
@@ -890,6 +973,15 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
                 prefetch_split(L, position, cta, splits, attn_area, tid);
             if (!barrier(ts + kTrQkvDone, ts + kTrQkvLeft))
                 return;
+            if (cta == 0 && l > 0)
+                reinterpret_cast<float4*>(p.hidden)[tid] = resid; // read next by o_proj's residual, a barrier on
+            if (cta == ctas - 1)
+            {
+                // every CTA has read the previous layer's sums: clear them for the next layer's down
+                longlong2* z = reinterpret_cast<longlong2*>(p.down_acc + ((layer_run + 1) & 1) * kDownRows);
+                z[2 * tid] = make_longlong2(0, 0);
+                z[2 * tid + 1] = make_longlong2(0, 0);
+            }
 
             // ---- attention: one CTA per context split, all eight heads
             if (cta < splits)
@@ -929,29 +1021,26 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
             if (!barrier(ts + kTrODone, ts + kTrOLeft))
                 return;
 
-            // ---- RMSNorm + gate/up + GeGLU
+            // ---- RMSNorm + gate/up + GeGLU on the CTA's activation blocks, then
+            // down over the same blocks into the fixed-point sums
             {
+                const Blocks blocks = act_blocks(p.intermediate, cta, ctas);
                 GemvArgs a = {};
                 a.N = 2 * p.intermediate;
                 a.out = p.act;
                 a.err = p.err;
+                a.act_local = attn_area;
+                a.act_base = blocks.b0 * kBlock;
                 stage(__ldcg(hidden4 + tid), true, ts + kTrGuStaged);
-                consume_tiles<Epi::GeGLU, NST, kPGroups>(a, cta_tiles(2 * p.intermediate, cta, ctas), ring, seq, bfrag,
-                                                         bfactor, red, position, best, best_i, group, 2 + group);
-            }
-            if (!barrier(ts + kTrGuDone, ts + kTrGuLeft))
-                return;
-
-            // ---- down + residual
-            {
-                GemvArgs a = {};
-                a.N = 2048;
-                a.out = p.hidden;
-                a.err = p.err;
-                stage_down_limbs(p.act, reinterpret_cast<uint2*>(attn_area), down_xexp, tid);
+                consume_tiles<Epi::GeGLU, NST, kPGroups>(a, Slab {4 * kTileRows * blocks.b0, 4 * kTileRows * blocks.b1},
+                                                         ring, seq, bfrag, bfactor, red, position, best, best_i, group,
+                                                         2 + group);
+                stamp(ts + kTrGuDone);
+                consumers_sync(); // the CTA's activation entries are in attn_area
+                const int nb = blocks.b1 - blocks.b0;
+                stage_slice_limbs(attn_area, nb, frags, xexp, tid);
                 stamp(ts + kTrDownStaged);
-                consume_down_tiles<NST>(a, cta_tiles(2048, cta, ctas), ring, seq, reinterpret_cast<const uint2*>(attn_area),
-                                        down_xexp, red, down_rowsum, group);
+                consume_down_slices<NST>(ring, seq, frags, xexp, nb, p.down_acc + (layer_run & 1) * kDownRows, p.err, group);
             }
             load_norm(l + 1 < p.n_layers ? p.layers[l + 1].in_norm : p.final_norm);
             if (!barrier(ts + kTrDownDone, ts + kTrDownLeft))
@@ -973,7 +1062,10 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
             a.err = p.err;
             float best = -INFINITY;
             unsigned best_i = 0xFFFFFFFFu;
-            stage(__ldcg(hidden4 + tid), true, ts + kTrLogitsStaged);
+            // the last layer's down sums complete the residual stream (read back as the step's hidden state)
+            resid = residual_after_down(p.hidden, p.down_acc + ((step * p.n_layers + p.n_layers - 1) & 1) * kDownRows,
+                                        tid);
+            stage(resid, true, ts + kTrLogitsStaged);
             consume_tiles<Epi::Logits, NST, kPGroups>(a, cta_tiles(p.vocab, cta, ctas), ring, seq, bfrag, bfactor, red,
                                                       position, best, best_i, group, 2 + group);
             warp_best(best, best_i);
@@ -981,6 +1073,8 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
         }
         if (!barrier(ts + kTrLogitsDone, ts + kTrLogitsLeft)) // the next step embeds the token just written
             return;
+        if (cta == 0)
+            reinterpret_cast<float4*>(p.hidden)[tid] = resid; // the step's final residual stream (its hidden state)
     }
     };
     run();

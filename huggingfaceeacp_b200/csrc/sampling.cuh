@@ -164,11 +164,10 @@ __global__ void __launch_bounds__(kSampleThreads) sample_row(const SampleArgs a)
         {
             const double total = red_d[0];
             double mass = red_d[1];
-            unsigned token = 0xFFFFFFFFu, last = 0xFFFFFFFFu;
+            unsigned token = 0xFFFFFFFFu;
             for (int i = lo; i < hi; ++i)
                 if (live(i))
                 {
-                    last = (unsigned) i;
                     mass += exp((double) a.logits[i] * inv_t - largest) / total;
                     if (u < mass)
                     {
@@ -184,7 +183,6 @@ __global__ void __launch_bounds__(kSampleThreads) sample_row(const SampleArgs a)
                         token = (unsigned) i;
                         break;
                     }
-                (void) last;
             }
             s_token = token;
         }
