@@ -51,6 +51,7 @@ constexpr int kAttnTileFloats = 2 * kAttnTile * 256;        // the K rows, then 
 constexpr int kAttnFoldFloats = 8 * kAttnHeads * 256 + 2 * 8 * kAttnHeads; // one group's warp fold
 constexpr int kAttnAreaFloats = kPGroups * kAttnFoldFloats; // the tile, then (reusing it) both folds
 static_assert(kAttnAreaFloats >= kAttnTileFloats, "the fold area holds the tile");
+static_assert(kAttnAreaFloats >= 8 * 2048, "the area holds eight splits' attention rows (the fused merge)");
 static_assert(kAttnAreaFloats * 4 >= 8 * kLimbFragBytes, "the attention area holds the down fragments");
 constexpr int kFusedMergeSplits = 8;                        // splits folded inside the o_proj x staging
 constexpr unsigned kBarrierSpinLimit = 1u << 20;
@@ -301,8 +302,7 @@ __device__ __forceinline__ float4 merged_attention(const float* acc, const float
                                                    float* land, float* sml, int tid, Stamp stamp)
 {
     const int head = (4 * tid) >> 8;
-    const int first = min(splits, 4);
-    for (int s = 0; s < first; ++s)
+    for (int s = 0; s < splits; ++s) // every split's rows in one round trip (the landing area holds eight)
         cp_async16(land + s * 2048 + 4 * tid, acc + (size_t) s * heads * 256 + 4 * tid);
     asm volatile("cp.async.commit_group;" ::: "memory");
     if (tid < splits * heads * 2)
@@ -330,17 +330,11 @@ __device__ __forceinline__ float4 merged_attention(const float* acc, const float
 #pragma unroll
     for (int s = 0; s < kFusedMergeSplits; ++s)
     {
-        if (s == 4 && splits > 4)
-        {
-            for (int r = 4; r < splits; ++r)
-                cp_async16(land + (r - 4) * 2048 + 4 * tid, acc + (size_t) r * heads * 256 + 4 * tid);
-            cp_async_wait_all();
-        }
         if (s >= splits || ms[s] == -INFINITY)
             continue;
         const float f = expf(ms[s] - mx);
         sum = fmaf(ls[s], f, sum);
-        const float4 a = *reinterpret_cast<const float4*>(land + (s & 3) * 2048 + 4 * tid);
+        const float4 a = *reinterpret_cast<const float4*>(land + s * 2048 + 4 * tid);
         value.x = fmaf(a.x, f, value.x);
         value.y = fmaf(a.y, f, value.y);
         value.z = fmaf(a.z, f, value.z);
