@@ -36,9 +36,9 @@ def _stale(target, sources):
 
 def build_host(force=False):
     os.makedirs(LIB, exist_ok=True)
-    sources = [os.path.join(PKG, "host", f) for f in ("int8_blocks.cpp", "synthetic.cpp")]
+    sources = [os.path.join(PKG, "host", f) for f in ("int8_blocks.cpp", "synthetic.cpp", "safetensors.cpp")]
     target = os.path.join(LIB, "libhf_host.so")
-    if force or _stale(target, sources + [os.path.join(INCLUDE, "hf_host.h")]):
+    if force or _stale(target, sources + [os.path.join(INCLUDE, "hf_host.h"), os.path.join(PKG, "host", "safetensors.h")]):
         _run(["g++", "-std=c++17", "-O3", "-mf16c", "-fPIC", "-shared", "-pthread", f"-I{INCLUDE}", *sources,
               "-o", target])
     return target
@@ -49,7 +49,7 @@ def build_cuda(force=False):
     csrc = os.path.join(PKG, "csrc")
     sources = [os.path.join(csrc, f) for f in os.listdir(csrc) if f.endswith((".cu", ".cuh"))]
     target = os.path.join(LIB, "libhf_cuda.so")
-    if force or _stale(target, sources + [os.path.join(INCLUDE, "hf_cuda.h")]):
+    if force or _stale(target, sources + [os.path.join(INCLUDE, "hf_cuda.h"), os.path.join(PKG, "host", "safetensors.h")]):
         _run([NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-shared", f"-I{INCLUDE}",
               os.path.join(csrc, "hf_cuda.cu"), "-o", target])
     return target

@@ -24,6 +24,7 @@
 #include "rows_mma.cuh"
 #include "sampling.cuh"
 #include "tc_gemm.cuh"
+#include "../host/safetensors.h"
 
 #include <algorithm>
 #include <cmath>
@@ -1429,7 +1430,10 @@ const char* hf_cuda_last_error(const hf_ctx* ctx)
     return ctx ? ctx->error.c_str() : "no context";
 }
 
-int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, uint64_t byte_count)
+// hf_cuda_upload_q8 for bytes in host or device memory (the copies infer the
+// direction): the checkpoint loader hands it Q8_0 bytes it quantized on the
+// device.
+static int upload_q8_any(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, uint64_t byte_count)
 {
     if (!ctx || !bytes)
         return HF_E_INVALID;
@@ -1461,7 +1465,7 @@ int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, 
 
     int rc;
     if (mode == 0 && dst_row0 == 0 && rows == target->rows)
-        rc = ctx->cuda(cudaMemcpy(target->base, bytes, expected, cudaMemcpyHostToDevice), "weight upload");
+        rc = ctx->cuda(cudaMemcpy(target->base, bytes, expected, cudaMemcpyDefault), "weight upload");
     else
     {
         if (ctx->staging_bytes < expected)
@@ -1474,7 +1478,7 @@ int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, 
                 return HF_E_CUDA;
             ctx->staging_bytes = expected;
         }
-        rc = ctx->cuda(cudaMemcpy(ctx->staging, bytes, expected, cudaMemcpyHostToDevice), "weight upload");
+        rc = ctx->cuda(cudaMemcpy(ctx->staging, bytes, expected, cudaMemcpyDefault), "weight upload");
         if (!rc)
         {
             permute_q8_rows<<<rows, 256>>>(ctx->staging, rows, cols, target->base, target->rows, dst_row0, mode, group);
@@ -1504,6 +1508,11 @@ int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, 
         return rc;
     ctx->loaded[global ? s.layers : layer] |= 1u << tensor;
     return HF_OK;
+}
+
+int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, uint64_t byte_count)
+{
+    return upload_q8_any(ctx, tensor, layer, bytes, byte_count);
 }
 
 int hf_cuda_upload_f32(hf_ctx* ctx, int tensor, int layer, const float* values, uint64_t count)
@@ -2283,3 +2292,179 @@ int hf_cuda_quantize_q8(const float* values, int64_t first, int64_t count, int64
     return cudaGetLastError() == cudaSuccess ? HF_OK : HF_E_CUDA;
 }
 }
+
+// ---- a safetensors checkpoint, quantized on the device ----------------------
+namespace
+{
+// One checkpoint tensor the decoder needs: its name, expected shape and where
+// it goes (tensor id, layer, element offset inside a stacked Q8_0 tensor).
+struct Wanted
+{
+    std::string name;
+    std::vector<int64_t> shape;
+    int tensor, layer;
+    bool q8;
+    int64_t offset = 0, total = 0; // elements before it in its upload, and the upload's elements
+    int part = 0, parts = 1;       // gate (0) and up (1) share one upload
+};
+
+std::string layer_name(int layer, const char* suffix)
+{
+    return "model.layers." + std::to_string(layer) + "." + suffix;
+}
+
+// GemmaTensors.cpp:25-62: every tensor of a Gemma decoder with its shape.
+std::vector<Wanted> gemma_tensors(const hf_shape& s)
+{
+    const int64_t W = s.width, QW = (int64_t) s.heads * s.head_width, KVW = (int64_t) s.kv_heads * s.head_width,
+                  I = s.intermediate, V = s.vocab;
+    std::vector<Wanted> w;
+    w.push_back({"model.embed_tokens.weight", {V, W}, HF_TENSOR_EMBEDDING, 0, true, 0, V * W});
+    for (int l = 0; l < s.layers; ++l)
+    {
+        w.push_back({layer_name(l, "self_attn.q_proj.weight"), {QW, W}, HF_TENSOR_QUERY, l, true, 0, QW * W});
+        w.push_back({layer_name(l, "self_attn.k_proj.weight"), {KVW, W}, HF_TENSOR_KEY, l, true, 0, KVW * W});
+        w.push_back({layer_name(l, "self_attn.v_proj.weight"), {KVW, W}, HF_TENSOR_VALUE, l, true, 0, KVW * W});
+        w.push_back({layer_name(l, "self_attn.o_proj.weight"), {W, QW}, HF_TENSOR_OUTPUT, l, true, 0, W * QW});
+        // gate rows first, then up: the stacked tensor (DecoderWeights.cpp:45-58)
+        w.push_back({layer_name(l, "mlp.gate_proj.weight"), {I, W}, HF_TENSOR_GATE_UP, l, true, 0, 2 * I * W, 0, 2});
+        w.push_back({layer_name(l, "mlp.up_proj.weight"), {I, W}, HF_TENSOR_GATE_UP, l, true, I * W, 2 * I * W, 1, 2});
+        w.push_back({layer_name(l, "mlp.down_proj.weight"), {W, I}, HF_TENSOR_DOWN, l, true, 0, W * I});
+        w.push_back({layer_name(l, "input_layernorm.weight"), {W}, HF_TENSOR_INPUT_NORM, l, false});
+        w.push_back({layer_name(l, "post_attention_layernorm.weight"), {W}, HF_TENSOR_POST_NORM, l, false});
+    }
+    w.push_back({"model.norm.weight", {W}, HF_TENSOR_FINAL_NORM, 0, false});
+    return w;
+}
+
+std::string dims_text(const std::vector<int64_t>& shape)
+{
+    std::string t = "[";
+    for (size_t i = 0; i < shape.size(); ++i)
+        t += (i ? ", " : "") + std::to_string(shape[i]);
+    return t + "]";
+}
+
+// Elements [first, first + count) of a raw checkpoint tensor on the device
+// into the Q8_0 destination at element `at` of `total`.
+cudaError_t launch_quantize(hfst::Dtype dtype, const void* raw, long long at, long long count, long long total,
+                            uint8_t* destination)
+{
+    const dim3 grid((unsigned) ((count / kBlock * 32 + 255) / 256));
+    switch (dtype)
+    {
+    case hfst::Dtype::F32: quantize_q8<<<grid, 256>>>((const float*) raw, at, count, total, destination); break;
+    case hfst::Dtype::F16: quantize_q8<<<grid, 256>>>((const __half*) raw, at, count, total, destination); break;
+    case hfst::Dtype::BF16:
+        quantize_q8<<<grid, 256>>>((const __nv_bfloat16*) raw, at, count, total, destination);
+        break;
+    case hfst::Dtype::F64: quantize_q8<<<grid, 256>>>((const double*) raw, at, count, total, destination); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+} // namespace
+
+extern "C" {
+int hf_cuda_load_safetensors(hf_ctx* ctx, const char* const* shard_paths, int shard_count)
+{
+    if (!ctx || !shard_paths || shard_count <= 0)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    const hf_shape& s = ctx->shape;
+
+    // Open and validate every shard, find every tensor and check its shape
+    // and type before anything is uploaded.
+    std::vector<hfst::File> files;
+    try
+    {
+        for (int i = 0; i < shard_count; ++i)
+        {
+            if (!shard_paths[i])
+                return ctx->fail(HF_E_INVALID, "shard path " + std::to_string(i) + " is null");
+            files.push_back(hfst::File::open(shard_paths[i]));
+        }
+    }
+    catch (const std::exception& e)
+    {
+        return ctx->fail(HF_E_INVALID, e.what());
+    }
+    const std::vector<Wanted> wanted = gemma_tensors(s);
+    std::vector<std::pair<const hfst::File*, const hfst::Tensor*>> found(wanted.size());
+    for (size_t i = 0; i < wanted.size(); ++i)
+    {
+        const Wanted& w = wanted[i];
+        for (const hfst::File& f: files)
+            if (const hfst::Tensor* t = f.find(w.name))
+            {
+                if (found[i].second)
+                    return ctx->fail(HF_E_INVALID, "tensor '" + w.name + "' is in more than one shard");
+                found[i] = {&f, t};
+            }
+        const hfst::Tensor* t = found[i].second;
+        if (!t)
+            return ctx->fail(HF_E_INVALID, "the gemma decoder needs a tensor named '" + w.name
+                                               + "', and the checkpoint has none");
+        if (t->shape != w.shape)
+            return ctx->fail(HF_E_SHAPE, "tensor '" + w.name + "' is " + dims_text(t->shape)
+                                             + ", and the gemma decoder was built for " + dims_text(w.shape));
+        if (!hfst::info_of(t->dtype).is_float)
+            return ctx->fail(HF_E_INVALID, "tensor '" + w.name + "' has type " + hfst::info_of(t->dtype).name
+                                               + ", which is not a float type");
+    }
+
+    // Device staging: a chunk of raw elements and the largest Q8_0 upload.
+    constexpr long long kChunk = 1ll << 25; // elements per copy (a multiple of 32)
+    int64_t largest = 0;
+    for (const Wanted& w: wanted)
+        if (w.q8)
+            largest = std::max(largest, w.total);
+    void* raw = nullptr;
+    uint8_t* q8 = nullptr;
+    int rc = ctx->cuda(cudaMalloc(&raw, (size_t) kChunk * 8), "checkpoint staging");
+    if (!rc)
+        rc = ctx->cuda(cudaMalloc((void**) &q8, (size_t) (largest + largest / 16)), "checkpoint staging");
+
+    for (size_t i = 0; i < wanted.size() && !rc; ++i)
+    {
+        const Wanted& w = wanted[i];
+        const hfst::File& file = *found[i].first;
+        const hfst::Tensor& t = *found[i].second;
+        const uint8_t* data = file.data(t);
+        if (!w.q8)
+        {
+            try
+            {
+                const std::vector<float> values = hfst::widen(file, t);
+                rc = hf_cuda_upload_f32(ctx, w.tensor, w.layer, values.data(), values.size());
+            }
+            catch (const std::exception& e)
+            {
+                rc = ctx->fail(HF_E_INVALID, e.what());
+            }
+            continue;
+        }
+        // Widen and quantize on the device, a chunk at a time, at the tensor's
+        // place in its upload (TensorLoader.cpp:162-184, 299-347).
+        const long long elements = t.elements();
+        const int esize = hfst::info_of(t.dtype).bytes;
+        for (long long first = 0; first < elements && !rc; first += kChunk)
+        {
+            const long long count = std::min(kChunk, elements - first);
+            rc = ctx->cuda(cudaMemcpy(raw, data + first * esize, (size_t) (count * esize), cudaMemcpyHostToDevice),
+                           "checkpoint copy");
+            if (!rc)
+                rc = ctx->cuda(launch_quantize(t.dtype, raw, w.offset + first, count, w.total, q8), "quantize launch");
+        }
+        if (!rc && w.part == w.parts - 1)
+        {
+            rc = ctx->cuda(cudaDeviceSynchronize(), "device quantize");
+            if (!rc)
+                rc = upload_q8_any(ctx, w.tensor, w.layer, q8, (uint64_t) (w.total + w.total / 16));
+        }
+    }
+    cudaFree(raw);
+    cudaFree(q8);
+    return rc;
+}
+} // extern "C"

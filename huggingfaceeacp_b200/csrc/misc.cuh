@@ -3,6 +3,8 @@
 // uploaded weights, and the on-device Q8_0 quantizer.
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 
 namespace hfk
@@ -288,17 +290,39 @@ __global__ void __launch_bounds__(256) build_down_slices(const uint8_t* src, int
         ds[i] = ss[(size_t) (g * kSliceRows + i) * kblocks + kb];
 }
 
+// A checkpoint element widened to float as SafeTensors.cpp:242-280 widens
+// it: F32 as is, F16 and BF16 exactly, F64 rounded to nearest.
+__device__ __forceinline__ float widen_element(float v)
+{
+    return v;
+}
+__device__ __forceinline__ float widen_element(__half v)
+{
+    return __half2float(v);
+}
+__device__ __forceinline__ float widen_element(__nv_bfloat16 v)
+{
+    return __bfloat162float(v);
+}
+__device__ __forceinline__ float widen_element(double v)
+{
+    return __double2float_rn(v);
+}
+
 // Int8Blocks.cpp:114-136 on the device, one warp per block of 32: the same
 // fp16 round-to-nearest-even scale and the same double division with
-// ties-to-even rounding, so the bytes equal the host quantizer's.
-__global__ void __launch_bounds__(256) quantize_q8(const float* values, long long first, long long count,
+// ties-to-even rounding, so the bytes equal the host quantizer's. The values
+// are floats, or a checkpoint's F16 / BF16 / F64 elements widened first
+// (TensorLoader.cpp:162-184 widens, then quantizes).
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_q8(const T* values, long long first, long long count,
                                                     long long element_count, uint8_t* destination)
 {
     const long long block = ((long long) blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (block * kBlock >= count)
         return;
-    const float x = values[block * kBlock + lane];
+    const float x = widen_element(values[block * kBlock + lane]);
     float largest = fabsf(x);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)

@@ -11,6 +11,7 @@ from __future__ import annotations
 import ctypes
 import math
 import os
+import re
 from dataclasses import dataclass
 
 import numpy as np
@@ -177,6 +178,7 @@ def host() -> ctypes.CDLL:
                                             ctypes.c_double, _vp, ctypes.c_int]
         lib.hf_synthetic_tokens.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, _vp]
         lib.hf_host_threads.restype = ctypes.c_int
+        lib.hf_safetensors_describe.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_uint64]
         _host = lib
     return _host
 
@@ -209,6 +211,7 @@ def cuda() -> ctypes.CDLL:
         lib.hf_cuda_last_error.restype = ctypes.c_char_p
         lib.hf_cuda_upload_q8.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_uint64]
         lib.hf_cuda_upload_f32.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_uint64]
+        lib.hf_cuda_load_safetensors.argtypes = [_vp, ctypes.POINTER(ctypes.c_char_p), ctypes.c_int]
         lib.hf_cuda_prepared.argtypes = [_vp]
         lib.hf_cuda_begin_sequence.argtypes = [_vp]
         lib.hf_cuda_position.argtypes = [_vp]
@@ -247,6 +250,32 @@ def _ptr(array: np.ndarray | None):
 
 # ---------------------------------------------------------------------------
 # Q8_0 blocks on the host (Kernels/Int8Blocks.h).
+
+class SafeTensorsError(ValueError):
+    """A safetensors file the reader refuses (hf_safetensors_describe)."""
+
+
+def describe_safetensors(path: str, capacity: int = 1 << 20) -> dict:
+    """The validated header of a safetensors file (hf_safetensors_describe):
+    {"tensors": [(name, dtype, shape, begin, end), ...], "metadata": {...}}."""
+    text = ctypes.create_string_buffer(capacity)
+    rc = host().hf_safetensors_describe(os.fsencode(path), text, capacity)
+    if rc < 0:
+        raise SafeTensorsError(text.value.decode(errors="replace"))
+    def unescape(field):
+        return re.sub(r"\\(.)", lambda m: {"t": "\t", "n": "\n"}.get(m.group(1), m.group(1)), field)
+
+    tensors, metadata = [], {}
+    for line in text.value.decode().split("\n")[:-1]:
+        parts = [unescape(f) for f in line.split("\t")]
+        if parts[0] == "__metadata__":
+            metadata[parts[1]] = parts[2]
+        else:
+            shape = tuple(int(d) for d in parts[2].split(",")) if parts[2] else ()
+            tensors.append((parts[0], parts[1], shape, int(parts[3]), int(parts[4])))
+    assert len(tensors) == rc
+    return {"tensors": tensors, "metadata": metadata}
+
 
 def int8_blocks_byte_count(elements: int) -> int:
     return int(host().hf_int8_blocks_byte_count(elements))
@@ -380,6 +409,13 @@ class Context:
             if keep:
                 kept[(tensor, layer)] = data
         return kept
+
+    def load_safetensors(self, paths):
+        """Every Gemma tensor from a (sharded) safetensors checkpoint, the
+        projection weights quantized on the device (hf_cuda_load_safetensors)."""
+        paths = [paths] if isinstance(paths, (str, os.PathLike)) else list(paths)
+        array = (ctypes.c_char_p * len(paths))(*[os.fsencode(p) for p in paths])
+        self.check(self.lib.hf_cuda_load_safetensors(self.handle, array, len(paths)))
 
     @property
     def prepared(self) -> bool:

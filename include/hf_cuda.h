@@ -87,6 +87,21 @@ const char* hf_cuda_last_error(const hf_ctx* ctx);
  * is exactly hf_int8_blocks_byte_count(rows*cols) for the tensor's shape. */
 int hf_cuda_upload_q8(hf_ctx* ctx, int tensor, int layer, const uint8_t* bytes, uint64_t byte_count);
 int hf_cuda_upload_f32(hf_ctx* ctx, int tensor, int layer, const float* values, uint64_t count);
+/* Replaces HF::DecoderWeights(file, shape, WeightPrecision::Int8Blocks) over a
+ * (possibly sharded) safetensors checkpoint (DecoderWeights.cpp:37-121,
+ * TensorLoader.cpp:162-347, GemmaTensors.cpp:25-62): every Gemma tensor
+ * (model.embed_tokens.weight, model.layers.<l>.self_attn.{q,k,v,o}_proj.weight,
+ * mlp.{gate,up,down}_proj.weight, input_layernorm.weight,
+ * post_attention_layernorm.weight, model.norm.weight) is found in one of the
+ * `shard_count` files, checked against the decoder's shape, and uploaded: the
+ * projection weights' F32 / F16 / BF16 / F64 elements are copied to the device,
+ * widened and quantized there to Q8_0 bytes identical to quantizeInt8Blocks'
+ * (gate and up stacked, gate first), the norms widened to fp32. Every file is
+ * validated and every tensor found and checked before anything is uploaded:
+ * a malformed file, a missing tensor, one present in two shards or a type that
+ * is not a float is HF_E_INVALID, a shape that differs HF_E_SHAPE, with the
+ * reason in hf_cuda_last_error. Allocates device staging for the call. */
+int hf_cuda_load_safetensors(hf_ctx* ctx, const char* const* shard_paths, int shard_count);
 /* 1 when every tensor is loaded (Decoder::requirePrepared), else 0. */
 int hf_cuda_prepared(const hf_ctx* ctx);
 

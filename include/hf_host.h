@@ -61,6 +61,20 @@ int hf_synthetic_tokens(uint64_t seed, int count, int vocab, uint32_t* out);
 /* Number of hardware threads the host offers (what "all host cores" means). */
 int hf_host_threads(void);
 
+/* ---- safetensors checkpoints ---------------------------------------------
+ * Replaces HF::SafeTensors::fromFile + tensors() / metadata()
+ * (Model/SafeTensors.h:100-183, SafeTensors.cpp:300-440): maps `path`,
+ * validates its header as SafeTensors.cpp does (length prefix, JSON object,
+ * dtype / shape / data_offsets present and consistent with the blob) and
+ * writes one line per tensor into `text`, "name<TAB>dtype<TAB>d0,d1,..<TAB>
+ * begin<TAB>end\n" in header order, then one "__metadata__<TAB>key<TAB>
+ * value\n" line per metadata entry, NUL-terminated (a backslash, tab or
+ * newline inside a name, key or value is written as \\, \t or \n). Returns the tensor count;
+ * HF_HOST_EINVAL with the refusal's text in `text` (truncated to fit) for a
+ * file that cannot be read or whose header is malformed; HF_HOST_ESHAPE when
+ * `capacity` is too small for the description. */
+int hf_safetensors_describe(const char* path, char* text, uint64_t capacity);
+
 #ifdef __cplusplus
 }
 #endif
