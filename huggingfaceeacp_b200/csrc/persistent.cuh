@@ -13,7 +13,7 @@
 // barrier:
 //
 //   embed (every CTA, locally) | per layer: q/k/v + RoPE + cache write |
-//   attention (one CTA per 16-key context split, a group per four heads) |
+//   attention (one CTA per context split, a group per four heads) |
 //   [split merge, long contexts only] | o_proj + residual (short contexts fold
 //   the splits while staging x) | gate/up + GeGLU on the CTA's own activation
 //   blocks, then down over those blocks (split over K, summed in fixed point)
@@ -45,12 +45,13 @@ constexpr int kPWarps = kPGroups * kConsumerWarps;          // 16 consumer warps
 constexpr int kPConsumers = kPWarps * 32;                   // 512 consumer threads
 constexpr int kPThreads = kPConsumers + 32;                 // and the producer warp
 constexpr int kAttnTile = 16;                               // keys per attention tile
-constexpr int kAttnKeysPerSplit = kAttnTile;                // context rows per split: one tile
+constexpr int kAttnKeysPerSplit = kAttnTile;                // context rows per split beyond the fused range
+constexpr int kFusedSplitTiles = 4;                         // tiles per split while the splits stay fusable
 constexpr int kAttnHeads = 4;                               // query heads per consumer group
 constexpr int kAttnTileFloats = 2 * kAttnTile * 256;        // the K rows, then the V rows
 constexpr int kAttnFoldFloats = 8 * kAttnHeads * 256 + 2 * 8 * kAttnHeads; // one group's warp fold
 constexpr int kAttnAreaFloats = kPGroups * kAttnFoldFloats; // the tile, then (reusing it) both folds
-static_assert(kAttnAreaFloats >= kAttnTileFloats, "the fold area holds the tile");
+static_assert(kAttnAreaFloats >= 2 * kAttnTileFloats, "the fold area holds two tiles");
 static_assert(kAttnAreaFloats >= 8 * 2048, "the area holds eight splits' attention rows (the fused merge)");
 static_assert(kAttnAreaFloats * 4 >= 8 * kLimbFragBytes, "the attention area holds the down fragments");
 constexpr int kFusedMergeSplits = 8;                        // splits folded inside the o_proj x staging
@@ -220,11 +221,17 @@ __device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch,
     return *abort == 0;
 }
 
-// Context splits of a decode step: one 16-key tile each, one CTA each.
+// Context splits of a decode step, one CTA each. Up to kFusedMergeSplits
+// splits of up to kFusedSplitTiles tiles (512 keys) the o_proj staging folds
+// them in place; past that a merge phase with its own grid barrier does, and
+// the splits are one 16-key tile each (as many as there are CTAs), so the
+// keys spread over as many SMs as possible.
 __device__ __forceinline__ int attention_splits(int keys, int max_splits)
 {
     const int limit = min(max_splits, (int) gridDim.x);
-    const int splits = (keys + kAttnKeysPerSplit - 1) / kAttnKeysPerSplit;
+    int splits = (keys + kAttnKeysPerSplit - 1) / kAttnKeysPerSplit;
+    if (keys <= kFusedMergeSplits * kFusedSplitTiles * kAttnTile)
+        splits = min(splits, kFusedMergeSplits);
     return splits < 1 ? 1 : (splits > limit ? limit : splits);
 }
 
@@ -426,18 +433,34 @@ __device__ void attend_split(const PersistentArgs& p, const LayerDev& L, unsigne
         for (int i = 0; i < 8; ++i)
             acc[h][i] = 0.f;
 
-    const float* tk = area;
-    const float* tv = area + kAttnTile * D;
-    for (int t0 = k0; t0 < k1; t0 += kAttnTile)
-    {
+    // Tiles alternate between two buffers of `area`: tile t + 1 lands while
+    // tile t is scored, and tile t + 2 is requested once tile t is read.
+    const int tiles = (k1 - k0 + kAttnTile - 1) / kAttnTile;
+    auto request = [&](int t) {
+        const int t0 = k0 + t * kAttnTile;
         const int nk = min(kAttnTile, k1 - t0);
         // The first tile's final rows were prefetched before the barrier.
-        const int from = t0 == k0 ? max(k0, min(t0 + nk, (int) position)) : t0;
-        load_kv_rows(L.k_cache, L.v_cache, t0, from, t0 + nk, area, tid);
-        cp_async_wait_all();
+        const int from = t == 0 ? max(k0, min(t0 + nk, (int) position)) : t0;
+        load_kv_rows(L.k_cache, L.v_cache, t0, from, t0 + nk, area + (t & 1) * kAttnTileFloats, tid);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (tiles > 0)
+        request(0);
+    if (tiles > 1)
+        request(1);
+    for (int t = 0; t < tiles; ++t)
+    {
+        const int t0 = k0 + t * kAttnTile;
+        const int nk = min(kAttnTile, k1 - t0);
+        if (t + 1 < tiles)
+            asm volatile("cp.async.wait_group 1;" ::: "memory"); // all but tile t + 1
+        else
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
         consumers_sync();
-        if (t0 == k0)
+        if (t == 0)
             stamp(kTrAttnLoaded);
+        const float* tk = area + (t & 1) * kAttnTileFloats;
+        const float* tv = tk + kAttnTile * D;
 
         float sc[2];
 #pragma unroll
@@ -461,7 +484,7 @@ __device__ void attend_split(const PersistentArgs& p, const LayerDev& L, unsigne
             const float total = transpose_reduce<QH>(part, lane);
             sc[j] = r < nk ? total : -INFINITY;
         }
-        if (t0 == k0)
+        if (t == 0)
             stamp(kTrAttnDots);
         const float m_new = fmaxf(m, fmaxf(sc[0], sc[1]));
         float carried = 1.f, pj[2] = {0.f, 0.f};
@@ -501,6 +524,8 @@ __device__ void attend_split(const PersistentArgs& p, const LayerDev& L, unsigne
                     acc[h][i] = fmaf(ph[h], vv[i], acc[h][i]);
         }
         consumers_sync(); // the tile is read before it is refilled or reused
+        if (t + 2 < tiles)
+            request(t + 2);
     }
     stamp(kTrAttnScored);
 

@@ -259,7 +259,8 @@ MINI_PERSISTENT = MINI.replace(intermediate=16384)
 
 def test_persistent_path_matches_reference_across_context_splits():
     """The whole-loop kernel (one cooperative launch per call) on a shape it
-    serves, token by token across 1, 2, 4 and 8 attention splits."""
+    serves, token by token across 1 to 8 attention splits, past 128 keys
+    eight splits of two and three double-buffered 16-key tiles."""
     p = Pair(MINI_PERSISTENT, seed=13)
     try:
         assert p.ctx.decode_path == native.DECODE_PERSISTENT
@@ -267,6 +268,23 @@ def test_persistent_path_matches_reference_across_context_splits():
         worst = p.step(prompt)
         for i in range(210):
             worst = max(worst, p.step([int(prompt[(7 * i) % 60])]))
+        assert worst <= TOLERANCE, worst
+    finally:
+        p.close()
+
+
+def test_persistent_path_matches_reference_across_the_merge_phase():
+    """Up to 512 keys eight splits of up to four tiles, folded while o_proj
+    stages its input; past 512 one 16-key split per CTA and a merge phase:
+    a 496-token prompt, then token by token from 497 to 536 keys."""
+    shape = MINI_PERSISTENT.replace(max_positions=544, max_step_rows=512)
+    p = Pair(shape, seed=17)
+    try:
+        assert p.ctx.decode_path == native.DECODE_PERSISTENT
+        prompt = native.synthetic_tokens(17, 496, shape.vocab)
+        worst = p.step(prompt)
+        for i in range(40):
+            worst = max(worst, p.step([int(prompt[(5 * i) % 496])]))
         assert worst <= TOLERANCE, worst
     finally:
         p.close()
