@@ -374,6 +374,25 @@ std::vector<TokenId> Gemma::generate(const std::vector<TokenId>& promptTokens)
     const int window = s.maxPositions - promptLength;
     const int limit = maximumTokenCount > 0 ? std::min(maximumTokenCount, window) : window;
 
+    if (samplingOptions.temperature > 0.f)
+    {
+        // Gemma::generateBySampling (Gemma.cpp:545-592): each step's last row
+        // is drawn from on the device into the slot the next step embeds.
+        const hf_sampling options {samplingOptions.temperature, samplingOptions.topK, samplingOptions.topP,
+                                   samplingOptions.seed};
+        std::vector<TokenId> out((std::size_t) std::max(limit, 1));
+        int count = 0;
+        const auto start = Clock::now();
+        check(ctx, hf_cuda_generate_sampled(ctx, promptTokens.data(), promptLength, limit, (int) endOfSequence,
+                                            &options, out.data(), &count));
+        decodeSeconds = seconds(start);
+        out.resize((std::size_t) count);
+        stepCount = count + (count < limit ? 1 : 0); // the end-of-sequence token was produced and dropped
+        for (TokenId t: out)
+            onToken(t);
+        return out;
+    }
+
     const auto prefillStart = Clock::now();
     check(ctx, hf_cuda_prefill_async(ctx, promptTokens.data(), promptLength));
     check(ctx, hf_cuda_sync(ctx));
@@ -416,5 +435,37 @@ std::vector<TokenId> Gemma::generate(const std::vector<TokenId>& promptTokens)
     }
     decodeSeconds = seconds(decodeStart);
     return generated;
+}
+void Gemma::setSampling(SamplingOptions options)
+{
+    samplingOptions = options.validated();
+}
+
+void Gemma::setTokenizer(TokenizerCalls calls)
+{
+    if (!calls.encodeWithBos || !calls.decode)
+        throw ModelError {"a tokenizer needs both its encodeWithBos and its decode call"};
+    tokenizer = std::move(calls);
+}
+
+std::vector<TokenId> Gemma::generateFromText(std::string_view prompt)
+{
+    if (!decoder)
+        throw ModelError {"Gemma::generateFromText before prepare"};
+    if (!hasTokenizer())
+        throw ModelError {"Gemma has no tokenizer: setTokenizer before generating from text"};
+    return generate(tokenizer.encodeWithBos(prompt));
+}
+
+std::string Gemma::generateText(std::string_view prompt)
+{
+    return textForTokens(generateFromText(prompt));
+}
+
+std::string Gemma::textForTokens(const std::vector<TokenId>& tokens) const
+{
+    if (!hasTokenizer())
+        throw ModelError {"Gemma has no tokenizer: setTokenizer before decoding tokens"};
+    return tokenizer.decode(tokens);
 }
 } // namespace HF

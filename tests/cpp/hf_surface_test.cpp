@@ -7,15 +7,22 @@
 // out.bin: int32 step_rows, then the logits of the prompt step's last row and
 // of three single-token steps (float32, 4 x vocab), the hidden row of the last
 // step (float32 x width), the Argmax and Sampler picks of those four rows
-// (uint32 x 8), the generated tokens (int32 count, uint32 x count), and one
-// int32 per refusal the surface must raise (1 = raised).
+// (uint32 x 8), the generated tokens (int32 count, uint32 x count), one int32
+// per refusal the surface must raise (int32 count, then 1 = raised), the
+// tokens of a seeded sampled run (int32 count, uint32 x count), the text of a
+// greedy run from text through a byte tokenizer (int32 length, bytes), and
+// one int32 per sampling option that must be refused (int32 count, 1 = raised).
 #include <HF/Argmax.h>
 #include <HF/Decoder.h>
 #include <HF/Gemma.h>
+#include <HF/Sampling.h>
 
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <string>
+#include <string_view>
 #include <vector>
 
 int main(int argc, char** argv)
@@ -102,6 +109,56 @@ int main(int argc, char** argv)
             return 1;
         }
 
+        // Text through the caller's tokenizer: a byte tokenizer stands in for
+        // the reference's (BOS 2 in front, byte b as token 3 + b; decode drops
+        // the special tokens and writes any other token as <id>).
+        refused([&] { gemma.generateText("hi"); }); // no tokenizer yet
+        gemma.setTokenizer({[](std::string_view text) {
+                                std::vector<HF::TokenId> ids {2u};
+                                for (unsigned char c: text)
+                                    ids.push_back(3u + c);
+                                return ids;
+                            },
+                            [](const std::vector<HF::TokenId>& ids) {
+                                std::string out;
+                                for (HF::TokenId t: ids)
+                                    if (t >= 3u && t < 259u)
+                                        out.push_back((char) (t - 3u));
+                                    else if (t >= 259u)
+                                        out += "<" + std::to_string(t) + ">";
+                                return out;
+                            }});
+        const std::string text = gemma.generateText("hi");
+
+        // Sampling: the reference's refusals, then a seeded run drawn on the
+        // device, twice (every run reseeds), then greedy again.
+        std::vector<int> samplingRefusals;
+        const auto samplingRefused = [&](HF::SamplingOptions o) {
+            try
+            {
+                gemma.setSampling(o);
+                samplingRefusals.push_back(0);
+            }
+            catch (const HF::SamplingError&)
+            {
+                samplingRefusals.push_back(1);
+            }
+        };
+        samplingRefused({-1.f, 0, 1.f, 0});
+        samplingRefused({std::nanf(""), 0, 1.f, 0});
+        samplingRefused({1.f, -1, 1.f, 0});
+        samplingRefused({1.f, 0, 0.f, 0});
+        samplingRefused({1.f, 0, 1.5f, 0});
+        gemma.setSampling({0.8f, 40, 0.9f, 7});
+        const auto sampled = gemma.generate(prompt);
+        const auto sampledAgain = gemma.generate(prompt);
+        gemma.setSampling(HF::SamplingOptions::greedy());
+        if (sampled != sampledAgain || gemma.generate(prompt) != generated || sampled.empty())
+        {
+            std::fprintf(stderr, "Gemma sampling bookkeeping is off\n");
+            return 1;
+        }
+
         FILE* f = std::fopen(argv[1], "wb");
         const int step_rows = shape.maxStepRows;
         std::fwrite(&step_rows, 4, 1, f);
@@ -112,7 +169,15 @@ int main(int argc, char** argv)
         const int count = (int) generated.size();
         std::fwrite(&count, 4, 1, f);
         std::fwrite(generated.data(), 4, generated.size(), f);
-        std::fwrite(refusals.data(), 4, refusals.size(), f);
+        const auto section = [&](const auto& v, std::size_t elementBytes) {
+            const int n = (int) v.size();
+            std::fwrite(&n, 4, 1, f);
+            std::fwrite(v.data(), elementBytes, v.size(), f);
+        };
+        section(refusals, 4);
+        section(sampled, 4);
+        section(text, 1);
+        section(samplingRefusals, 4);
         std::fclose(f);
     }
     catch (const HF::ModelError& e)

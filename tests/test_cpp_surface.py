@@ -1,7 +1,8 @@
-"""The C++ HF surface (include/HF/*.h over libhf.so): HF::Decoder, HF::Gemma,
-HF::Argmax, HF::Sampler and HF::DecoderWeights with the reference's names
+"""The C++ HF surface (include/HF/*.h over libhf.so): HF::Decoder, HF::Gemma
+(greedy, sampled and text generation), HF::Argmax, HF::Sampler,
+HF::SamplingOptions and HF::DecoderWeights with the reference's names
 (Decoder/Decoder.h:72-136, Generation/Gemma.h:65-251, Kernels/Argmax.h:206-257,
-Sampling/Sampler.h:70, Decoder/DecoderWeights.h:53-116), driven by
+Sampling/Sampler.h:20-70, Decoder/DecoderWeights.h:53-116), driven by
 tests/cpp/hf_surface_test.cpp and checked against the Python binding over the
 same engine and the same seeded weights.
 """
@@ -19,6 +20,22 @@ SHAPE = native.DecoderShape(width=2048, heads=8, kv_heads=1, head_width=256, lay
                             max_positions=64, max_step_rows=16, embed_scale=1.0)
 SEED = 31
 PROMPT = [2, 5, 41, 3, 17, 28, 9, 60]
+EOS = 1  # HF::Gemma::endOfSequence (GemmaConfig.h:62)
+
+
+def byte_encode(text: str) -> list[int]:
+    """The test program's stand-in tokenizer: BOS 2, then byte b as token 3 + b."""
+    return [2] + [3 + b for b in text.encode()]
+
+
+def byte_decode(tokens) -> bytes:
+    out = b""
+    for t in (int(v) for v in tokens):
+        if 3 <= t < 259:
+            out += bytes([t - 3])
+        elif t >= 259:
+            out += f"<{t}>".encode()
+    return out
 
 
 @pytest.fixture(scope="module")
@@ -50,9 +67,19 @@ def test_cpp_surface_matches_the_python_binding(program, tmp_path):
     picks = np.frombuffer(raw[at:at + 16], np.uint32)
     host = np.frombuffer(raw[at + 16:at + 32], np.uint32)
     at += 32
-    count = int(np.frombuffer(raw[at:at + 4], np.int32)[0])
-    generated = np.frombuffer(raw[at + 4:at + 4 + 4 * count], np.uint32)
-    refusals = np.frombuffer(raw[at + 4 + 4 * count:], np.int32)
+    def section(dtype, size):
+        nonlocal at
+        n = int(np.frombuffer(raw[at:at + 4], np.int32)[0])
+        values = np.frombuffer(raw[at + 4:at + 4 + size * n], dtype)
+        at += 4 + size * n
+        return values
+
+    generated = section(np.uint32, 4)
+    refusals = section(np.int32, 4)
+    sampled = section(np.uint32, 4)
+    text = section(np.uint8, 1).tobytes()
+    sampling_refusals = section(np.int32, 4)
+    assert at == raw.size
 
     with native.Context(s) as ctx:
         ctx.load_synthetic(seed=SEED)
@@ -64,8 +91,14 @@ def test_cpp_surface_matches_the_python_binding(program, tmp_path):
             expected.append(lg[-1])
         np.testing.assert_array_equal(rows, np.stack(expected))
         np.testing.assert_array_equal(hidden, hd[-1])
-        reference_tokens = ctx.generate(np.array(PROMPT, np.uint32), 12)
+        reference_tokens = ctx.generate(np.array(PROMPT, np.uint32), 12, eos=EOS)
+        text_tokens = ctx.generate(np.array(byte_encode("hi"), np.uint32), 12, eos=EOS)
+        sampled_tokens = ctx.generate_sampled(np.array(PROMPT, np.uint32), 12, 0.8, top_k=40, top_p=0.9, seed=7,
+                                              eos=EOS)
     np.testing.assert_array_equal(picks, [int(np.argmax(r)) for r in rows])
     np.testing.assert_array_equal(host, picks)
     np.testing.assert_array_equal(generated, reference_tokens)
-    assert list(refusals) == [1, 1, 1, 1, 1]
+    assert list(refusals) == [1, 1, 1, 1, 1, 1]
+    assert text == byte_decode(text_tokens)
+    np.testing.assert_array_equal(sampled, sampled_tokens)
+    assert list(sampling_refusals) == [1, 1, 1, 1, 1]
