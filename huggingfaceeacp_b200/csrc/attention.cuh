@@ -38,6 +38,7 @@ struct AttnArgs
     // k_cache / v_cache + r * cache_seq_stride. 0: the rows are consecutive
     // positions of one sequence.
     size_t cache_seq_stride;
+    int rows; // mqa_rows: the step's rows
 };
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src)
@@ -357,6 +358,243 @@ __global__ void __launch_bounds__(256) mqa_merge(const AttnArgs a)
         value = fmaf(a.part_acc[slot * D + d], f, value);
     }
     a.out[(size_t) row * H * D + idx] = value / sum;
+}
+
+// ---- many consecutive rows of one sequence (prefill steps) -----------------
+// mqa_fast gives every row its own CTA, so every row re-reads the whole
+// context from L2 and its scores and values are dot products folded across
+// the warp. mqa_rows gives a CTA kRowsPerCta consecutive rows x the 8 query
+// heads of a kv head: 32 queries share every 32-key K/V tile (double-buffered
+// with cp.async), and both products are register-blocked on fp32 FMAs.
+// Warp w owns the queries 4w .. 4w + 3: row w / 2, heads 4 (w % 2) .. + 3, so
+// a warp's causal limit is uniform.
+//  scores   lane (kb, c), kb = lane >> 2, c = lane & 3: keys 4 kb .. 4 kb + 3 of
+//           the tile for the warp's four queries, over the float4 columns
+//           c, c + 4, ..., c + 60 (quarters interleaved: the eight lanes of a
+//           16-byte phase touch eight distinct bank groups with the 260-float
+//           K stride), then two shuffles sum the quarters;
+//  softmax  online per query (Kernels/MultiQueryAttention.h:138-341): the
+//           tile maximum and sum fold over the lanes' kb bits, old rows are
+//           rescaled by exp(m_old - m_new), keys past the row's position
+//           are left out;
+//  values   lane owns channels [8 lane, 8 lane + 8) of the four queries: per
+//           key four broadcast probabilities and two float4 of the V row.
+// Grid (ceil(M / kRowsPerCta), kv_heads), 256 threads; D = 256, 8 query heads
+// per kv head; rows r are at positions state[0] + r.
+constexpr int kRowsPerCta = 4;
+constexpr int kRowsMinRows = 16;                 // steps of fewer rows keep mqa_fast (one CTA a row)
+constexpr int kRowsTile = 32;                    // keys per tile
+constexpr int kRowsQueries = kRowsPerCta * 8;    // 32 query vectors
+constexpr int kRowsKStride = 260;                // floats per staged K (and q) row
+constexpr int kRowsKFloats = kRowsTile * kRowsKStride;
+constexpr int kRowsVFloats = kRowsTile * 256;
+constexpr int kRowsBufFloats = kRowsKFloats + kRowsVFloats;
+
+constexpr size_t mqa_rows_smem()
+{
+    return ((size_t) kRowsQueries * kRowsKStride + 2 * kRowsBufFloats + 8 * 4 * kRowsTile) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
+{
+    constexpr int D = 256, QH = 8, T = kRowsTile, KS = kRowsKStride;
+    extern __shared__ __align__(16) float sm[];
+    float* sq = sm;                                        // [32][KS] scaled queries
+    float* bufs = sq + kRowsQueries * KS;                  // 2 x {K [T][KS], V [T][D]}
+    float* sp = bufs + 2 * kRowsBufFloats;                 // [8 warps][4 queries][T] probabilities
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int H = a.heads;
+
+    pdl_wait();
+    const int position = (int) *(volatile const unsigned*) a.state;
+    pdl_trigger();
+
+    const int row0 = blockIdx.x * kRowsPerCta;
+    const int rows_here = min(kRowsPerCta, a.rows - row0);
+    const int head0 = blockIdx.y * QH;
+    const int kvw = a.kv_heads * D;
+    const size_t kv_off = (size_t) blockIdx.y * D;
+
+    // ---- the CTA's queries, scaled (the reference scales q before the dot)
+    for (int i = tid; i < kRowsQueries * (D / 4); i += 256)
+    {
+        const int qi = i / (D / 4), c4 = i % (D / 4);
+        const int r = qi / QH, h = qi % QH;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < rows_here)
+        {
+            v = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t) (row0 + r) * H * D + (size_t) (head0 + h) * D) + c4);
+            v.x *= a.scale;
+            v.y *= a.scale;
+            v.z *= a.scale;
+            v.w *= a.scale;
+        }
+        *reinterpret_cast<float4*>(sq + qi * KS + 4 * c4) = v;
+    }
+
+    const int base = position + row0;      // the position of the CTA's first row
+    const int keys = base + rows_here;     // its last row sees keys [0, base + rows_here - 1]
+    const int tiles = (keys + T - 1) / T;
+    auto request = [&](int t) {
+        float* kb = bufs + (t & 1) * kRowsBufFloats;
+        float* vb = kb + kRowsKFloats;
+        const int t0 = t * T, nk = min(T, keys - t0);
+        for (int i = tid; i < nk * (D / 4); i += 256)
+        {
+            const int r = i / (D / 4), c = (i % (D / 4)) * 4;
+            const size_t at = (size_t) (t0 + r) * kvw + kv_off + c;
+            cp_async16(kb + r * KS + c, a.k_cache + at);
+            cp_async16(vb + r * D + c, a.v_cache + at);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    const int wrow = warp >> 1;                    // the warp's row within the CTA
+    const bool active = wrow < rows_here;          // warp-uniform
+    const int limit = base + wrow;                 // its last key
+    const int kb = lane >> 2, quarter = lane & 3;
+    const float* qw = sq + (4 * warp) * KS;        // the warp's four queries
+    float* pw = sp + warp * 4 * T;
+    float m[4], l[4], acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        m[i] = -INFINITY;
+        l[i] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+            acc[i][c] = 0.f;
+    }
+
+    if (tiles > 0)
+        request(0);
+    if (tiles > 1)
+        request(1);
+    for (int t = 0; t < tiles; ++t)
+    {
+        if (t + 1 < tiles)
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        else
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads(); // tile t (and, at t = 0, the queries) visible to every warp
+        const float* kt = bufs + (t & 1) * kRowsBufFloats;
+        const float* vt = kt + kRowsKFloats;
+        const int t0 = t * T, nk = min(T, keys - t0);
+        if (active && t0 <= limit)
+        {
+            // ---- scores of keys 4 kb + j for queries i, this lane's quarter
+            float s[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    s[i][j] = 0.f;
+#pragma unroll 4
+            for (int step = 0; step < D / 16; ++step)
+            {
+                const int col = 4 * (4 * step + quarter);
+                float4 qv[4], kv[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    qv[i] = *reinterpret_cast<const float4*>(qw + i * KS + col);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    kv[j] = *reinterpret_cast<const float4*>(kt + (4 * kb + j) * KS + col);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                    {
+                        s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
+                        s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
+                        s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
+                        s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
+                    }
+            }
+            float carried[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+            {
+                float tile_max = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                {
+                    s[i][j] += __shfl_xor_sync(0xFFFFFFFFu, s[i][j], 1);
+                    s[i][j] += __shfl_xor_sync(0xFFFFFFFFu, s[i][j], 2);
+                    const int key = t0 + 4 * kb + j;
+                    if (key > limit || 4 * kb + j >= nk)
+                        s[i][j] = -INFINITY;
+                    tile_max = fmaxf(tile_max, s[i][j]);
+                }
+                tile_max = fmaxf(tile_max, __shfl_xor_sync(0xFFFFFFFFu, tile_max, 4));
+                tile_max = fmaxf(tile_max, __shfl_xor_sync(0xFFFFFFFFu, tile_max, 8));
+                tile_max = fmaxf(tile_max, __shfl_xor_sync(0xFFFFFFFFu, tile_max, 16));
+                const float m_new = fmaxf(m[i], tile_max); // finite: key t0 <= limit is in the tile
+                carried[i] = expf(m[i] - m_new);            // 0 on the first tile
+                float p[4], sum = 0.f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                {
+                    p[j] = s[i][j] == -INFINITY ? 0.f : expf(s[i][j] - m_new);
+                    sum += p[j];
+                }
+                sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 4);
+                sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 8);
+                sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 16);
+                l[i] = fmaf(l[i], carried[i], sum);
+                m[i] = m_new;
+                if (quarter == i)
+                    *reinterpret_cast<float4*>(pw + i * T + 4 * kb) = make_float4(p[0], p[1], p[2], p[3]);
+            }
+            __syncwarp();
+
+            // ---- values: acc = acc * carried + P V over the tile's keys
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    acc[i][c] *= carried[i];
+            const int last = min(nk, limit - t0 + 1);
+#pragma unroll 4
+            for (int k = 0; k < last; ++k)
+            {
+                const float4 v0 = *reinterpret_cast<const float4*>(vt + k * D + 8 * lane);
+                const float4 v1 = *reinterpret_cast<const float4*>(vt + k * D + 8 * lane + 4);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                {
+                    const float pk = pw[i * T + k];
+                    acc[i][0] = fmaf(pk, v0.x, acc[i][0]);
+                    acc[i][1] = fmaf(pk, v0.y, acc[i][1]);
+                    acc[i][2] = fmaf(pk, v0.z, acc[i][2]);
+                    acc[i][3] = fmaf(pk, v0.w, acc[i][3]);
+                    acc[i][4] = fmaf(pk, v1.x, acc[i][4]);
+                    acc[i][5] = fmaf(pk, v1.y, acc[i][5]);
+                    acc[i][6] = fmaf(pk, v1.z, acc[i][6]);
+                    acc[i][7] = fmaf(pk, v1.w, acc[i][7]);
+                }
+            }
+            __syncwarp(); // the probabilities are read before the next tile rewrites them
+        }
+        __syncthreads(); // every warp is done with buffer t & 1
+        if (t + 2 < tiles)
+            request(t + 2);
+    }
+
+    if (active)
+    {
+        const int row = row0 + wrow;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+        {
+            const int head = head0 + 4 * (warp & 1) + i;
+            float* o = a.out + (size_t) row * H * D + (size_t) head * D + 8 * lane;
+            *reinterpret_cast<float4*>(o) =
+                make_float4(acc[i][0] / l[i], acc[i][1] / l[i], acc[i][2] / l[i], acc[i][3] / l[i]);
+            *reinterpret_cast<float4*>(o + 4) =
+                make_float4(acc[i][4] / l[i], acc[i][5] / l[i], acc[i][6] / l[i], acc[i][7] / l[i]);
+        }
+    }
 }
 
 // Any head width (D % 4 == 0, D <= 256) and any grouping: one CTA per (head,

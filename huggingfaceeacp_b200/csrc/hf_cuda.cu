@@ -134,6 +134,7 @@ void configure_kernels()
     cudaFuncSetAttribute(mqa_fast<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<2>());
     cudaFuncSetAttribute(mqa_fast<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<1>());
     cudaFuncSetAttribute(mqa_generic, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(mqa_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
     cudaFuncSetAttribute(decode_persistent<kPersistentStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int) persistent_smem<kPersistentStages>());
 #define HF_TC_SMEM(E)                                                                                          \
@@ -973,7 +974,14 @@ struct hf_ctx
             at.nsplit = 1;
             at.state = state;
             at.err = err_word();
-            if (fast)
+            if (fast && QH == 8 && rows >= kRowsMinRows)
+            {
+                // many consecutive rows: the K/V tiles shared by a CTA's rows
+                at.rows = rows;
+                e = launch(true, mqa_rows, dim3((unsigned) ((rows + kRowsPerCta - 1) / kRowsPerCta), s.kv_heads),
+                           dim3(256), mqa_rows_smem(), stream, at);
+            }
+            else if (fast)
             {
                 e = launch_attention(QH, dim3(1, s.kv_heads, rows), stream, at);
             }
