@@ -372,13 +372,16 @@ __global__ void __launch_bounds__(256) mqa_merge(const AttnArgs a)
 //           the tile for the warp's four queries, over the float4 columns
 //           c, c + 4, ..., c + 60 (quarters interleaved: the eight lanes of a
 //           16-byte phase touch eight distinct bank groups with the 260-float
-//           K stride), then two shuffles sum the quarters;
+//           K stride; the next step's operands load while a step multiplies),
+//           then two shuffles sum the quarters;
 //  softmax  online per query (Kernels/MultiQueryAttention.h:138-341): the
 //           tile maximum and sum fold over the lanes' kb bits, old rows are
 //           rescaled by exp(m_old - m_new), keys past the row's position
 //           are left out;
-//  values   lane owns channels [8 lane, 8 lane + 8) of the four queries: per
-//           key four broadcast probabilities and two float4 of the V row.
+//  values   lane owns channels [4 lane, 4 lane + 4) and [128 + 4 lane, 132 +
+//           4 lane) of the four queries: per key one broadcast float4 of the
+//           four probabilities (stored key-major) and two float4 of the V row,
+//           each a conflict-free 512-byte run across the warp.
 // Grid (ceil(M / kRowsPerCta), kv_heads), 256 threads; D = 256, 8 query heads
 // per kv head; rows r are at positions state[0] + r.
 constexpr int kRowsPerCta = 4;
@@ -401,7 +404,7 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
     extern __shared__ __align__(16) float sm[];
     float* sq = sm;                                        // [32][KS] scaled queries
     float* bufs = sq + kRowsQueries * KS;                  // 2 x {K [T][KS], V [T][D]}
-    float* sp = bufs + 2 * kRowsBufFloats;                 // [8 warps][4 queries][T] probabilities
+    float* sp = bufs + 2 * kRowsBufFloats;                 // [8 warps][T keys][4 queries] probabilities
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int H = a.heads;
 
@@ -489,26 +492,39 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     s[i][j] = 0.f;
-#pragma unroll 4
+            // operands of step + 1 are loaded while step's products run
+            float4 qv[2][4], kv[2][4];
+            const float* krow = kt + (4 * kb) * KS + 4 * quarter;
+            const float* qrow = qw + 4 * quarter;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+            {
+                qv[0][i] = *reinterpret_cast<const float4*>(qrow + i * KS);
+                kv[0][i] = *reinterpret_cast<const float4*>(krow + i * KS);
+            }
+#pragma unroll
             for (int step = 0; step < D / 16; ++step)
             {
-                const int col = 4 * (4 * step + quarter);
-                float4 qv[4], kv[4];
+                const int cur = step & 1;
+                if (step + 1 < D / 16)
+                {
+                    const int col = 16 * (step + 1);
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    qv[i] = *reinterpret_cast<const float4*>(qw + i * KS + col);
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    kv[j] = *reinterpret_cast<const float4*>(kt + (4 * kb + j) * KS + col);
+                    for (int i = 0; i < 4; ++i)
+                    {
+                        qv[cur ^ 1][i] = *reinterpret_cast<const float4*>(qrow + i * KS + col);
+                        kv[cur ^ 1][i] = *reinterpret_cast<const float4*>(krow + i * KS + col);
+                    }
+                }
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
                     {
-                        s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
-                        s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
-                        s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
-                        s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
+                        s[i][j] = fmaf(qv[cur][i].x, kv[cur][j].x, s[i][j]);
+                        s[i][j] = fmaf(qv[cur][i].y, kv[cur][j].y, s[i][j]);
+                        s[i][j] = fmaf(qv[cur][i].z, kv[cur][j].z, s[i][j]);
+                        s[i][j] = fmaf(qv[cur][i].w, kv[cur][j].w, s[i][j]);
                     }
             }
             float carried[4];
@@ -544,7 +560,9 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
                 l[i] = fmaf(l[i], carried[i], sum);
                 m[i] = m_new;
                 if (quarter == i)
-                    *reinterpret_cast<float4*>(pw + i * T + 4 * kb) = make_float4(p[0], p[1], p[2], p[3]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        pw[(4 * kb + j) * 4 + i] = p[j];
             }
             __syncwarp();
 
@@ -558,12 +576,14 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
 #pragma unroll 4
             for (int k = 0; k < last; ++k)
             {
-                const float4 v0 = *reinterpret_cast<const float4*>(vt + k * D + 8 * lane);
-                const float4 v1 = *reinterpret_cast<const float4*>(vt + k * D + 8 * lane + 4);
+                const float4 v0 = *reinterpret_cast<const float4*>(vt + k * D + 4 * lane);
+                const float4 v1 = *reinterpret_cast<const float4*>(vt + k * D + 128 + 4 * lane);
+                const float4 p4 = *reinterpret_cast<const float4*>(pw + 4 * k);
+                const float pq[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
                 {
-                    const float pk = pw[i * T + k];
+                    const float pk = pq[i];
                     acc[i][0] = fmaf(pk, v0.x, acc[i][0]);
                     acc[i][1] = fmaf(pk, v0.y, acc[i][1]);
                     acc[i][2] = fmaf(pk, v0.z, acc[i][2]);
@@ -588,10 +608,10 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
         for (int i = 0; i < 4; ++i)
         {
             const int head = head0 + 4 * (warp & 1) + i;
-            float* o = a.out + (size_t) row * H * D + (size_t) head * D + 8 * lane;
+            float* o = a.out + (size_t) row * H * D + (size_t) head * D + 4 * lane;
             *reinterpret_cast<float4*>(o) =
                 make_float4(acc[i][0] / l[i], acc[i][1] / l[i], acc[i][2] / l[i], acc[i][3] / l[i]);
-            *reinterpret_cast<float4*>(o + 4) =
+            *reinterpret_cast<float4*>(o + 128) =
                 make_float4(acc[i][4] / l[i], acc[i][5] / l[i], acc[i][6] / l[i], acc[i][7] / l[i]);
         }
     }
