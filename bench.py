@@ -514,6 +514,30 @@ def run_profile_batched(args):
     return 0
 
 
+def run_profile_prefill(args):
+    """A small case of prefill for ncu captures (not a bench line): Gemma-2B's
+    layer and head shapes with 2 layers and a 64,000-token vocabulary, a
+    2048-token seeded prompt (seed 4, config 4's) prefilled twice in 512-row
+    blocks. Per prefill and block the attention launches are one per layer
+    (mqa_rows): `-k regex:mqa_rows -s 2 -c 1` captures block 1 of layer 0
+    (rows 512..1023 over keys up to 1024). Prints the algorithmic FLOPs of that
+    launch (2 per multiply-add of scores and values, causal)."""
+    from huggingfaceeacp_b200 import native
+
+    shape = native.GEMMA_2B.replace(layers=2, vocab=64000, max_step_rows=512, max_positions=2056)
+    prompt = native.synthetic_tokens(4, 2048, shape.vocab)
+    with native.Context(shape) as ctx:
+        ctx.load_synthetic(seed=4)
+        for _ in range(2):
+            ctx.prefill_async(prompt)
+            ctx.sync()
+    pairs = sum(512 + r + 1 for r in range(512))  # (row, key) pairs of block 1
+    flops = pairs * shape.heads * shape.head_width * 2 * 2
+    print(json.dumps({"profile_case": "Gemma-2B shapes, 2 layers, vocab 64000, one 2048-token prompt, 512-row blocks",
+                      "captured_attention_flops": flops}), flush=True)
+    return 0
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--gpus", type=int, default=1)
@@ -524,13 +548,15 @@ def main():
     parser.add_argument("--batched-steps", type=int, default=256,
                         help="batched decode steps timed for the b=64/GPU half of the metric")
     parser.add_argument("--no-cpu-baseline", action="store_true")
-    parser.add_argument("--profile-case", nargs="?", const="decode", choices=["decode", "batched"],
-                        help="run a small ncu capture case instead of the bench: the decode kernel (default) or "
-                             "a batched step's tensor-core products")
+    parser.add_argument("--profile-case", nargs="?", const="decode", choices=["decode", "batched", "prefill"],
+                        help="run a small ncu capture case instead of the bench: the decode kernel (default), "
+                             "a batched step's tensor-core products, or a prompt's prefill")
     args = parser.parse_args()
     args.warmup = max(3, args.warmup)
     if args.profile_case == "batched":
         return run_profile_batched(args)
+    if args.profile_case == "prefill":
+        return run_profile_prefill(args)
     if args.profile_case:
         return run_profile_case(args)
     if args.impl == "reference":
