@@ -52,6 +52,19 @@ def test_surface_compiles_and_links(program):
     assert os.path.exists(program)
 
 
+def test_host_side_refusals(tmp_path):
+    """SamplingOptions refused as the reference's Sampler refuses them, and the
+    text entry points refused without a tokenizer or a prepared decoder: no
+    device is touched (tests/cpp/hf_host_refusals.cpp)."""
+    lib = build.build_cpp_surface()
+    out = str(tmp_path / "hf_host_refusals")
+    subprocess.run(["g++", "-std=c++20", "-O1", f"-I{os.path.join(ROOT, 'include')}",
+                    os.path.join(ROOT, "tests", "cpp", "hf_host_refusals.cpp"), f"-L{os.path.dirname(lib)}", "-lhf",
+                    f"-Wl,-rpath,{os.path.dirname(lib)}", "-o", out], check=True)
+    result = subprocess.run([out], capture_output=True, text=True)
+    assert result.returncode == 0, result.stderr
+
+
 @pytest.mark.gpu
 def test_cpp_surface_matches_the_python_binding(program, tmp_path):
     out = str(tmp_path / "out.bin")
