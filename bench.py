@@ -192,6 +192,19 @@ def cpu_decode_rate(shape, tensors, prompt, steps: int, warmup: int = 1):
     return steps / elapsed, threads, elapsed
 
 
+def max_over_ranks(dist, values, device="cuda"):
+    """The element-wise maximum of `values` over all ranks (every rank gets it):
+    a multi-GPU time is the slowest rank's. Every rank must call it at the same
+    point; `dist` None (one process) returns the values unchanged."""
+    if not dist:
+        return [float(v) for v in values]
+    import torch
+
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t.tolist()]
+
+
 def run_reference(args):
     """--impl reference: the reference's arithmetic on the host cores, same metric and workload."""
     rank = int(os.environ.get("RANK", "0"))
@@ -269,10 +282,7 @@ def run_ours(args):
         torch.cuda.synchronize()
     elapsed_ms = start.elapsed_time(stop)
     barrier()
-    if dist:
-        t = torch.tensor([elapsed_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
+    (elapsed_ms,) = max_over_ranks(dist, [elapsed_ms])
     tokens = ctx.read_slots(first_pos + 1, args.steps)
     ms_per_step = elapsed_ms / args.steps
     value = world * args.steps / (elapsed_ms / 1000.0)
@@ -286,10 +296,7 @@ def run_ours(args):
     e2e_start = time.perf_counter()
     generated = ctx.generate(pinned_prompt, args.steps)
     e2e_s = time.perf_counter() - e2e_start
-    if dist:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    (e2e_s,) = max_over_ranks(dist, [e2e_s])
     e2e = {"value": world * len(generated) / e2e_s, "unit": "tok/s",
            "h2d_bytes_per_step": 4.0 * PROMPT_LENGTH / max(1, len(generated)), "d2h_bytes_per_step": 4,
            "call": "hf_cuda_generate_greedy (prefill + decode, wall clock)"}
@@ -318,10 +325,7 @@ def run_ours(args):
     batch_ms = b_start.elapsed_time(b_stop)
     prefill_ms = p_start.elapsed_time(p_stop)
     barrier()
-    if dist:
-        t = torch.tensor([batch_ms, prefill_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        batch_ms, prefill_ms = float(t[0].item()), float(t[1].item())
+    batch_ms, prefill_ms = max_over_ranks(dist, [batch_ms, prefill_ms])
     batch_tokens = ctx.read_batch_slots(batch_first + 1, min(4, args.batched_steps))
     batch_step_ms = batch_ms / args.batched_steps
     batch_keys = batch_first + args.batched_steps // 2
@@ -353,10 +357,7 @@ def run_ours(args):
     ctx.sync()
     long_prefill_ms, long_decode_ms = l_start.elapsed_time(l_mid), l_mid.elapsed_time(l_stop)
     barrier()
-    if dist:
-        t = torch.tensor([long_prefill_ms, long_decode_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        long_prefill_ms, long_decode_ms = float(t[0].item()), float(t[1].item())
+    long_prefill_ms, long_decode_ms = max_over_ranks(dist, [long_prefill_ms, long_decode_ms])
     long_bytes = sum(native.decode_bytes(shape, LONG_PROMPT + i + 1) for i in range(1, 128))
     long_gbs = long_bytes / (long_decode_ms * 1e6)
     long_context = {
@@ -381,10 +382,7 @@ def run_ours(args):
     ctx.sync()
     prefill_run_ms = f_start.elapsed_time(f_stop)
     barrier()
-    if dist:
-        t = torch.tensor([prefill_run_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        prefill_run_ms = float(t[0].item())
+    (prefill_run_ms,) = max_over_ranks(dist, [prefill_run_ms])
     tensor_peak, tensor_peak_kind = measured_tensor_peak()
     flops = PREFILL_SEQUENCES * prefill_flops(shape, PREFILL_PROMPT)
     tflops = world * flops / (prefill_run_ms * 1e9)
