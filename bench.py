@@ -248,6 +248,9 @@ def run_ours(args):
 
         import torch.distributed as dist
 
+        # NCCL writes its log (its version banner included, at NCCL_DEBUG=WARN or
+        # VERSION) to stdout unless told otherwise; stdout carries the one JSON line.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
 
     def barrier():
