@@ -47,7 +47,7 @@ import numpy as np  # noqa: E402
 
 METRIC = "Gemma-2B Q8_0 decode tok/s (b=1, b=64/GPU) and achieved HBM GB/s vs peak"
 WORKLOAD = "config0: Gemma-2B Q8_0 batch-1 greedy decode, BOS + 15 seeded prompt ids (seed 0)"
-PUBLISHED_TOK_S = 161.6  # the reference's int8-blocks decode, 16 tokens (Apple M4 Max, Metal)
+PUBLISHED_TOK_S = 161.6  # the reference's published int8-blocks decode, 16 tokens (Apple M4 Max, Metal; plan.md:1083)
 PROMPT_LENGTH = 16
 SEED = 0
 BATCH_SEQUENCES = 64      # configs[3]: sequences per GPU

@@ -4,7 +4,7 @@
 # two small shims in oracle/ref_shim (eacp's fp16 helpers, ea_data_structures'
 # Span/Vector), into oracle/_ref/libhf_ref.so. Nothing from the reference is
 # copied into this repository; the output directory is git-ignored.
-# Usage: build_ref.sh [reference-root]   (default /root/reference)
+# Usage: build_ref.sh [reference-root]   (the checkout of the reference project)
 set -e
 here="$(cd "$(dirname "$0")" && pwd)"
 ref="${1:-/root/reference}"
