@@ -68,11 +68,20 @@ def build_cpp_surface(force=False):
     return target
 
 
+def reference_root():
+    """The reference project's checkout that oracle/build_ref.sh compiles from:
+    $HF_REFERENCE_ROOT, else a directory named `reference` beside this
+    repository, else None."""
+    root = os.environ.get("HF_REFERENCE_ROOT") or os.path.join(os.path.dirname(ROOT), "reference")
+    return root if os.path.isdir(os.path.join(root, "Lib", "HuggingFaceEACP")) else None
+
+
 def build_oracle():
     """Test infrastructure: the C oracle, and oracle/_ref when the reference tree is present."""
     _run(["sh", os.path.join(ROOT, "oracle", "build.sh")])
-    if os.path.isdir("/root/reference"):
-        _run(["sh", os.path.join(ROOT, "oracle", "build_ref.sh"), "/root/reference"])
+    ref = reference_root()
+    if ref:
+        _run(["sh", os.path.join(ROOT, "oracle", "build_ref.sh"), ref])
 
 
 def build(force=False, oracle=True):

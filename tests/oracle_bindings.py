@@ -89,6 +89,8 @@ def ref() -> ctypes.CDLL:
                                            ctypes.c_ulonglong, ctypes.c_int, _vp]
         lib.ref_sampler_sample_at.argtypes = [_vp, ctypes.c_longlong, ctypes.c_float, ctypes.c_int, ctypes.c_float,
                                               ctypes.c_ulonglong, ctypes.c_int, _vp]
+        lib.ref_reference_decode.argtypes = [_vp, ctypes.c_float, ctypes.c_double, ctypes.c_float, _vp, ctypes.c_int,
+                                             _vp, ctypes.c_int, _vp, _vp]
         _ref = lib
     return _ref
 
@@ -222,6 +224,80 @@ def greedy_reference(shape, tensors, prompt, count, precision="double", eos=-1, 
             break
     model.close()
     return (tokens, margins) if with_margins else tokens
+
+
+# Raw (unquantized) fp32 tensors of one layer, in the order the reference's
+# ReferenceLayer holds them (Tests/Decoder/ReferenceDecoder.h:18-29).
+REFERENCE_LAYER_ORDER = ("input_norm", "query", "key", "value", "output", "gate", "up", "down", "post_norm")
+
+
+def ref_decode(shape, raw, tokens, quantize=True):
+    """The reference's own referenceDecode (Tests/Decoder/ReferenceDecoder.h:
+    294-375), compiled from the reference tree into oracle/_ref: the whole
+    sequence from position 0 in double. raw = {"embedding", "final_norm",
+    "layers": [{name: fp32 array} per layer]} holds the unquantized weights;
+    quantize takes them through the reference's Int8Blocks round trip first
+    (quantizedReferenceModel, :79-103). Returns (hidden [n, width], logits
+    [n, vocab]) in float64."""
+    tokens = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+    extents = np.array([shape.width, shape.heads, shape.kv_heads, shape.head_width, shape.layers,
+                        shape.intermediate, shape.vocab, shape.max_positions], dtype=np.int32)
+    arrays = [np.ascontiguousarray(raw["embedding"], dtype=np.float32),
+              np.ascontiguousarray(raw["final_norm"], dtype=np.float32)]
+    for layer in raw["layers"]:
+        arrays += [np.ascontiguousarray(layer[name], dtype=np.float32) for name in REFERENCE_LAYER_ORDER]
+    pointers = (_vp * len(arrays))(*[a.ctypes.data for a in arrays])
+    hidden = np.empty((tokens.size, shape.width), dtype=np.float64)
+    logits = np.empty((tokens.size, shape.vocab), dtype=np.float64)
+    rc = ref().ref_reference_decode(p(extents), shape.rms_eps, shape.rope_theta, shape.scale, pointers,
+                                    1 if quantize else 0, p(tokens), tokens.size, p(hidden), p(logits))
+    assert rc == 0, "the reference decode threw"
+    return hidden, logits
+
+
+def q8_model_tensors(raw):
+    """The same raw weights as the engine and the oracle take them: every
+    projection and the embedding quantized (oracle.c's quantizer, pinned to the
+    reference's), gate and up stacked gate first (DecoderWeights.cpp:45-58),
+    norms fp32. Keys are (tensor id, layer) as in native.model_tensors."""
+    from huggingfaceeacp_b200 import native
+
+    out = {(native.EMBEDDING, -1): quantize(raw["embedding"]), (native.FINAL_NORM, -1): raw["final_norm"]}
+    for l, layer in enumerate(raw["layers"]):
+        out[(native.INPUT_NORM, l)] = layer["input_norm"]
+        out[(native.QUERY, l)] = quantize(layer["query"])
+        out[(native.KEY, l)] = quantize(layer["key"])
+        out[(native.VALUE, l)] = quantize(layer["value"])
+        out[(native.OUTPUT, l)] = quantize(layer["output"])
+        out[(native.GATE_UP, l)] = quantize(np.concatenate([layer["gate"], layer["up"]]))
+        out[(native.DOWN, l)] = quantize(layer["down"])
+        out[(native.POST_NORM, l)] = layer["post_norm"]
+    return out
+
+
+def reference_synthetic_raw(shape):
+    """The reference's synthetic checkpoint values (Tests/Decoder/Common.h:
+    179-237): every tensor from spreadValues with seeds counting up from 7100,
+    embedding range 0.2, norms 0.1, projections 1/sqrtf(fan-in)."""
+    seed = [7100]
+
+    def spread(count, value_range):
+        values = spread_values(count, seed[0], value_range)
+        seed[0] += 1
+        return values
+
+    def fan_in(inner):
+        return float(np.float32(1.0) / np.sqrt(np.float32(inner)))
+
+    w, q, kv, f = shape.width, shape.query_width, shape.kv_width, shape.intermediate
+    raw = {"embedding": spread(shape.vocab * w, 0.2), "layers": []}
+    for _ in range(shape.layers):
+        raw["layers"].append({
+            "input_norm": spread(w, 0.1), "query": spread(q * w, fan_in(w)), "key": spread(kv * w, fan_in(w)),
+            "value": spread(kv * w, fan_in(w)), "output": spread(w * q, fan_in(q)), "gate": spread(f * w, fan_in(w)),
+            "up": spread(f * w, fan_in(w)), "down": spread(w * f, fan_in(f)), "post_norm": spread(w, 0.1)})
+    raw["final_norm"] = spread(w, 0.1)
+    return raw
 
 
 def ref_sample(logits, mask, temperature, top_k, top_p, seed, draws):
