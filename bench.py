@@ -84,11 +84,24 @@ def prefill_flops(shape, prompt: int) -> float:
 
 
 def measured_tensor_peak():
+    """The bf16 tensor peak for a region of hundreds of milliseconds: the
+    measured sustained figure (a long cuBLAS loop under the power cap)."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         with open(path) as f:
-            return float(json.load(f)["bf16_tflops"]), "measured (cuBLAS bf16, burst)"
-    return 1590.0, "fallback"
+            peaks = json.load(f)
+        if "bf16_tflops_sustained" in peaks:
+            return float(peaks["bf16_tflops_sustained"]), "measured (cuBLAS bf16, sustained)"
+        return float(peaks["bf16_tflops"]), "measured (cuBLAS bf16, burst)"
+    return 1400.0, "fallback (sustained)"
+
+
+def prefill_roofline(flops_per_gpu: float, ms: float, peak: float, peak_kind: str) -> dict:
+    """Tensor roofline of one GPU's prefill: its own algorithmic FLOPs over the
+    max-over-ranks time, against one GPU's peak (every rank does the same work)."""
+    achieved = flops_per_gpu / (ms * 1e9)
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_kind": peak_kind, "algorithmic_flops_per_gpu": flops_per_gpu}
 
 
 def committed_traffic():
@@ -210,13 +223,16 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    from huggingfaceeacp_b200 import native
+    import oracle_bindings as ob
+    from huggingfaceeacp_b200.native import GEMMA_2B  # a shape description; loads no library
 
-    shape = native.GEMMA_2B
-    tensors = {}
-    for tensor, layer in native.model_tensors(shape):
-        tensors[(tensor, layer)] = native.synthetic_tensor(shape, tensor, layer, SEED)
-    prompt = native.synthetic_tokens(SEED, PROMPT_LENGTH, shape.vocab)
+    # The model and prompt come from oracle.c's restatement of the seeded
+    # generator and quantizer (pinned bit for bit to the product's host
+    # library by tests/test_oracle_generator.py): this arm loads none of the
+    # product's libraries.
+    shape = GEMMA_2B
+    tensors = ob.synthetic_model(shape, SEED)
+    prompt = ob.synthetic_tokens(SEED, PROMPT_LENGTH, shape.vocab)
     rate, threads, elapsed = cpu_decode_rate(shape, tensors, prompt, args.steps, args.warmup)
     sample = f"{args.steps} fp32 decode steps after a {PROMPT_LENGTH}-token prefill and {args.warmup} warm-up steps"
     line = {
@@ -264,7 +280,11 @@ def run_ours(args):
     shape = native.GEMMA_2B.replace(max_step_rows=BATCH_PROMPT, max_positions=window)
     keep = rank == 0 and world == 1 and not args.no_cpu_baseline
     ctx, tensors = build_model(native, shape, keep, BATCH_SEQUENCES)
-    prompt = native.synthetic_tokens(SEED, PROMPT_LENGTH, shape.vocab)
+    # Every rank decodes its own sequences: rank r's batch-1 prompt has seed
+    # SEED + r (rank 0 is config 0's), its batched sequence q is global sequence
+    # r * 64 + q (seed BATCH_SEED + r * 64 + q), its long prompt seed LONG_SEED + r,
+    # its prefill prompt q seed PREFILL_SEED + r * 8 + q.
+    prompt = native.synthetic_tokens(SEED + rank, PROMPT_LENGTH, shape.vocab)
 
     # ---- device-timed decode: K steps with the weights resident
     ctx.prefill_async(prompt)
@@ -305,7 +325,7 @@ def run_ours(args):
            "call": "hf_cuda_generate_greedy (prefill + decode, wall clock)"}
 
     # ---- batched decode: 64 sequences, device-timed batched steps
-    prompts = np.stack([native.synthetic_tokens(BATCH_SEED + q, BATCH_PROMPT, shape.vocab)
+    prompts = np.stack([native.synthetic_tokens(BATCH_SEED + rank * BATCH_SEQUENCES + q, BATCH_PROMPT, shape.vocab)
                         for q in range(BATCH_SEQUENCES)])
     barrier()
     torch.cuda.synchronize()
@@ -347,7 +367,7 @@ def run_ours(args):
     }
 
     # ---- long context: prefill 8064 tokens, decode 128 steps to 8192
-    long_prompt = native.synthetic_tokens(LONG_SEED, LONG_PROMPT, shape.vocab)
+    long_prompt = native.synthetic_tokens(LONG_SEED + rank, LONG_PROMPT, shape.vocab)
     ctx.begin_sequence()
     barrier()
     torch.cuda.synchronize()
@@ -372,7 +392,7 @@ def run_ours(args):
     }
 
     # ---- prefill throughput: 8 x 2048-token prompts, device-timed
-    prefill_prompts = [native.synthetic_tokens(PREFILL_SEED + q, PREFILL_PROMPT, shape.vocab)
+    prefill_prompts = [native.synthetic_tokens(PREFILL_SEED + rank * PREFILL_SEQUENCES + q, PREFILL_PROMPT, shape.vocab)
                        for q in range(PREFILL_SEQUENCES)]
     barrier()
     torch.cuda.synchronize()
@@ -388,15 +408,12 @@ def run_ours(args):
     (prefill_run_ms,) = max_over_ranks(dist, [prefill_run_ms])
     tensor_peak, tensor_peak_kind = measured_tensor_peak()
     flops = PREFILL_SEQUENCES * prefill_flops(shape, PREFILL_PROMPT)
-    tflops = world * flops / (prefill_run_ms * 1e9)
+    prefill_rl = prefill_roofline(flops, prefill_run_ms, tensor_peak, tensor_peak_kind)
+    prefill_rl["note"] = ("per GPU: 2 FLOPs per weight multiply-add of every row, causal attention, last-row logits; "
+                          "each Q8_0 product runs as three exact f16 tensor-core products")
     prefill = {
         "workload": PREFILL_WORKLOAD, "value": world * PREFILL_SEQUENCES * PREFILL_PROMPT / (prefill_run_ms / 1000.0),
-        "unit": "tok/s", "n_gpus": world, "ms": prefill_run_ms, "scaling": "weak",
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": tensor_peak, "unit": "TFLOP/s",
-                     "frac": tflops / tensor_peak, "peak_kind": tensor_peak_kind,
-                     "algorithmic_flops_per_gpu": flops,
-                     "note": "2 FLOPs per weight multiply-add of every row, causal attention, last-row logits; each "
-                             "Q8_0 product runs as three exact f16 tensor-core products"},
+        "unit": "tok/s", "n_gpus": world, "ms": prefill_run_ms, "scaling": "weak", "roofline": prefill_rl,
     }
 
     # ---- roofline of every decode kernel, live (cycling layers: HBM, not L2)
@@ -437,7 +454,9 @@ def run_ours(args):
         "data": "synthetic: random-init Gemma-2B, N(0,0.02) weights quantized to Q8_0, seeded prompt",
         "config": {"workload": WORKLOAD, "batch_per_gpu": 1, "seq_len": first_pos + args.steps,
                    "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (2.66 GB of weights per step)",
-                   "step_bytes": step_bytes},
+                   "step_bytes": step_bytes,
+                   "sequences": "rank r: batch-1 prompt seed 0 + r; batched sequence q is global r*64 + q (seed 3 + "
+                                "r*64 + q); long prompt seed 2 + r; prefill prompt q seed 4 + r*8 + q"},
         "step_roofline": {"achieved": step_bytes / (ms_per_step * 1e6), "peak": peak, "unit": "GB/s",
                           "frac": step_bytes / (ms_per_step * 1e6) / peak},
         "roofline": roofline,

@@ -1724,10 +1724,19 @@ int hf_cuda_argmax_noalloc(const float* logits, const float* mask, int rows, int
     float* cand_values = static_cast<float*>(scratch);
     unsigned* cand_indices = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(scratch)
                                                          + HF_ARGMAX_SCRATCH_CANDIDATES * sizeof(float));
+    // An error already pending on this thread belongs to earlier work: it is
+    // reported before anything is launched and left pending for its owner.
+    if (cudaPeekAtLastError() != cudaSuccess)
+        return HF_E_CUDA;
     cudaStream_t s = (cudaStream_t) stream;
-    argmax_partial<<<dim3(parts, rows), 256, 0, s>>>(logits, row_length, mask, parts, cand_values, cand_indices);
-    argmax_final<<<rows, 32, 0, s>>>(cand_values, cand_indices, parts, rows, indices, nullptr, nullptr, 0);
-    return cudaGetLastError() == cudaSuccess ? HF_OK : HF_E_CUDA;
+    if (launch(false, argmax_partial, dim3(parts, rows), dim3(256), 0, s, logits, row_length, mask, parts,
+               cand_values, cand_indices) != cudaSuccess)
+        return HF_E_CUDA;
+    if (launch(false, argmax_final, dim3(rows), dim3(32), 0, s, (const float*) cand_values,
+               (const unsigned*) cand_indices, parts, rows, (unsigned*) indices, (unsigned*) nullptr,
+               (unsigned*) nullptr, 0) != cudaSuccess)
+        return HF_E_CUDA;
+    return HF_OK;
 }
 
 int hf_cuda_prefill_async(hf_ctx* ctx, const uint32_t* prompt, int prompt_length)

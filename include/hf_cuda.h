@@ -132,9 +132,14 @@ int hf_cuda_argmax(hf_ctx* ctx, const float* logits, const float* mask, int rows
  * rows * ceil(row_length / 2048) (at most 64 per row) must not exceed it, else
  * HF_E_CAPACITY and nothing is launched. The first call on a device looks up
  * that array's address on the current device (make that first call before any
- * stream capture). Every call shares the one array: calls that overlap on the
- * GPU (different streams, or different host threads) race on it. Asynchronous
- * on `stream` (a cudaStream_t, null = the legacy default stream). */
+ * stream capture) and keeps it for the life of the process: it assumes the
+ * device's primary context throughout (the runtime API's own), so neither a
+ * cudaDeviceReset nor a caller-made driver context on that device may come
+ * between calls. Every call shares the one array: calls that overlap on the
+ * GPU (different streams, or different host threads) race on it. A CUDA error
+ * already pending on the calling thread is returned as HF_E_CUDA before
+ * anything is launched and is left pending. Asynchronous on `stream` (a
+ * cudaStream_t, null = the legacy default stream). */
 #define HF_ARGMAX_SCRATCH_CANDIDATES 8192
 int hf_cuda_argmax_noalloc(const float* logits, const float* mask, int rows, int row_length, uint32_t* indices,
                            void* stream);
@@ -199,8 +204,8 @@ int hf_cuda_decode_launches(const hf_ctx* ctx, int steps);
 
 /* Which kernels run a decode step (no reference counterpart; the reference
  * has one kernel sequence): HF_DECODE_PERSISTENT, one cooperative kernel that
- * runs every step of an hf_cuda_decode_async call with 2 resident CTAs per SM
- * and grid barriers between phases (Gemma's MQA grouping and feed-forward);
+ * runs every step of an hf_cuda_decode_async call with one CTA per SM and
+ * grid barriers between phases (Gemma's MQA grouping and feed-forward);
  * HF_DECODE_GRAPH, one CUDA graph of PDL-chained kernels per step (any shape
  * the streaming kernels serve); HF_DECODE_AUTO picks the first that serves
  * the shape. Both compute the same arithmetic. hf_cuda_decode_path reports the
@@ -215,8 +220,8 @@ int hf_cuda_decode_path(const hf_ctx* ctx);
  * (Decoder.cpp:400). A batch context holds `sequences` sequences that share
  * the weights and one position: each has its own token slots and K/V caches
  * ([layer][sequence][position][kv width] fp32). A batched step runs one row
- * per sequence through the multi-row int8 tensor-core products, so the
- * weights stream from HBM once per eight sequences, and every sequence's
+ * per sequence through the multi-row tensor-core products (64 sequences to
+ * one MMA tile), so the weights stream from HBM once per step, and every sequence's
  * tokens equal what hf_cuda_generate_greedy produces for that sequence alone.
  * Refusals: sequences > the step capacity (HF_E_CAPACITY), and shapes the
  * stage records do not serve (HF_E_SHAPE; they need width 2048, 8 query

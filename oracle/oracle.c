@@ -288,6 +288,82 @@ static void parallel_for(int threads, int64_t n, range_fn fn, void* context)
 }
 
 /* ======================================================================== */
+/* The seeded random-init weights and prompts of the BASELINE configs: a
+ * counter-based generator (splitmix64 over (seed, stream, index), Box-Muller
+ * in double), restated so that the CPU baseline builds its model without the
+ * product's host library. tests/test_oracle_generator.py pins it bit for bit
+ * against hf_synthetic_normal / hf_synthetic_tokens. */
+
+static uint64_t splitmix64(uint64_t x)
+{
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+static uint64_t synthetic_key(uint64_t seed, uint64_t stream)
+{
+    return splitmix64(seed ^ splitmix64(stream + 0x632BE59BD9B4E019ull));
+}
+
+uint64_t oracle_synthetic_stream(int tensor, int layer)
+{
+    return ((uint64_t) (uint32_t) tensor << 32) | (uint32_t) (layer + 1);
+}
+
+/* Element pair p: u1 in (0, 1], u2 in [0, 1) from the top 53 bits of two
+ * consecutive counters; radius sqrt(-2 ln u1), angle 2 pi u2. */
+static void synthetic_pair(uint64_t key, int64_t p, double stddev, float* two)
+{
+    const double unit = 1.0 / 9007199254740992.0;
+    const double u1 = (double) ((splitmix64(key + 2 * (uint64_t) p) >> 11) + 1) * unit;
+    const double u2 = (double) (splitmix64(key + 2 * (uint64_t) p + 1) >> 11) * unit;
+    const double radius = sqrt(-2.0 * log(u1));
+    const double angle = 6.283185307179586476925286766559 * u2;
+    two[0] = (float) (stddev * radius * cos(angle));
+    two[1] = (float) (stddev * radius * sin(angle));
+}
+
+typedef struct {
+    uint64_t key;
+    int64_t first_pair;
+    double stddev;
+    float* out;
+} synthetic_job;
+
+static void synthetic_range(void* context, int64_t begin, int64_t end)
+{
+    const synthetic_job* job = (const synthetic_job*) context;
+    for (int64_t p = begin; p < end; ++p) synthetic_pair(job->key, job->first_pair + p, job->stddev, job->out + 2 * p);
+}
+
+int oracle_synthetic_normal(uint64_t seed, uint64_t stream, int64_t first, int64_t count, double stddev, float* out,
+                            int threads)
+{
+    if (!out || first < 0 || count < 0 || first % 2) return -1;
+    synthetic_job job = {synthetic_key(seed, stream), first / 2, stddev, out};
+    const int64_t whole = count / 2;
+    if (threads <= 0) threads = (int) sysconf(_SC_NPROCESSORS_ONLN);
+    parallel_for(whole >= 65536 ? threads : 1, whole, synthetic_range, &job);
+    if (count % 2) {
+        float two[2];
+        synthetic_pair(job.key, job.first_pair + whole, stddev, two);
+        out[count - 1] = two[0];
+    }
+    return 0;
+}
+
+int oracle_synthetic_tokens(uint64_t seed, int count, int vocab, uint32_t* out)
+{
+    if (!out || count < 0 || vocab <= 3) return -1;
+    const uint64_t key = synthetic_key(seed, 0xFFFFFFFFull);
+    for (int i = 0; i < count; ++i)
+        out[i] = i == 0 ? 2u : 3u + (uint32_t) (splitmix64(key + (uint64_t) i) % (uint64_t) (vocab - 3));
+    return 0;
+}
+
+/* ======================================================================== */
 /* The model. */
 
 typedef struct {

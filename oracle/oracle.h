@@ -52,6 +52,15 @@ void oracle_dequantize_int8_blocks(const uint8_t* stored, int64_t element_count,
 void oracle_spread_values(int count, uint32_t seed, float range, float* out);
 void oracle_mt19937_raw(uint32_t seed, int count, uint32_t* out);
 
+/* ---- the BASELINE configs' seeded random-init weights and prompts --------
+ * Counter-based: element pair p of stream (tensor, layer) depends only on
+ * (seed, stream, p). Normal values N(0, stddev); first must be even. Tokens:
+ * BOS = 2, then uniform ids in [3, vocab). threads <= 0 = every core. */
+uint64_t oracle_synthetic_stream(int tensor, int layer);
+int oracle_synthetic_normal(uint64_t seed, uint64_t stream, int64_t first, int64_t count, double stddev,
+                            float* out, int threads);
+int oracle_synthetic_tokens(uint64_t seed, int count, int vocab, uint32_t* out);
+
 /* ---- scalar pieces ------------------------------------------------------- */
 /* Kernels/RoPE.cpp:7-34: angle pos * theta^(-2i/D) in double, stored float. */
 void oracle_rotary_table(int max_positions, int head_dim, double theta,

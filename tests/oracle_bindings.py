@@ -65,6 +65,11 @@ def oracle() -> ctypes.CDLL:
         lib.oracle_position.argtypes = [_vp]
         lib.oracle_threads.argtypes = [_vp]
         lib.oracle_step.argtypes = [_vp, _vp, ctypes.c_int, _vp, _vp, ctypes.c_int]
+        lib.oracle_synthetic_stream.restype = ctypes.c_uint64
+        lib.oracle_synthetic_stream.argtypes = [ctypes.c_int, ctypes.c_int]
+        lib.oracle_synthetic_normal.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64,
+                                                ctypes.c_double, _vp, ctypes.c_int]
+        lib.oracle_synthetic_tokens.argtypes = [ctypes.c_uint64, ctypes.c_int, ctypes.c_int, _vp]
         _oracle = lib
     return _oracle
 
@@ -115,6 +120,25 @@ def quantize(values: np.ndarray) -> np.ndarray:
     return out
 
 
+def quantize_threaded(values: np.ndarray, threads: int | None = None) -> np.ndarray:
+    """quantize() over pieces of whole 32-element blocks on several threads
+    (ctypes releases the GIL): the bytes are the same as one call's."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    values = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+    out = np.zeros(int(oracle().oracle_int8_blocks_byte_count(values.size)), dtype=np.uint8)
+    threads = threads or os.cpu_count() or 1
+    piece = max(32, (values.size // threads + 31) // 32 * 32)
+
+    def run(first):
+        count = min(piece, values.size - first)
+        oracle().oracle_quantize_int8_blocks(p(values[first:]), first, count, values.size, p(out))
+
+    with ThreadPoolExecutor(threads) as pool:
+        list(pool.map(run, range(0, values.size, piece)))
+    return out
+
+
 def dequantize(stored: np.ndarray, elements: int) -> np.ndarray:
     out = np.empty(elements, dtype=np.float32)
     oracle().oracle_dequantize_int8_blocks(p(np.ascontiguousarray(stored)), elements, p(out))
@@ -135,6 +159,42 @@ def argmax(logits: np.ndarray, mask: np.ndarray | None = None) -> int:
         return int(oracle().oracle_argmax_double(p(logits), p(m), logits.size))
     logits = logits.astype(np.float32, copy=False)
     return int(oracle().oracle_argmax(p(logits), p(m), logits.size))
+
+
+# ---- the BASELINE configs' seeded inputs, without the product's libraries ----
+
+LINEAR_STDDEV = 0.02  # linear weights and the embedding
+NORM_STDDEV = 0.1     # norm weights
+
+
+def synthetic_normal(seed: int, tensor: int, layer: int, count: int, stddev: float) -> np.ndarray:
+    out = np.empty(count, dtype=np.float32)
+    lib = oracle()
+    rc = lib.oracle_synthetic_normal(seed, lib.oracle_synthetic_stream(tensor, layer), 0, count, stddev, p(out), 0)
+    assert rc == 0
+    return out
+
+
+def synthetic_tokens(seed: int, count: int, vocab: int) -> np.ndarray:
+    out = np.empty(count, dtype=np.uint32)
+    assert oracle().oracle_synthetic_tokens(seed, count, vocab, p(out)) == 0
+    return out
+
+
+def synthetic_model(shape, seed: int) -> dict:
+    """Every tensor of the random-init model, {(tensor id, layer): Q8_0 bytes
+    or fp32 norm}, as native.Context.load_synthetic(keep=True) returns them,
+    built from oracle.c alone (generator and quantizer)."""
+    from huggingfaceeacp_b200.native import model_tensors, NORM_TENSORS, FINAL_NORM
+
+    out = {}
+    for tensor, layer in model_tensors(shape):
+        count = int(np.prod(shape.tensor_shape(tensor)))
+        if tensor in NORM_TENSORS or tensor == FINAL_NORM:
+            out[(tensor, layer)] = synthetic_normal(seed, tensor, layer, count, NORM_STDDEV)
+        else:
+            out[(tensor, layer)] = quantize_threaded(synthetic_normal(seed, tensor, layer, count, LINEAR_STDDEV))
+    return out
 
 
 def worst_error(actual: np.ndarray, expected: np.ndarray) -> float:

@@ -1,0 +1,119 @@
+"""Parity at the BASELINE configs' own sizes, against the double oracle.
+
+- config 0's full 18-layer Gemma-2B, 16-token prompt and 32 greedy steps, on
+  the whole-loop decode kernel. The embedding scale is 1: with sqrt(2048) the
+  random tied embeddings make greedy decoding repeat one token, so the token
+  feedback would not be checked (the config-0 fixture test covers the scaled
+  model's logits). Here the 32 tokens all differ, with top-2 margins of 0.003
+  or more.
+- config 2's regime: an 8,064-token prompt (seed 2), then greedy decode until
+  the cache holds 8,192 positions. This runs the 128-split attention and its
+  merge phase on the whole-loop kernel and on the graph path. One Gemma-width
+  layer keeps the oracle's prefill to seconds.
+- config 3's regime: 64 sequences with 512-token prompts (seed 3 + q), batched
+  greedy steps on the tensor-core products. Two Gemma-width layers. Four
+  sequences, the first and last among them, are checked against their own
+  oracle loops.
+
+Tokens must be equal. Logits and hidden rows must agree within the decoder
+tolerance of DecoderTests.cpp:41 (5e-6 relative, Tests/Decoder/Common.h:391-400).
+"""
+import numpy as np
+import pytest
+
+import oracle_bindings as ob
+from huggingfaceeacp_b200 import native
+
+pytestmark = pytest.mark.gpu
+
+TOLERANCE = 5e-6
+
+
+def test_gemma2b_varied_tokens_on_the_whole_loop_kernel_equal_the_oracle():
+    shape = native.GEMMA_2B.replace(embed_scale=1.0, max_positions=64, max_step_rows=16)
+    prompt = native.synthetic_tokens(0, 16, shape.vocab)
+    with native.Context(shape) as ctx:
+        tensors = ctx.load_synthetic(seed=0, keep=True)
+        assert ctx.decode_path == native.DECODE_PERSISTENT
+        generated = ctx.generate(prompt, 32)
+        expected, margins = ob.greedy_reference(shape, tensors, prompt, 32, with_margins=True)
+        assert list(generated) == expected
+        assert len(set(expected)) > 24 and min(margins) > 1e-3
+        # The first step's rows against the oracle's.
+        ctx.begin_sequence()
+        logits, hidden = ctx.step(prompt)
+        oracle = ob.OracleModel(shape, tensors, precision="double")
+        ref_hidden, ref_logits = oracle.step(prompt)
+        oracle.close()
+        assert ob.worst_error(logits, ref_logits) <= TOLERANCE
+        assert ob.worst_error(hidden, ref_hidden) <= TOLERANCE
+
+
+LONG = native.DecoderShape(width=2048, heads=8, kv_heads=1, head_width=256, layers=1, intermediate=16384,
+                           vocab=8192, max_positions=8192, max_step_rows=512, embed_scale=1.0)
+LONG_PROMPT = 8064
+
+
+@pytest.fixture(scope="module")
+def long_context():
+    ctx = native.Context(LONG)
+    tensors = ctx.load_synthetic(seed=2, keep=True)
+    prompt = native.synthetic_tokens(2, LONG_PROMPT, LONG.vocab)
+    # The oracle's greedy run to the end of the window, with its state kept
+    # for the logits check after it.
+    oracle = ob.OracleModel(LONG, tensors, precision="double")
+    _, logits = oracle.step(prompt, last_row_only=True, want_hidden=False)
+    tokens = []
+    while True:
+        tokens.append(ob.argmax(logits[-1]))
+        if oracle.position == LONG.max_positions - 1:
+            break
+        _, logits = oracle.step([tokens[-1]], want_hidden=False)
+    yield ctx, tensors, prompt, tokens, oracle
+    oracle.close()
+    ctx.close()
+
+
+@pytest.mark.parametrize("path", [native.DECODE_PERSISTENT, native.DECODE_GRAPH])
+def test_decode_to_the_end_of_an_8192_window_equals_the_oracle(long_context, path):
+    ctx, tensors, prompt, expected, oracle = long_context
+    assert len(expected) == LONG.max_positions - LONG_PROMPT
+    ctx.set_decode_path(path)
+    ctx.begin_sequence()
+    ctx.prefill_async(prompt)
+    ctx.decode_async(len(expected) - 1)
+    generated = ctx.read_slots(LONG_PROMPT, len(expected))
+    assert ctx.position == LONG.max_positions - 1
+    assert list(generated) == expected, path
+
+
+def test_last_window_position_rows_equal_the_oracle(long_context):
+    ctx, tensors, prompt, expected, oracle = long_context
+    ctx.set_decode_path(native.DECODE_PERSISTENT)
+    ctx.begin_sequence()
+    ctx.prefill_async(prompt)
+    ctx.decode_async(len(expected) - 1)
+    ctx.sync()
+    # Position 8191 attends to all 8,192 keys (the split-and-merge regime).
+    logits, hidden = ctx.step([expected[-1]])
+    ref_hidden, ref_logits = oracle.step([expected[-1]])
+    assert ob.worst_error(logits, ref_logits) <= TOLERANCE
+    assert ob.worst_error(hidden, ref_hidden) <= TOLERANCE
+
+
+BATCH = native.DecoderShape(width=2048, heads=8, kv_heads=1, head_width=256, layers=2, intermediate=16384,
+                            vocab=8192, max_positions=528, max_step_rows=512, embed_scale=1.0)
+BATCH_SEQUENCES = 64
+BATCH_PROMPT = 512
+BATCH_TOKENS = 8
+CHECKED = (0, 21, 42, 63)
+
+
+def test_64_sequences_of_512_token_prompts_equal_their_own_oracle_loops():
+    prompts = np.stack([native.synthetic_tokens(3 + q, BATCH_PROMPT, BATCH.vocab) for q in range(BATCH_SEQUENCES)])
+    with native.Context(BATCH, sequences=BATCH_SEQUENCES) as ctx:
+        tensors = ctx.load_synthetic(seed=3, keep=True)
+        out = ctx.generate_batch(prompts, BATCH_TOKENS)
+        for q in CHECKED:
+            assert list(out[q]) == ob.greedy_reference(BATCH, tensors, prompts[q], BATCH_TOKENS), q
+        assert len({tuple(row) for row in out}) == BATCH_SEQUENCES
