@@ -179,8 +179,8 @@ def physical_index(local_rank: int) -> int:
     return local_rank
 
 
-def build_model(native, shape, keep: bool, sequences: int = 1):
-    ctx = native.Context(shape, device=int(os.environ.get("LOCAL_RANK", "0")), sequences=sequences)
+def build_model(native, shape, keep: bool, sequences: int = 1, pages: int | None = None):
+    ctx = native.Context(shape, device=int(os.environ.get("LOCAL_RANK", "0")), sequences=sequences, pages=pages)
     tensors = ctx.load_synthetic(seed=SEED, keep=keep)
     return ctx, tensors
 
@@ -216,6 +216,49 @@ def max_over_ranks(dist, values, device="cuda"):
     t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return [float(v) for v in t.tolist()]
+
+
+CONFIG1_SHAPES = [(2048, 2048), (2048, 256), (2048, 16384), (16384, 2048), (2048, 256000)]  # configs[1] (K -> N)
+CONFIG1_ROWS = (1, 8, 64)
+
+
+def run_config1(native, peak, peak_kind, reps=10):
+    """the Q8_0 op sweep (W[N,K] ~ N(0, 0.02) quantized, x[M,K] ~
+    N(0, 1), seed 1) through prepared weights (hf_cuda_linear_*), so each row
+    count runs the kernel the decoder runs for it. Every launch is timed alone
+    with CUDA events on its stream after a write of 256 MiB (twice the L2),
+    so the weight comes from HBM. Algorithmic bytes = 17/16 N K + 4 M K + 4 M N."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    x = torch.from_numpy(native.synthetic_normal(1, 200, 64, 64 * 16384, 1.0)).cuda()
+    cases = []
+    for K, N in CONFIG1_SHAPES:
+        q = native.quantize(native.synthetic_normal(1, 100 + N % 97, K, N * K, 0.02))
+        out = torch.empty(64 * N, dtype=torch.float32, device="cuda")
+        with native.Linear(q, K, N, max(CONFIG1_ROWS)) as lin:
+            for M in CONFIG1_ROWS:
+                times = []
+                for rep in range(reps + 2):
+                    flush.zero_()
+                    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    start.record(stream)
+                    lin.run(x.data_ptr(), out.data_ptr(), M, stream=stream.cuda_stream)
+                    stop.record(stream)
+                    stop.synchronize()
+                    if rep >= 2:
+                        times.append(start.elapsed_time(stop) * 1000.0)
+                us = statistics.mean(times)
+                nbytes = 17 * N * K // 16 + 4 * M * K + 4 * M * N
+                gbs = nbytes / us / 1e3
+                cases.append({"K": K, "N": N, "M": M, "kernel": native.LINEAR_PATH_NAMES[lin.path(M)],
+                              "us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 3),
+                              "tflops": round(2.0 * M * N * K / us / 1e6, 2)})
+        del out
+    return {"workload": "config1: Q8_0 op sweep, seed 1, through prepared weights (hf_cuda_linear_run)",
+            "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "bound": "hbm",
+            "l2": "256 MiB written before every timed launch", "reps": reps, "cases": cases}
 
 
 def run_reference(args):
@@ -279,7 +322,11 @@ def run_ours(args):
                  PROMPT_LENGTH + 2 * (args.warmup + args.steps) + 8)
     shape = native.GEMMA_2B.replace(max_step_rows=BATCH_PROMPT, max_positions=window)
     keep = rank == 0 and world == 1 and not args.no_cpu_baseline
-    ctx, tensors = build_model(native, shape, keep, BATCH_SEQUENCES)
+    # The batched sequences' K/V live in pages: enough for each sequence's
+    # prompt and every step it takes here (not its whole window).
+    batch_positions = BATCH_PROMPT + args.warmup + args.batched_steps + 1
+    pages = BATCH_SEQUENCES * -(-batch_positions // native.PAGE_ROWS)
+    ctx, tensors = build_model(native, shape, keep, BATCH_SEQUENCES, pages)
     # Every rank decodes its own sequences: rank r's batch-1 prompt has seed
     # SEED + r (rank 0 is config 0's), its batched sequence q is global sequence
     # r * 64 + q (seed BATCH_SEED + r * 64 + q), its long prompt seed LONG_SEED + r,
@@ -335,7 +382,7 @@ def run_ours(args):
     p_stop.record(stream)
     ctx.decode_batch_async(args.warmup)
     ctx.sync()
-    batch_first = ctx.position
+    batch_first = ctx.sequence_position(0)  # every batched sequence is at the same position here
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(physical_index(local_rank)) as batch_clocks:
@@ -364,6 +411,7 @@ def run_ours(args):
                      "note": "weights once per step + every sequence's K/V rows and logits"},
         "clocks": batch_clocks.summary(),
         "tokens_head": [[int(t) for t in row] for row in batch_tokens[:2]],
+        "kv_cache": f"paged: {pages} pages of {native.PAGE_ROWS} positions shared by the {BATCH_SEQUENCES} sequences",
     }
 
     # ---- long context: prefill 8064 tokens, decode 128 steps to 8192
@@ -416,6 +464,9 @@ def run_ours(args):
         "unit": "tok/s", "n_gpus": world, "ms": prefill_run_ms, "scaling": "weak", "roofline": prefill_rl,
     }
 
+    # ---- config 1: the op sweep (rank 0 only; a per-GPU kernel measurement)
+    config1 = run_config1(native, peak, peak_kind) if rank == 0 and not args.no_config1 else None
+
     # ---- roofline of every decode kernel, live (cycling layers: HBM, not L2)
     ctx.begin_sequence()
     ctx.prefill_async(prompt)
@@ -464,6 +515,7 @@ def run_ours(args):
         "batched": batched,
         "long_context": long_context,
         "prefill": prefill,
+        "config1": config1,
         "gpu_launches": launches,
         "decode_path": {0: "generic", 1: "graph", 2: "persistent"}[path],
         "clocks": clocks.summary(),
@@ -568,6 +620,7 @@ def main():
     parser.add_argument("--batched-steps", type=int, default=256,
                         help="batched decode steps timed for the b=64/GPU half of the metric")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-config1", action="store_true", help="skip the configs[1] op sweep")
     parser.add_argument("--profile-case", nargs="?", const="decode", choices=["decode", "batched", "prefill"],
                         help="run a small ncu capture case instead of the bench: the decode kernel (default), "
                              "a batched step's tensor-core products, or a prompt's prefill")

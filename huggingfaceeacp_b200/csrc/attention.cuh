@@ -38,6 +38,14 @@ struct AttnArgs
     // k_cache / v_cache + r * cache_seq_stride. 0: the rows are consecutive
     // positions of one sequence.
     size_t cache_seq_stride;
+    // Paged batched decode (page_table non-null): row r is sequence r at its
+    // own position seq_pos[r], attending to keys [0, seq_pos[r]]; key p is row
+    // p % page_rows of page page_table[r * table_stride + p / page_rows] of
+    // k_cache / v_cache (this layer's page pool [pages][page_rows][kv width]).
+    const int* page_table;
+    const unsigned* seq_pos;
+    int table_stride;
+    int page_rows;
     int rows; // mqa_rows: the step's rows
 };
 
@@ -140,9 +148,10 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int H = a.heads;
     const int kvw = a.kv_heads * D;
-    const int keys = (int) position + (a.cache_seq_stride ? 0 : row) + 1;
-    const float* k_cache = a.k_cache + (size_t) row * a.cache_seq_stride;
-    const float* v_cache = a.v_cache + (size_t) row * a.cache_seq_stride;
+    const int* table = a.page_table ? a.page_table + (size_t) row * a.table_stride : nullptr;
+    const int keys = table ? (int) a.seq_pos[row] + 1 : (int) position + (a.cache_seq_stride ? 0 : row) + 1;
+    const float* k_cache = a.k_cache + (table ? 0 : (size_t) row * a.cache_seq_stride);
+    const float* v_cache = a.v_cache + (table ? 0 : (size_t) row * a.cache_seq_stride);
     const int chunk = (keys + a.nsplit - 1) / a.nsplit;
     const int k0 = min(keys, split * chunk);
     const int k1 = min(keys, k0 + chunk);
@@ -174,7 +183,10 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
         for (int i = tid; i < nk * (D / 4); i += 256)
         {
             const int r = i / (D / 4), c = (i % (D / 4)) * 4;
-            const size_t at = (size_t) (t0 + r) * kvw + (size_t) kv_head * D + c;
+            const int key = t0 + r;
+            const size_t cache_row =
+                table ? (size_t) table[key / a.page_rows] * a.page_rows + key % a.page_rows : (size_t) key;
+            const size_t at = cache_row * kvw + (size_t) kv_head * D + c;
             cp_async16(tk + r * D + c, k_cache + at);
             cp_async16(tv + r * D + c, v_cache + at);
         }

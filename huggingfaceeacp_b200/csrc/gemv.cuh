@@ -75,6 +75,14 @@ struct GemvArgs
     // QkvRope of a batched decode step: row m of x is sequence m, whose cache
     // rows start at k_cache / v_cache + m * cache_seq_stride. 0: one sequence.
     size_t cache_seq_stride;
+    // QkvRope of a paged batched step (page_table non-null): row m of x is
+    // sequence m at its own position seq_pos[m], and the cache row of position
+    // p is row p % page_rows of page page_table[m * table_stride + p / page_rows]
+    // of k_cache / v_cache, this layer's page pool [pages][page_rows][kv width].
+    const int* page_table;
+    const unsigned* seq_pos;
+    int table_stride;
+    int page_rows;
     // GeGLU of the whole-loop kernel: the activation entries also land in
     // act_local[unit - act_base] (shared memory), or act_local is null.
     float* act_local;
@@ -95,6 +103,15 @@ __device__ __forceinline__ void qkv_pair_store(const GemvArgs& a, unsigned unit,
     const int block = (int) (2u * unit) / D; // head block in device row order
     const int pair = (int) (unit % (unsigned) half);
     const int kvw = a.kv_heads * D;
+    size_t cache_row; // the row's K/V cache row, counted in kv widths from k_cache / v_cache
+    if (a.page_table)
+    {
+        position = a.seq_pos[m];
+        const int page = a.page_table[(size_t) m * a.table_stride + position / (unsigned) a.page_rows];
+        cache_row = (size_t) page * a.page_rows + position % (unsigned) a.page_rows;
+    }
+    else
+        cache_row = (size_t) m * (a.cache_seq_stride / kvw) + position;
     if (block < a.heads + a.kv_heads)
     {
         const float c = a.rope_cos_row ? a.rope_cos_row[pair] : a.rope_cos[(size_t) position * half + pair];
@@ -109,15 +126,14 @@ __device__ __forceinline__ void qkv_pair_store(const GemvArgs& a, unsigned unit,
         }
         else
         {
-            float* k = a.k_cache + m * a.cache_seq_stride + (size_t) position * kvw + (size_t) (block - a.heads) * D;
+            float* k = a.k_cache + cache_row * kvw + (size_t) (block - a.heads) * D;
             k[pair] = r0;
             k[pair + half] = r1;
         }
     }
     else
     {
-        float* v = a.v_cache + m * a.cache_seq_stride + (size_t) position * kvw
-                   + (size_t) (block - a.heads - a.kv_heads) * D;
+        float* v = a.v_cache + cache_row * kvw + (size_t) (block - a.heads - a.kv_heads) * D;
         v[pair] = v0;
         v[pair + half] = v1;
     }

@@ -44,6 +44,10 @@ namespace
 constexpr int kStages = 3; // shared-memory ring depth of the streaming products (3 x 34 KiB)
 constexpr int kBatchSplits = 8;       // most attention splits per sequence of a batched step
 constexpr int kBatchArgmaxParts = 64; // argmax candidates per sequence of a batched step
+constexpr int kPageRows = HF_PAGE_ROWS; // positions per KV page of a batched sequence
+// The whole-loop decode computes attention in every CTA up to this many keys
+// (no grid barrier between attention and o_proj), beyond it in split CTAs.
+constexpr int kLocalAttentionKeys = 64;
 
 // Dynamic shared memory of q8_gemv_stream<K>: the stage ring plus either the
 // x vector (K = 2048) or the per-slab row partials (K > 2048). Two CTAs fit on
@@ -129,6 +133,11 @@ void configure_kernels()
     cudaFuncSetAttribute(q8_rows_mma<Epi::GeGLU, 2048>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
     cudaFuncSetAttribute(q8_rows_mma<Epi::Logits, 2048>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
     cudaFuncSetAttribute(q8_rows_mma<Epi::Residual, 16384>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
+    // The plain folds of a prepared linear (hf_cuda_linear_run).
+    cudaFuncSetAttribute(q8_rows_mma<Epi::Store, 2048>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
+    cudaFuncSetAttribute(q8_rows_mma<Epi::Gelu, 2048>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
+    cudaFuncSetAttribute(q8_rows_mma<Epi::Store, 16384>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
+    cudaFuncSetAttribute(q8_rows_mma<Epi::Gelu, 16384>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) rows_mma_smem());
     cudaFuncSetAttribute(mqa_fast<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<8>());
     cudaFuncSetAttribute(mqa_fast<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<4>());
     cudaFuncSetAttribute(mqa_fast<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<2>());
@@ -144,6 +153,8 @@ void configure_kernels()
     HF_TC_SMEM(Epi::Residual)
     HF_TC_SMEM(Epi::GeGLU)
     HF_TC_SMEM(Epi::Logits)
+    HF_TC_SMEM(Epi::Store)
+    HF_TC_SMEM(Epi::Gelu)
 #undef HF_TC_SMEM
 }
 
@@ -250,6 +261,47 @@ cudaError_t generic_product(bool pdl, int units, cudaStream_t stream, const Gemv
     return launch(pdl, q8_rows_generic<E>, dim3(grid), dim3(256), 0, stream, a);
 }
 
+// A product of a.M > 8 rows of x on the tensor cores (tc_gemm.cuh): the
+// input's fp16 pieces (RMS-normalised on the way when a.norm_w is set), then
+// the tiles with the epilogue, or, with K split across CTAs, the partial sums
+// and tc_finish. tc is the weight's tensor-core blocks; tc_x, tc_xunscale and
+// tc_ws the input pieces, their scales and the split workspace, sized for a.M.
+template <Epi E>
+cudaError_t tc_product_on(const uint8_t* tc, const GemvArgs& a, cudaStream_t stream, __half* tc_x, float* tc_xunscale,
+                          float* tc_ws, int sms)
+{
+    const TcPlan p = tc_plan(a.M, a.N, a.K, sms);
+    const size_t split_stride = p.m_pad * (size_t) a.N;
+    const dim3 grid(p.tiles_n, p.tiles_m, p.splits);
+    cudaError_t e;
+    if (p.nx == 64)
+    {
+        e = a.K == 16384 ? launch(true, prep_x_pieces<64, 16384>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x,
+                                  a.norm_w, a.eps, a.M, tc_x, tc_xunscale)
+                         : launch(true, prep_x_pieces<64, 2048>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x,
+                                  a.norm_w, a.eps, a.M, tc_x, tc_xunscale);
+        if (e == cudaSuccess)
+            e = launch(true, q8_tc_gemm_ts<E>, grid, dim3(kTsThreads), kTsSmem, stream, a, tc, (const __half*) tc_x,
+                       (const float*) tc_xunscale, tc_ws, split_stride, p.cps);
+    }
+    else
+    {
+        e = a.K == 16384 ? launch(true, prep_x_pieces<128, 16384>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x,
+                                  a.norm_w, a.eps, a.M, tc_x, tc_xunscale)
+                         : launch(true, prep_x_pieces<128, 2048>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x,
+                                  a.norm_w, a.eps, a.M, tc_x, tc_xunscale);
+        if (e == cudaSuccess)
+            e = launch(true, q8_tc_gemm<E>, grid, dim3(kTcThreads), kTcSmem, stream, a, tc, (const __half*) tc_x,
+                       (const float*) tc_xunscale, tc_ws, split_stride, p.cps);
+    }
+    if (e != cudaSuccess || p.splits == 1)
+        return e;
+    const int units = (E == Epi::QkvRope || E == Epi::GeGLU) ? a.N / 2 : a.N;
+    const size_t threads = (size_t) a.M * units;
+    return launch(true, tc_finish<E>, dim3((unsigned) ((threads + 255) / 256)), dim3(256), 0, stream, a,
+                  (const float*) tc_ws, p.splits, split_stride);
+}
+
 std::string shape_refusal(const hf_shape& s)
 {
     auto positive = [](int v) { return v > 0; };
@@ -322,6 +374,7 @@ struct hf_ctx
     int max_splits = 1;
     bool persistent_ok = false; // the cooperative whole-loop kernel serves this shape on this device
     int gate_point = 1; // HF_GATE overrides (a tuning knob of the whole-loop kernel)
+    int local_keys = kLocalAttentionKeys; // HF_LOCAL_ATTN overrides (0: always split the context)
     bool tc_off = false; // HF_TC=0 keeps multi-row products on the int8 MMA (for comparisons)
     int decode_path = HF_DECODE_AUTO;
     LayerDev* layer_dev = nullptr;
@@ -329,12 +382,33 @@ struct hf_ctx
     int position = 0;
     std::map<int, cudaGraphExec_t> graphs; // decode step by attention split count
 
-    // Batched decode: `sequences` independent sequences share the weights and
-    // the position; each has its own slots and caches. The single-sequence
-    // calls act on sequence `seq` (0 outside a batched prefill): the decode
-    // graphs and the whole-loop kernel hold sequence 0's buffers.
+    // Batched decode (batch contexts): `sequences` independent sequences share
+    // the weights; each has its own position, token slots and KV pages. The
+    // K/V rows of every batched sequence live in fixed pages of kPageRows
+    // positions ([layer][page][row][kv width], page `pages` a trash page that
+    // the rows of inactive sequences write), found through the sequence's row
+    // of the page table. The single-sequence calls use their own window: the
+    // contiguous caches kcache/vcache and the last slot row. A batched prompt
+    // is prefilled into the contiguous scratch admit_k/admit_v by the ordinary
+    // kernels, then copied into its pages (scatter_rows_to_pages).
     int sequences = 1;
-    int seq = 0;
+    int seq = -1; // the batched sequence being admitted, or -1: the single-sequence window
+    bool paged = false;
+    int pages = 0;
+    int table_stride = 0; // page-table entries per sequence
+    float* kpages = nullptr;
+    float* vpages = nullptr;
+    float* admit_k = nullptr;
+    float* admit_v = nullptr;
+    int* page_table_dev = nullptr;    // [sequences][table_stride]
+    unsigned* seq_pos_dev = nullptr;  // [sequences] positions, advanced by each batched step
+    unsigned* seq_active_dev = nullptr;
+    std::vector<int> page_table;      // the host's copy
+    std::vector<int> seq_len;         // positions per sequence (-1: not active)
+    std::vector<int> free_pages;
+    float* kbase = nullptr; // the contiguous cache the prefill and single-sequence kernels write
+    float* vbase = nullptr;
+    unsigned* single_slots = nullptr;
 
     int fail(int code, const std::string& text)
     {
@@ -367,16 +441,32 @@ struct hf_ctx
     {
         return persistent_ok && decode_path != HF_DECODE_GRAPH;
     }
-    // Caches are [layer][sequence][position][kv width]: one layer's caches of
-    // every sequence are contiguous, sequence to sequence seq_cache_stride().
+    // A contiguous cache is [layer][position][kv width], layer to layer
+    // seq_cache_stride(); a page pool [layer][pages + 1][kPageRows][kv width].
     size_t seq_cache_stride() const { return (size_t) shape.max_positions * kv_width(); }
-    float* layer_k(int l) const { return kcache + ((size_t) l * sequences + seq) * seq_cache_stride(); }
-    float* layer_v(int l) const { return vcache + ((size_t) l * sequences + seq) * seq_cache_stride(); }
+    float* layer_k(int l) const { return kbase + (size_t) l * seq_cache_stride(); }
+    float* layer_v(int l) const { return vbase + (size_t) l * seq_cache_stride(); }
+    size_t page_stride() const { return (size_t) (pages + 1) * kPageRows * kv_width(); }
+    float* layer_kpages(int l) const { return kpages + (size_t) l * page_stride(); }
+    float* layer_vpages(int l) const { return vpages + (size_t) l * page_stride(); }
 
+    // q >= 0: the prefill kernels write batched sequence q's slots and the
+    // admit scratch; q < 0: the single-sequence window.
     void select_sequence(int q)
     {
         seq = q;
-        slots = slot_base + (size_t) q * (shape.max_positions + 1);
+        slots = q < 0 ? single_slots : slot_base + (size_t) q * (shape.max_positions + 1);
+        kbase = q < 0 ? kcache : admit_k;
+        vbase = q < 0 ? vcache : admit_v;
+    }
+
+    int pages_for(int positions) const { return (positions + kPageRows - 1) / kPageRows; }
+    int pages_held(int q) const
+    {
+        int n = 0;
+        while (n < table_stride && page_table[(size_t) q * table_stride + n] != pages)
+            ++n;
+        return n;
     }
 
     bool all_loaded() const
@@ -411,7 +501,8 @@ struct hf_ctx
         const hf_shape& s = shape;
         return launch(false, embed_q8, dim3((s.width + 255) / 256, 1), dim3(256), 0, stream,
                       (const uint8_t*) embedding.base, embedding.scales(), s.width, s.vocab, s.embed_scale,
-                      (const unsigned*) slots, (const unsigned*) state, 1, hidden, err_word(), 0);
+                      (const unsigned*) slots, (const unsigned*) state, 1, hidden, err_word(), 0,
+                      (const unsigned*) nullptr);
     }
 
     cudaError_t launch_qkv(int l)
@@ -611,6 +702,7 @@ struct hf_ctx
         p.exit_ticket = exit_ticket();
         p.steps = steps;
         p.gate_point = gate_point;
+        p.local_keys = local_keys;
         p.down_acc = down_acc;
         p.trace = trace;
         cudaLaunchConfig_t config = {};
@@ -692,45 +784,11 @@ struct hf_ctx
     }
 
     // ---------------------------------------------------------------------
-    // A product of a.M > 8 rows of x on the tensor cores (tc_gemm.cuh): the
-    // input's fp16 pieces (RMS-normalised on the way when a.norm_w is set),
-    // then the tiles with the epilogue, or, with K split across CTAs, the
-    // partial sums and tc_finish.
+    // A product of a.M > 8 rows of x on the tensor cores (tc_product_on).
     template <Epi E>
     cudaError_t tc_product(const Q8& w, const GemvArgs& a)
     {
-        const TcPlan p = tc_plan(a.M, a.N, a.K, sms);
-        const size_t split_stride = p.m_pad * (size_t) a.N;
-        const dim3 grid(p.tiles_n, p.tiles_m, p.splits);
-        cudaError_t e;
-        if (p.nx == 64)
-        {
-            e = a.K == 16384 ? launch(true, prep_x_pieces<64, 16384>, dim3((unsigned) p.m_pad), dim3(256), 0, stream,
-                                      a.x, a.norm_w, a.eps, a.M, tc_x, tc_xunscale)
-                             : launch(true, prep_x_pieces<64, 2048>, dim3((unsigned) p.m_pad), dim3(256), 0, stream,
-                                      a.x, a.norm_w, a.eps, a.M, tc_x, tc_xunscale);
-            if (e == cudaSuccess)
-                e = launch(true, q8_tc_gemm_ts<E>, grid, dim3(kTsThreads), kTsSmem, stream, a,
-                           (const uint8_t*) w.tc, (const __half*) tc_x, (const float*) tc_xunscale, tc_ws,
-                           split_stride, p.cps);
-        }
-        else
-        {
-            e = a.K == 16384 ? launch(true, prep_x_pieces<128, 16384>, dim3((unsigned) p.m_pad), dim3(256), 0, stream,
-                                      a.x, a.norm_w, a.eps, a.M, tc_x, tc_xunscale)
-                             : launch(true, prep_x_pieces<128, 2048>, dim3((unsigned) p.m_pad), dim3(256), 0, stream,
-                                      a.x, a.norm_w, a.eps, a.M, tc_x, tc_xunscale);
-            if (e == cudaSuccess)
-                e = launch(true, q8_tc_gemm<E>, grid, dim3(kTcThreads), kTcSmem, stream, a,
-                           (const uint8_t*) w.tc, (const __half*) tc_x, (const float*) tc_xunscale, tc_ws,
-                           split_stride, p.cps);
-        }
-        if (e != cudaSuccess || p.splits == 1)
-            return e;
-        const int units = (E == Epi::QkvRope || E == Epi::GeGLU) ? a.N / 2 : a.N;
-        const size_t threads = (size_t) a.M * units;
-        return launch(true, tc_finish<E>, dim3((unsigned) ((threads + 255) / 256)), dim3(256), 0, stream, a,
-                      (const float*) tc_ws, p.splits, split_stride);
+        return tc_product_on<E>(w.tc, a, stream, tc_x, tc_xunscale, tc_ws, sms);
     }
 
     // The generic product (any shape), RMS-normalising x into `normed` first
@@ -772,30 +830,29 @@ struct hf_ctx
     }
 
     // ---------------------------------------------------------------------
-    // One batched decode step: every sequence's next token at the shared
-    // position, row r of each product being sequence r, on the multi-row
-    // int8 MMA products over the stage records (the weights stream once per
-    // eight sequences).
+    // One batched decode step: every sequence's next token at its own
+    // position, row r of each product being sequence r, on the tensor-core
+    // products (the weights stream once per step); K/V through the pages.
     int enqueue_batch_step()
     {
         const hf_shape& s = shape;
         const int S = sequences;
         const int P1 = s.max_positions + 1;
-        const size_t stride = seq_cache_stride();
         cudaError_t e = launch(false, embed_q8, dim3((s.width + 255) / 256, S), dim3(256), 0, stream,
                                (const uint8_t*) embedding.base, embedding.scales(), s.width, s.vocab, s.embed_scale,
-                               (const unsigned*) slot_base, (const unsigned*) state, S, hidden, err_word(), P1);
+                               (const unsigned*) slot_base, (const unsigned*) state, S, hidden, err_word(), P1,
+                               (const unsigned*) seq_pos_dev);
         if (e != cudaSuccess)
             return cuda(e, "embed launch");
-        const int keys = position + 1;
+        int keys = 1; // the longest context of this step
+        for (int q = 0; q < S; ++q)
+            keys = std::max(keys, seq_len[q] + 1);
         int splits = 1;
         while (splits < kBatchSplits && splits * 64 < keys)
             splits *= 2;
         for (int l = 0; l < s.layers; ++l)
         {
             const Layer& L = layers[l];
-            float* k0 = kcache + (size_t) l * S * stride; // sequence 0's rows of this layer
-            float* v0 = vcache + (size_t) l * S * stride;
 
             GemvArgs qkv = {};
             qkv.w = L.qkv.base;
@@ -807,9 +864,12 @@ struct hf_ctx
             qkv.norm_w = L.in_norm;
             qkv.eps = s.rms_eps;
             qkv.out = qbuf;
-            qkv.k_cache = k0;
-            qkv.v_cache = v0;
-            qkv.cache_seq_stride = stride;
+            qkv.k_cache = layer_kpages(l);
+            qkv.v_cache = layer_vpages(l);
+            qkv.page_table = page_table_dev;
+            qkv.seq_pos = seq_pos_dev;
+            qkv.table_stride = table_stride;
+            qkv.page_rows = kPageRows;
             qkv.rope_cos = rope_cos;
             qkv.rope_sin = rope_sin;
             qkv.heads = s.heads;
@@ -823,9 +883,12 @@ struct hf_ctx
 
             AttnArgs at = {};
             at.q = qbuf;
-            at.k_cache = k0;
-            at.v_cache = v0;
-            at.cache_seq_stride = stride;
+            at.k_cache = layer_kpages(l);
+            at.v_cache = layer_vpages(l);
+            at.page_table = page_table_dev;
+            at.seq_pos = seq_pos_dev;
+            at.table_stride = table_stride;
+            at.page_rows = kPageRows;
             at.out = attended;
             at.part_acc = attn_acc;
             at.part_ml = attn_ml;
@@ -910,11 +973,93 @@ struct hf_ctx
         if (e != cudaSuccess)
             return cuda(e, "argmax launch");
         e = launch(true, argmax_final_batch, dim3(S), dim3(32), 0, stream, (const float*) cand_val,
-                   (const unsigned*) cand_idx, kBatchArgmaxParts, slot_base, P1, (unsigned) position, state);
+                   (const unsigned*) cand_idx, kBatchArgmaxParts, slot_base, P1, 0u, state, seq_pos_dev,
+                   (const unsigned*) seq_active_dev);
         if (e != cudaSuccess)
             return cuda(e, "argmax launch");
-        ++position;
+        for (int q = 0; q < S; ++q)
+            if (seq_len[q] >= 0)
+                ++seq_len[q];
         return HF_OK;
+    }
+
+    // ---------------------------------------------------------------------
+    // Paged sequences: the host's page table is the truth between calls; the
+    // device copy and the positions are written in stream order.
+    int upload_paging()
+    {
+        std::vector<unsigned> pos(sequences), active(sequences);
+        for (int q = 0; q < sequences; ++q)
+        {
+            pos[q] = seq_len[q] < 0 ? 0u : (unsigned) seq_len[q];
+            active[q] = seq_len[q] < 0 ? 0u : 1u;
+        }
+        int rc = cuda(cudaMemcpyAsync(page_table_dev, page_table.data(), page_table.size() * sizeof(int),
+                                      cudaMemcpyHostToDevice, stream), "page table upload");
+        if (!rc)
+            rc = cuda(cudaMemcpyAsync(seq_pos_dev, pos.data(), pos.size() * sizeof(unsigned), cudaMemcpyHostToDevice,
+                                      stream), "positions upload");
+        if (!rc)
+            rc = cuda(cudaMemcpyAsync(seq_active_dev, active.data(), active.size() * sizeof(unsigned),
+                                      cudaMemcpyHostToDevice, stream), "positions upload");
+        return rc;
+    }
+
+    // Pages so that sequence q holds positions [0, positions): false when the
+    // pool has too few free pages (nothing is taken then).
+    bool reserve(int q, int positions)
+    {
+        const int have = pages_held(q), need = pages_for(positions);
+        if (need - have > (int) free_pages.size())
+            return false;
+        for (int j = have; j < need; ++j)
+        {
+            page_table[(size_t) q * table_stride + j] = free_pages.back();
+            free_pages.pop_back();
+        }
+        return true;
+    }
+
+    void release(int q)
+    {
+        for (int j = 0; j < table_stride; ++j)
+        {
+            int& entry = page_table[(size_t) q * table_stride + j];
+            if (entry != pages)
+                free_pages.push_back(entry);
+            entry = pages;
+        }
+        seq_len[q] = -1;
+    }
+
+    // Enqueues sequence q's prompt: prefilled into the admit scratch by the
+    // ordinary kernels (its first generated token lands in slot
+    // prompt_length), then copied into its pages. Checked by the caller.
+    int admit(int q, const uint32_t* prompt, int prompt_length)
+    {
+        const int saved = position;
+        select_sequence(q);
+        int rc = set_position(0);
+        if (!rc)
+            rc = cuda(cudaMemcpyAsync(slots, prompt, (size_t) prompt_length * 4, cudaMemcpyHostToDevice, stream),
+                      "prompt upload");
+        if (!rc)
+            rc = enqueue_prompt(prompt_length, false);
+        if (!rc)
+        {
+            seq_len[q] = prompt_length;
+            rc = upload_paging();
+        }
+        if (!rc)
+            rc = cuda(launch(true, scatter_rows_to_pages, dim3((unsigned) prompt_length, (unsigned) shape.layers),
+                             dim3(256), 0, stream, (const float*) admit_k, (const float*) admit_v, seq_cache_stride(),
+                             kv_width(), (const int*) (page_table_dev + (size_t) q * table_stride), kPageRows, kpages,
+                             vpages, page_stride()),
+                      "page copy launch");
+        select_sequence(-1);
+        position = saved;
+        const int restore = set_position(saved);
+        return rc ? rc : restore;
     }
 
     // ---------------------------------------------------------------------
@@ -931,7 +1076,8 @@ struct hf_ctx
         const hf_shape& s = shape;
         cudaError_t e = launch(false, embed_q8, dim3((s.width + 255) / 256, rows), dim3(256), 0, stream,
                                (const uint8_t*) embedding.base, embedding.scales(), s.width, s.vocab, s.embed_scale,
-                               (const unsigned*) slots, (const unsigned*) state, rows, hidden, err_word(), 0);
+                               (const unsigned*) slots, (const unsigned*) state, rows, hidden, err_word(), 0,
+                               (const unsigned*) nullptr);
         if (e != cudaSuccess)
             return cuda(e, "embed launch");
         const int QH = s.heads / s.kv_heads;
@@ -1123,7 +1269,7 @@ struct hf_ctx
             const int rows = std::min(capacity, count - first);
             const bool last = first + rows == count;
             int rc;
-            if (rows == 1 && last && fast && !all_logits && seq == 0)
+            if (rows == 1 && last && fast && !all_logits && seq < 0)
                 rc = enqueue_decode_steps(1);
             else
                 rc = enqueue_rows(rows, all_logits, last);
@@ -1169,7 +1315,7 @@ namespace
 {
 // A context of `sequences` sequences (1 for hf_cuda_create); the shape is
 // already checked.
-int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** out)
+int create_context(int device, const hf_shape* shape, int sequences, int pages, hf_ctx** out)
 {
     *out = nullptr;
     auto* ctx = new hf_ctx();
@@ -1178,6 +1324,8 @@ int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** ou
     const hf_shape& s = ctx->shape;
     ctx->capacity = s.max_step_rows > 0 ? s.max_step_rows : s.max_positions;
     ctx->sequences = sequences;
+    ctx->paged = pages > 0;
+    ctx->pages = pages;
     auto bail = [&](int rc) {
         hf_cuda_destroy(ctx);
         return rc;
@@ -1188,6 +1336,8 @@ int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** ou
     ctx->sms = sm_count(device);
     if (const char* knob = std::getenv("HF_GATE"))
         ctx->gate_point = std::max(0, std::min(2, std::atoi(knob)));
+    if (const char* knob = std::getenv("HF_LOCAL_ATTN"))
+        ctx->local_keys = std::max(0, std::atoi(knob));
     if (const char* knob = std::getenv("HF_TC"))
         ctx->tc_off = std::atoi(knob) == 0;
     ctx->max_splits = 128;
@@ -1242,11 +1392,11 @@ int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** ou
     if (device_alloc(ctx, &ctx->hidden, cap * W, "hidden") || device_alloc(ctx, &ctx->normed, cap * W, "normed")
         || device_alloc(ctx, &ctx->qbuf, cap * QW, "queries") || device_alloc(ctx, &ctx->attended, cap * QW, "attended")
         || device_alloc(ctx, &ctx->act, cap * I, "activated") || device_alloc(ctx, &ctx->logits, cap * V, "logits")
-        || device_alloc(ctx, &ctx->kcache, (size_t) s.layers * sequences * P * KVW, "key cache")
-        || device_alloc(ctx, &ctx->vcache, (size_t) s.layers * sequences * P * KVW, "value cache")
+        || device_alloc(ctx, &ctx->kcache, (size_t) s.layers * P * KVW, "key cache")
+        || device_alloc(ctx, &ctx->vcache, (size_t) s.layers * P * KVW, "value cache")
         || device_alloc(ctx, &ctx->rope_cos, P * (s.head_width / 2), "rotary cosines")
         || device_alloc(ctx, &ctx->rope_sin, P * (s.head_width / 2), "rotary sines")
-        || device_alloc(ctx, &ctx->slot_base, sequences * (P + 1), "sequence slots")
+        || device_alloc(ctx, &ctx->slot_base, (ctx->paged ? sequences + 1 : 1) * (P + 1), "sequence slots")
         || device_alloc(ctx, &ctx->state, 8, "step state")
         || device_alloc(ctx, &ctx->cand_val, cand, "argmax candidates")
         || device_alloc(ctx, &ctx->cand_idx, cand, "argmax candidates")
@@ -1255,11 +1405,33 @@ int create_context(int device, const hf_shape* shape, int sequences, hf_ctx** ou
         || device_alloc(ctx, &ctx->sample_uniforms, P + 1, "sampling uniforms")
         || device_alloc(ctx, &ctx->sample_mask, V, "sampling mask"))
         return bail(HF_E_CUDA);
-    ctx->select_sequence(0);
+    ctx->single_slots = ctx->slot_base + (ctx->paged ? (size_t) sequences * (P + 1) : 0);
     cudaMemset(ctx->state, 0, 8 * sizeof(unsigned));
-    cudaMemset(ctx->slot_base, 0, sequences * (P + 1) * sizeof(unsigned));
-    cudaMemset(ctx->kcache, 0, (size_t) s.layers * sequences * P * KVW * sizeof(float));
-    cudaMemset(ctx->vcache, 0, (size_t) s.layers * sequences * P * KVW * sizeof(float));
+    cudaMemset(ctx->slot_base, 0, (ctx->paged ? sequences + 1 : 1) * (P + 1) * sizeof(unsigned));
+    cudaMemset(ctx->kcache, 0, (size_t) s.layers * P * KVW * sizeof(float));
+    cudaMemset(ctx->vcache, 0, (size_t) s.layers * P * KVW * sizeof(float));
+    if (ctx->paged)
+    {
+        // pages + 1: page `pages` is the trash page of inactive sequences.
+        ctx->table_stride = (int) ((P + kPageRows - 1) / kPageRows);
+        const size_t pool = (size_t) s.layers * (pages + 1) * kPageRows * KVW;
+        if (device_alloc(ctx, &ctx->kpages, pool, "key pages") || device_alloc(ctx, &ctx->vpages, pool, "value pages")
+            || device_alloc(ctx, &ctx->admit_k, (size_t) s.layers * P * KVW, "prompt key rows")
+            || device_alloc(ctx, &ctx->admit_v, (size_t) s.layers * P * KVW, "prompt value rows")
+            || device_alloc(ctx, &ctx->page_table_dev, (size_t) sequences * ctx->table_stride, "page table")
+            || device_alloc(ctx, &ctx->seq_pos_dev, sequences, "sequence positions")
+            || device_alloc(ctx, &ctx->seq_active_dev, sequences, "sequence positions"))
+            return bail(HF_E_CUDA);
+        cudaMemset(ctx->kpages, 0, pool * sizeof(float));
+        cudaMemset(ctx->vpages, 0, pool * sizeof(float));
+        ctx->page_table.assign((size_t) sequences * ctx->table_stride, pages);
+        ctx->seq_len.assign(sequences, -1);
+        for (int p = pages - 1; p >= 0; --p)
+            ctx->free_pages.push_back(p);
+        if (ctx->upload_paging())
+            return bail(HF_E_CUDA);
+    }
+    ctx->select_sequence(-1);
 
     // Kernels/RoPE.cpp:7-34: angle = pos * theta^(-2i/D) in double, stored as float.
     const int half = s.head_width / 2;
@@ -1381,12 +1553,20 @@ int hf_cuda_create(int device, const hf_shape* shape, hf_ctx** out)
     *out = nullptr;
     if (!shape_refusal(*shape).empty())
         return HF_E_SHAPE;
-    return create_context(device, shape, 1, out);
+    return create_context(device, shape, 1, 0, out);
 }
 
 int hf_cuda_create_batch(int device, const hf_shape* shape, int sequences, hf_ctx** out)
 {
-    if (!shape || !out || sequences < 1)
+    if (!shape || sequences < 1 || shape->max_positions < 1)
+        return HF_E_INVALID;
+    const int per_sequence = (shape->max_positions + HF_PAGE_ROWS - 1) / HF_PAGE_ROWS;
+    return hf_cuda_create_paged(device, shape, sequences, sequences * per_sequence, out);
+}
+
+int hf_cuda_create_paged(int device, const hf_shape* shape, int sequences, int pages, hf_ctx** out)
+{
+    if (!shape || !out || sequences < 1 || pages < 1)
         return HF_E_INVALID;
     *out = nullptr;
     if (!shape_refusal(*shape).empty())
@@ -1395,7 +1575,7 @@ int hf_cuda_create_batch(int device, const hf_shape* shape, int sequences, hf_ct
     if (sequences > capacity)
         return HF_E_CAPACITY; // a batched step carries one row per sequence
     hf_ctx* ctx = nullptr;
-    const int rc = create_context(device, shape, sequences, &ctx);
+    const int rc = create_context(device, shape, sequences, pages, &ctx);
     if (rc)
         return rc;
     if (!ctx->record_pool) // the batched products run on the stage records only
@@ -1424,7 +1604,8 @@ void hf_cuda_destroy(hf_ctx* ctx)
     void* buffers[] = {ctx->pool, ctx->record_pool, ctx->slice_pool, ctx->down_acc, ctx->tc_pool, ctx->tc_x, ctx->tc_xunscale, ctx->tc_ws, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
                        ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slot_base, ctx->state,
                        ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev,
-                       ctx->sample_uniforms, ctx->sample_mask};
+                       ctx->sample_uniforms, ctx->sample_mask, ctx->kpages, ctx->vpages, ctx->admit_k, ctx->admit_v,
+                       ctx->page_table_dev, ctx->seq_pos_dev, ctx->seq_active_dev};
     for (void* b: buffers)
         if (b)
             cudaFree(b);
@@ -1856,25 +2037,101 @@ int hf_cuda_generate_greedy(hf_ctx* ctx, const uint32_t* prompt, int prompt_leng
     return HF_OK;
 }
 
+namespace
+{
+int batch_ready(hf_ctx* ctx)
+{
+    if (!ctx->all_loaded())
+        return ctx->fail(HF_E_NOT_READY, "this decoder has not been prepared: every weight must be uploaded");
+    if (!ctx->paged || !ctx->record_pool)
+        return ctx->fail(HF_E_SHAPE, "batched steps need a batch context of a shape the stage records serve");
+    return HF_OK;
+}
+
+int prompt_refusal(hf_ctx* ctx, const uint32_t* prompt, int prompt_length)
+{
+    if (prompt_length <= 0)
+        return ctx->fail(HF_E_INVALID, "a run needs at least one prompt token");
+    if (prompt_length > ctx->shape.max_positions)
+        return ctx->fail(HF_E_WINDOW, "this prompt holds " + std::to_string(prompt_length) + " tokens and the window is "
+                                          + std::to_string(ctx->shape.max_positions));
+    return check_tokens(ctx, prompt, prompt_length);
+}
+} // namespace
+
+int hf_cuda_admit_async(hf_ctx* ctx, int sequence, const uint32_t* prompt, int prompt_length)
+{
+    if (!ctx || !prompt)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    if (const int rc = batch_ready(ctx))
+        return rc;
+    if (sequence < 0 || sequence >= ctx->sequences)
+        return ctx->fail(HF_E_INVALID, "there is no sequence " + std::to_string(sequence) + " in this batch");
+    if (ctx->seq_len[sequence] >= 0)
+        return ctx->fail(HF_E_INVALID, "sequence " + std::to_string(sequence) + " is active: release it first");
+    if (const int rc = prompt_refusal(ctx, prompt, prompt_length))
+        return rc;
+    if (!ctx->reserve(sequence, prompt_length))
+        return ctx->fail(HF_E_CAPACITY, "the KV page pool has " + std::to_string(ctx->free_pages.size())
+                                            + " free pages and this prompt needs "
+                                            + std::to_string(ctx->pages_for(prompt_length)));
+    const int rc = ctx->admit(sequence, prompt, prompt_length);
+    if (rc)
+        ctx->release(sequence);
+    return rc;
+}
+
+int hf_cuda_release(hf_ctx* ctx, int sequence)
+{
+    if (!ctx)
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    if (!ctx->paged || sequence < 0 || sequence >= ctx->sequences)
+        return ctx->fail(HF_E_INVALID, "there is no batched sequence " + std::to_string(sequence));
+    if (ctx->seq_len[sequence] < 0)
+        return ctx->fail(HF_E_INVALID, "sequence " + std::to_string(sequence) + " is not active");
+    ctx->release(sequence);
+    return ctx->upload_paging();
+}
+
+int hf_cuda_sequence_position(const hf_ctx* ctx, int sequence)
+{
+    if (!ctx || !ctx->paged || sequence < 0 || sequence >= ctx->sequences)
+        return HF_E_INVALID;
+    return ctx->seq_len[sequence];
+}
+
+int hf_cuda_free_pages(const hf_ctx* ctx)
+{
+    if (!ctx || !ctx->paged)
+        return HF_E_INVALID;
+    return (int) ctx->free_pages.size();
+}
+
 int hf_cuda_prefill_batch_async(hf_ctx* ctx, const uint32_t* prompts, int prompt_length)
 {
     if (!ctx || !prompts)
         return HF_E_INVALID;
     cudaSetDevice(ctx->device);
+    if (const int rc = batch_ready(ctx))
+        return rc;
     for (int q = 0; q < ctx->sequences; ++q)
-        if (const int rc = check_tokens(ctx, prompts + (size_t) q * prompt_length, std::max(prompt_length, 0)))
+        if (const int rc = prompt_refusal(ctx, prompts + (size_t) q * std::max(prompt_length, 0), prompt_length))
             return rc;
+    if ((long long) ctx->sequences * ctx->pages_for(prompt_length) > ctx->pages)
+        return ctx->fail(HF_E_CAPACITY, "the KV page pool holds " + std::to_string(ctx->pages) + " pages and "
+                                            + std::to_string(ctx->sequences) + " prompts of "
+                                            + std::to_string(prompt_length) + " tokens need more");
+    for (int q = 0; q < ctx->sequences; ++q)
+        if (ctx->seq_len[q] >= 0)
+            ctx->release(q);
     for (int q = 0; q < ctx->sequences; ++q)
     {
-        ctx->select_sequence(q);
-        const int rc = hf_cuda_prefill_async(ctx, prompts + (size_t) q * prompt_length, prompt_length);
-        if (rc)
-        {
-            ctx->select_sequence(0);
+        ctx->reserve(q, prompt_length);
+        if (const int rc = ctx->admit(q, prompts + (size_t) q * prompt_length, prompt_length))
             return rc;
-        }
     }
-    ctx->select_sequence(0);
     return HF_OK;
 }
 
@@ -1883,14 +2140,31 @@ int hf_cuda_decode_batch_async(hf_ctx* ctx, int steps)
     if (!ctx || steps < 0)
         return HF_E_INVALID;
     cudaSetDevice(ctx->device);
-    if (!ctx->all_loaded())
-        return ctx->fail(HF_E_NOT_READY, "this decoder has not been prepared: every weight must be uploaded");
-    if (!ctx->record_pool)
-        return ctx->fail(HF_E_SHAPE, "batched steps run on the stage records, which this shape has none of");
-    if (ctx->position + steps > ctx->shape.max_positions)
-        return ctx->fail(HF_E_WINDOW, "these steps would carry the sequences past the window");
-    if (ctx->position == 0 && steps > 0)
-        return ctx->fail(HF_E_INVALID, "a decode step follows a prefill: the sequences are empty");
+    if (const int rc = batch_ready(ctx))
+        return rc;
+    int active = 0, needed = 0;
+    for (int q = 0; q < ctx->sequences; ++q)
+    {
+        const int len = ctx->seq_len[q];
+        if (len < 0)
+            continue;
+        ++active;
+        if (len + steps > ctx->shape.max_positions)
+            return ctx->fail(HF_E_WINDOW, "these steps would carry sequence " + std::to_string(q) + " past the window");
+        needed += std::max(0, ctx->pages_for(len + steps) - ctx->pages_held(q));
+    }
+    if (active == 0 && steps > 0)
+        return ctx->fail(HF_E_INVALID, "a decode step follows a prefill: no sequence of the batch is active");
+    if (needed > (int) ctx->free_pages.size())
+        return ctx->fail(HF_E_CAPACITY, "these steps need " + std::to_string(needed) + " more KV pages and the pool has "
+                                            + std::to_string(ctx->free_pages.size()));
+    if (steps == 0)
+        return HF_OK;
+    for (int q = 0; q < ctx->sequences; ++q)
+        if (ctx->seq_len[q] >= 0)
+            ctx->reserve(q, ctx->seq_len[q] + steps);
+    if (const int rc = ctx->upload_paging())
+        return rc;
     for (int i = 0; i < steps; ++i)
     {
         const int rc = ctx->enqueue_batch_step();
@@ -2296,6 +2570,168 @@ int hf_cuda_linear_q8(const float* input, const uint8_t* weights, const float* b
     return err == cudaSuccess ? HF_OK : HF_E_CUDA;
 }
 
+} // extern "C"
+
+// A Q8_0 weight prepared for the decoder's product kernels (hf_cuda_linear_*).
+struct hf_linear
+{
+    int device = 0;
+    int sms = 1;
+    uint32_t inner = 0, outputs = 0, max_rows = 0;
+    uint8_t* base = nullptr;    // the two-region bytes
+    uint8_t* records = nullptr; // stage records (int8 MMA rows kernel), or null
+    uint8_t* tc = nullptr;      // tensor-core blocks, or null
+    __half* tc_x = nullptr;
+    float* tc_xunscale = nullptr;
+    float* tc_ws = nullptr;
+
+    bool records_serve() const { return (inner == 2048 || inner == 16384) && outputs % kTileRows == 0; }
+    bool tc_serve() const { return (inner == 2048 || inner == 16384) && outputs % kTcRows == 0; }
+
+    int path(uint32_t rows) const
+    {
+        if (rows == 1 && (inner == 2048 || inner == 4096 || inner == 8192 || inner == 16384))
+            return HF_LINEAR_STREAM;
+        if (rows <= (uint32_t) kRowsBlock && records)
+            return HF_LINEAR_ROWS_MMA;
+        if (rows > (uint32_t) kRowsBlock && tc)
+            return HF_LINEAR_TENSOR_CORES;
+        return HF_LINEAR_GENERIC;
+    }
+};
+
+namespace
+{
+template <Epi E>
+cudaError_t linear_run(const hf_linear& lin, const GemvArgs& a, cudaStream_t s)
+{
+    switch (lin.path((uint32_t) a.M))
+    {
+    case HF_LINEAR_STREAM:
+    {
+        cudaError_t err = cudaSuccess;
+        stream_product<E>(a.K, false, stream_grid(a.K, a.N, lin.sms), s, a, &err);
+        return err;
+    }
+    case HF_LINEAR_ROWS_MMA:
+        return a.K == 16384 ? rows_mma_product<E, 16384>(false, lin.records, s, a, lin.sms)
+                            : rows_mma_product<E, 2048>(false, lin.records, s, a, lin.sms);
+    case HF_LINEAR_TENSOR_CORES:
+        return tc_product_on<E>(lin.tc, a, s, lin.tc_x, lin.tc_xunscale, lin.tc_ws, lin.sms);
+    default:
+        return generic_product<E>(false, a.N, s, a, lin.sms);
+    }
+}
+} // namespace
+
+extern "C" {
+void hf_cuda_linear_destroy(hf_linear* lin)
+{
+    if (!lin)
+        return;
+    cudaSetDevice(lin->device);
+    cudaFree(lin->base);
+    cudaFree(lin->records);
+    cudaFree(lin->tc);
+    cudaFree(lin->tc_x);
+    cudaFree(lin->tc_xunscale);
+    cudaFree(lin->tc_ws);
+    delete lin;
+}
+
+int hf_cuda_linear_create(int device, const uint8_t* weights, uint32_t inner, uint32_t outputs, uint32_t max_rows,
+                          hf_linear** out)
+{
+    if (!out)
+        return HF_E_INVALID;
+    *out = nullptr;
+    if (!weights || inner == 0 || outputs == 0 || max_rows == 0)
+        return HF_E_INVALID;
+    if (inner % 32 != 0 || ((uint64_t) inner * outputs) % 64 != 0)
+        return HF_E_SHAPE;
+    if (cudaSetDevice(device) != cudaSuccess)
+        return HF_E_CUDA;
+    configure_once(device);
+    auto* lin = new hf_linear();
+    lin->device = device;
+    lin->sms = sm_count(device);
+    lin->inner = inner;
+    lin->outputs = outputs;
+    lin->max_rows = max_rows;
+    auto bail = [&](int rc) {
+        hf_cuda_linear_destroy(lin);
+        return rc;
+    };
+    const size_t elements = (size_t) inner * outputs;
+    const size_t bytes = elements + elements / 16;
+    if (cudaMalloc(&lin->base, bytes) != cudaSuccess
+        || cudaMemcpy(lin->base, weights, bytes, cudaMemcpyDefault) != cudaSuccess)
+        return bail(HF_E_CUDA);
+    const __half* scales = reinterpret_cast<const __half*>(lin->base + elements);
+    if (lin->records_serve() && max_rows > 1)
+    {
+        if (cudaMalloc(&lin->records, bytes) != cudaSuccess)
+            return bail(HF_E_CUDA);
+        build_records<<<(outputs / 16) * (inner / 2048), 256>>>(lin->base, (int) outputs, (int) inner, lin->records);
+    }
+    if (lin->tc_serve() && max_rows > (uint32_t) kRowsBlock)
+    {
+        size_t ws = 1;
+        for (uint32_t m = kRowsBlock + 1; m <= max_rows; ++m)
+        {
+            const TcPlan plan = tc_plan((int) m, (int) outputs, (int) inner, lin->sms);
+            if (plan.splits > 1)
+                ws = std::max(ws, (size_t) plan.splits * plan.m_pad * outputs);
+        }
+        const size_t m_pad = tc_plan((int) max_rows, (int) outputs, (int) inner, lin->sms).m_pad;
+        if (cudaMalloc(&lin->tc, tc_weight_bytes(outputs, inner)) != cudaSuccess
+            || cudaMalloc(&lin->tc_x, tc_x_bytes(m_pad, inner)) != cudaSuccess
+            || cudaMalloc(&lin->tc_xunscale, m_pad * sizeof(float)) != cudaSuccess
+            || cudaMalloc(&lin->tc_ws, ws * sizeof(float)) != cudaSuccess)
+            return bail(HF_E_CUDA);
+        build_tc_blocks<<<outputs / kTcRows, kTcRows>>>(lin->base, scales, (int) inner, lin->tc);
+    }
+    if (cudaDeviceSynchronize() != cudaSuccess)
+        return bail(HF_E_CUDA);
+    *out = lin;
+    return HF_OK;
+}
+
+int hf_cuda_linear_path(const hf_linear* lin, uint32_t rows)
+{
+    if (!lin || rows == 0 || rows > lin->max_rows)
+        return HF_E_INVALID;
+    return lin->path(rows);
+}
+
+int hf_cuda_linear_run(const hf_linear* lin, const float* input, const float* bias, float* output, uint32_t rows,
+                       int gelu, int residual, void* stream)
+{
+    if (!lin || !input || !output || rows == 0)
+        return HF_E_INVALID;
+    if (rows > lin->max_rows)
+        return HF_E_CAPACITY;
+    if (gelu && residual)
+        return HF_E_INVALID;
+    if ((uintptr_t) input % 16 != 0)
+        return HF_E_INVALID;
+    if (cudaSetDevice(lin->device) != cudaSuccess)
+        return HF_E_CUDA;
+    GemvArgs a = {};
+    a.w = lin->base;
+    a.scales = reinterpret_cast<const __half*>(lin->base + (size_t) lin->inner * lin->outputs);
+    a.N = (int) lin->outputs;
+    a.K = (int) lin->inner;
+    a.M = (int) rows;
+    a.x = input;
+    a.bias = bias;
+    a.out = output;
+    cudaStream_t s = (cudaStream_t) stream;
+    const cudaError_t err = gelu ? linear_run<Epi::Gelu>(*lin, a, s)
+                                 : (residual ? linear_run<Epi::Residual>(*lin, a, s) : linear_run<Epi::Store>(*lin, a, s));
+    return err == cudaSuccess ? HF_OK : HF_E_CUDA;
+}
+
 int hf_cuda_quantize_q8(const float* values, int64_t first, int64_t count, int64_t element_count, uint8_t* destination,
                         void* stream)
 {
@@ -2305,8 +2741,9 @@ int hf_cuda_quantize_q8(const float* values, int64_t first, int64_t count, int64
         return HF_OK;
     const long long threads = count; // one lane per element, a warp per block
     const int grid = (int) ((threads + 255) / 256);
-    quantize_q8<<<grid, 256, 0, (cudaStream_t) stream>>>(values, first, count, element_count, destination);
-    return cudaGetLastError() == cudaSuccess ? HF_OK : HF_E_CUDA;
+    const cudaError_t e = launch(false, quantize_q8<float>, dim3(grid), dim3(256), 0, (cudaStream_t) stream, values,
+                                 (long long) first, (long long) count, (long long) element_count, destination);
+    return e == cudaSuccess ? HF_OK : HF_E_CUDA;
 }
 }
 
@@ -2370,15 +2807,20 @@ cudaError_t launch_quantize(hfst::Dtype dtype, const void* raw, long long at, lo
     const dim3 grid((unsigned) ((count / kBlock * 32 + 255) / 256));
     switch (dtype)
     {
-    case hfst::Dtype::F32: quantize_q8<<<grid, 256>>>((const float*) raw, at, count, total, destination); break;
-    case hfst::Dtype::F16: quantize_q8<<<grid, 256>>>((const __half*) raw, at, count, total, destination); break;
+    case hfst::Dtype::F32:
+        return launch(false, quantize_q8<float>, grid, dim3(256), 0, nullptr, (const float*) raw, at, count, total,
+                      destination);
+    case hfst::Dtype::F16:
+        return launch(false, quantize_q8<__half>, grid, dim3(256), 0, nullptr, (const __half*) raw, at, count, total,
+                      destination);
     case hfst::Dtype::BF16:
-        quantize_q8<<<grid, 256>>>((const __nv_bfloat16*) raw, at, count, total, destination);
-        break;
-    case hfst::Dtype::F64: quantize_q8<<<grid, 256>>>((const double*) raw, at, count, total, destination); break;
+        return launch(false, quantize_q8<__nv_bfloat16>, grid, dim3(256), 0, nullptr, (const __nv_bfloat16*) raw, at,
+                      count, total, destination);
+    case hfst::Dtype::F64:
+        return launch(false, quantize_q8<double>, grid, dim3(256), 0, nullptr, (const double*) raw, at, count, total,
+                      destination);
     default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 } // namespace
 

@@ -15,7 +15,7 @@ namespace hfk
 // slots start at slots + r * slot_stride, every row at `position`.
 __global__ void __launch_bounds__(256) embed_q8(const uint8_t* table, const __half* scales, int width, int vocab,
                                                  float scale, const unsigned* slots, const unsigned* state, int rows,
-                                                 float* out, unsigned* err, int slot_stride)
+                                                 float* out, unsigned* err, int slot_stride, const unsigned* seq_pos)
 {
     pdl_wait();
     const unsigned position = state ? *(volatile const unsigned*) state : 0u;
@@ -24,7 +24,9 @@ __global__ void __launch_bounds__(256) embed_q8(const uint8_t* table, const __ha
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (row >= rows || c >= width)
         return;
-    unsigned token = slot_stride ? slots[(size_t) row * slot_stride + position] : slots[position + row];
+    // slot_stride: row r is sequence r, at seq_pos[r] when given, else at the shared position.
+    unsigned token = slot_stride ? slots[(size_t) row * slot_stride + (seq_pos ? seq_pos[row] : position)]
+                                 : slots[position + row];
     if (token >= (unsigned) vocab)
     {
         if (c == 0)
@@ -171,11 +173,14 @@ __global__ void argmax_final(const float* cand_val, const unsigned* cand_idx, in
 }
 
 // The batched decode's last fold: row r's token (argmax_final's rule) into
-// sequence r's slot after `position` (slots[r * slot_stride + position + 1]);
-// row 0 advances the shared position. `position` is the step's, from the host:
-// the rows may not read the state that row 0 writes.
+// sequence r's slot after its position. With seq_pos (paged sequences) the
+// position is seq_pos[r], and an active sequence's slot seq_pos[r] + 1 is
+// written and seq_pos[r] advanced; an inactive one (active[r] == 0) is left as
+// it is. Without, `position` is the step's shared one, from the host (the rows
+// may not read the state that row 0 writes), and row 0 advances it.
 __global__ void argmax_final_batch(const float* cand_val, const unsigned* cand_idx, int parts, unsigned* slots,
-                                   int slot_stride, unsigned position, unsigned* state)
+                                   int slot_stride, unsigned position, unsigned* state, unsigned* seq_pos,
+                                   const unsigned* active)
 {
     pdl_wait();
     pdl_trigger();
@@ -184,9 +189,43 @@ __global__ void argmax_final_batch(const float* cand_val, const unsigned* cand_i
     const unsigned best_i = fold_candidates(cand_val, cand_idx, parts, row, lane);
     if (lane == 0)
     {
-        slots[(size_t) row * slot_stride + position + 1] = best_i == 0xFFFFFFFFu ? 0u : best_i;
-        if (row == 0)
-            *state = position + 1;
+        const unsigned token = best_i == 0xFFFFFFFFu ? 0u : best_i;
+        if (seq_pos)
+        {
+            if (active[row])
+            {
+                const unsigned p = seq_pos[row];
+                slots[(size_t) row * slot_stride + p + 1] = token;
+                seq_pos[row] = p + 1;
+            }
+        }
+        else
+        {
+            slots[(size_t) row * slot_stride + position + 1] = token;
+            if (row == 0)
+                *state = position + 1;
+        }
+    }
+}
+
+// Copies rows [0, rows) of one sequence's contiguous caches ([layer][positions]
+// [kv width], layer stride contiguous_stride floats) into its pages (pool
+// [layer][pages][page_rows][kv width], layer stride page_stride floats; the
+// page of position p is table[p / page_rows]). Grid (rows, layers), 256 threads.
+__global__ void __launch_bounds__(256) scatter_rows_to_pages(const float* k_rows, const float* v_rows,
+                                                             size_t contiguous_stride, int kv_width, const int* table,
+                                                             int page_rows, float* k_pages, float* v_pages,
+                                                             size_t page_stride)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int p = blockIdx.x, layer = blockIdx.y;
+    const size_t from = layer * contiguous_stride + (size_t) p * kv_width;
+    const size_t to = layer * page_stride + ((size_t) table[p / page_rows] * page_rows + p % page_rows) * kv_width;
+    for (int c = threadIdx.x * 4; c < kv_width; c += blockDim.x * 4)
+    {
+        *reinterpret_cast<float4*>(k_pages + to + c) = __ldcg(reinterpret_cast<const float4*>(k_rows + from + c));
+        *reinterpret_cast<float4*>(v_pages + to + c) = __ldcg(reinterpret_cast<const float4*>(v_rows + from + c));
     }
 }
 

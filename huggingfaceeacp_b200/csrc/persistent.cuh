@@ -108,6 +108,7 @@ struct PersistentArgs
     int steps;
     int gate_point;            // where a layer's gate/up records are released: 0 never held, 1 after the
                                // attention phase, 2 after the o_proj staging
+    int local_keys;            // contexts of up to this many keys: every CTA computes the whole attention
     unsigned long long* trace; // [gridDim.x][kTraceEvents] first-step phase stamps, or null
     unsigned long long* down_acc; // [2][2048] the down sums in units of 2^-32, by layer parity
 };
@@ -396,10 +397,11 @@ __device__ __forceinline__ void prefetch_split(const LayerDev& L, unsigned posit
 // and keeps the running (max, sum) of head head_of_lane<4>(lane) with the
 // four heads' unnormalised rows. The eight warps of a group fold at the end
 // through `area`, which then holds both groups' folds. Writes the attended row
-// (one split) or the split's (max, sum, unnormalised row).
+// (one split: to `local` in shared memory when given, else to p.attended) or
+// the split's (max, sum, unnormalised row).
 template <typename Stamp>
 __device__ void attend_split(const PersistentArgs& p, const LayerDev& L, unsigned position, int split, int splits,
-                             float* area, int tid, Stamp stamp)
+                             float* area, int tid, Stamp stamp, float* local = nullptr)
 {
     constexpr int D = 256, QH = kAttnHeads;
     const int group = tid >> 8, warp = (tid >> 5) & 7, lane = tid & 31;
@@ -572,7 +574,7 @@ __device__ void attend_split(const PersistentArgs& p, const LayerDev& L, unsigne
         const float head_max = __shfl_sync(0xFFFFFFFFu, mx, h * 8);
         const int head = head0 + h;
         if (splits == 1)
-            p.attended[head * D + d] = value / sum;
+            (local ? local : p.attended)[head * D + d] = value / sum;
         else
         {
             const size_t slot = (size_t) split * p.heads + head;
@@ -851,7 +853,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
     __shared__ float red[kPGroups * 2 * 8 * kTileRows];
 
     const Ring ring {smem, smem + kRecordQuants, full, empty, kRecordBytes, kRecordBytes}; // a record per slot
-    float* sx = reinterpret_cast<float*>(smem + NST * kRecordBytes); // down: k-block factors, row sums
+    float* sx = reinterpret_cast<float*>(smem + NST * kRecordBytes); // the attended row of a local attention
     uint2* frags = reinterpret_cast<uint2*>(sx + 2048);             // limb B fragments (8 KiB)
     float* attn_area = sx + 4096; // attention K/V tile and folds; the merge's landing; the CTA's activation blocks
 
@@ -920,7 +922,11 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
             trace_row = nullptr; // the first step only
         const unsigned position = position0 + (unsigned) step;
         const int keys = (int) position + 1;
-        const int splits = attention_splits(keys, p.max_splits);
+        // Short contexts: every CTA attends over all keys itself (the K/V rows
+        // come from L2), so o_proj starts without a grid barrier or a fold of
+        // splits. Longer ones: one CTA per split, a barrier, then the fold.
+        const bool local_attn = keys <= p.local_keys;
+        const int splits = local_attn ? 1 : attention_splits(keys, p.max_splits);
 
         // ---- embed: every CTA gathers the row; CTA 0 also writes the residual
         // stream (Kernels/Embed.h:45-77). The step's rotary row and layer 0's
@@ -988,8 +994,8 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
                 consume_tiles<Epi::QkvRope, NST, kPGroups>(a, cta_tiles(p.qkv_rows, cta, ctas), ring, seq, bfrag,
                                                            bfactor, red, position, best, best_i, group, 2 + group);
             }
-            if (cta < splits)
-                prefetch_split(L, position, cta, splits, attn_area, tid);
+            if (local_attn || cta < splits)
+                prefetch_split(L, position, local_attn ? 0 : cta, splits, attn_area, tid);
             if (!barrier(ts + kTrQkvDone, ts + kTrQkvLeft))
                 return;
             if (cta == 0 && l > 0)
@@ -1002,11 +1008,21 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
                 z[2 * tid + 1] = make_longlong2(0, 0);
             }
 
-            // ---- attention: one CTA per context split, all eight heads
-            if (cta < splits)
-                attend_split(p, L, position, cta, splits, attn_area, tid, [&](int event) { stamp(ts + event); });
-            if (!barrier(ts + kTrAttnDone, ts + kTrAttnLeft))
-                return;
+            // ---- attention: all eight heads, in every CTA (short contexts) or
+            // one CTA per context split
+            if (local_attn)
+            {
+                attend_split(p, L, position, 0, 1, attn_area, tid, [&](int event) { stamp(ts + event); }, sx);
+                stamp(ts + kTrAttnDone);
+                consumers_sync(); // the whole attended row is in sx
+            }
+            else
+            {
+                if (cta < splits)
+                    attend_split(p, L, position, cta, splits, attn_area, tid, [&](int event) { stamp(ts + event); });
+                if (!barrier(ts + kTrAttnDone, ts + kTrAttnLeft))
+                    return;
+            }
             if (tid == 0 && p.gate_point == 1)
                 mbar_arrive(&gate); // the producer may stream this layer's gate/up records now
             const bool fused_merge = splits > 1 && splits <= kFusedMergeSplits;
@@ -1027,9 +1043,10 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
                 a.N = 2048;
                 a.out = p.hidden;
                 a.err = p.err;
-                stage(fused_merge ? merged_attention(p.attn_acc, p.attn_ml, splits, p.heads, attn_area, red, tid,
-                                                     [&](int event) { stamp(ts + event); })
-                                  : __ldcg(reinterpret_cast<const float4*>(p.attended) + tid),
+                stage(local_attn    ? reinterpret_cast<const float4*>(sx)[tid]
+                      : fused_merge ? merged_attention(p.attn_acc, p.attn_ml, splits, p.heads, attn_area, red, tid,
+                                                       [&](int event) { stamp(ts + event); })
+                                    : __ldcg(reinterpret_cast<const float4*>(p.attended) + tid),
                       false, ts + kTrOStaged);
                 if (tid == 0 && p.gate_point == 2)
                     mbar_arrive(&gate);

@@ -198,6 +198,12 @@ def cuda() -> ctypes.CDLL:
         lib.hf_cuda_create_batch.argtypes = [ctypes.c_int, ctypes.POINTER(ShapeStruct), ctypes.c_int,
                                              ctypes.POINTER(_vp)]
         lib.hf_cuda_sequences.argtypes = [_vp]
+        lib.hf_cuda_create_paged.argtypes = [ctypes.c_int, ctypes.POINTER(ShapeStruct), ctypes.c_int, ctypes.c_int,
+                                             ctypes.POINTER(_vp)]
+        lib.hf_cuda_admit_async.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int]
+        lib.hf_cuda_release.argtypes = [_vp, ctypes.c_int]
+        lib.hf_cuda_sequence_position.argtypes = [_vp, ctypes.c_int]
+        lib.hf_cuda_free_pages.argtypes = [_vp]
         lib.hf_cuda_prefill_batch_async.argtypes = [_vp, _vp, ctypes.c_int]
         lib.hf_cuda_decode_batch_async.argtypes = [_vp, ctypes.c_int]
         lib.hf_cuda_read_batch_slots.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp]
@@ -234,6 +240,12 @@ def cuda() -> ctypes.CDLL:
         lib.hf_cuda_linear_q8.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
                                           ctypes.c_int, ctypes.c_int, _vp]
         lib.hf_cuda_quantize_q8.argtypes = [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _vp]
+        lib.hf_cuda_linear_create.argtypes = [ctypes.c_int, _vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                              ctypes.POINTER(_vp)]
+        lib.hf_cuda_linear_run.argtypes = [_vp, _vp, _vp, _vp, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, _vp]
+        lib.hf_cuda_linear_path.argtypes = [_vp, ctypes.c_uint32]
+        lib.hf_cuda_linear_destroy.argtypes = [_vp]
+        lib.hf_cuda_linear_destroy.restype = None
         lib.hf_cuda_argmax_noalloc.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, _vp]
         lib.hf_cuda_time_kernel.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_float),
                                             ctypes.POINTER(ctypes.c_double)]
@@ -349,20 +361,27 @@ def model_tensors(shape: DecoderShape):
 
 # ---------------------------------------------------------------------------
 
+PAGE_ROWS = 64  # hf_cuda.h HF_PAGE_ROWS: positions per KV page of a batched sequence
+
+
 class Context:
     """One hf_ctx: a prepared decoder on one device (HF::Decoder + DecoderWeights).
 
-    sequences > 1 makes a batch context (hf_cuda_create_batch): that many
-    independent sequences decoded together by the *_batch methods; the other
-    methods act on sequence 0."""
+    sequences > 1 (or pages given) makes a batch context: that many independent
+    sequences over a paged KV cache, decoded together by the *_batch methods
+    and admitted / released one by one; `pages` sizes the page pool
+    (hf_cuda_create_paged), None reserves every sequence's whole window
+    (hf_cuda_create_batch). The other methods use the single-sequence window."""
 
-    def __init__(self, shape: DecoderShape, device: int = 0, sequences: int = 1):
+    def __init__(self, shape: DecoderShape, device: int = 0, sequences: int = 1, pages: int | None = None):
         self.lib = cuda()
         self.shape = shape
         self.sequences = sequences
         handle = _vp()
         struct = shape.struct()
-        if sequences == 1:
+        if pages is not None:
+            rc = self.lib.hf_cuda_create_paged(device, ctypes.byref(struct), sequences, pages, ctypes.byref(handle))
+        elif sequences == 1:
             rc = self.lib.hf_cuda_create(device, ctypes.byref(struct), ctypes.byref(handle))
         else:
             rc = self.lib.hf_cuda_create_batch(device, ctypes.byref(struct), sequences, ctypes.byref(handle))
@@ -506,6 +525,22 @@ class Context:
     def decode_batch_async(self, steps: int):
         self.check(self.lib.hf_cuda_decode_batch_async(self.handle, steps))
 
+    def admit_async(self, sequence: int, prompt):
+        """Admits one sequence of a batch with its prompt (hf_cuda_admit_async)."""
+        prompt = np.ascontiguousarray(prompt, dtype=np.uint32)
+        self.check(self.lib.hf_cuda_admit_async(self.handle, sequence, _ptr(prompt), prompt.size))
+
+    def release(self, sequence: int):
+        self.check(self.lib.hf_cuda_release(self.handle, sequence))
+
+    def sequence_position(self, sequence: int) -> int:
+        """Tokens in a batched sequence's cache, -1 when it is not active."""
+        return int(self.lib.hf_cuda_sequence_position(self.handle, sequence))
+
+    @property
+    def free_pages(self) -> int:
+        return int(self.lib.hf_cuda_free_pages(self.handle))
+
     def read_batch_slots(self, first: int, count: int) -> np.ndarray:
         out = np.empty((self.sequences, count), dtype=np.uint32)
         self.check(self.lib.hf_cuda_read_batch_slots(self.handle, first, count, _ptr(out)))
@@ -547,6 +582,51 @@ class Context:
         nbytes = ctypes.c_double(0.0)
         self.check(self.lib.hf_cuda_time_kernel(self.handle, kernel, reps, ctypes.byref(us), ctypes.byref(nbytes)))
         return float(us.value), float(nbytes.value)
+
+
+# Kernels a prepared linear runs (hf_cuda.h HF_LINEAR_*).
+LINEAR_STREAM, LINEAR_ROWS_MMA, LINEAR_TENSOR_CORES, LINEAR_GENERIC = range(4)
+LINEAR_PATH_NAMES = ("q8_gemv_stream", "q8_rows_mma", "q8_tc_gemm", "q8_rows_generic")
+
+
+class Linear:
+    """One Q8_0 weight prepared for the product kernels (hf_cuda_linear_*):
+    LinearProductFor<Int8Blocks> bound to its stored weight. `weights` is the
+    two-region bytes (host array, or a device address as an int); run() takes
+    device addresses (ints) and enqueues on `stream`."""
+
+    def __init__(self, weights, inner: int, outputs: int, max_rows: int, device: int = 0):
+        self.lib = cuda()
+        handle = _vp()
+        pointer = weights if isinstance(weights, int) else _ptr(np.ascontiguousarray(weights, dtype=np.uint8))
+        rc = self.lib.hf_cuda_linear_create(device, pointer, inner, outputs, max_rows, ctypes.byref(handle))
+        if rc:
+            raise HFError(rc, "the engine refused the linear weight")
+        self.handle, self.inner, self.outputs, self.max_rows = handle, inner, outputs, max_rows
+
+    def path(self, rows: int) -> int:
+        return int(self.lib.hf_cuda_linear_path(self.handle, rows))
+
+    def run(self, input_ptr: int, output_ptr: int, rows: int, bias_ptr: int | None = None, gelu: bool = False,
+            residual: bool = False, stream: int | None = None):
+        rc = self.lib.hf_cuda_linear_run(self.handle, input_ptr, bias_ptr, output_ptr, rows, int(gelu), int(residual),
+                                         stream)
+        if rc:
+            raise HFError(rc, "linear run refused")
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.hf_cuda_linear_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
 
 
 def device_count() -> int:

@@ -214,29 +214,57 @@ enum { HF_DECODE_AUTO = 0, HF_DECODE_GRAPH = 1, HF_DECODE_PERSISTENT = 2 };
 int hf_cuda_set_decode_path(hf_ctx* ctx, int path);
 int hf_cuda_decode_path(const hf_ctx* ctx);
 
-/* ---- batched greedy decode of independent sequences ----------------------
- * No counterpart in the reference, whose Decoder holds one sequence
- * (Decoder.h:69-136) and runs several rows only for a prefill block
- * (Decoder.cpp:400). A batch context holds `sequences` sequences that share
- * the weights and one position: each has its own token slots and K/V caches
- * ([layer][sequence][position][kv width] fp32). A batched step runs one row
- * per sequence through the multi-row tensor-core products (64 sequences to
- * one MMA tile), so the weights stream from HBM once per step, and every sequence's
- * tokens equal what hf_cuda_generate_greedy produces for that sequence alone.
- * Refusals: sequences > the step capacity (HF_E_CAPACITY), and shapes the
- * stage records do not serve (HF_E_SHAPE; they need width 2048, 8 query
- * heads of 256 over 1 KV head, a 16384-wide feed-forward and a vocabulary of
- * whole 16-row tiles: Gemma-2B's). The single-sequence calls of a batch
- * context act on sequence 0. */
+/* ---- batched greedy decode of independent sequences over a paged KV cache --
+ * No counterpart in the reference, whose Decoder holds one sequence with one
+ * contiguous cache of maxPositions rows per layer (Decoder.h:69-136,
+ * DecoderShape.h:105, Decoder.cpp:199-203) and runs several rows only for a
+ * prefill block (Decoder.cpp:400). A batch context holds `sequences`
+ * sequences that share the weights; each has its own position, token slots
+ * and K/V cache. The caches are paged: fixed pages of HF_PAGE_ROWS positions
+ * ([layer][page][position][kv width] fp32) drawn from one pool as a sequence
+ * grows and returned when it is released, each sequence finding its pages
+ * through its row of a page table, so sequences of different lengths share a
+ * step and are admitted and retired independently. A batched step runs one
+ * row per sequence through the multi-row tensor-core products (64 sequences to
+ * one MMA tile), so the weights stream from HBM once per step, and every
+ * sequence's tokens equal what hf_cuda_generate_greedy produces for that
+ * sequence alone. Refusals: sequences > the step capacity (HF_E_CAPACITY),
+ * and shapes the stage records do not serve (HF_E_SHAPE; they need width
+ * 2048, 8 query heads of 256 over 1 KV head, a 16384-wide feed-forward and a
+ * vocabulary of whole 16-row tiles: Gemma-2B's). The single-sequence calls of
+ * a batch context (hf_cuda_step, hf_cuda_generate_greedy, hf_cuda_*_async)
+ * use a window of their own, apart from the batched sequences. */
+#define HF_PAGE_ROWS 64
+/* A batch context whose pool reserves every sequence's whole window. */
 int hf_cuda_create_batch(int device, const hf_shape* shape, int sequences, hf_ctx** out);
+/* A batch context whose pool holds `pages` pages (each HF_PAGE_ROWS positions
+ * of every layer's K and V: 2 * layers * HF_PAGE_ROWS * kv width * 4 bytes). */
+int hf_cuda_create_paged(int device, const hf_shape* shape, int sequences, int pages, hf_ctx** out);
 /* The sequences a context holds (1 for hf_cuda_create). */
 int hf_cuda_sequences(const hf_ctx* ctx);
-/* Begins every sequence and enqueues its prompt's prefill: prompts is
- * [sequences, prompt_length] host token ids; each sequence's first generated
- * token lands in its slot prompt_length. */
+/* Admits one sequence: takes the pages its prompt needs and enqueues the
+ * prompt's prefill; its first generated token lands in its slot
+ * prompt_length, and the batched steps that follow advance it. Refused with
+ * HF_E_INVALID when the sequence is active, HF_E_CAPACITY when the pool has
+ * too few free pages, HF_E_WINDOW for a prompt longer than the window. */
+int hf_cuda_admit_async(hf_ctx* ctx, int sequence, const uint32_t* prompt, int prompt_length);
+/* Retires a sequence: its pages return to the pool and the batched steps
+ * leave it (its row still runs in a step, on a page of its own that nothing
+ * reads, and its slots and position stay as they are). */
+int hf_cuda_release(hf_ctx* ctx, int sequence);
+/* A sequence's position (tokens in its cache), -1 when it is not active. */
+int hf_cuda_sequence_position(const hf_ctx* ctx, int sequence);
+/* Pages of the pool not held by any sequence. */
+int hf_cuda_free_pages(const hf_ctx* ctx);
+/* Releases every active sequence and admits every sequence with its prompt:
+ * prompts is [sequences, prompt_length] host token ids; each sequence's first
+ * generated token lands in its slot prompt_length. */
 int hf_cuda_prefill_batch_async(hf_ctx* ctx, const uint32_t* prompts, int prompt_length);
-/* Enqueues `steps` batched greedy steps, each embedding every sequence's slot
- * `position` and writing its argmax into slot position + 1. */
+/* Enqueues `steps` batched greedy steps: each active sequence embeds the
+ * token in its slot at its position p, attends over its pages, and writes its
+ * argmax into slot p + 1. Pages for the steps are taken up front: refused with
+ * HF_E_CAPACITY when the pool is short, HF_E_WINDOW when a sequence would
+ * pass the window, HF_E_INVALID when no sequence is active. */
 int hf_cuda_decode_batch_async(hf_ctx* ctx, int steps);
 /* Synchronises and copies slots [first, first + count) of every sequence into
  * out [sequences, count]. */
@@ -285,6 +313,33 @@ int hf_cuda_time_kernel(hf_ctx* ctx, int kernel, int reps, float* mean_us, doubl
  * stream is a cudaStream_t (null = the legacy default stream). */
 int hf_cuda_linear_q8(const float* input, const uint8_t* weights, const float* bias, float* output, uint32_t inner,
                       uint32_t outputs, uint32_t rows, int gelu, int residual, void* stream);
+/* Replaces a LinearProductFor<Int8Blocks> bound to one stored weight: the
+ * reference's SplitLinearProgram (rows <= 3, Kernels/Linear.h:128-357) and
+ * its tiled product (SimdTiledMatMul.h:545-563, TiledMatMul.h:95-106), which
+ * hold the weight the way storedWeight<Int8Blocks> left it
+ * (Kernels/WeightStorage.h:80-191). hf_cuda_linear_create copies `weights`
+ * (the two-region layout, a host or device pointer) to `device` and builds
+ * there the layouts the decoder's product kernels stream: stage records for
+ * the int8 tensor-core rows kernel and tensor-core blocks for the tcgen05
+ * product, with input and split workspaces for up to max_rows rows.
+ * hf_cuda_linear_run computes output[r, o] = sum_k input[r, k] * w[o, k]
+ * (+ bias[o]), gelu when `gelu`, added to what output holds when `residual`
+ * (not both), for rows <= max_rows (else HF_E_CAPACITY); input and output are
+ * device pointers, input 16-byte aligned; asynchronous on `stream` (null = the
+ * legacy default stream). The kernel it runs, hf_cuda_linear_path:
+ * HF_LINEAR_STREAM (one row, K of 2048, 4096, 8192 or 16384), HF_LINEAR_ROWS_MMA
+ * (2-8 rows; K 2048 or 16384, outputs a multiple of 16), HF_LINEAR_TENSOR_CORES
+ * (more than 8 rows; K 2048 or 16384, outputs a multiple of 128) or
+ * HF_LINEAR_GENERIC (any other shape). */
+enum { HF_LINEAR_STREAM = 0, HF_LINEAR_ROWS_MMA = 1, HF_LINEAR_TENSOR_CORES = 2, HF_LINEAR_GENERIC = 3 };
+typedef struct hf_linear hf_linear;
+int hf_cuda_linear_create(int device, const uint8_t* weights, uint32_t inner, uint32_t outputs, uint32_t max_rows,
+                          hf_linear** out);
+int hf_cuda_linear_run(const hf_linear* lin, const float* input, const float* bias, float* output, uint32_t rows,
+                       int gelu, int residual, void* stream);
+int hf_cuda_linear_path(const hf_linear* lin, uint32_t rows);
+void hf_cuda_linear_destroy(hf_linear* lin);
+
 /* Replaces HF::quantizeInt8Blocks on the device (Int8Blocks.cpp:176-199),
  * byte-identical to the host quantizer: values[0, count) are elements
  * [first, first + count) of a tensor of element_count; destination is that

@@ -5,7 +5,7 @@ hf_cuda_read_batch_slots, hf_cuda_generate_batch.
 Every sequence of a batch must produce exactly the tokens the host-driven
 reference loop (Tests/Generation/Common.h:248-300) produces for that sequence
 alone, on a Gemma-shaped decoder whose embedding scale is 1 so the greedy
-sequences vary; the context's single-sequence calls keep acting on sequence 0.
+sequences vary; the context's single-sequence calls use a window of their own.
 """
 import numpy as np
 import pytest
@@ -59,10 +59,14 @@ def test_identical_prompts_give_identical_rows(batch):
     assert all(np.array_equal(row, out[0]) for row in out)
 
 
-def test_single_sequence_calls_act_on_sequence_zero(batch):
+def test_single_sequence_calls_use_their_own_window(batch):
     ctx, tensors, prompts = batch
+    ctx.prefill_batch_async(prompts)
     expected = ob.greedy_reference(SHAPE, tensors, prompts[2], 8)
     assert list(ctx.generate(prompts[2], 8)) == expected
+    # The batched sequences are untouched by the single-sequence run.
+    ctx.decode_batch_async(TOKENS - 1)
+    assert np.array_equal(ctx.read_batch_slots(PROMPT, TOKENS), ctx.generate_batch(prompts, TOKENS))
 
 
 def test_batch_refusals():

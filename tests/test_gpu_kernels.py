@@ -52,6 +52,69 @@ def test_config1_op_sweep_matches_double_reference(K, N, M):
     assert ob.worst_error(got, expected) <= ob.dot_product_tolerance(K)
 
 
+def _prepared(x, q, K, N, M, bias=None, out=None, gelu=False, residual=False, max_rows=64):
+    """The product through a prepared weight (hf_cuda_linear_create/run)."""
+    dx = torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).cuda()
+    dy = torch.zeros(M, N, device="cuda") if out is None else torch.from_numpy(out.copy()).cuda()
+    db = None if bias is None else torch.from_numpy(bias).cuda()
+    with native.Linear(q, K, N, max_rows) as lin:
+        path = lin.path(M)
+        lin.run(dx.data_ptr(), dy.data_ptr(), M, None if db is None else db.data_ptr(), gelu, residual)
+        torch.cuda.synchronize()
+    return dy.cpu().numpy(), path
+
+
+@pytest.mark.parametrize("K,N", SWEEP)
+@pytest.mark.parametrize("M", [1, 8, 64])
+def test_config1_op_sweep_on_the_decoders_kernels(K, N, M):
+    """The same sweep through a prepared weight, which runs the kernels the
+    decoder runs: the streaming product at one row, the int8 tensor-core rows
+    kernel at 8, the tcgen05 product at 64."""
+    q, deq = _weights(K, N)
+    x = native.synthetic_normal(1, 200, M, M * K, 1.0).reshape(M, K)
+    expected = x.astype(np.float64) @ deq.astype(np.float64).T
+    got, path = _prepared(x, q, K, N, M)
+    assert path == {1: native.LINEAR_STREAM, 8: native.LINEAR_ROWS_MMA, 64: native.LINEAR_TENSOR_CORES}[M]
+    assert ob.worst_error(got, expected) <= ob.dot_product_tolerance(K)
+
+
+@pytest.mark.parametrize("M", [5, 8, 9, 40, 64, 130])
+@pytest.mark.parametrize("fold", ["bias", "gelu", "residual"])
+def test_prepared_linear_folds_on_every_path(M, fold):
+    K, N = 2048, 512
+    q, deq = _weights(K, N, seed=6)
+    x = ob.spread_values(M * K, 23 + M, 2.0).reshape(M, K)
+    bias = ob.spread_values(N, 29, 1.0)
+    prior = ob.spread_values(M * N, 31, 3.0).reshape(M, N)
+    product = x.astype(np.float64) @ deq.astype(np.float64).T + bias
+    if fold == "gelu":
+        expected = np.vectorize(ob.oracle().oracle_tanh_gelu_double)(product)
+        got, _ = _prepared(x, q, K, N, M, bias=bias, gelu=True, max_rows=130)
+    elif fold == "residual":
+        expected = product + prior
+        got, _ = _prepared(x, q, K, N, M, bias=bias, out=prior, residual=True, max_rows=130)
+    else:
+        expected = product
+        got, _ = _prepared(x, q, K, N, M, bias=bias, max_rows=130)
+    assert ob.worst_error(got, expected) <= ob.dot_product_tolerance(K)
+
+
+def test_prepared_linear_refusals():
+    q, _ = _weights(2048, 256)
+    with native.Linear(q, 2048, 256, 8) as lin:
+        x = torch.zeros(9, 2048, device="cuda")
+        y = torch.zeros(9, 256, device="cuda")
+        with pytest.raises(native.HFError) as too_many:
+            lin.run(x.data_ptr(), y.data_ptr(), 9)
+        assert too_many.value.code == native.HF_E_CAPACITY
+        with pytest.raises(native.HFError) as both:
+            lin.run(x.data_ptr(), y.data_ptr(), 1, gelu=True, residual=True)
+        assert both.value.code == native.HF_E_INVALID
+    with pytest.raises(native.HFError) as shape:
+        native.Linear(q[:100], 30, 10, 1)
+    assert shape.value.code == native.HF_E_SHAPE
+
+
 @pytest.mark.parametrize("M", [1, 3])
 def test_residual_bias_and_gelu_folds(M):
     K, N = 2048, 512
