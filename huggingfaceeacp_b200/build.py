@@ -62,7 +62,7 @@ def build_cpp_surface(force=False):
     target = os.path.join(LIB, "libhf.so")
     headers = [os.path.join(INCLUDE, "HF", f) for f in os.listdir(os.path.join(INCLUDE, "HF"))] if os.path.isdir(
         os.path.join(INCLUDE, "HF")) else []
-    if force or _stale(target, [source, *headers]):
+    if force or _stale(target, [source, os.path.join(PKG, "host", "safetensors.h"), *headers]):
         _run(["g++", "-std=c++20", "-O2", "-fPIC", "-shared", f"-I{INCLUDE}", source, f"-L{LIB}", "-lhf_cuda",
               "-lhf_host", "-Wl,-rpath,$ORIGIN", "-o", target])
     return target

@@ -65,10 +65,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes)
 
 // Polls the phase with the given parity; returns false when the poll budget
 // runs out (the caller records kErrWaitTimeout and skips the stage).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, unsigned limit = kSpinLimit)
 {
     const uint32_t addr = smem_addr(bar);
-    for (unsigned spin = 0; spin < kSpinLimit; ++spin)
+    for (unsigned spin = 0; spin < limit; ++spin)
     {
         uint32_t done;
         asm volatile(

@@ -1243,6 +1243,8 @@ struct hf_ctx
             text += " a step ran past the window;";
         if (word & kErrSampleSet)
             text += " a top-p set needed more than the device sampler's 1024 candidates;";
+        if (word & kErrBarrierTimeout)
+            text += " a grid barrier of the whole-loop kernel ran out of polls;";
         return fail(HF_E_DEVICE, text);
     }
 
@@ -2479,6 +2481,23 @@ int hf_cuda_time_kernel(hf_ctx* ctx, int kernel, int reps, float* mean_us, doubl
     if (bytes_per_launch)
         *bytes_per_launch = bytes;
     return HF_OK;
+}
+
+int hf_cuda_probe_wait_timeout(hf_ctx* ctx, int kind)
+{
+    if (!ctx || (kind != HF_PROBE_STAGE_WAIT && kind != HF_PROBE_GRID_BARRIER))
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    unsigned* counter = ctx->state + 7; // a word of the step state no kernel else uses
+    int rc = ctx->cuda(cudaMemsetAsync(counter, 0, sizeof(unsigned), ctx->stream), "probe counter");
+    if (rc)
+        return rc;
+    // 2^12 mbarrier polls, 2^16 acquire polls of the counter: milliseconds.
+    const unsigned limit = kind == HF_PROBE_STAGE_WAIT ? 1u << 12 : 1u << 16;
+    const int threads = kind == HF_PROBE_STAGE_WAIT ? 32 : kPConsumers;
+    return ctx->cuda(launch(false, wait_timeout_probe, dim3(1), dim3(threads), 0, ctx->stream, kind, counter,
+                            ctx->err_word(), limit),
+                     "probe launch");
 }
 
 int hf_cuda_trace_decode(hf_ctx* ctx, int steps, uint64_t* stamps, int capacity, int* ctas, int* events)

@@ -58,7 +58,7 @@ constexpr int kFusedMergeSplits = 8;                        // splits folded ins
 constexpr unsigned kBarrierSpinLimit = 1u << 20;
 enum : unsigned
 {
-    kErrBarrierTimeout = 8u
+    kErrBarrierTimeout = 16u // (8 is the sampler's kErrSampleSet)
 };
 constexpr unsigned kErrAbort = kErrWaitTimeout | kErrBarrierTimeout; // a wait gave up: every CTA leaves
 
@@ -194,7 +194,8 @@ __device__ __forceinline__ void consumers_sync()
 // in the same poll. Returns false when any CTA has given up a wait (the error
 // word says which): the caller then leaves, so one failure ends the launch
 // instead of making every later wait time out in turn.
-__device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch, unsigned* err, unsigned* abort)
+__device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch, unsigned* err, unsigned* abort,
+                                             unsigned spin_limit = kBarrierSpinLimit)
 {
     consumers_sync();
     ++epoch;
@@ -209,7 +210,7 @@ __device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch,
             errs = ld_relaxed(err);
             if (arrived >= target || (errs & kErrAbort))
                 break;
-            if (spin > kBarrierSpinLimit)
+            if (spin > spin_limit)
             {
                 flag_error(err, kErrBarrierTimeout);
                 errs |= kErrBarrierTimeout;
@@ -1128,6 +1129,29 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
             __threadfence();
         }
     }
+}
+
+// A self-check of the bounded waits: one wait whose arrival never comes, with a
+// short poll limit, which must give up, set its bit in the error word and
+// return. kind 0: an mbarrier phase nobody completes (1 CTA, 32 threads);
+// kind 1: a grid barrier whose counter (zero at launch) never reaches its
+// target (1 CTA, kPConsumers threads, entered at epoch 1 so the target is 2).
+__global__ void wait_timeout_probe(int kind, unsigned* counter, unsigned* err, unsigned limit)
+{
+    __shared__ uint64_t bar;
+    __shared__ unsigned abort_flag;
+    if (kind == 0)
+    {
+        if (threadIdx.x == 0)
+            mbar_init(&bar, 1);
+        __syncthreads();
+        if (threadIdx.x == 0 && !mbar_wait(&bar, 0u, limit))
+            flag_error(err, kErrWaitTimeout);
+        __syncthreads();
+        return;
+    }
+    unsigned epoch = 1;
+    grid_barrier(counter, epoch, err, &abort_flag, limit);
 }
 
 // Dynamic shared memory: the ring, the down factors and row sums (8 KiB), the

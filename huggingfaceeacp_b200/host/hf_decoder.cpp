@@ -10,8 +10,12 @@
 #include <hf_cuda.h>
 #include <hf_host.h>
 
+#include "safetensors.h" // its strict JSON reader reads config.json
+
 #include <algorithm>
 #include <chrono>
+#include <cstdio>
+#include <filesystem>
 #include <cmath>
 #include <string>
 #include <utility>
@@ -165,9 +169,108 @@ DecoderWeights DecoderWeights::synthetic(const DecoderShape& shape, std::uint64_
     return w;
 }
 
+ShardedTensors ShardedTensors::fromFile(const std::filesystem::path& weights)
+{
+    return ShardedTensors {{weights}};
+}
+
+ShardedTensors ShardedTensors::fromDirectory(const std::filesystem::path& directory)
+{
+    std::error_code error;
+    if (!std::filesystem::is_directory(directory, error))
+        throw ModelError {"the model directory " + directory.string() + " does not exist"};
+    const auto single = directory / "model.safetensors";
+    if (std::filesystem::is_regular_file(single, error))
+        return fromFile(single);
+    ShardedTensors file;
+    for (const auto& entry: std::filesystem::directory_iterator(directory, error))
+        if (entry.is_regular_file() && entry.path().extension() == ".safetensors")
+            file.shards.push_back(entry.path());
+    if (file.shards.empty())
+        throw ModelError {"the model directory " + directory.string() + " holds no .safetensors weights"};
+    std::sort(file.shards.begin(), file.shards.end());
+    return file;
+}
+
+DecoderWeights::DecoderWeights(const ShardedTensors& file, const DecoderShape& shapeToUse)
+    : shape(shapeToUse)
+    , checkpoint(file.shards)
+{
+    if (checkpoint.empty())
+        throw ModelError {"a checkpoint needs at least one safetensors file"};
+    shape.validate();
+}
+
+DecoderShape DecoderShape::fromConfigFile(const std::filesystem::path& configJson)
+{
+    const std::string name = configJson.string();
+    std::FILE* f = std::fopen(name.c_str(), "rb");
+    if (!f)
+        throw ModelError {"the model's config file " + name + " is missing"};
+    std::string text;
+    char chunk[4096];
+    for (std::size_t n; (n = std::fread(chunk, 1, sizeof chunk, f)) > 0;)
+        text.append(chunk, n);
+    std::fclose(f);
+    hfst::Json root;
+    try
+    {
+        root = hfst::JsonReader(text.data(), text.size()).document();
+    }
+    catch (const std::exception& e)
+    {
+        throw ModelError {name + " is not valid JSON (" + e.what() + ")"};
+    }
+    if (root.kind != hfst::Json::Object)
+        throw ModelError {name + " is not a JSON object"};
+    if (const auto* type = root.member("model_type"); type && type->kind == hfst::Json::String && type->text != "gemma")
+        throw ModelError {name + " describes a '" + type->text + "' model, not a gemma one"};
+    const auto integer = [&](const char* key, int fallback) {
+        const auto* v = root.member(key);
+        if (!v || v->kind == hfst::Json::Null)
+            return fallback;
+        if (v->kind != hfst::Json::Number || !v->integral || v->integer <= 0 || v->integer > 1 << 30)
+            throw ModelError {name + " field '" + key + "' must be a positive integer"};
+        return (int) v->integer;
+    };
+    const auto real = [&](const char* key, double fallback) {
+        const auto* v = root.member(key);
+        if (!v || v->kind == hfst::Json::Null)
+            return fallback;
+        const double x = v->kind == hfst::Json::Number ? (v->integral ? (double) v->integer : v->number) : -1.0;
+        if (!(x > 0.0))
+            throw ModelError {name + " field '" + key + "' must be positive"};
+        return x;
+    };
+    DecoderShape shape;
+    shape.vocabularySize = integer("vocab_size", 256000);
+    shape.width = integer("hidden_size", 2048);
+    shape.intermediate = integer("intermediate_size", 16384);
+    shape.layers = integer("num_hidden_layers", 18);
+    shape.heads = integer("num_attention_heads", 8);
+    shape.kvHeads = integer("num_key_value_heads", 1);
+    shape.headWidth = integer("head_dim", 256);
+    shape.maxPositions = integer("max_position_embeddings", 8192);
+    shape.rmsNormEpsilon = (float) real("rms_norm_eps", 1.0e-6);
+    shape.ropeTheta = real("rope_theta", 10000.0);
+    if (shape.heads % shape.kvHeads != 0)
+        throw ModelError {name + " num_key_value_heads does not divide num_attention_heads"};
+    shape.embeddingScale = std::sqrt((float) shape.width);
+    shape.validate();
+    return shape;
+}
+
 void DecoderWeights::validate() const
 {
     shape.validate();
+    if (inCheckpoint())
+    {
+        std::error_code error;
+        for (const auto& path: checkpoint)
+            if (!std::filesystem::is_regular_file(path, error))
+                throw ModelError {"the checkpoint file " + path.string() + " is missing"};
+        return;
+    }
     const int W = shape.width, QW = shape.queryWidth(), KVW = shape.kvWidth();
     checkTensor(tokenEmbedding, shape.vocabularySize, W, "tokenEmbedding", -1);
     checkNorm(finalNorm, W, "finalNorm", -1);
@@ -231,6 +334,17 @@ void Decoder::prepare(const DecoderWeights& weights)
     if (!(weights.shape == decoderShape))
         throw ModelError {"these weights were loaded for another decoder shape"};
     weights.validate();
+    if (weights.inCheckpoint())
+    {
+        std::vector<std::string> names;
+        for (const auto& path: weights.checkpoint)
+            names.push_back(path.string());
+        std::vector<const char*> paths;
+        for (const auto& n: names)
+            paths.push_back(n.c_str());
+        check(ctx, hf_cuda_load_safetensors(ctx, paths.data(), (int) paths.size()));
+        return;
+    }
     const auto q8 = [&](int tensor, int layer, const QuantizedTensor& t) {
         check(ctx, hf_cuda_upload_q8(ctx, tensor, layer, t.bytes.data(), t.bytes.size()));
     };
@@ -305,6 +419,12 @@ void Gemma::load(DecoderWeights weightsToUse)
     weightsToUse.validate();
     weights = std::move(weightsToUse);
     decoder.reset();
+}
+
+void Gemma::load(const std::filesystem::path& modelDirectory)
+{
+    const DecoderShape shape = DecoderShape::fromConfigFile(modelDirectory / "config.json");
+    load(DecoderWeights(ShardedTensors::fromDirectory(modelDirectory), shape));
 }
 
 void Gemma::prepare(int device)

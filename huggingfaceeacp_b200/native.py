@@ -28,6 +28,9 @@ HF_E_CUDA = -6
 HF_E_DEVICE = -7
 HF_E_TOKEN = -8
 
+# Failure-detection probes (hf_cuda.h HF_PROBE_*).
+PROBE_STAGE_WAIT, PROBE_GRID_BARRIER = 0, 1
+
 # Decode paths (hf_cuda.h HF_DECODE_*).
 DECODE_AUTO, DECODE_GRAPH, DECODE_PERSISTENT = 0, 1, 2
 
@@ -233,6 +236,7 @@ def cuda() -> ctypes.CDLL:
         lib.hf_cuda_stream.restype = _vp
         lib.hf_cuda_decode_launches.argtypes = [_vp, ctypes.c_int]
         lib.hf_cuda_set_decode_path.argtypes = [_vp, ctypes.c_int]
+        lib.hf_cuda_probe_wait_timeout.argtypes = [_vp, ctypes.c_int]
         lib.hf_cuda_trace_decode.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                              ctypes.POINTER(ctypes.c_int)]
         lib.hf_cuda_decode_path.argtypes = [_vp]
@@ -568,6 +572,10 @@ class Context:
         self.check(self.lib.hf_cuda_trace_decode(self.handle, steps, _ptr(stamps), stamps.size, ctypes.byref(ctas),
                                                  ctypes.byref(events)))
         return stamps[: ctas.value * events.value].reshape(ctas.value, events.value)
+
+    def probe_wait_timeout(self, kind: int):
+        """Enqueues one bounded wait that must give up (hf_cuda_probe_wait_timeout)."""
+        self.check(self.lib.hf_cuda_probe_wait_timeout(self.handle, kind))
 
     def set_decode_path(self, path: int):
         self.check(self.lib.hf_cuda_set_decode_path(self.handle, path))

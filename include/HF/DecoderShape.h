@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cmath>
+#include <filesystem>
 
 namespace HF
 {
@@ -26,6 +27,14 @@ struct DecoderShape
     // google/gemma-2b (GemmaConfig.h:45-65; embeddingScale is sqrtf(width) as
     // GemmaConfig::embeddingScale computes it), at a window of maxPositionsToUse.
     static DecoderShape gemma2B(int maxPositionsToUse = 8192, int maxStepRowsToUse = 0);
+
+    // A Hugging Face config.json (GemmaConfig::fromFile, GemmaConfig.cpp:
+    // 132-200, then DecoderShape::fromConfig, DecoderShape.cpp:21-39): the
+    // extents, rms_norm_eps and rope_theta, google/gemma-2b's values for any
+    // field that is absent, embeddingScale sqrtf(hidden_size). A ModelError
+    // naming the file when it is missing or not a JSON object, the field when
+    // a count is not positive, and the model when model_type is not "gemma".
+    static DecoderShape fromConfigFile(const std::filesystem::path& configJson);
 
     friend bool operator==(const DecoderShape&, const DecoderShape&) = default;
 

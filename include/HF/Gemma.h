@@ -11,6 +11,7 @@
 #include <HF/Decoder.h>
 #include <HF/Sampling.h>
 
+#include <filesystem>
 #include <functional>
 #include <memory>
 #include <optional>
@@ -27,9 +28,16 @@ public:
     Gemma(const Gemma&) = delete;
     Gemma& operator=(const Gemma&) = delete;
 
-    // Takes the weights of the decoder to run (Gemma::load reads them from a
-    // checkpoint; here the caller has).
+    // Takes the weights of the decoder to run: host tensors, or a checkpoint's
+    // (DecoderWeights(file, shape)).
     void load(DecoderWeights weightsToUse);
+    // Gemma::load(modelDirectory) (Gemma.h:81): a Hugging Face Gemma directory,
+    // its config.json (DecoderShape::fromConfigFile) and its safetensors
+    // weights (ShardedTensors::fromDirectory). Nothing is read from the weights
+    // and no device is touched until prepare(). A missing config.json or a
+    // directory without weights is a ModelError naming it. The tokenizer stays
+    // the caller's (setTokenizer).
+    void load(const std::filesystem::path& modelDirectory);
     bool isLoaded() const { return weights.has_value(); }
 
     // Builds the decoder on `device` with the step capacity set to the prompt

@@ -283,6 +283,17 @@ int hf_cuda_generate_batch(hf_ctx* ctx, const uint32_t* prompts, int prompt_leng
  * the logits events at 2 + 32 layers (unused entries 0).
  * capacity >= SMs * 1024. */
 int hf_cuda_trace_decode(hf_ctx* ctx, int steps, uint64_t* stamps, int capacity, int* ctas, int* events);
+/* A self-check of the engine's failure detection (no reference counterpart;
+ * the reference's GPU waits are the platform's): enqueues on the context's
+ * stream one bounded wait whose arrival never comes -- HF_PROBE_STAGE_WAIT an
+ * mbarrier phase of a shared-memory stage, HF_PROBE_GRID_BARRIER a grid
+ * barrier of the whole-loop kernel -- with a poll limit of milliseconds. The
+ * wait must give up, set its bit in the context's error word and let the
+ * kernel return: the next hf_cuda_sync reports HF_E_DEVICE naming the wait,
+ * clears the word, and the context stays usable. Nothing faults or hangs. */
+enum { HF_PROBE_STAGE_WAIT = 0, HF_PROBE_GRID_BARRIER = 1 };
+int hf_cuda_probe_wait_timeout(hf_ctx* ctx, int kind);
+
 /* 1 when the sm_100a streaming kernels serve this shape, 0 for the generic path. */
 int hf_cuda_fast_path(const hf_ctx* ctx);
 
