@@ -45,9 +45,12 @@ constexpr int kStages = 3; // shared-memory ring depth of the streaming products
 constexpr int kBatchSplits = 8;       // most attention splits per sequence of a batched step
 constexpr int kBatchArgmaxParts = 64; // argmax candidates per sequence of a batched step
 constexpr int kPageRows = HF_PAGE_ROWS; // positions per KV page of a batched sequence
-// The whole-loop decode computes attention in every CTA up to this many keys
-// (no grid barrier between attention and o_proj), beyond it in split CTAs.
-constexpr int kLocalAttentionKeys = 64;
+// The whole-loop decode can compute attention in every CTA up to this many
+// keys (no grid barrier between attention and o_proj) instead of in split
+// CTAs. Off: measured slower at every context from 20 to 76 keys (730-771
+// against 724-727 us a token), since all 148 CTAs then read the same newly
+// written q and K/V rows from L2. HF_LOCAL_ATTN sets it for measurements.
+constexpr int kLocalAttentionKeys = 0;
 
 // Dynamic shared memory of q8_gemv_stream<K>: the stage ring plus either the
 // x vector (K = 2048) or the per-slab row partials (K > 2048). Two CTAs fit on
@@ -375,6 +378,7 @@ struct hf_ctx
     bool persistent_ok = false; // the cooperative whole-loop kernel serves this shape on this device
     int gate_point = 1; // HF_GATE overrides (a tuning knob of the whole-loop kernel)
     int local_keys = kLocalAttentionKeys; // HF_LOCAL_ATTN overrides (0: always split the context)
+    int barrier_poll = 0; // HF_BARRIER_POLL overrides (a tuning knob of the whole-loop kernel's grid barrier)
     bool tc_off = false; // HF_TC=0 keeps multi-row products on the int8 MMA (for comparisons)
     int decode_path = HF_DECODE_AUTO;
     LayerDev* layer_dev = nullptr;
@@ -703,6 +707,7 @@ struct hf_ctx
         p.steps = steps;
         p.gate_point = gate_point;
         p.local_keys = local_keys;
+        p.barrier_poll = barrier_poll;
         p.down_acc = down_acc;
         p.trace = trace;
         cudaLaunchConfig_t config = {};
@@ -1338,6 +1343,8 @@ int create_context(int device, const hf_shape* shape, int sequences, int pages, 
     ctx->sms = sm_count(device);
     if (const char* knob = std::getenv("HF_GATE"))
         ctx->gate_point = std::max(0, std::min(2, std::atoi(knob)));
+    if (const char* knob = std::getenv("HF_BARRIER_POLL"))
+        ctx->barrier_poll = std::atoi(knob) != 0;
     if (const char* knob = std::getenv("HF_LOCAL_ATTN"))
         ctx->local_keys = std::max(0, std::atoi(knob));
     if (const char* knob = std::getenv("HF_TC"))

@@ -109,6 +109,7 @@ struct PersistentArgs
     int gate_point;            // where a layer's gate/up records are released: 0 never held, 1 after the
                                // attention phase, 2 after the o_proj staging
     int local_keys;            // contexts of up to this many keys: every CTA computes the whole attention
+    int barrier_poll;          // 0: the grid barrier reads the error word at every poll, 1: once at the end
     unsigned long long* trace; // [gridDim.x][kTraceEvents] first-step phase stamps, or null
     unsigned long long* down_acc; // [2][2048] the down sums in units of 2^-32, by layer parity
 };
@@ -195,7 +196,7 @@ __device__ __forceinline__ void consumers_sync()
 // word says which): the caller then leaves, so one failure ends the launch
 // instead of making every later wait time out in turn.
 __device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch, unsigned* err, unsigned* abort,
-                                             unsigned spin_limit = kBarrierSpinLimit)
+                                             unsigned spin_limit = kBarrierSpinLimit, bool error_each_poll = true)
 {
     consumers_sync();
     ++epoch;
@@ -207,7 +208,12 @@ __device__ __forceinline__ bool grid_barrier(unsigned* counter, unsigned& epoch,
         for (unsigned spin = 0;; ++spin)
         {
             const unsigned arrived = ld_acquire(counter);
-            errs = ld_relaxed(err);
+            // error_each_poll: a CTA that gave up a wait ends everyone's poll at
+            // once; else the word is read once the count is reached (a poll is
+            // then one L2 round trip, and a CTA that left is noticed at the
+            // spin limit).
+            if (error_each_poll || arrived >= target)
+                errs = ld_relaxed(err);
             if (arrived >= target || (errs & kErrAbort))
                 break;
             if (spin > spin_limit)
@@ -376,15 +382,20 @@ __device__ __forceinline__ void split_range(unsigned position, int split, int sp
     k1 = min(keys, k0 + chunk);
 }
 
-// Rows of the split's first tile that are final before this step's q/k/v
-// phase ends (every row but the newest), fetched while the grid barrier runs.
-__device__ __forceinline__ void prefetch_split(const LayerDev& L, unsigned position, int split, int splits, float* tile,
-                                               int tid)
+// Rows of the split's first `tiles` tiles (1 or 2: the two tile buffers of
+// `area`) that are final before this step's q/k/v phase ends (every row but
+// the newest), fetched while the grid barrier runs.
+__device__ __forceinline__ void prefetch_split(const LayerDev& L, unsigned position, int split, int splits, float* area,
+                                               int tid, int tiles = 1)
 {
     int k0, k1;
     split_range(position, split, splits, k0, k1);
-    const int end = min(min(k1, k0 + kAttnTile), (int) position);
-    load_kv_rows(L.k_cache, L.v_cache, k0, k0, max(k0, end), tile, tid);
+    for (int t = 0; t < tiles; ++t)
+    {
+        const int t0 = k0 + t * kAttnTile;
+        const int end = min(min(k1, t0 + kAttnTile), (int) position);
+        load_kv_rows(L.k_cache, L.v_cache, t0, t0, max(t0, end), area + t * kAttnTileFloats, tid);
+    }
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
@@ -402,7 +413,7 @@ __device__ __forceinline__ void prefetch_split(const LayerDev& L, unsigned posit
 // the split's (max, sum, unnormalised row).
 template <typename Stamp>
 __device__ void attend_split(const PersistentArgs& p, const LayerDev& L, unsigned position, int split, int splits,
-                             float* area, int tid, Stamp stamp, float* local = nullptr)
+                             float* area, int tid, Stamp stamp, float* local = nullptr, int prefetched = 1)
 {
     constexpr int D = 256, QH = kAttnHeads;
     const int group = tid >> 8, warp = (tid >> 5) & 7, lane = tid & 31;
@@ -442,8 +453,8 @@ __device__ void attend_split(const PersistentArgs& p, const LayerDev& L, unsigne
     auto request = [&](int t) {
         const int t0 = k0 + t * kAttnTile;
         const int nk = min(kAttnTile, k1 - t0);
-        // The first tile's final rows were prefetched before the barrier.
-        const int from = t == 0 ? max(k0, min(t0 + nk, (int) position)) : t0;
+        // The first `prefetched` tiles' final rows were fetched before the barrier.
+        const int from = t < prefetched ? max(t0, min(t0 + nk, (int) position)) : t0;
         load_kv_rows(L.k_cache, L.v_cache, t0, from, t0 + nk, area + (t & 1) * kAttnTileFloats, tid);
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
@@ -910,7 +921,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
     const float4* hidden4 = reinterpret_cast<const float4*>(p.hidden);
     auto barrier = [&](int entry_slot, int exit_slot) {
         stamp(entry_slot);
-        const bool alive = grid_barrier(p.barrier, epoch, p.err, &abort_flag);
+        const bool alive = grid_barrier(p.barrier, epoch, p.err, &abort_flag, kBarrierSpinLimit, p.barrier_poll == 0);
         stamp(exit_slot);
         return alive;
     };
@@ -996,7 +1007,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
                                                            bfactor, red, position, best, best_i, group, 2 + group);
             }
             if (local_attn || cta < splits)
-                prefetch_split(L, position, local_attn ? 0 : cta, splits, attn_area, tid);
+                prefetch_split(L, position, local_attn ? 0 : cta, splits, attn_area, tid, local_attn ? 2 : 1);
             if (!barrier(ts + kTrQkvDone, ts + kTrQkvLeft))
                 return;
             if (cta == 0 && l > 0)
@@ -1013,7 +1024,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
             // one CTA per context split
             if (local_attn)
             {
-                attend_split(p, L, position, 0, 1, attn_area, tid, [&](int event) { stamp(ts + event); }, sx);
+                attend_split(p, L, position, 0, 1, attn_area, tid, [&](int event) { stamp(ts + event); }, sx, 2);
                 stamp(ts + kTrAttnDone);
                 consumers_sync(); // the whole attended row is in sx
             }

@@ -317,11 +317,19 @@ __global__ void __launch_bounds__(kSampleThreads) sample_row(const SampleArgs a)
         double rest = 0.0;
         if (!cut_k && K < total_n)
         {
-            // the candidates below the K-th key: their share of the total
+            // the candidates past the sorted K: their share of the total. They
+            // are the keys below the K-th key and the ties at it that were not
+            // taken (the taken ties are the lowest tokens, the last of them
+            // ranked K - 1).
+            const unsigned last_tie = token_of((int) K - 1);
             double part = 0.0;
             for (int i = tid; i < V; i += kSampleThreads)
-                if (live(i) && order_key(a.logits[i]) < tau)
-                    part += exp((double) a.logits[i] * inv_t - largest);
+                if (live(i))
+                {
+                    const unsigned key = order_key(a.logits[i]);
+                    if (key < tau || (key == tau && (unsigned) i > last_tie))
+                        part += exp((double) a.logits[i] * inv_t - largest);
+                }
             for (int o = 16; o > 0; o >>= 1)
                 part += __shfl_xor_sync(0xFFFFFFFFu, part, o);
             if (lane == 0)
