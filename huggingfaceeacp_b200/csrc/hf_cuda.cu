@@ -380,6 +380,7 @@ struct hf_ctx
     int local_keys = kLocalAttentionKeys; // HF_LOCAL_ATTN overrides (0: always split the context)
     int barrier_poll = 0; // HF_BARRIER_POLL overrides (a tuning knob of the whole-loop kernel's grid barrier)
     bool tc_off = false; // HF_TC=0 keeps multi-row products on the int8 MMA (for comparisons)
+    bool batch_graph_off = false; // HF_BATCH_GRAPH=0 launches a batched step's kernels one by one
     int decode_path = HF_DECODE_AUTO;
     LayerDev* layer_dev = nullptr;
 
@@ -838,7 +839,55 @@ struct hf_ctx
     // One batched decode step: every sequence's next token at its own
     // position, row r of each product being sequence r, on the tensor-core
     // products (the weights stream once per step); K/V through the pages.
+    // The kernels of a batched step read every per-sequence value (positions,
+    // page table, slots) from device memory, so one captured graph per
+    // attention split count serves every step.
+    std::map<int, cudaGraphExec_t> batch_graphs;
+
     int enqueue_batch_step()
+    {
+        int keys = 1; // the longest context of this step
+        for (int q = 0; q < sequences; ++q)
+            keys = std::max(keys, seq_len[q] + 1);
+        int splits = 1;
+        while (splits < kBatchSplits && splits * 64 < keys)
+            splits *= 2;
+        int rc = HF_OK;
+        if (batch_graph_off)
+            rc = record_batch_step(splits);
+        else
+        {
+            auto found = batch_graphs.find(splits);
+            if (found == batch_graphs.end())
+            {
+                cudaGraph_t graph = nullptr;
+                rc = cuda(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+                if (rc)
+                    return rc;
+                rc = record_batch_step(splits);
+                const cudaError_t e = cudaStreamEndCapture(stream, &graph);
+                if (!rc && e != cudaSuccess)
+                    rc = cuda(e, "end capture");
+                cudaGraphExec_t exec = nullptr;
+                if (!rc)
+                    rc = cuda(cudaGraphInstantiate(&exec, graph, 0), "graph instantiate");
+                if (graph)
+                    cudaGraphDestroy(graph);
+                if (rc)
+                    return rc;
+                found = batch_graphs.emplace(splits, exec).first;
+            }
+            rc = cuda(cudaGraphLaunch(found->second, stream), "graph launch");
+        }
+        if (rc)
+            return rc;
+        for (int q = 0; q < sequences; ++q)
+            if (seq_len[q] >= 0)
+                ++seq_len[q];
+        return HF_OK;
+    }
+
+    int record_batch_step(int splits)
     {
         const hf_shape& s = shape;
         const int S = sequences;
@@ -849,12 +898,6 @@ struct hf_ctx
                                (const unsigned*) seq_pos_dev);
         if (e != cudaSuccess)
             return cuda(e, "embed launch");
-        int keys = 1; // the longest context of this step
-        for (int q = 0; q < S; ++q)
-            keys = std::max(keys, seq_len[q] + 1);
-        int splits = 1;
-        while (splits < kBatchSplits && splits * 64 < keys)
-            splits *= 2;
         for (int l = 0; l < s.layers; ++l)
         {
             const Layer& L = layers[l];
@@ -982,9 +1025,6 @@ struct hf_ctx
                    (const unsigned*) seq_active_dev);
         if (e != cudaSuccess)
             return cuda(e, "argmax launch");
-        for (int q = 0; q < S; ++q)
-            if (seq_len[q] >= 0)
-                ++seq_len[q];
         return HF_OK;
     }
 
@@ -1347,6 +1387,8 @@ int create_context(int device, const hf_shape* shape, int sequences, int pages, 
         ctx->barrier_poll = std::atoi(knob) != 0;
     if (const char* knob = std::getenv("HF_LOCAL_ATTN"))
         ctx->local_keys = std::max(0, std::atoi(knob));
+    if (const char* knob = std::getenv("HF_BATCH_GRAPH"))
+        ctx->batch_graph_off = std::atoi(knob) == 0;
     if (const char* knob = std::getenv("HF_TC"))
         ctx->tc_off = std::atoi(knob) == 0;
     ctx->max_splits = 128;
@@ -1609,6 +1651,8 @@ void hf_cuda_destroy(hf_ctx* ctx)
     if (ctx->stream)
         cudaStreamSynchronize(ctx->stream);
     for (auto& g: ctx->graphs)
+        cudaGraphExecDestroy(g.second);
+    for (auto& g: ctx->batch_graphs)
         cudaGraphExecDestroy(g.second);
     void* buffers[] = {ctx->pool, ctx->record_pool, ctx->slice_pool, ctx->down_acc, ctx->tc_pool, ctx->tc_x, ctx->tc_xunscale, ctx->tc_ws, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
                        ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slot_base, ctx->state,
