@@ -537,6 +537,70 @@ def run_ours(args):
     return 0
 
 
+def run_tp_prefill(args):
+    """Tensor-parallel prefill (configs[4]'s tensor-parallel variant) of
+    configs[2]'s single 8,064-token prompt: `--gpus N` ranks, one context per
+    GPU holding the whole model, the feed-forward split over the ranks with one
+    NCCL allreduce per layer (hf_cuda_set_tensor_parallel); N = 1 is the
+    one-GPU prefill. Device-timed over `--steps` prefills after `--warmup`,
+    max over ranks. Not the bench line: one JSON object {"tp_prefill": ...}."""
+    import datetime
+
+    import torch
+
+    from huggingfaceeacp_b200 import native
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    shape = native.GEMMA_2B.replace(max_step_rows=args.tp_rows, max_positions=LONG_PROMPT + 128)
+    with native.Context(shape, device=local_rank) as ctx:
+        ctx.load_synthetic(seed=SEED)
+        if dist:
+            nccl_id = native.broadcast_bytes(dist, native.nccl_unique_id() if rank == 0 else None,
+                                             native.NCCL_ID_BYTES, device="cuda")
+            ctx.set_tensor_parallel(rank, world, nccl_id)
+        prompt = native.synthetic_tokens(LONG_SEED, LONG_PROMPT, shape.vocab)
+        stream = torch.cuda.ExternalStream(ctx.stream)
+        for _ in range(args.warmup):
+            ctx.prefill_async(prompt)
+        ctx.sync()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            ctx.prefill_async(prompt)
+        stop.record(stream)
+        ctx.sync()
+        ms = start.elapsed_time(stop) / args.steps
+        first = int(ctx.read_slots(LONG_PROMPT, 1)[0])
+        (ms,) = max_over_ranks(dist, [ms])
+        firsts = [first]
+        if dist:
+            gathered = [None] * world
+            dist.all_gather_object(gathered, first)
+            firsts = gathered
+    if dist:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({"tp_prefill": {
+            "workload": "config2's prompt: one 8064-token seeded prompt (seed 2), Gemma-2B, prefill only",
+            "n_gpus": world, "step_rows": args.tp_rows, "ms": ms, "tok_s": LONG_PROMPT / (ms / 1000.0),
+            "first_token_per_rank": firsts, "steps": args.steps, "warmup": args.warmup,
+            "parallelism": f"tensor-parallel feed-forward x{world}, q/k/v, attention and o_proj on every rank"
+                           if world > 1 else "one GPU"}}), flush=True)
+    return 0
+
+
 def run_profile_case(args):
     """A small case of the bench's decode kernel for ncu captures (not a bench
     line): Gemma-2B's layer and head shapes with 4 layers and a 32,000-token
@@ -621,6 +685,9 @@ def main():
                         help="batched decode steps timed for the b=64/GPU half of the metric")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-config1", action="store_true", help="skip the configs[1] op sweep")
+    parser.add_argument("--tp-prefill", action="store_true",
+                        help="time tensor-parallel prefill of config 2's prompt over --gpus ranks (not the bench line)")
+    parser.add_argument("--tp-rows", type=int, default=512, help="prefill rows per step for --tp-prefill")
     parser.add_argument("--profile-case", nargs="?", const="decode", choices=["decode", "batched", "prefill"],
                         help="run a small ncu capture case instead of the bench: the decode kernel (default), "
                              "a batched step's tensor-core products, or a prompt's prefill")
@@ -634,6 +701,8 @@ def main():
         return run_profile_case(args)
     if args.impl == "reference":
         return run_reference(args)
+    if args.tp_prefill:
+        return run_tp_prefill(args)
     return run_ours(args)
 
 

@@ -16,6 +16,9 @@
 // the device: a step embeds the token in slot[pos] and writes slot[pos + 1]
 // (Gemma.cpp:320-333).
 #include <hf_cuda.h>
+#include <nccl.h> // types and constants only: the library is opened at run time (tensor_parallel_library)
+
+#include <dlfcn.h>
 
 #include "attention.cuh"
 #include "gemv.cuh"
@@ -70,6 +73,38 @@ int stream_grid(int K, int units, int sms)
     if (K > 2048)
         grid = std::max(grid, (units + kMaxSlabRows - 1) / kMaxSlabRows);
     return std::max(1, std::min(grid, units));
+}
+
+// NCCL for tensor-parallel prefill, opened with dlopen the first time it is
+// asked for, so the engine has no link-time dependency on it (a process that
+// already loaded libnccl.so.2, as torch does, gets that copy).
+struct NcclLibrary
+{
+    ncclResult_t (*unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+    bool ok = false;
+};
+
+const NcclLibrary& tensor_parallel_library()
+{
+    static const NcclLibrary library = [] {
+        NcclLibrary n;
+        void* handle = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!handle)
+            return n;
+        n.unique_id = reinterpret_cast<decltype(n.unique_id)>(dlsym(handle, "ncclGetUniqueId"));
+        n.comm_init_rank = reinterpret_cast<decltype(n.comm_init_rank)>(dlsym(handle, "ncclCommInitRank"));
+        n.all_reduce = reinterpret_cast<decltype(n.all_reduce)>(dlsym(handle, "ncclAllReduce"));
+        n.comm_destroy = reinterpret_cast<decltype(n.comm_destroy)>(dlsym(handle, "ncclCommDestroy"));
+        n.error_string = reinterpret_cast<decltype(n.error_string)>(dlsym(handle, "ncclGetErrorString"));
+        n.ok = n.unique_id && n.comm_init_rank && n.all_reduce && n.comm_destroy && n.error_string;
+        return n;
+    }();
+    return library;
 }
 
 struct Q8
@@ -269,6 +304,31 @@ cudaError_t generic_product(bool pdl, int units, cudaStream_t stream, const Gemv
 // the tiles with the epilogue, or, with K split across CTAs, the partial sums
 // and tc_finish. tc is the weight's tensor-core blocks; tc_x, tc_xunscale and
 // tc_ws the input pieces, their scales and the split workspace, sized for a.M.
+// The input split of a product of inner extent K (2048, 4096, 8192 or 16384;
+// the last two are a tensor-parallel rank's share of the down product).
+template <int NX>
+cudaError_t prep_pieces(const GemvArgs& a, size_t m_pad, cudaStream_t stream, __half* tc_x, float* tc_xunscale)
+{
+    const dim3 grid((unsigned) m_pad);
+    switch (a.K)
+    {
+    case 16384:
+        return launch(true, prep_x_pieces<NX, 16384>, grid, dim3(256), 0, stream, a.x, a.norm_w, a.eps, a.M, tc_x,
+                      tc_xunscale);
+    case 8192:
+        return launch(true, prep_x_pieces<NX, 8192>, grid, dim3(256), 0, stream, a.x, a.norm_w, a.eps, a.M, tc_x,
+                      tc_xunscale);
+    case 4096:
+        return launch(true, prep_x_pieces<NX, 4096>, grid, dim3(256), 0, stream, a.x, a.norm_w, a.eps, a.M, tc_x,
+                      tc_xunscale);
+    case 2048:
+        return launch(true, prep_x_pieces<NX, 2048>, grid, dim3(256), 0, stream, a.x, a.norm_w, a.eps, a.M, tc_x,
+                      tc_xunscale);
+    default:
+        return cudaErrorInvalidValue;
+    }
+}
+
 template <Epi E>
 cudaError_t tc_product_on(const uint8_t* tc, const GemvArgs& a, cudaStream_t stream, __half* tc_x, float* tc_xunscale,
                           float* tc_ws, int sms)
@@ -279,20 +339,14 @@ cudaError_t tc_product_on(const uint8_t* tc, const GemvArgs& a, cudaStream_t str
     cudaError_t e;
     if (p.nx == 64)
     {
-        e = a.K == 16384 ? launch(true, prep_x_pieces<64, 16384>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x,
-                                  a.norm_w, a.eps, a.M, tc_x, tc_xunscale)
-                         : launch(true, prep_x_pieces<64, 2048>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x,
-                                  a.norm_w, a.eps, a.M, tc_x, tc_xunscale);
+        e = prep_pieces<64>(a, p.m_pad, stream, tc_x, tc_xunscale);
         if (e == cudaSuccess)
             e = launch(true, q8_tc_gemm_ts<E>, grid, dim3(kTsThreads), kTsSmem, stream, a, tc, (const __half*) tc_x,
                        (const float*) tc_xunscale, tc_ws, split_stride, p.cps);
     }
     else
     {
-        e = a.K == 16384 ? launch(true, prep_x_pieces<128, 16384>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x,
-                                  a.norm_w, a.eps, a.M, tc_x, tc_xunscale)
-                         : launch(true, prep_x_pieces<128, 2048>, dim3((unsigned) p.m_pad), dim3(256), 0, stream, a.x,
-                                  a.norm_w, a.eps, a.M, tc_x, tc_xunscale);
+        e = prep_pieces<128>(a, p.m_pad, stream, tc_x, tc_xunscale);
         if (e == cudaSuccess)
             e = launch(true, q8_tc_gemm<E>, grid, dim3(kTcThreads), kTcSmem, stream, a, tc, (const __half*) tc_x,
                        (const float*) tc_xunscale, tc_ws, split_stride, p.cps);
@@ -348,6 +402,7 @@ struct hf_ctx
     __half* tc_x = nullptr;         // a product input's fp16 pieces
     float* tc_xunscale = nullptr;   // their per-row powers of two
     float* tc_ws = nullptr;         // split partial sums / unfused outputs of the tensor-core product
+    size_t tc_ws_count = 0;         // its floats
     Q8 embedding;
     float* final_norm = nullptr;
     std::vector<Layer> layers;
@@ -414,6 +469,18 @@ struct hf_ctx
     float* kbase = nullptr; // the contiguous cache the prefill and single-sequence kernels write
     float* vbase = nullptr;
     unsigned* single_slots = nullptr;
+
+    // Tensor-parallel prefill (hf_cuda_set_tensor_parallel): on tp_world GPUs,
+    // each rank's prefill blocks run the feed-forward on its share of it --
+    // gate/up units [r I / w, (r + 1) I / w) (the gate/up rows, which the pair
+    // permutation keeps contiguous) and the same columns of down -- and the
+    // down partial sums of all ranks are added by one NCCL allreduce a layer.
+    int tp_rank = 0;
+    int tp_world = 1;
+    ncclComm_t tp_comm = nullptr;
+    std::vector<Q8> tp_gu, tp_down; // this rank's shards, per layer (two-region bytes + tensor-core blocks)
+    uint8_t* tp_pool = nullptr;
+    float* tp_partial = nullptr;    // [capacity, width] the down partial sums, reduced in place
 
     int fail(int code, const std::string& text)
     {
@@ -1198,6 +1265,14 @@ struct hf_ctx
                 return cuda(e, "o_proj launch");
 
 
+            if (tp_world > 1 && rows > kRowsBlock && !tc_off)
+            {
+                const int rc = tp_feed_forward(l, rows);
+                if (rc)
+                    return rc;
+                continue;
+            }
+
             GemvArgs gu = {};
             gu.w = L.gu.base;
             gu.scales = L.gu.scales();
@@ -1268,6 +1343,69 @@ struct hf_ctx
         if (e != cudaSuccess)
             return cuda(e, "argmax launch");
         return HF_OK;
+    }
+
+    // This rank's feed-forward of a prefill block on the tensor cores: its
+    // gate/up units into act [rows, I / w], its down partial sums [rows, width]
+    // over those units, the allreduce of the partial sums over the ranks, and
+    // their residual add.
+    int tp_feed_forward(int l, int rows)
+    {
+        const hf_shape& s = shape;
+        const int units = s.intermediate / tp_world;
+        GemvArgs gu = {};
+        gu.w = tp_gu[l].base;
+        gu.scales = tp_gu[l].scales();
+        gu.N = 2 * units;
+        gu.K = s.width;
+        gu.M = rows;
+        gu.x = hidden;
+        gu.norm_w = layers[l].post_norm;
+        gu.eps = s.rms_eps;
+        gu.out = act;
+        gu.state = state;
+        gu.err = err_word();
+        cudaError_t e = tc_product_on<Epi::GeGLU>(tp_gu[l].tc, gu, stream, tc_x, tc_xunscale, tc_ws, sms);
+        if (e != cudaSuccess)
+            return cuda(e, "gate/up launch");
+        GemvArgs dn = {};
+        dn.w = tp_down[l].base;
+        dn.scales = tp_down[l].scales();
+        dn.N = s.width;
+        dn.K = units;
+        dn.M = rows;
+        dn.x = act;
+        dn.out = tp_partial;
+        dn.state = state;
+        dn.err = err_word();
+        e = tc_product_on<Epi::Store>(tp_down[l].tc, dn, stream, tc_x, tc_xunscale, tc_ws, sms);
+        if (e != cudaSuccess)
+            return cuda(e, "down launch");
+        const size_t count = (size_t) rows * s.width;
+        const NcclLibrary& nccl = tensor_parallel_library();
+        const ncclResult_t r = nccl.all_reduce(tp_partial, tp_partial, count, ncclFloat32, ncclSum, tp_comm, stream);
+        if (r != ncclSuccess)
+            return fail(HF_E_CUDA, std::string("allreduce of the down partial sums: ") + nccl.error_string(r));
+        e = launch(false, add_rows, dim3((unsigned) ((count / 4 + 255) / 256)), dim3(256), 0, stream, hidden,
+                   (const float*) tp_partial, count);
+        return e != cudaSuccess ? cuda(e, "residual launch") : HF_OK;
+    }
+
+    void drop_tensor_parallel()
+    {
+        if (tp_comm)
+            tensor_parallel_library().comm_destroy(tp_comm);
+        tp_comm = nullptr;
+        if (tp_pool)
+            cudaFree(tp_pool);
+        if (tp_partial)
+            cudaFree(tp_partial);
+        tp_pool = nullptr;
+        tp_partial = nullptr;
+        tp_gu.clear();
+        tp_down.clear();
+        tp_rank = 0;
+        tp_world = 1;
     }
 
     int check_device_error()
@@ -1543,6 +1681,7 @@ int create_context(int device, const hf_shape* shape, int sequences, int pages, 
                 || device_alloc(ctx, &ctx->tc_xunscale, m_pad, "product input scales")
                 || device_alloc(ctx, &ctx->tc_ws, ws, "product workspace"))
                 return bail(HF_E_CUDA);
+            ctx->tc_ws_count = ws;
             uint8_t* at_tc = ctx->tc_pool;
             auto place = [&](Q8& t) {
                 t.tc = at_tc;
@@ -1654,6 +1793,7 @@ void hf_cuda_destroy(hf_ctx* ctx)
         cudaGraphExecDestroy(g.second);
     for (auto& g: ctx->batch_graphs)
         cudaGraphExecDestroy(g.second);
+    ctx->drop_tensor_parallel();
     void* buffers[] = {ctx->pool, ctx->record_pool, ctx->slice_pool, ctx->down_acc, ctx->tc_pool, ctx->tc_x, ctx->tc_xunscale, ctx->tc_ws, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
                        ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slot_base, ctx->state,
                        ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev,
@@ -2531,6 +2671,136 @@ int hf_cuda_time_kernel(hf_ctx* ctx, int kernel, int reps, float* mean_us, doubl
     *mean_us = ms * 1000.f / (float) reps;
     if (bytes_per_launch)
         *bytes_per_launch = bytes;
+    return HF_OK;
+}
+
+int hf_cuda_nccl_unique_id(uint8_t* id)
+{
+    if (!id)
+        return HF_E_INVALID;
+    const NcclLibrary& nccl = tensor_parallel_library();
+    if (!nccl.ok)
+        return HF_E_CUDA;
+    ncclUniqueId unique;
+    if (nccl.unique_id(&unique) != ncclSuccess)
+        return HF_E_CUDA;
+    static_assert(sizeof(ncclUniqueId) == HF_NCCL_ID_BYTES, "the id's size is part of the C-ABI");
+    std::memcpy(id, &unique, sizeof unique);
+    return HF_OK;
+}
+
+int hf_cuda_set_tensor_parallel(hf_ctx* ctx, int rank, int world, const uint8_t* id)
+{
+    if (!ctx || world < 1 || rank < 0 || rank >= world || (world > 1 && !id))
+        return HF_E_INVALID;
+    cudaSetDevice(ctx->device);
+    int rc = ctx->sync();
+    if (rc)
+        return rc;
+    ctx->drop_tensor_parallel();
+    if (world == 1)
+        return HF_OK;
+    const hf_shape& s = ctx->shape;
+    const int I = s.intermediate, W = s.width;
+    if (!ctx->all_loaded())
+        return ctx->fail(HF_E_NOT_READY, "tensor parallelism splits the loaded weights: upload every weight first");
+    if (!ctx->tc_pool || !ctx->fast)
+        return ctx->fail(HF_E_SHAPE, "tensor-parallel prefill runs on the tensor-core products, which this shape has none of");
+    if ((world != 2 && world != 4 && world != 8) || (I / world) % 2048 != 0)
+        return ctx->fail(HF_E_SHAPE, "the feed-forward splits into 2, 4 or 8 shares of whole 2048-unit ranges");
+    const NcclLibrary& nccl = tensor_parallel_library();
+    if (!nccl.ok)
+        return ctx->fail(HF_E_CUDA, "libnccl.so.2 could not be opened");
+
+    // This rank's shards, cut from the device-resident weights: gate/up rows
+    // [2 j0, 2 j1) (gate row j at device row 2j, up row j at 2j + 1) and down
+    // columns [j0, j1), each a two-region tensor with its tensor-core blocks.
+    const int units = I / world, j0 = rank * units;
+    auto round256 = [](size_t b) { return (b + 255) / 256 * 256; };
+    auto q8bytes = [](size_t rows, size_t cols) { return rows * cols + rows * cols / 16; };
+    const size_t gu_bytes = round256(q8bytes(2 * (size_t) units, W)) + round256(tc_weight_bytes(2 * (size_t) units, W));
+    const size_t dn_bytes = round256(q8bytes(W, units)) + round256(tc_weight_bytes(W, units));
+    if (ctx->cuda(cudaMalloc(&ctx->tp_pool, (gu_bytes + dn_bytes) * s.layers), "tensor-parallel shards")
+        || ctx->cuda(cudaMalloc(&ctx->tp_partial, (size_t) ctx->capacity * W * sizeof(float)), "partial sums"))
+    {
+        ctx->drop_tensor_parallel();
+        return HF_E_CUDA;
+    }
+    for (int l = 0; l < s.layers; ++l)
+    {
+        const Layer& L = ctx->layers[l];
+        uint8_t* at = ctx->tp_pool + (gu_bytes + dn_bytes) * l;
+        Q8 gu, dn;
+        gu.rows = 2 * units;
+        gu.cols = W;
+        gu.base = at;
+        gu.tc = at + round256(q8bytes(gu.rows, W));
+        dn.rows = W;
+        dn.cols = units;
+        dn.base = at + gu_bytes;
+        dn.tc = dn.base + round256(q8bytes(W, units));
+        const size_t gu_quants = (size_t) gu.rows * W;
+        cudaError_t e = cudaMemcpy(gu.base, L.gu.base + (size_t) 2 * j0 * W, gu_quants, cudaMemcpyDeviceToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(gu.base + gu_quants, reinterpret_cast<const uint8_t*>(L.gu.scales()) + (size_t) 2 * j0 * W / 16,
+                           gu_quants / 16, cudaMemcpyDeviceToDevice);
+        if (e == cudaSuccess) // down: for each of the W rows, columns [j0, j1) and their scales
+            e = cudaMemcpy2D(dn.base, units, L.down.base + j0, I, units, W, cudaMemcpyDeviceToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2D(dn.base + (size_t) W * units, units / 16,
+                             reinterpret_cast<const uint8_t*>(L.down.scales()) + j0 / 16, I / 16, units / 16, W,
+                             cudaMemcpyDeviceToDevice);
+        if (e == cudaSuccess)
+        {
+            build_tc_blocks<<<gu.rows / kTcRows, kTcRows>>>(gu.base, gu.scales(), W, gu.tc);
+            build_tc_blocks<<<W / kTcRows, kTcRows>>>(dn.base, dn.scales(), units, dn.tc);
+            e = cudaDeviceSynchronize();
+        }
+        if (e != cudaSuccess)
+        {
+            ctx->drop_tensor_parallel();
+            return ctx->cuda(e, "tensor-parallel shard build");
+        }
+        ctx->tp_gu.push_back(gu);
+        ctx->tp_down.push_back(dn);
+    }
+    // The split workspace must also serve the shards' products (split_stride =
+    // m_pad x the product's outputs per split).
+    size_t ws = 1;
+    for (int m = kRowsBlock + 1; m <= ctx->capacity; ++m)
+    {
+        const TcPlan gate_up = tc_plan(m, 2 * units, W, ctx->sms), down = tc_plan(m, W, units, ctx->sms);
+        if (gate_up.splits > 1)
+            ws = std::max(ws, (size_t) gate_up.splits * gate_up.m_pad * 2 * units);
+        if (down.splits > 1)
+            ws = std::max(ws, (size_t) down.splits * down.m_pad * W);
+    }
+    if (ws > ctx->tc_ws_count)
+    {
+        float* grown = nullptr;
+        if (ctx->cuda(cudaMalloc(&grown, ws * sizeof(float)), "product workspace"))
+        {
+            ctx->drop_tensor_parallel();
+            return HF_E_CUDA;
+        }
+        cudaFree(ctx->tc_ws);
+        ctx->tc_ws = grown;
+        ctx->tc_ws_count = ws;
+        for (auto& g: ctx->batch_graphs) // they hold the old workspace
+            cudaGraphExecDestroy(g.second);
+        ctx->batch_graphs.clear();
+    }
+    ncclUniqueId unique;
+    std::memcpy(&unique, id, sizeof unique);
+    const ncclResult_t r = nccl.comm_init_rank(&ctx->tp_comm, world, unique, rank);
+    if (r != ncclSuccess)
+    {
+        ctx->tp_comm = nullptr;
+        ctx->drop_tensor_parallel();
+        return ctx->fail(HF_E_CUDA, std::string("NCCL communicator: ") + nccl.error_string(r));
+    }
+    ctx->tp_rank = rank;
+    ctx->tp_world = world;
     return HF_OK;
 }
 

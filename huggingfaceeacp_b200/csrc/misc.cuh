@@ -229,6 +229,25 @@ __global__ void __launch_bounds__(256) scatter_rows_to_pages(const float* k_rows
     }
 }
 
+// hidden[i] += partial[i] for i < count (count a multiple of 4): the residual
+// fold of a product whose K range was split across GPUs and summed by an
+// allreduce.
+__global__ void __launch_bounds__(256) add_rows(float* hidden, const float* partial, size_t count)
+{
+    pdl_wait();
+    pdl_trigger();
+    const size_t i = ((size_t) blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i >= count)
+        return;
+    float4 h = *reinterpret_cast<float4*>(hidden + i);
+    const float4 q = __ldcg(reinterpret_cast<const float4*>(partial + i));
+    h.x += q.x;
+    h.y += q.y;
+    h.z += q.z;
+    h.w += q.w;
+    *reinterpret_cast<float4*>(hidden + i) = h;
+}
+
 // Advances the step position without sampling (a step whose caller only wants
 // logits still moves the sequence on, Decoder.cpp:705).
 __global__ void advance_position(unsigned* state, int advance)

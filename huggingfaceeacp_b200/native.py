@@ -237,6 +237,8 @@ def cuda() -> ctypes.CDLL:
         lib.hf_cuda_decode_launches.argtypes = [_vp, ctypes.c_int]
         lib.hf_cuda_set_decode_path.argtypes = [_vp, ctypes.c_int]
         lib.hf_cuda_probe_wait_timeout.argtypes = [_vp, ctypes.c_int]
+        lib.hf_cuda_nccl_unique_id.argtypes = [_vp]
+        lib.hf_cuda_set_tensor_parallel.argtypes = [_vp, ctypes.c_int, ctypes.c_int, _vp]
         lib.hf_cuda_trace_decode.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                              ctypes.POINTER(ctypes.c_int)]
         lib.hf_cuda_decode_path.argtypes = [_vp]
@@ -573,6 +575,14 @@ class Context:
                                                  ctypes.byref(events)))
         return stamps[: ctas.value * events.value].reshape(ctas.value, events.value)
 
+    def set_tensor_parallel(self, rank: int, world: int, nccl_id: bytes | None):
+        """Tensor-parallel prefill on `world` GPUs (hf_cuda_set_tensor_parallel);
+        every rank calls it at the same time with the id rank 0 made."""
+        buf = None
+        if nccl_id is not None:
+            buf = (ctypes.c_uint8 * NCCL_ID_BYTES).from_buffer_copy(nccl_id)
+        self.check(self.lib.hf_cuda_set_tensor_parallel(self.handle, rank, world, buf))
+
     def probe_wait_timeout(self, kind: int):
         """Enqueues one bounded wait that must give up (hf_cuda_probe_wait_timeout)."""
         self.check(self.lib.hf_cuda_probe_wait_timeout(self.handle, kind))
@@ -635,6 +645,29 @@ class Linear:
 
     def __exit__(self, *exc):
         self.close()
+
+
+NCCL_ID_BYTES = 128  # hf_cuda.h HF_NCCL_ID_BYTES
+
+
+def nccl_unique_id() -> bytes:
+    """A new NCCL communicator id (hf_cuda_nccl_unique_id), made by rank 0."""
+    buf = (ctypes.c_uint8 * NCCL_ID_BYTES)()
+    rc = cuda().hf_cuda_nccl_unique_id(buf)
+    if rc:
+        raise HFError(rc, "libnccl.so.2 could not make a communicator id")
+    return bytes(buf)
+
+
+def broadcast_bytes(dist, payload: bytes | None, size: int, device="cpu") -> bytes:
+    """rank 0's `size` bytes on every rank (torch.distributed broadcast)."""
+    import torch
+
+    t = torch.zeros(size, dtype=torch.uint8, device=device)
+    if dist.get_rank() == 0:
+        t.copy_(torch.frombuffer(bytearray(payload), dtype=torch.uint8))
+    dist.broadcast(t, src=0)
+    return bytes(t.cpu().numpy().tobytes())
 
 
 def device_count() -> int:

@@ -273,6 +273,28 @@ int hf_cuda_read_batch_slots(hf_ctx* ctx, int first, int count, uint32_t* out);
  * tokens] receives every sequence's first `tokens` generated ids. */
 int hf_cuda_generate_batch(hf_ctx* ctx, const uint32_t* prompts, int prompt_length, int tokens, uint32_t* out);
 
+/* ---- tensor-parallel prefill over NCCL --------------------------------------
+ * No counterpart in the reference (one GPU, no distributed code). One prompt's
+ * prefill on `world` GPUs of one box, one process and one context per GPU,
+ * each context holding the whole model: every rank runs the q/k/v, attention
+ * and o_proj of each prefill block of more than 8 rows itself (they are 8% of
+ * a layer's weight multiply-adds, and attention needs every head's keys), and
+ * the feed-forward on its share -- gate/up units [r I / world, (r + 1) I /
+ * world) and the same columns of down -- after which one NCCL allreduce per
+ * layer sums the ranks' down partial sums into every rank's residual stream.
+ * Every rank ends the prefill with the same hidden rows and caches, so decode
+ * continues on each as on one GPU. libnccl.so.2 is opened at run time.
+ * hf_cuda_nccl_unique_id writes the HF_NCCL_ID_BYTES communicator id that rank
+ * 0 creates and hands to the others (any channel); every rank then calls
+ * hf_cuda_set_tensor_parallel at the same time with its rank and that id, after
+ * its weights are loaded (the shards are cut from them on the device); world
+ * 1 switches it off. Refused: a world other than 1, 2, 4 or 8, a feed-forward
+ * that does not split into whole 2048-unit shares, a shape without the
+ * tensor-core products (HF_E_SHAPE), weights not loaded (HF_E_NOT_READY). */
+#define HF_NCCL_ID_BYTES 128
+int hf_cuda_nccl_unique_id(uint8_t* id);
+int hf_cuda_set_tensor_parallel(hf_ctx* ctx, int rank, int world, const uint8_t* id);
+
 /* Phase tracing of the whole-loop kernel (the reference has wall-clock
  * timings only, Gemma.h:205-224): decodes `steps` tokens like
  * hf_cuda_decode_async, synchronously, and writes the first step's

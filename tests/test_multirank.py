@@ -74,3 +74,34 @@ def test_reference_arm_rank_other_than_zero_does_no_work(monkeypatch, capsys):
 
     assert bench.run_reference(Args()) == 0
     assert capsys.readouterr().out == ""
+
+
+def _id_rank_main(rank: int, world: int, port: int, out):
+    sys.path.insert(0, ROOT)
+    import torch.distributed as dist
+
+    from huggingfaceeacp_b200 import native
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        # rank 0's communicator id reaches every rank unchanged (the tensor-parallel
+        # prefill's set-up; the id's bytes stand in for hf_cuda_nccl_unique_id's)
+        payload = bytes((i * 37 + 11) % 256 for i in range(native.NCCL_ID_BYTES)) if rank == 0 else None
+        out.put((rank, native.broadcast_bytes(dist, payload, native.NCCL_ID_BYTES)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_id_reaches_every_rank():
+    ctx = multiprocessing.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_id_rank_main, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(out.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    expected = bytes((i * 37 + 11) % 256 for i in range(128))
+    assert got[0] == expected and got[1] == expected
