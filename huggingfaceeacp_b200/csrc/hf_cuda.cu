@@ -398,6 +398,8 @@ struct hf_ctx
     uint8_t* record_pool = nullptr; // stage records of every Q8 weight (the whole-loop kernel's copy)
     uint8_t* slice_pool = nullptr;  // every layer's down matrix as K-split slices (the whole-loop kernel's)
     unsigned long long* down_acc = nullptr; // [2][width] the whole-loop kernel's fixed-point down sums
+    unsigned* act_ready = nullptr;          // [intermediate / 32] its activation blocks' publish counts
+    int balance_ffn = 1;                    // HF_FFN_BALANCE=0 keeps each CTA's down on its own blocks
     uint8_t* tc_pool = nullptr;     // tensor-core weight blocks of every Q8 weight
     __half* tc_x = nullptr;         // a product input's fp16 pieces
     float* tc_xunscale = nullptr;   // their per-row powers of two
@@ -777,6 +779,8 @@ struct hf_ctx
         p.local_keys = local_keys;
         p.barrier_poll = barrier_poll;
         p.down_acc = down_acc;
+        p.act_ready = act_ready;
+        p.balance_ffn = balance_ffn;
         p.trace = trace;
         cudaLaunchConfig_t config = {};
         config.gridDim = dim3(persistent_grid());
@@ -1521,6 +1525,8 @@ int create_context(int device, const hf_shape* shape, int sequences, int pages, 
     ctx->sms = sm_count(device);
     if (const char* knob = std::getenv("HF_GATE"))
         ctx->gate_point = std::max(0, std::min(2, std::atoi(knob)));
+    if (const char* knob = std::getenv("HF_FFN_BALANCE"))
+        ctx->balance_ffn = std::atoi(knob) != 0;
     if (const char* knob = std::getenv("HF_BARRIER_POLL"))
         ctx->barrier_poll = std::atoi(knob) != 0;
     if (const char* knob = std::getenv("HF_LOCAL_ATTN"))
@@ -1707,6 +1713,7 @@ int create_context(int device, const hf_shape* shape, int sequences, int pages, 
             const size_t slice_bytes = (size_t) (W / kSliceRows) * act_blocks * kSliceUnitBytes;
             if (ctx->cuda(cudaMalloc(&ctx->slice_pool, slice_bytes * s.layers), "down slices")
                 || device_alloc(ctx, &ctx->down_acc, 2 * (size_t) W, "down sums")
+                || device_alloc(ctx, &ctx->act_ready, I / kBlock, "activation block counts")
                 || ctx->cuda(cudaMemset(ctx->down_acc, 0, 2 * (size_t) W * sizeof(unsigned long long)), "down sums"))
                 return bail(HF_E_CUDA);
             for (int l = 0; l < s.layers; ++l)
@@ -1794,7 +1801,7 @@ void hf_cuda_destroy(hf_ctx* ctx)
     for (auto& g: ctx->batch_graphs)
         cudaGraphExecDestroy(g.second);
     ctx->drop_tensor_parallel();
-    void* buffers[] = {ctx->pool, ctx->record_pool, ctx->slice_pool, ctx->down_acc, ctx->tc_pool, ctx->tc_x, ctx->tc_xunscale, ctx->tc_ws, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
+    void* buffers[] = {ctx->pool, ctx->record_pool, ctx->slice_pool, ctx->down_acc, ctx->act_ready, ctx->tc_pool, ctx->tc_x, ctx->tc_xunscale, ctx->tc_ws, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
                        ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slot_base, ctx->state,
                        ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev,
                        ctx->sample_uniforms, ctx->sample_mask, ctx->kpages, ctx->vpages, ctx->admit_k, ctx->admit_v,

@@ -112,6 +112,8 @@ struct PersistentArgs
     int barrier_poll;          // 0: the grid barrier reads the error word at every poll, 1: once at the end
     unsigned long long* trace; // [gridDim.x][kTraceEvents] first-step phase stamps, or null
     unsigned long long* down_acc; // [2][2048] the down sums in units of 2^-32, by layer parity
+    unsigned* act_ready;          // [intermediate / 32] per activation block: layers whose block is published
+    int balance_ffn;              // 1: CTAs with more activation blocks hand one block's down to a partner
 };
 
 // Phase tracing: thread 0 of every CTA stamps %globaltimer (ns) into fixed
@@ -615,6 +617,75 @@ __device__ __forceinline__ Blocks act_blocks(int intermediate, int cta, int ctas
     return Blocks {n * cta / ctas, n * (cta + 1) / ctas};
 }
 
+// The feed-forward work of a CTA. Blocks of 32 activations divide unevenly
+// over the CTAs (512 over 148: 68 CTAs take 4, 80 take 3), and a CTA's
+// feed-forward takes about one ring-slot cycle per record whatever the
+// record's size, so the 4-block CTAs (16 gate/up + 8 down records against
+// 12 + 8) set the phase's length. With balancing, the k-th 4-block CTA lends
+// the last two gate/up records of its last block (activations 16..31) to the
+// k-th 3-block CTA, which computes them first and publishes them (act_ready);
+// the lender reads them back before its down product, which still covers all
+// four of its blocks: 14 + 8 records against 2 + 12 + 8.
+struct FfnRoles
+{
+    Blocks blocks; // the CTA's activation blocks (its down product covers them all)
+    int gu_end;    // its own gate/up records are [4 b0, gu_end)
+    int lent;      // the block whose last two gate/up records a partner computes, or -1
+    int borrowed;  // the partner's block whose last two gate/up records this CTA computes, or -1
+};
+
+__device__ __forceinline__ FfnRoles ffn_roles(int intermediate, int cta, int ctas, bool balance)
+{
+    FfnRoles f;
+    f.blocks = act_blocks(intermediate, cta, ctas);
+    f.gu_end = 4 * f.blocks.b1;
+    f.lent = -1;
+    f.borrowed = -1;
+    const int n = intermediate / kBlock, few = n / ctas;
+    if (!balance || n % ctas == 0)
+        return f;
+    auto big = [&](int i) {
+        const Blocks b = act_blocks(intermediate, i, ctas);
+        return b.b1 - b.b0 > few;
+    };
+    int my_big = 0, my_small = 0, bigs = 0, smalls = 0;
+    for (int i = 0; i < ctas; ++i)
+    {
+        const bool b = big(i);
+        if (i < cta)
+            (b ? my_big : my_small) += 1;
+        (b ? bigs : smalls) += 1;
+    }
+    if (big(cta))
+    {
+        if (my_big < smalls)
+        {
+            f.lent = f.blocks.b1 - 1;
+            f.gu_end = 4 * f.blocks.b1 - 2;
+        }
+    }
+    else if (my_small < bigs)
+    {
+        for (int i = 0, k = 0; i < ctas; ++i)
+            if (big(i) && k++ == my_small)
+            {
+                f.borrowed = act_blocks(intermediate, i, ctas).b1 - 1;
+                break;
+            }
+    }
+    return f;
+}
+
+// Waits (thread 0, acquire) until *word reaches target; false after the
+// barrier's spin limit.
+__device__ __forceinline__ bool wait_count(const unsigned* word, unsigned target)
+{
+    for (unsigned spin = 0; spin < kBarrierSpinLimit; ++spin)
+        if (ld_acquire(word) >= target)
+            return true;
+    return false;
+}
+
 constexpr int kDownRows = 2048;                        // down outputs (the model width)
 constexpr int kDownRecords = kDownRows / kSliceRows;   // 256-row slice records per CTA and layer
 constexpr int kMaxActBlocks = kRecordBytes / kSliceUnitBytes; // 4: a slice record fits a ring slot
@@ -744,36 +815,54 @@ __device__ bool consume_down_slices(const Ring& ring, unsigned& seq, const uint2
 // of the schedule is a pure function of k.
 struct Plan
 {
-    Slab slab[5]; // rows of q/k/v, o, gate/up, (down: unused), logits
-    int stages[5];
+    Slab slab[6]; // rows of q/k/v, o, gate/up, (down, extra down: unused), logits
+    int stages[6];
     int per_layer;
     int per_step;
-    Blocks blocks; // the CTA's activation blocks
+    FfnRoles ffn; // the CTA's activation blocks and their down work
+};
+
+enum : int
+{
+    kPlanQkv = 0,
+    kPlanO = 1,
+    kPlanGateUp = 2,
+    kPlanDown = 3,
+    kPlanExtraDown = 4, // a partner's block's down (balanced feed-forward)
+    kPlanLogits = 5,
+    kPlanLayerProducts = 5
 };
 
 __device__ __forceinline__ Plan make_plan(const PersistentArgs& p, int cta, int ctas)
 {
     Plan plan;
-    plan.slab[0] = cta_tiles(p.qkv_rows, cta, ctas);
-    plan.slab[1] = cta_tiles(2048, cta, ctas);
-    plan.blocks = act_blocks(p.intermediate, cta, ctas);
-    plan.slab[2] = Slab {4 * kTileRows * plan.blocks.b0, 4 * kTileRows * plan.blocks.b1}; // a gate/up pair per row pair
-    plan.slab[3] = Slab {0, 0};
-    plan.slab[4] = cta_tiles(p.vocab, cta, ctas);
-    for (int i = 0; i < 5; ++i)
-        plan.stages[i] = i == 3 ? kDownRecords : (plan.slab[i].r1 - plan.slab[i].r0) / kTileRows;
-    plan.per_layer = plan.stages[0] + plan.stages[1] + plan.stages[2] + plan.stages[3];
-    plan.per_step = p.n_layers * plan.per_layer + plan.stages[4];
+    plan.slab[kPlanQkv] = cta_tiles(p.qkv_rows, cta, ctas);
+    plan.slab[kPlanO] = cta_tiles(2048, cta, ctas);
+    plan.ffn = ffn_roles(p.intermediate, cta, ctas, p.balance_ffn != 0);
+    // a gate/up pair per row pair: four 16-row records a block (and two borrowed ones first)
+    plan.slab[kPlanGateUp] = Slab {4 * kTileRows * plan.ffn.blocks.b0, kTileRows * plan.ffn.gu_end};
+    plan.slab[kPlanDown] = Slab {0, 0};
+    plan.slab[kPlanExtraDown] = Slab {0, 0};
+    plan.slab[kPlanLogits] = cta_tiles(p.vocab, cta, ctas);
+    for (int i = 0; i < 6; ++i)
+        plan.stages[i] = (plan.slab[i].r1 - plan.slab[i].r0) / kTileRows;
+    plan.stages[kPlanGateUp] += plan.ffn.borrowed >= 0 ? 2 : 0;
+    plan.stages[kPlanDown] = kDownRecords;
+    plan.stages[kPlanExtraDown] = 0; // (unused: the balancing lends gate/up records)
+    plan.per_layer = 0;
+    for (int i = 0; i < kPlanLayerProducts; ++i)
+        plan.per_layer += plan.stages[i];
+    plan.per_step = p.n_layers * plan.per_layer + plan.stages[kPlanLogits];
     return plan;
 }
 
-// The record stage k of the schedule streams, with its product (0 q/k/v, 1 o,
-// 2 gate/up, 3 down, 4 logits), its index within the CTA's slab and its size.
+// The record stage k of the schedule streams, with its product (kPlan*), its
+// index within the product and its size.
 __device__ __forceinline__ const uint8_t* plan_stage(const PersistentArgs& p, const Plan& plan, long long k,
                                                      int& product, int& index, unsigned& bytes)
 {
     int r = (int) (k % plan.per_step);
-    product = 4;
+    product = kPlanLogits;
     const uint8_t* records = p.embed_records;
     if (r < p.n_layers * plan.per_layer)
     {
@@ -782,16 +871,24 @@ __device__ __forceinline__ const uint8_t* plan_stage(const PersistentArgs& p, co
         product = 0;
         while (r >= plan.stages[product])
             r -= plan.stages[product++];
-        if (product == 3)
+        const int blocks = p.intermediate / kBlock;
+        if (product == kPlanDown)
         {
             // slice record r: units (r, b0) .. (r, b1 - 1), contiguous
             index = r;
-            const int nb = plan.blocks.b1 - plan.blocks.b0;
-            bytes = (unsigned) (nb * kSliceUnitBytes);
-            return L.down_slices + ((size_t) r * (p.intermediate / kBlock) + plan.blocks.b0) * kSliceUnitBytes;
+            bytes = (unsigned) ((plan.ffn.blocks.b1 - plan.ffn.blocks.b0) * kSliceUnitBytes);
+            return L.down_slices + ((size_t) r * blocks + plan.ffn.blocks.b0) * kSliceUnitBytes;
         }
         const uint8_t* rs[3] = {L.qkv, L.o, L.gu};
         records = rs[product];
+        if (product == kPlanGateUp && plan.ffn.borrowed >= 0)
+        {
+            // the partner's two records first, then the CTA's own
+            index = r;
+            bytes = kRecordBytes;
+            const int record = r < 2 ? 4 * plan.ffn.borrowed + 2 + r : 4 * plan.ffn.blocks.b0 + (r - 2);
+            return records + (size_t) record * kRecordBytes;
+        }
     }
     else
         r -= p.n_layers * plan.per_layer;
@@ -826,7 +923,7 @@ __device__ void persistent_producer(const PersistentArgs& p, const Ring& ring, u
         int product, index;
         unsigned bytes;
         const uint8_t* record = plan_stage(p, plan, k, product, index, bytes);
-        if (product == 2 && index == 0 && p.gate_point != 0)
+        if (product == kPlanGateUp && index == 0 && p.gate_point != 0)
         {
             if (!mbar_wait(gate, gates & 1u))
             {
@@ -898,9 +995,13 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
     {
         reinterpret_cast<longlong2*>(p.down_acc)[2 * tid] = make_longlong2(0, 0);
         reinterpret_cast<longlong2*>(p.down_acc)[2 * tid + 1] = make_longlong2(0, 0);
+        // the activation blocks' publish counts (first read after three grid barriers)
+        for (int b = tid; b < p.intermediate / kBlock; b += kPConsumers)
+            p.act_ready[b] = 0u;
     }
     unsigned seq = 0, epoch = 0;
     float4 nw;
+    const FfnRoles ffn = ffn_roles(p.intermediate, cta, ctas, p.balance_ffn != 0);
 
     unsigned long long* trace_row = p.trace && tid == 0 ? p.trace + (size_t) cta * kTraceEvents : nullptr;
     auto stamp = [&](int slot) {
@@ -1072,7 +1173,8 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
             // ---- RMSNorm + gate/up + GeGLU on the CTA's activation blocks, then
             // down over the same blocks into the fixed-point sums
             {
-                const Blocks blocks = act_blocks(p.intermediate, cta, ctas);
+                const Blocks blocks = ffn.blocks;
+                unsigned long long* sums = p.down_acc + (layer_run & 1) * kDownRows;
                 GemvArgs a = {};
                 a.N = 2 * p.intermediate;
                 a.out = p.act;
@@ -1080,15 +1182,39 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent(const Persiste
                 a.act_local = attn_area;
                 a.act_base = blocks.b0 * kBlock;
                 stage(__ldcg(hidden4 + tid), true, ts + kTrGuStaged);
-                consume_tiles<Epi::GeGLU, NST, kPGroups>(a, Slab {4 * kTileRows * blocks.b0, 4 * kTileRows * blocks.b1},
+                if (ffn.borrowed >= 0)
+                {
+                    // the partner's two records first: activations 16..31 of its
+                    // last block, into p.act only, then published
+                    GemvArgs lent = a;
+                    lent.act_local = nullptr;
+                    consume_tiles<Epi::GeGLU, NST, kPGroups>(
+                        lent, Slab {4 * kTileRows * ffn.borrowed + 2 * kTileRows, 4 * kTileRows * (ffn.borrowed + 1)},
+                        ring, seq, bfrag, bfactor, red, position, best, best_i, group, 2 + group);
+                    consumers_sync();
+                    if (tid == 0)
+                        red_release_add(p.act_ready + ffn.borrowed, 1u);
+                }
+                consume_tiles<Epi::GeGLU, NST, kPGroups>(a, Slab {4 * kTileRows * blocks.b0, kTileRows * ffn.gu_end},
                                                          ring, seq, bfrag, bfactor, red, position, best, best_i, group,
                                                          2 + group);
                 stamp(ts + kTrGuDone);
                 consumers_sync(); // the CTA's activation entries are in attn_area
+                if (ffn.lent >= 0)
+                {
+                    // activations 16..31 of the lent block, from the partner
+                    if (tid == 0 && !wait_count(p.act_ready + ffn.lent, (unsigned) layer_run + 1u))
+                        flag_error(p.err, kErrBarrierTimeout);
+                    consumers_sync();
+                    if (tid < 4)
+                        reinterpret_cast<float4*>(attn_area + (ffn.lent - blocks.b0) * kBlock + 16)[tid] =
+                            __ldcg(reinterpret_cast<const float4*>(p.act + (size_t) ffn.lent * kBlock + 16) + tid);
+                    consumers_sync();
+                }
                 const int nb = blocks.b1 - blocks.b0;
                 stage_slice_limbs(attn_area, nb, frags, xexp, tid);
                 stamp(ts + kTrDownStaged);
-                consume_down_slices<NST>(ring, seq, frags, xexp, nb, p.down_acc + (layer_run & 1) * kDownRows, p.err, group);
+                consume_down_slices<NST>(ring, seq, frags, xexp, nb, sums, p.err, group);
             }
             load_norm(l + 1 < p.n_layers ? p.layers[l + 1].in_norm : p.final_norm);
             if (!barrier(ts + kTrDownDone, ts + kTrDownLeft))
