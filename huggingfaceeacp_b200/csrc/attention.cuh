@@ -410,9 +410,16 @@ constexpr size_t mqa_rows_smem()
     return ((size_t) kRowsQueries * kRowsKStride + 2 * kRowsBufFloats + 8 * 4 * kRowsTile) * sizeof(float);
 }
 
+//
+// QH < 8 (a tensor-parallel rank's share of the heads, a.heads = QH per kv
+// head): the CTA still holds 32 queries, now 32 / QH rows x QH heads; a warp's
+// four queries may then span rows, each with its own causal limit.
+template <int QH>
 __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
 {
-    constexpr int D = 256, QH = 8, T = kRowsTile, KS = kRowsKStride;
+    constexpr int D = 256, T = kRowsTile, KS = kRowsKStride;
+    constexpr int R = kRowsQueries / QH; // rows per CTA
+    static_assert(QH == 8 || QH == 4 || QH == 2 || QH == 1, "a warp's four queries are whole rows or one row");
     extern __shared__ __align__(16) float sm[];
     float* sq = sm;                                        // [32][KS] scaled queries
     float* bufs = sq + kRowsQueries * KS;                  // 2 x {K [T][KS], V [T][D]}
@@ -424,8 +431,8 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
     const int position = (int) *(volatile const unsigned*) a.state;
     pdl_trigger();
 
-    const int row0 = blockIdx.x * kRowsPerCta;
-    const int rows_here = min(kRowsPerCta, a.rows - row0);
+    const int row0 = blockIdx.x * R;
+    const int rows_here = min(R, a.rows - row0);
     const int head0 = blockIdx.y * QH;
     const int kvw = a.kv_heads * D;
     const size_t kv_off = (size_t) blockIdx.y * D;
@@ -464,9 +471,18 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
 
-    const int wrow = warp >> 1;                    // the warp's row within the CTA
-    const bool active = wrow < rows_here;          // warp-uniform
-    const int limit = base + wrow;                 // its last key
+    // Query i of the warp is CTA query 4 warp + i: row qrow[i], head qhead[i].
+    // Queries past the block's rows compute their last row's again and are
+    // not written (their sums stay finite).
+    int qrow[4], qlimit[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+    {
+        qrow[i] = (4 * warp + i) / QH;
+        qlimit[i] = base + min(qrow[i], rows_here - 1); // the query's last key
+    }
+    const bool active = qrow[0] < rows_here;        // warp-uniform
+    const int limit = qlimit[3];                    // the warp's last key
     const int kb = lane >> 2, quarter = lane & 3;
     const float* qw = sq + (4 * warp) * KS;        // the warp's four queries
     float* pw = sp + warp * 4 * T;
@@ -550,14 +566,16 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
                     s[i][j] += __shfl_xor_sync(0xFFFFFFFFu, s[i][j], 1);
                     s[i][j] += __shfl_xor_sync(0xFFFFFFFFu, s[i][j], 2);
                     const int key = t0 + 4 * kb + j;
-                    if (key > limit || 4 * kb + j >= nk)
+                    if (key > qlimit[i] || 4 * kb + j >= nk)
                         s[i][j] = -INFINITY;
                     tile_max = fmaxf(tile_max, s[i][j]);
                 }
                 tile_max = fmaxf(tile_max, __shfl_xor_sync(0xFFFFFFFFu, tile_max, 4));
                 tile_max = fmaxf(tile_max, __shfl_xor_sync(0xFFFFFFFFu, tile_max, 8));
                 tile_max = fmaxf(tile_max, __shfl_xor_sync(0xFFFFFFFFu, tile_max, 16));
-                const float m_new = fmaxf(m[i], tile_max); // finite: key t0 <= limit is in the tile
+                // finite: key 0 is in every query's first tile, and a later tile
+                // wholly past a query's limit leaves its maximum as it was
+                const float m_new = fmaxf(m[i], tile_max);
                 carried[i] = expf(m[i] - m_new);            // 0 on the first tile
                 float p[4], sum = 0.f;
 #pragma unroll
@@ -615,11 +633,13 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
 
     if (active)
     {
-        const int row = row0 + wrow;
 #pragma unroll
         for (int i = 0; i < 4; ++i)
         {
-            const int head = head0 + 4 * (warp & 1) + i;
+            if (qrow[i] >= rows_here)
+                continue;
+            const int row = row0 + qrow[i];
+            const int head = head0 + (4 * warp + i) % QH;
             float* o = a.out + (size_t) row * H * D + (size_t) head * D + 4 * lane;
             *reinterpret_cast<float4*>(o) =
                 make_float4(acc[i][0] / l[i], acc[i][1] / l[i], acc[i][2] / l[i], acc[i][3] / l[i]);

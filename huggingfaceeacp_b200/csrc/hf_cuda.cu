@@ -181,7 +181,10 @@ void configure_kernels()
     cudaFuncSetAttribute(mqa_fast<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<2>());
     cudaFuncSetAttribute(mqa_fast<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<1>());
     cudaFuncSetAttribute(mqa_generic, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    cudaFuncSetAttribute(mqa_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
+    cudaFuncSetAttribute(mqa_rows<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
+    cudaFuncSetAttribute(mqa_rows<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
+    cudaFuncSetAttribute(mqa_rows<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
+    cudaFuncSetAttribute(mqa_rows<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
     cudaFuncSetAttribute(decode_persistent<kPersistentStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int) persistent_smem<kPersistentStages>());
 #define HF_TC_SMEM(E)                                                                                          \
@@ -323,6 +326,15 @@ cudaError_t prep_pieces(const GemvArgs& a, size_t m_pad, cudaStream_t stream, __
                       tc_xunscale);
     case 2048:
         return launch(true, prep_x_pieces<NX, 2048>, grid, dim3(256), 0, stream, a.x, a.norm_w, a.eps, a.M, tc_x,
+                      tc_xunscale);
+    case 1024: // o_proj's share of the heads on 2, 4 or 8 tensor-parallel ranks
+        return launch(true, prep_x_pieces<NX, 1024>, grid, dim3(256), 0, stream, a.x, a.norm_w, a.eps, a.M, tc_x,
+                      tc_xunscale);
+    case 512:
+        return launch(true, prep_x_pieces<NX, 512>, grid, dim3(256), 0, stream, a.x, a.norm_w, a.eps, a.M, tc_x,
+                      tc_xunscale);
+    case 256:
+        return launch(true, prep_x_pieces<NX, 256>, grid, dim3(256), 0, stream, a.x, a.norm_w, a.eps, a.M, tc_x,
                       tc_xunscale);
     default:
         return cudaErrorInvalidValue;
@@ -481,6 +493,7 @@ struct hf_ctx
     int tp_world = 1;
     ncclComm_t tp_comm = nullptr;
     std::vector<Q8> tp_gu, tp_down; // this rank's shards, per layer (two-region bytes + tensor-core blocks)
+    std::vector<Q8> tp_qkv, tp_o;   // its query heads (plus the shared k/v rows) and those heads' o_proj columns
     uint8_t* tp_pool = nullptr;
     float* tp_partial = nullptr;    // [capacity, width] the down partial sums, reduced in place
 
@@ -1220,6 +1233,15 @@ struct hf_ctx
             qkv.head_dim = s.head_width;
             qkv.state = state;
             qkv.err = err_word();
+            if (tp_world > 1 && rows > kRowsBlock && !tc_off)
+            {
+                int rc = tp_attention(l, rows);
+                if (!rc)
+                    rc = tp_feed_forward(l, rows);
+                if (rc)
+                    return rc;
+                continue;
+            }
             e = L.qkv.records ? multi_row<Epi::QkvRope, 2048>(L.qkv, qkv) : normed_generic<Epi::QkvRope>(L.qkv.rows / 2, qkv);
             if (e != cudaSuccess)
                 return cuda(e, "q/k/v launch");
@@ -1240,7 +1262,7 @@ struct hf_ctx
             {
                 // many consecutive rows: the K/V tiles shared by a CTA's rows
                 at.rows = rows;
-                e = launch(true, mqa_rows, dim3((unsigned) ((rows + kRowsPerCta - 1) / kRowsPerCta), s.kv_heads),
+                e = launch(true, mqa_rows<8>, dim3((unsigned) ((rows + kRowsPerCta - 1) / kRowsPerCta), s.kv_heads),
                            dim3(256), mqa_rows_smem(), stream, at);
             }
             else if (fast)
@@ -1268,14 +1290,6 @@ struct hf_ctx
             if (e != cudaSuccess)
                 return cuda(e, "o_proj launch");
 
-
-            if (tp_world > 1 && rows > kRowsBlock && !tc_off)
-            {
-                const int rc = tp_feed_forward(l, rows);
-                if (rc)
-                    return rc;
-                continue;
-            }
 
             GemvArgs gu = {};
             gu.w = L.gu.base;
@@ -1385,13 +1399,88 @@ struct hf_ctx
         e = tc_product_on<Epi::Store>(tp_down[l].tc, dn, stream, tc_x, tc_xunscale, tc_ws, sms);
         if (e != cudaSuccess)
             return cuda(e, "down launch");
-        const size_t count = (size_t) rows * s.width;
+        return tp_reduce_into_hidden(rows);
+    }
+
+    // This rank's attention half of a prefill block's layer: q for its heads
+    // (and the shared k/v rows into the cache) on the tensor cores, attention
+    // over its heads, o_proj over those heads' columns as partial sums, their
+    // allreduce over the ranks and the residual add.
+    int tp_attention(int l, int rows)
+    {
+        const hf_shape& s = shape;
+        const int heads = s.heads / tp_world;
+        GemvArgs qkv = {};
+        qkv.w = tp_qkv[l].base;
+        qkv.scales = tp_qkv[l].scales();
+        qkv.N = tp_qkv[l].rows;
+        qkv.K = s.width;
+        qkv.M = rows;
+        qkv.x = hidden;
+        qkv.norm_w = layers[l].in_norm;
+        qkv.eps = s.rms_eps;
+        qkv.out = qbuf; // [rows, heads * D]: this rank's heads only
+        qkv.k_cache = layer_k(l);
+        qkv.v_cache = layer_v(l);
+        qkv.rope_cos = rope_cos;
+        qkv.rope_sin = rope_sin;
+        qkv.heads = heads;
+        qkv.kv_heads = s.kv_heads;
+        qkv.head_dim = s.head_width;
+        qkv.state = state;
+        qkv.err = err_word();
+        cudaError_t e = tc_product_on<Epi::QkvRope>(tp_qkv[l].tc, qkv, stream, tc_x, tc_xunscale, tc_ws, sms);
+        if (e != cudaSuccess)
+            return cuda(e, "q/k/v launch");
+        AttnArgs at = {};
+        at.q = qbuf;
+        at.k_cache = layer_k(l);
+        at.v_cache = layer_v(l);
+        at.out = attended; // [rows, heads * D]
+        at.heads = heads;
+        at.kv_heads = s.kv_heads;
+        at.head_dim = s.head_width;
+        at.scale = 1.f / std::sqrt((float) s.head_width);
+        at.nsplit = 1;
+        at.state = state;
+        at.err = err_word();
+        at.rows = rows;
+        const int per_kv = heads / s.kv_heads, block_rows = kRowsQueries / per_kv;
+        const dim3 grid((unsigned) ((rows + block_rows - 1) / block_rows), (unsigned) s.kv_heads);
+        switch (per_kv)
+        {
+        case 4: e = launch(true, mqa_rows<4>, grid, dim3(256), mqa_rows_smem(), stream, at); break;
+        case 2: e = launch(true, mqa_rows<2>, grid, dim3(256), mqa_rows_smem(), stream, at); break;
+        default: e = launch(true, mqa_rows<1>, grid, dim3(256), mqa_rows_smem(), stream, at); break;
+        }
+        if (e != cudaSuccess)
+            return cuda(e, "attention launch");
+        GemvArgs o = {};
+        o.w = tp_o[l].base;
+        o.scales = tp_o[l].scales();
+        o.N = s.width;
+        o.K = heads * s.head_width;
+        o.M = rows;
+        o.x = attended;
+        o.out = tp_partial;
+        o.state = state;
+        o.err = err_word();
+        e = tc_product_on<Epi::Store>(tp_o[l].tc, o, stream, tc_x, tc_xunscale, tc_ws, sms);
+        if (e != cudaSuccess)
+            return cuda(e, "o_proj launch");
+        return tp_reduce_into_hidden(rows);
+    }
+
+    // The ranks' partial sums [rows, width] added by one allreduce, then to the residual stream.
+    int tp_reduce_into_hidden(int rows)
+    {
+        const size_t count = (size_t) rows * shape.width;
         const NcclLibrary& nccl = tensor_parallel_library();
         const ncclResult_t r = nccl.all_reduce(tp_partial, tp_partial, count, ncclFloat32, ncclSum, tp_comm, stream);
         if (r != ncclSuccess)
-            return fail(HF_E_CUDA, std::string("allreduce of the down partial sums: ") + nccl.error_string(r));
-        e = launch(false, add_rows, dim3((unsigned) ((count / 4 + 255) / 256)), dim3(256), 0, stream, hidden,
-                   (const float*) tp_partial, count);
+            return fail(HF_E_CUDA, std::string("allreduce of the partial sums: ") + nccl.error_string(r));
+        const cudaError_t e = launch(false, add_rows, dim3((unsigned) ((count / 4 + 255) / 256)), dim3(256), 0, stream,
+                                     hidden, (const float*) tp_partial, count);
         return e != cudaSuccess ? cuda(e, "residual launch") : HF_OK;
     }
 
@@ -1408,6 +1497,8 @@ struct hf_ctx
         tp_partial = nullptr;
         tp_gu.clear();
         tp_down.clear();
+        tp_qkv.clear();
+        tp_o.clear();
         tp_rank = 0;
         tp_world = 1;
     }
@@ -2713,8 +2804,10 @@ int hf_cuda_set_tensor_parallel(hf_ctx* ctx, int rank, int world, const uint8_t*
         return ctx->fail(HF_E_NOT_READY, "tensor parallelism splits the loaded weights: upload every weight first");
     if (!ctx->tc_pool || !ctx->fast)
         return ctx->fail(HF_E_SHAPE, "tensor-parallel prefill runs on the tensor-core products, which this shape has none of");
-    if ((world != 2 && world != 4 && world != 8) || (I / world) % 2048 != 0)
-        return ctx->fail(HF_E_SHAPE, "the feed-forward splits into 2, 4 or 8 shares of whole 2048-unit ranges");
+    if ((world != 2 && world != 4 && world != 8) || (I / world) % 2048 != 0 || s.heads % world != 0
+        || s.kv_heads != 1)
+        return ctx->fail(HF_E_SHAPE, "the heads and the feed-forward split into 2, 4 or 8 shares (whole heads over one "
+                                     "kv head, whole 2048-unit ranges)");
     const NcclLibrary& nccl = tensor_parallel_library();
     if (!nccl.ok)
         return ctx->fail(HF_E_CUDA, "libnccl.so.2 could not be opened");
@@ -2727,7 +2820,14 @@ int hf_cuda_set_tensor_parallel(hf_ctx* ctx, int rank, int world, const uint8_t*
     auto q8bytes = [](size_t rows, size_t cols) { return rows * cols + rows * cols / 16; };
     const size_t gu_bytes = round256(q8bytes(2 * (size_t) units, W)) + round256(tc_weight_bytes(2 * (size_t) units, W));
     const size_t dn_bytes = round256(q8bytes(W, units)) + round256(tc_weight_bytes(W, units));
-    if (ctx->cuda(cudaMalloc(&ctx->tp_pool, (gu_bytes + dn_bytes) * s.layers), "tensor-parallel shards")
+    // the rank's query heads [h0, h1) (rows 256 h0 .. 256 h1 of the fused q/k/v, each head's rows kept
+    // in their rotate-half pair order) and the shared k/v rows; o_proj's columns of those heads
+    const int D = s.head_width, heads = s.heads / world, h0 = rank * heads, KVW = ctx->kv_width();
+    const int qkv_rows = heads * D + 2 * KVW, o_cols = heads * D;
+    const size_t qkv_bytes = round256(q8bytes(qkv_rows, W)) + round256(tc_weight_bytes(qkv_rows, W));
+    const size_t o_bytes = round256(q8bytes(W, o_cols)) + round256(tc_weight_bytes(W, o_cols));
+    const size_t layer_bytes = gu_bytes + dn_bytes + qkv_bytes + o_bytes;
+    if (ctx->cuda(cudaMalloc(&ctx->tp_pool, layer_bytes * s.layers), "tensor-parallel shards")
         || ctx->cuda(cudaMalloc(&ctx->tp_partial, (size_t) ctx->capacity * W * sizeof(float)), "partial sums"))
     {
         ctx->drop_tensor_parallel();
@@ -2736,8 +2836,16 @@ int hf_cuda_set_tensor_parallel(hf_ctx* ctx, int rank, int world, const uint8_t*
     for (int l = 0; l < s.layers; ++l)
     {
         const Layer& L = ctx->layers[l];
-        uint8_t* at = ctx->tp_pool + (gu_bytes + dn_bytes) * l;
-        Q8 gu, dn;
+        uint8_t* at = ctx->tp_pool + layer_bytes * l;
+        Q8 gu, dn, qkv, o;
+        qkv.rows = qkv_rows;
+        qkv.cols = W;
+        qkv.base = at + gu_bytes + dn_bytes;
+        qkv.tc = qkv.base + round256(q8bytes(qkv_rows, W));
+        o.rows = W;
+        o.cols = o_cols;
+        o.base = qkv.base + qkv_bytes;
+        o.tc = o.base + round256(q8bytes(W, o_cols));
         gu.rows = 2 * units;
         gu.cols = W;
         gu.base = at;
@@ -2757,10 +2865,34 @@ int hf_cuda_set_tensor_parallel(hf_ctx* ctx, int rank, int world, const uint8_t*
             e = cudaMemcpy2D(dn.base + (size_t) W * units, units / 16,
                              reinterpret_cast<const uint8_t*>(L.down.scales()) + j0 / 16, I / 16, units / 16, W,
                              cudaMemcpyDeviceToDevice);
+        // q/k/v: the heads' rows, then the k and v rows, quants then scales
+        const size_t q_quants = (size_t) heads * D * W, kv_quants = (size_t) 2 * KVW * W;
+        const uint8_t* qkv_scales = reinterpret_cast<const uint8_t*>(L.qkv.scales());
+        if (e == cudaSuccess)
+            e = cudaMemcpy(qkv.base, L.qkv.base + (size_t) h0 * D * W, q_quants, cudaMemcpyDeviceToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(qkv.base + q_quants, L.qkv.base + (size_t) s.heads * D * W, kv_quants,
+                           cudaMemcpyDeviceToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(qkv.base + q_quants + kv_quants, qkv_scales + (size_t) h0 * D * W / 16, q_quants / 16,
+                           cudaMemcpyDeviceToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(qkv.base + q_quants + kv_quants + q_quants / 16, qkv_scales + (size_t) s.heads * D * W / 16,
+                           kv_quants / 16, cudaMemcpyDeviceToDevice);
+        // o_proj: for each of the W rows, the heads' columns [h0 D, h1 D) and their scales
+        const int QW = ctx->query_width();
+        if (e == cudaSuccess)
+            e = cudaMemcpy2D(o.base, o_cols, L.o.base + (size_t) h0 * D, QW, o_cols, W, cudaMemcpyDeviceToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2D(o.base + (size_t) W * o_cols, o_cols / 16,
+                             reinterpret_cast<const uint8_t*>(L.o.scales()) + (size_t) h0 * D / 16, QW / 16,
+                             o_cols / 16, W, cudaMemcpyDeviceToDevice);
         if (e == cudaSuccess)
         {
             build_tc_blocks<<<gu.rows / kTcRows, kTcRows>>>(gu.base, gu.scales(), W, gu.tc);
             build_tc_blocks<<<W / kTcRows, kTcRows>>>(dn.base, dn.scales(), units, dn.tc);
+            build_tc_blocks<<<qkv.rows / kTcRows, kTcRows>>>(qkv.base, qkv.scales(), W, qkv.tc);
+            build_tc_blocks<<<W / kTcRows, kTcRows>>>(o.base, o.scales(), o_cols, o.tc);
             e = cudaDeviceSynchronize();
         }
         if (e != cudaSuccess)
@@ -2770,17 +2902,20 @@ int hf_cuda_set_tensor_parallel(hf_ctx* ctx, int rank, int world, const uint8_t*
         }
         ctx->tp_gu.push_back(gu);
         ctx->tp_down.push_back(dn);
+        ctx->tp_qkv.push_back(qkv);
+        ctx->tp_o.push_back(o);
     }
     // The split workspace must also serve the shards' products (split_stride =
     // m_pad x the product's outputs per split).
     size_t ws = 1;
     for (int m = kRowsBlock + 1; m <= ctx->capacity; ++m)
     {
-        const TcPlan gate_up = tc_plan(m, 2 * units, W, ctx->sms), down = tc_plan(m, W, units, ctx->sms);
-        if (gate_up.splits > 1)
-            ws = std::max(ws, (size_t) gate_up.splits * gate_up.m_pad * 2 * units);
-        if (down.splits > 1)
-            ws = std::max(ws, (size_t) down.splits * down.m_pad * W);
+        const TcPlan plans[4] = {tc_plan(m, 2 * units, W, ctx->sms), tc_plan(m, W, units, ctx->sms),
+                                 tc_plan(m, qkv_rows, W, ctx->sms), tc_plan(m, W, o_cols, ctx->sms)};
+        const int outputs[4] = {2 * units, W, qkv_rows, W};
+        for (int i = 0; i < 4; ++i)
+            if (plans[i].splits > 1)
+                ws = std::max(ws, (size_t) plans[i].splits * plans[i].m_pad * outputs[i]);
     }
     if (ws > ctx->tc_ws_count)
     {

@@ -244,7 +244,7 @@ template <int NX, int K>
 __global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float* norm_w, float eps, int M,
                                                      __half* pieces, float* unscale)
 {
-    constexpr int G = K / 2048; // 8-column groups per thread
+    constexpr int G = (K + 2047) / 2048; // 8-column groups per thread (the last partly idle when K < 2048)
     __shared__ float red[8];
     pdl_wait();
     pdl_trigger();
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float
     for (int q = 0; q < G; ++q)
     {
         const int k = (tid + 256 * q) * 8;
-        if (live)
+        if (live && k < K)
         {
             const float4 a = __ldcg(reinterpret_cast<const float4*>(row + k));
             const float4 b = __ldcg(reinterpret_cast<const float4*>(row + k + 4));
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float
 #pragma unroll
         for (int i = 0; i < 8; ++i)
         {
-            if (norm_w && live)
+            if (norm_w && live && k < K)
                 v[q][i] = v[q][i] * scale * (1.f + norm_w[k + i]);
             mx = fmaxf(mx, fabsf(v[q][i]));
         }
@@ -322,6 +322,8 @@ __global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float
     for (int q = 0; q < G; ++q)
     {
         const int k = (tid + 256 * q) * 8, c = k / kTcChunk, cc = (k % kTcChunk) / 8;
+        if (k >= K)
+            continue;
         __align__(16) __half hi[8];
         __align__(16) __half mid[8];
 #pragma unroll
