@@ -57,6 +57,7 @@ BATCH_WORKLOAD = "config3: 64 independent sequences per GPU, 512-token seeded pr
 LONG_PROMPT = 8064        # configs[2]: prompt tokens, then decode to an 8,192-position window
 LONG_SEED = 2
 LONG_WORKLOAD = "config2: Gemma-2B batch-1 prefill of 8064 seeded ids (seed 2), greedy decode to 8192 positions"
+PREFILL_STEP_ROWS = 2048  # prefill rows per step (long prompts: 354 ms at 2048 against 368.5 at 512)
 PREFILL_SEQUENCES = 8     # configs[4]: 8 x 2048-token prompts
 PREFILL_PROMPT = 2048
 PREFILL_SEED = 4
@@ -320,7 +321,7 @@ def run_ours(args):
     # the batched steps (the weights are uploaded once).
     window = max(LONG_PROMPT + 128, BATCH_PROMPT + args.batched_steps + args.warmup,
                  PROMPT_LENGTH + 2 * (args.warmup + args.steps) + 8)
-    shape = native.GEMMA_2B.replace(max_step_rows=BATCH_PROMPT, max_positions=window)
+    shape = native.GEMMA_2B.replace(max_step_rows=PREFILL_STEP_ROWS, max_positions=window)
     keep = rank == 0 and world == 1 and not args.no_cpu_baseline
     # The batched sequences' K/V live in pages: enough for each sequence's
     # prompt and every step it takes here (not its whole window).
@@ -687,7 +688,7 @@ def main():
     parser.add_argument("--no-config1", action="store_true", help="skip the configs[1] op sweep")
     parser.add_argument("--tp-prefill", action="store_true",
                         help="time tensor-parallel prefill of config 2's prompt over --gpus ranks (not the bench line)")
-    parser.add_argument("--tp-rows", type=int, default=512, help="prefill rows per step for --tp-prefill")
+    parser.add_argument("--tp-rows", type=int, default=PREFILL_STEP_ROWS, help="prefill rows per step for --tp-prefill")
     parser.add_argument("--profile-case", nargs="?", const="decode", choices=["decode", "batched", "prefill"],
                         help="run a small ncu capture case instead of the bench: the decode kernel (default), "
                              "a batched step's tensor-core products, or a prompt's prefill")

@@ -47,3 +47,24 @@ def test_tensor_core_batched_decode_matches_reference_per_sequence():
         out = ctx.generate_batch(prompts, tokens)
         for q in range(sequences):
             assert list(out[q]) == ob.greedy_reference(SHAPE, tensors, prompts[q], tokens), q
+
+
+def test_tensor_core_prefill_blocks_of_1024_and_2048_rows_match_reference():
+    """Prefill blocks of up to 2048 rows, the step capacity the bench's prefill runs at (one layer,
+    Gemma widths): 16 x tiles of 128 rows, the logits of the last rows and every hidden row checked."""
+    shape = SHAPE.replace(layers=1, max_positions=3200, max_step_rows=2048)
+    with native.Context(shape) as ctx:
+        tensors = ctx.load_synthetic(seed=19, keep=True)
+        oracle = ob.OracleModel(shape, tensors)
+        prompt = native.synthetic_tokens(19, 3072, shape.vocab)
+        try:
+            first = 0
+            for rows in (2048, 1024):
+                block = prompt[first:first + rows]
+                first += rows
+                logits, hidden = ctx.step(block)
+                ref_hidden, ref_logits = oracle.step(block)
+                assert ob.worst_error(logits[-16:], ref_logits[-16:]) <= TOLERANCE, rows
+                assert ob.worst_error(hidden, ref_hidden) <= TOLERANCE, rows
+        finally:
+            oracle.close()
