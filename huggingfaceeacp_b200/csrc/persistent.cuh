@@ -815,8 +815,8 @@ __device__ bool consume_down_slices(const Ring& ring, unsigned& seq, const uint2
 // of the schedule is a pure function of k.
 struct Plan
 {
-    Slab slab[6]; // rows of q/k/v, o, gate/up, (down, extra down: unused), logits
-    int stages[6];
+    Slab slab[5]; // rows of q/k/v, o, gate/up, (down: unused), logits
+    int stages[5];
     int per_layer;
     int per_step;
     FfnRoles ffn; // the CTA's activation blocks and their down work
@@ -828,9 +828,8 @@ enum : int
     kPlanO = 1,
     kPlanGateUp = 2,
     kPlanDown = 3,
-    kPlanExtraDown = 4, // a partner's block's down (balanced feed-forward)
-    kPlanLogits = 5,
-    kPlanLayerProducts = 5
+    kPlanLogits = 4,
+    kPlanLayerProducts = 4
 };
 
 __device__ __forceinline__ Plan make_plan(const PersistentArgs& p, int cta, int ctas)
@@ -842,13 +841,11 @@ __device__ __forceinline__ Plan make_plan(const PersistentArgs& p, int cta, int 
     // a gate/up pair per row pair: four 16-row records a block (and two borrowed ones first)
     plan.slab[kPlanGateUp] = Slab {4 * kTileRows * plan.ffn.blocks.b0, kTileRows * plan.ffn.gu_end};
     plan.slab[kPlanDown] = Slab {0, 0};
-    plan.slab[kPlanExtraDown] = Slab {0, 0};
     plan.slab[kPlanLogits] = cta_tiles(p.vocab, cta, ctas);
-    for (int i = 0; i < 6; ++i)
+    for (int i = 0; i < 5; ++i)
         plan.stages[i] = (plan.slab[i].r1 - plan.slab[i].r0) / kTileRows;
     plan.stages[kPlanGateUp] += plan.ffn.borrowed >= 0 ? 2 : 0;
     plan.stages[kPlanDown] = kDownRecords;
-    plan.stages[kPlanExtraDown] = 0; // (unused: the balancing lends gate/up records)
     plan.per_layer = 0;
     for (int i = 0; i < kPlanLayerProducts; ++i)
         plan.per_layer += plan.stages[i];
