@@ -59,6 +59,20 @@ __device__ __forceinline__ void cp_async_wait_all()
     asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
 
+__device__ __forceinline__ void cp_async_commit()
+{
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Waits until at most N of this thread's committed groups are in flight.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+constexpr int kAttnFastTile = 16; // keys per K/V tile of mqa_fast (two tiles in flight)
+
 // Sums part[h] (h < QH) across the warp so that lane L ends with the total of
 // head head_of_lane<QH>(L): log2(QH) halving exchanges, then full reduction of
 // what is left -- 9 shuffles for 8 heads instead of 40.
@@ -130,19 +144,29 @@ __device__ __forceinline__ int lane_of_head(int h)
 // D = 256, QH query heads in one CTA's group (all reading kv head `kv_head`),
 // one CTA per (split, head group, row). A lane owns channels [8 lane, 8 lane + 8)
 // of every head of the group; K/V tiles of TILE keys are staged in shared
-// memory by the 256 threads at once, each warp takes TILE / 8 keys of the tile,
-// scores them for all heads, and keeps its own running (max, sum, row) per head;
-// the warps fold at the end. `sync` is the barrier of the 256 threads.
-// Shared memory: max(2 TILE, 8 QH) x 256 floats + 16 QH.
-template <int QH, int TILE, typename Sync>
+// memory by the 256 threads at once, two tiles in flight (tile t + 1 lands
+// while tile t is scored); each warp takes TILE / 8 keys of a tile, scores
+// them for all heads, and keeps its own running (max, sum, row) per head; the
+// warps fold at the end. `sync` is the barrier of the 256 threads. The sums
+// run on the f32x2 pipe: the scores of two heads at once (each head's chain
+// over a lane's 8 channels in the same order as scalar FMAs), the rows two
+// channels at once.
+// Shared memory: max(4 TILE, 8 QH) x 256 floats + 16 QH.
+//
+// `ready` waits for the kernels before this one (programmatic dependent
+// launch). A paged row's keys below its own position were written by earlier
+// steps (this step writes only key seq_pos[row]), and its position and page
+// table are set before the step, so its first tile is staged before `ready`
+// when that tile stops short of the newest key; the query is read after it.
+template <int QH, int TILE, typename Sync, typename Ready>
 __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int head0, int kv_head, int split,
-                          float* sm, Sync sync)
+                          float* sm, Sync sync, Ready ready)
 {
     constexpr int D = 256;
-    float* tk = sm;                 // [TILE][D]
-    float* tv = sm + TILE * D;      // [TILE][D]
+    constexpr int KPW = TILE / 8;                // keys of a tile per warp
+    constexpr int HP = QH >= 2 ? QH / 2 : 1;     // f32x2 head pairs (QH = 1: one head, the high half idle)
     float* wacc = sm;               // after the loop: [8][QH][D] (reuses the tiles)
-    float* wm = sm + (2 * TILE > 8 * QH ? 2 * TILE : 8 * QH) * D; // [8][QH]
+    float* wm = sm + (4 * TILE > 8 * QH ? 4 * TILE : 8 * QH) * D; // [8][QH]
     float* wl = wm + 8 * QH;        // [8][QH]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -152,80 +176,130 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
     const int keys = table ? (int) a.seq_pos[row] + 1 : (int) position + (a.cache_seq_stride ? 0 : row) + 1;
     const float* k_cache = a.k_cache + (table ? 0 : (size_t) row * a.cache_seq_stride);
     const float* v_cache = a.v_cache + (table ? 0 : (size_t) row * a.cache_seq_stride);
-    const int chunk = (keys + a.nsplit - 1) / a.nsplit;
+    const int chunk = ((keys + a.nsplit - 1) / a.nsplit + TILE - 1) / TILE * TILE; // whole tiles
     const int k0 = min(keys, split * chunk);
     const int k1 = min(keys, k0 + chunk);
     const int my_head = head_of_lane<QH>(lane);
 
-    float qv[QH][8];
+    // The tile of keys [t0, t0 + TILE) into buffer `buf`: K then V rows. A
+    // thread keeps one 16-byte column of every fourth row; page sizes are
+    // powers of two.
+    const int page_shift = table ? __ffs(a.page_rows) - 1 : 0;
+    const int col = (tid & (D / 4 - 1)) * 4;
+    const float* k_col = k_cache + (size_t) kv_head * D + col;
+    const float* v_col = v_cache + (size_t) kv_head * D + col;
+    auto stage = [&](int t0, int buf) {
+        float* bk = sm + buf * 2 * TILE * D + col;
+        float* bv = bk + TILE * D;
+        const int nk = min(TILE, k1 - t0);
+        for (int r = tid / (D / 4); r < nk; r += 256 / (D / 4))
+        {
+            const int key = t0 + r;
+            const size_t cache_row =
+                table ? ((size_t) table[key >> page_shift] << page_shift) + (key & (a.page_rows - 1)) : (size_t) key;
+            cp_async16(bk + r * D, k_col + cache_row * kvw);
+            cp_async16(bv + r * D, v_col + cache_row * kvw);
+        }
+        cp_async_commit();
+    };
+
+    const bool early = table && k0 < k1 && k0 + min(TILE, k1 - k0) < keys;
+    if (early)
+        stage(k0, 0);
+    ready();
+
+    // q (scaled) as head pairs: qp[hp][d] = (head 2 hp, head 2 hp + 1) at channel d.
+    uint64_t qp[HP][8];
     const float* qrow = a.q + (size_t) row * H * D + (size_t) head0 * D + lane * 8;
 #pragma unroll
-    for (int h = 0; h < QH; ++h)
+    for (int hp = 0; hp < HP; ++hp)
     {
-        const float4 lo = __ldcg(reinterpret_cast<const float4*>(qrow + h * D));
-        const float4 hi = __ldcg(reinterpret_cast<const float4*>(qrow + h * D + 4));
-        qv[h][0] = lo.x * a.scale; qv[h][1] = lo.y * a.scale; qv[h][2] = lo.z * a.scale; qv[h][3] = lo.w * a.scale;
-        qv[h][4] = hi.x * a.scale; qv[h][5] = hi.y * a.scale; qv[h][6] = hi.z * a.scale; qv[h][7] = hi.w * a.scale;
+        float q0[8], q1[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const float4 a0 = __ldcg(reinterpret_cast<const float4*>(qrow + 2 * hp * D));
+        const float4 b0 = __ldcg(reinterpret_cast<const float4*>(qrow + 2 * hp * D + 4));
+        q0[0] = a0.x; q0[1] = a0.y; q0[2] = a0.z; q0[3] = a0.w; q0[4] = b0.x; q0[5] = b0.y; q0[6] = b0.z; q0[7] = b0.w;
+        if (QH >= 2)
+        {
+            const float4 a1 = __ldcg(reinterpret_cast<const float4*>(qrow + (2 * hp + 1) * D));
+            const float4 b1 = __ldcg(reinterpret_cast<const float4*>(qrow + (2 * hp + 1) * D + 4));
+            q1[0] = a1.x; q1[1] = a1.y; q1[2] = a1.z; q1[3] = a1.w; q1[4] = b1.x; q1[5] = b1.y; q1[6] = b1.z; q1[7] = b1.w;
+        }
+#pragma unroll
+        for (int d = 0; d < 8; ++d)
+            qp[hp][d] = pack2(q0[d] * a.scale, q1[d] * a.scale);
     }
 
     float m = -INFINITY, l = 0.f; // of head my_head, replicated across its lanes
-    float acc[QH][8];
+    uint64_t acc[QH][4];          // channel pairs (8 lane + 2 i, 8 lane + 2 i + 1)
 #pragma unroll
     for (int h = 0; h < QH; ++h)
 #pragma unroll
-        for (int d = 0; d < 8; ++d)
-            acc[h][d] = 0.f;
+        for (int i = 0; i < 4; ++i)
+            acc[h][i] = 0; // (0.f, 0.f)
 
-    for (int t0 = k0; t0 < k1; t0 += TILE)
+    if (k0 < k1 && !early)
+        stage(k0, 0);
+    int buf = 0;
+    for (int t0 = k0; t0 < k1; t0 += TILE, buf ^= 1)
     {
         const int nk = min(TILE, k1 - t0);
-        // ---- stage the tile: nk rows of K and of V, 16 bytes a thread at a time
-        for (int i = tid; i < nk * (D / 4); i += 256)
+        // The next tile goes to the other buffer, read by the previous
+        // iteration before its closing barrier.
+        if (t0 + TILE < k1)
         {
-            const int r = i / (D / 4), c = (i % (D / 4)) * 4;
-            const int key = t0 + r;
-            const size_t cache_row =
-                table ? (size_t) table[key / a.page_rows] * a.page_rows + key % a.page_rows : (size_t) key;
-            const size_t at = cache_row * kvw + (size_t) kv_head * D + c;
-            cp_async16(tk + r * D + c, k_cache + at);
-            cp_async16(tv + r * D + c, v_cache + at);
+            stage(t0 + TILE, buf ^ 1);
+            cp_async_wait_group<1>();
         }
-        cp_async_wait_all();
+        else
+            cp_async_wait_group<0>();
         sync();
+        const float* tk = sm + buf * 2 * TILE * D;
+        const float* tv = tk + TILE * D;
 
         // ---- this warp's keys of the tile: warp, warp + 8, ...
-        float s[TILE / 8];
+        float s[KPW];
 #pragma unroll
-        for (int j = 0; j < TILE / 8; ++j)
+        for (int j = 0; j < KPW; ++j)
         {
             const int r = warp + 8 * j;
-            float part[QH];
             const float4 lo = *reinterpret_cast<const float4*>(tk + (r < nk ? r : 0) * D + lane * 8);
             const float4 hi = *reinterpret_cast<const float4*>(tk + (r < nk ? r : 0) * D + lane * 8 + 4);
             const float kk[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+            uint64_t v[HP];
 #pragma unroll
-            for (int h = 0; h < QH; ++h)
+            for (int hp = 0; hp < HP; ++hp)
+                v[hp] = 0;
+#pragma unroll
+            for (int d = 0; d < 8; ++d)
             {
-                float v = 0.f;
+                const uint64_t kd = pack2(kk[d], kk[d]);
 #pragma unroll
-                for (int d = 0; d < 8; ++d)
-                    v = fmaf(qv[h][d], kk[d], v);
-                part[h] = v;
+                for (int hp = 0; hp < HP; ++hp)
+                    v[hp] = fma2(qp[hp][d], kd, v[hp]);
+            }
+            float part[QH];
+#pragma unroll
+            for (int hp = 0; hp < HP; ++hp)
+            {
+                const float2 pr = unpack2(v[hp]);
+                part[2 * hp] = pr.x;
+                if (QH >= 2)
+                    part[(2 * hp + 1) % QH] = pr.y;
             }
             const float total = transpose_reduce<QH>(part, lane);
             s[j] = r < nk ? total : -INFINITY;
         }
         float tile_max = s[0];
 #pragma unroll
-        for (int j = 1; j < TILE / 8; ++j)
+        for (int j = 1; j < KPW; ++j)
             tile_max = fmaxf(tile_max, s[j]);
         const float m_new = fmaxf(m, tile_max);
-        float carried = 0.f, p[TILE / 8], psum = 0.f;
+        float carried = 0.f, p[KPW], psum = 0.f;
         if (m_new != -INFINITY)
         {
             carried = expf(m - m_new); // 0 while nothing was seen
 #pragma unroll
-            for (int j = 0; j < TILE / 8; ++j)
+            for (int j = 0; j < KPW; ++j)
             {
                 p[j] = expf(s[j] - m_new);
                 psum += p[j];
@@ -235,7 +309,7 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
         else
         {
 #pragma unroll
-            for (int j = 0; j < TILE / 8; ++j)
+            for (int j = 0; j < KPW; ++j)
                 p[j] = 0.f;
             carried = 1.f;
         }
@@ -246,38 +320,42 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
         for (int h = 0; h < QH; ++h)
         {
             const float c = __shfl_sync(0xFFFFFFFFu, carried, lane_of_head<QH>(h));
+            const uint64_t c2 = pack2(c, c);
 #pragma unroll
-            for (int d = 0; d < 8; ++d)
-                acc[h][d] *= c;
+            for (int i = 0; i < 4; ++i)
+                acc[h][i] = mul2(acc[h][i], c2);
         }
 #pragma unroll
-        for (int j = 0; j < TILE / 8; ++j)
+        for (int j = 0; j < KPW; ++j)
         {
             const int r = warp + 8 * j;
             if (r >= nk) // warp-uniform
                 break;
-            const float4 lo = *reinterpret_cast<const float4*>(tv + r * D + lane * 8);
-            const float4 hi = *reinterpret_cast<const float4*>(tv + r * D + lane * 8 + 4);
-            const float vv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+            const ulonglong2 lo = *reinterpret_cast<const ulonglong2*>(tv + r * D + lane * 8);
+            const ulonglong2 hi = *reinterpret_cast<const ulonglong2*>(tv + r * D + lane * 8 + 4);
+            const uint64_t vv[4] = {lo.x, lo.y, hi.x, hi.y};
 #pragma unroll
             for (int h = 0; h < QH; ++h)
             {
                 const float ph = __shfl_sync(0xFFFFFFFFu, p[j], lane_of_head<QH>(h));
+                const uint64_t p2 = pack2(ph, ph);
 #pragma unroll
-                for (int d = 0; d < 8; ++d)
-                    acc[h][d] = fmaf(ph, vv[d], acc[h][d]);
+                for (int i = 0; i < 4; ++i)
+                    acc[h][i] = fma2(p2, vv[i], acc[h][i]);
             }
         }
-        sync(); // the tile is read before the next one lands
+        sync(); // the tile is read before the stage two tiles on lands in its buffer
     }
 
     // ---- fold the 8 warps
 #pragma unroll
     for (int h = 0; h < QH; ++h)
 #pragma unroll
-        for (int d = 0; d < 8; d += 4)
-            *reinterpret_cast<float4*>(wacc + (warp * QH + h) * D + lane * 8 + d) =
-                make_float4(acc[h][d], acc[h][d + 1], acc[h][d + 2], acc[h][d + 3]);
+        for (int i = 0; i < 4; i += 2)
+        {
+            const float2 x = unpack2(acc[h][i]), y = unpack2(acc[h][i + 1]);
+            *reinterpret_cast<float4*>(wacc + (warp * QH + h) * D + lane * 8 + 2 * i) = make_float4(x.x, x.y, y.x, y.y);
+        }
     if (lane == lane_of_head<QH>(my_head))
     {
         wm[warp * QH + my_head] = m;
@@ -322,24 +400,40 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
     }
 }
 
-// The standalone decode/prefill attention: grid (nsplit, kv_heads, rows), 256
-// threads, all query heads of a kv head in one CTA, 32-key tiles.
+// The standalone decode/prefill attention: grid (nsplit, heads / QH, rows), 256
+// threads, QH query heads of one kv head in a CTA (all of them, or half of
+// eight: 98 registers a thread instead of 168 lets two CTAs share an SM, and
+// the second CTA's K/V reads hit L2), 16-key tiles, two in flight.
 template <int QH>
 __global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
 {
     extern __shared__ __align__(16) float sm[];
-    pdl_wait();
-    const unsigned position = *(volatile const unsigned*) a.state;
-    pdl_trigger();
-    mqa_block<QH, 32>(a, position, blockIdx.z, blockIdx.y * QH, blockIdx.y, blockIdx.x, sm, [] { __syncthreads(); });
+    const bool paged = a.page_table != nullptr;
+    unsigned position = 0;
+    if (!paged)
+    {
+        pdl_wait();
+        position = *(volatile const unsigned*) a.state;
+        pdl_trigger();
+    }
+    const int head0 = blockIdx.y * QH; // QH divides the heads of one kv head
+    mqa_block<QH, kAttnFastTile>(a, position, blockIdx.z, head0, head0 / (a.heads / a.kv_heads), blockIdx.x, sm,
+                                 [] { __syncthreads(); },
+                                 [paged] {
+                                     if (paged)
+                                     {
+                                         pdl_wait();
+                                         pdl_trigger();
+                                     }
+                                 });
 }
 
 
-// Shared memory of mqa_fast<QH>: the K/V tile, or the warp fold after it.
-template <int QH, int TILE = 32>
+// Shared memory of mqa_fast<QH>: the two K/V tiles, or the warp fold after them.
+template <int QH, int TILE = kAttnFastTile>
 constexpr size_t mqa_fast_smem()
 {
-    constexpr size_t tiles = 2 * TILE * 256;
+    constexpr size_t tiles = 4 * TILE * 256;
     constexpr size_t fold = 8 * QH * 256;
     return ((tiles > fold ? tiles : fold) + 16 * QH) * sizeof(float);
 }

@@ -48,6 +48,7 @@ constexpr int kStages = 3; // shared-memory ring depth of the streaming products
 constexpr int kBatchSplits = 8;       // most attention splits per sequence of a batched step
 constexpr int kBatchArgmaxParts = 64; // argmax candidates per sequence of a batched step
 constexpr int kPageRows = HF_PAGE_ROWS; // positions per KV page of a batched sequence
+static_assert((kPageRows & (kPageRows - 1)) == 0, "the attention kernels index pages by shifts");
 // The whole-loop decode can compute attention in every CTA up to this many
 // keys (no grid barrier between attention and o_proj) instead of in split
 // CTAs. Off: measured slower at every context from 20 to 76 keys (730-771
@@ -412,6 +413,7 @@ struct hf_ctx
     unsigned long long* down_acc = nullptr; // [2][width] the whole-loop kernel's fixed-point down sums
     unsigned* act_ready = nullptr;          // [intermediate / 32] its activation blocks' publish counts
     int balance_ffn = 1;                    // HF_FFN_BALANCE=0 keeps each CTA's down on its own blocks
+    int batch_splits = kBatchSplits;        // most attention splits of a batched step (HF_BATCH_SPLITS)
     uint8_t* tc_pool = nullptr;     // tensor-core weight blocks of every Q8 weight
     __half* tc_x = nullptr;         // a product input's fp16 pieces
     float* tc_xunscale = nullptr;   // their per-row powers of two
@@ -933,8 +935,13 @@ struct hf_ctx
         int keys = 1; // the longest context of this step
         for (int q = 0; q < sequences; ++q)
             keys = std::max(keys, seq_len[q] + 1);
+        // Splits of a sequence's context: while the attention CTAs (sequences x
+        // head groups x splits, two resident an SM) still fit one wave.
+        // Measured at 64 sequences of ~520 keys: a step took 2.87 ms with 2
+        // splits, 2.98 with 4 and 3.08 with 8.
+        const int groups = shape.heads / std::min(4, shape.heads / shape.kv_heads);
         int splits = 1;
-        while (splits < kBatchSplits && splits * 64 < keys)
+        while (splits < batch_splits && splits * 64 < keys && sequences * groups * 2 * splits <= 2 * sms)
             splits *= 2;
         int rc = HF_OK;
         if (batch_graph_off)
@@ -1031,7 +1038,8 @@ struct hf_ctx
             at.nsplit = splits;
             at.state = state;
             at.err = err_word();
-            e = launch_attention(s.heads / s.kv_heads, dim3(splits, s.kv_heads, S), stream, at);
+            const int group = std::min(4, s.heads / s.kv_heads); // query heads a CTA serves
+            e = launch_attention(group, dim3(splits, s.heads / group, S), stream, at);
             if (e == cudaSuccess && splits > 1)
                 e = launch(true, mqa_merge, dim3((query_width() + 255) / 256, S), dim3(256), 0, stream, at);
             if (e != cudaSuccess)
@@ -1267,7 +1275,8 @@ struct hf_ctx
             }
             else if (fast)
             {
-                e = launch_attention(QH, dim3(1, s.kv_heads, rows), stream, at);
+                const int group = std::min(4, QH);
+                e = launch_attention(group, dim3(1, s.heads / group, rows), stream, at);
             }
             else
                 e = launch(true, mqa_generic, dim3(s.heads, rows), dim3(128), (size_t) s.max_positions * sizeof(float),
@@ -1626,6 +1635,8 @@ int create_context(int device, const hf_shape* shape, int sequences, int pages, 
         ctx->batch_graph_off = std::atoi(knob) == 0;
     if (const char* knob = std::getenv("HF_TC"))
         ctx->tc_off = std::atoi(knob) == 0;
+    if (const char* knob = std::getenv("HF_BATCH_SPLITS"))
+        ctx->batch_splits = std::max(1, std::min(kBatchSplits, std::atoi(knob)));
     ctx->max_splits = 128;
     const int QH = s.heads / s.kv_heads;
     ctx->fast = s.width == 2048 && s.heads * s.head_width == 2048 && s.head_width == 256 && QH <= 8

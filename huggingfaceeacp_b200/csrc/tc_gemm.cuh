@@ -79,7 +79,12 @@ constexpr size_t kTcSmem = (size_t) 4 * kTcTileBytes + kTcStageBytes * kTcStages
 constexpr int kTcThreads = 352; // producer, 2 MMA issuers, 8 convert-and-drain warps
 
 // q8_tc_gemm_ts's shared memory: a ring of 8 load stages (x block, raw block).
+// Its TMEM: kTsBuffers converted weight tiles (64 columns each: hi, lo) and
+// kTsAccSets accumulator sets (128 columns each).
 constexpr int kTsStages = 8;
+constexpr int kTsBuffers = 4; // measured: 2 -> 4 buffers took a 71 MB product from 52.2 to 48.1 us
+constexpr int kTsAccSets = 2; // a third set measured no faster
+static_assert(64 * kTsBuffers + 128 * kTsAccSets <= 512, "TMEM holds 512 columns");
 constexpr size_t kTsStageBytes = ((size_t) 2 * 64 * 128 + kTcBlockBytes + 1023) / 1024 * 1024;
 constexpr size_t kTsSmem = kTsStageBytes * kTsStages + 1024;
 constexpr int kTsThreads = 480; // producer, 2 MMA issuers, 8 converters, 4 drain warps
@@ -448,24 +453,23 @@ __device__ __forceinline__ void tc_drain(uint32_t large, uint32_t small_off, flo
     }
 }
 
-// Drains q8_tc_gemm_ts's accumulator set at `d1` (x_hi.w_hi at d1, x_mid.w_hi
-// 64 columns on, x_hi.w_lo 128 on) of one TMEM lane quarter into sum.
+// Drains q8_tc_gemm_ts's accumulator set at `d` (x_hi.w_hi at d, the small
+// products x_mid.w_hi + x_hi.w_lo 64 columns on) of one TMEM lane quarter
+// into sum.
 template <int DN>
-__device__ __forceinline__ void tc_drain3(uint32_t d1, float (&sum)[DN])
+__device__ __forceinline__ void tc_drain2(uint32_t d, float (&sum)[DN])
 {
 #pragma unroll
     for (int j0 = 0; j0 < DN; j0 += 16)
     {
-        uint32_t u[16], v[16], w[16];
-        tc_ld16(d1 + (uint32_t) j0, u);
-        tc_ld16(d1 + 64u + (uint32_t) j0, v);
-        tc_ld16(d1 + 128u + (uint32_t) j0, w);
+        uint32_t u[16], v[16];
+        tc_ld16(d + (uint32_t) j0, u);
+        tc_ld16(d + 64u + (uint32_t) j0, v);
         tc_wait_ld(u);
         tc_wait_ld(v);
-        tc_wait_ld(w);
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj)
-            sum[j0 + jj] += __uint_as_float(u[jj]) + (__uint_as_float(v[jj]) + __uint_as_float(w[jj]));
+            sum[j0 + jj] += __uint_as_float(u[jj]) + __uint_as_float(v[jj]);
     }
 }
 
@@ -566,10 +570,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         for (int b = 0; b < 2; ++b)
         {
-            mbar_init(&converted[b], 256);
+            mbar_init(&converted[b], 8); // one arrival per converter warp
             mbar_init(&a_free[b], 1);
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 256);
+            mbar_init(&acc_empty[b], 8);
         }
         mbar_fence_init();
     }
@@ -640,7 +644,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_after();
             tc_drain<DN>(tmem + lanes + (uint32_t) (2 * b * NX + col0), NX, sum);
             tc_fence_before();
-            mbar_arrive(&acc_empty[b]);
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&acc_empty[b]);
             return true;
         };
         auto convert = [&](int i) -> bool {
@@ -668,7 +674,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 *reinterpret_cast<uint4*>(arow + kTcTileBytes + (((2 * ch + 1) ^ sw) << 4)) = l1;
             }
             fence_proxy_async();
-            mbar_arrive(&converted[b]);
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&converted[b]);
             return true;
         };
         bool ok = true;
@@ -709,21 +717,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // TMEM as the MMA's A operand, and two MMAs per k-step instead of three: the
 // x block's hi and mid pieces are consecutive in shared memory, so one N = 128
 // MMA multiplies w_hi by both (the tensor core's full rate; N = 64 runs at
-// two thirds of it), and one N = 64 MMA multiplies w_lo by x_hi. TMEM columns:
-// tile buffer b (chunk i: b = i % 2) hi at 64 b, lo at 64 b + 32 (a 64-column
-// chunk of fp16 is 32 columns); accumulator set c (chunk i: c = i % 2) at
-// 128 + 192 c: [x_hi.w_hi | x_mid.w_hi] (128 columns), then x_hi.w_lo (64).
-// Each of the three terms has its own accumulator.
+// two thirds of it) into [x_hi.w_hi | x_mid.w_hi], and one N = 64 MMA adds
+// w_lo times x_hi into the second half, so the small products share one
+// accumulator apart from the large one. TMEM columns: tile buffer b (chunk i:
+// b = i % kTsBuffers) hi at 64 b, lo at 64 b + 32 (a 64-column chunk of fp16
+// is 32 columns); accumulator set c (chunk i: c = i % kTsAccSets) at
+// 64 kTsBuffers + 128 c. Four tile buffers let the converters run three
+// chunks ahead of the tensor core.
 template <Epi E>
 __global__ void __launch_bounds__(kTsThreads, 1)
     q8_tc_gemm_ts(const GemvArgs a, const uint8_t* wblocks, const __half* xpieces, const float* xunscale, float* ws,
                   size_t split_stride, int chunks_per_split)
 {
-    constexpr int NX = 64, LS = kTsStages;
+    constexpr int NX = 64, LS = kTsStages, NB = kTsBuffers, NA = kTsAccSets;
     constexpr size_t LSB = kTsStageBytes;
     constexpr int XB = 2 * NX * 128;
+    constexpr uint32_t kAcc0 = 64u * NB; // first accumulator column
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t full[LS], empty[LS], converted[2], a_free[2], acc_full[2], acc_empty[2];
+    __shared__ uint64_t full[LS], empty[LS], converted[NB], a_free[NB], acc_full[NA], acc_empty[NA];
     __shared__ uint32_t tmem_slot;
     __shared__ int tile_ok;
 
@@ -743,15 +754,15 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b)
+        for (int b = 0; b < NB; ++b)
         {
-            mbar_init(&converted[b], 256);
+            mbar_init(&converted[b], 8); // one arrival per converter warp
             mbar_init(&a_free[b], 1);
         }
-        for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < NA; ++c)
         {
             mbar_init(&acc_full[c], 1);
-            mbar_init(&acc_empty[c], 128);
+            mbar_init(&acc_empty[c], 4); // one arrival per drain warp
         }
         mbar_fence_init();
     }
@@ -781,9 +792,9 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             const uint32_t idesc = tc_idesc(NX), idesc128 = tc_idesc(2 * NX);
             for (int i = warp == 1 ? 0 : 1; i < count; i += 2)
             {
-                const int s = i % LS, b = i & 1, c = i & 1;
-                if (!mbar_wait(&converted[b], (i >> 1) & 1u)
-                    || (i >= 2 && !mbar_wait(&acc_empty[c], ((i >> 1) - 1) & 1u)))
+                const int s = i % LS, b = i % NB, c = i % NA;
+                if (!mbar_wait(&converted[b], (i / NB) & 1u)
+                    || (i >= NA && !mbar_wait(&acc_empty[c], ((i / NA) - 1) & 1u)))
                 {
                     flag_error(err, kErrWaitTimeout);
                     break;
@@ -791,13 +802,14 @@ __global__ void __launch_bounds__(kTsThreads, 1)
                 tc_fence_after();
                 const uint32_t xbase = smem_addr(loads + s * LSB);
                 const uint32_t a_hi = tmem + (uint32_t) (64 * b);
-                const uint32_t d1 = tmem + 128u + (uint32_t) (192 * c), d2 = d1 + 128u;
+                const uint32_t d = tmem + kAcc0 + (uint32_t) (128 * c);
                 const uint64_t b_both = tc_desc(xbase); // x_hi rows 0-63, x_mid rows 64-127
 #pragma unroll
                 for (int k = 0; k < kTcChunk / 16; ++k)
                 {
-                    tc_mma_ts(d1, a_hi + 8u * k, b_both + 2 * k, idesc128, k > 0 ? 1u : 0u);
-                    tc_mma_ts(d2, a_hi + 32u + 8u * k, b_both + 2 * k, idesc, k > 0 ? 1u : 0u);
+                    // [x_hi.w_hi | x_mid.w_hi], then x_hi.w_lo into the second half (in issue order)
+                    tc_mma_ts(d, a_hi + 8u * k, b_both + 2 * k, idesc128, k > 0 ? 1u : 0u);
+                    tc_mma_ts(d + 64u, a_hi + 32u + 8u * k, b_both + 2 * k, idesc, 1u);
                 }
                 tc_commit(&empty[s]);
                 tc_commit(&a_free[b]);
@@ -816,9 +828,9 @@ __global__ void __launch_bounds__(kTsThreads, 1)
         const uint32_t lanes = (uint32_t) (quarter * 32) << 16;
         for (int i = 0; i < count; ++i)
         {
-            const int s = i % LS, b = i & 1;
+            const int s = i % LS, b = i % NB;
             const bool ready =
-                mbar_wait(&full[s], (i / LS) & 1u) && (i < 2 || mbar_wait(&a_free[b], ((i >> 1) - 1) & 1u));
+                mbar_wait(&full[s], (i / LS) & 1u) && (i < NB || mbar_wait(&a_free[b], ((i / NB) - 1) & 1u));
             if (!__all_sync(0xFFFFFFFFu, ready)) // warp-uniform: the TMEM stores are warp-collective
             {
                 flag_error(err, kErrWaitTimeout);
@@ -841,7 +853,9 @@ __global__ void __launch_bounds__(kTsThreads, 1)
             tc_st16(col + 32u, lo);
             tc_wait_st();
             tc_fence_before();
-            mbar_arrive(&converted[b]);
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&converted[b]);
         }
         __syncwarp();
     }
@@ -857,16 +871,18 @@ __global__ void __launch_bounds__(kTsThreads, 1)
         bool ok = true;
         for (int i = 0; i < count; ++i)
         {
-            const int c = i & 1;
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[c], (i >> 1) & 1u)))
+            const int c = i % NA;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[c], (i / NA) & 1u)))
             {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            tc_drain3<NX>(tmem + lanes + 128u + (uint32_t) (192 * c), sum);
+            tc_drain2<NX>(tmem + lanes + kAcc0 + (uint32_t) (128 * c), sum);
             tc_fence_before();
-            mbar_arrive(&acc_empty[c]);
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&acc_empty[c]);
         }
         if (!ok)
         {
