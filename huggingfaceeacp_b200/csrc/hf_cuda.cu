@@ -189,7 +189,9 @@ void configure_kernels()
     cudaFuncSetAttribute(decode_persistent<kPersistentStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int) persistent_smem<kPersistentStages>());
 #define HF_TC_SMEM(E)                                                                                          \
-    cudaFuncSetAttribute(q8_tc_gemm_ts<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kTsSmem);           \
+    cudaFuncSetAttribute(q8_tc_gemm_ts<E, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kTsSmem);       \
+    cudaFuncSetAttribute(q8_tc_gemm_ts<E, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kTsSmem);       \
+    cudaFuncSetAttribute(q8_tc_gemm_ts<E, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kTsSmem);       \
     cudaFuncSetAttribute(q8_tc_gemm<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kTcSmem);
     HF_TC_SMEM(Epi::QkvRope)
     HF_TC_SMEM(Epi::Residual)
@@ -256,7 +258,8 @@ cudaError_t launch_attention(int QH, dim3 grid, cudaStream_t stream, const AttnA
 // A product of a.M rows of x on the int8 tensor cores over the weight's stage
 // records, in blocks of kRowsBlock rows.
 // How the tensor-core product tiles M rows of x against an [N, K] weight: the
-// x tile width (64 or 128 rows, the MMA's N), and a split of K when the
+// x tile width (the fewest of 16, 32, 64 or 128 rows that hold M: a chunk's x
+// bytes set the batched kernel's pace), and a split of K when the
 // output tiles alone would leave SMs idle: the most splits that still fit in
 // one wave of CTAs (a second, nearly empty wave would double the time), each
 // keeping >= 4 chunks.
@@ -269,7 +272,7 @@ struct TcPlan
 TcPlan tc_plan(int M, int N, int K, int sms)
 {
     TcPlan p;
-    p.nx = M <= 64 ? 64 : 128;
+    p.nx = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
     p.tiles_m = (M + p.nx - 1) / p.nx;
     p.tiles_n = N / kTcRows;
     p.m_pad = (size_t) p.tiles_m * p.nx;
@@ -350,12 +353,26 @@ cudaError_t tc_product_on(const uint8_t* tc, const GemvArgs& a, cudaStream_t str
     const size_t split_stride = p.m_pad * (size_t) a.N;
     const dim3 grid(p.tiles_n, p.tiles_m, p.splits);
     cudaError_t e;
-    if (p.nx == 64)
+    if (p.nx == 16)
+    {
+        e = prep_pieces<16>(a, p.m_pad, stream, tc_x, tc_xunscale);
+        if (e == cudaSuccess)
+            e = launch(true, q8_tc_gemm_ts<E, 16>, grid, dim3(kTsThreads), kTsSmem, stream, a, tc,
+                       (const __half*) tc_x, (const float*) tc_xunscale, tc_ws, split_stride, p.cps);
+    }
+    else if (p.nx == 32)
+    {
+        e = prep_pieces<32>(a, p.m_pad, stream, tc_x, tc_xunscale);
+        if (e == cudaSuccess)
+            e = launch(true, q8_tc_gemm_ts<E, 32>, grid, dim3(kTsThreads), kTsSmem, stream, a, tc,
+                       (const __half*) tc_x, (const float*) tc_xunscale, tc_ws, split_stride, p.cps);
+    }
+    else if (p.nx == 64)
     {
         e = prep_pieces<64>(a, p.m_pad, stream, tc_x, tc_xunscale);
         if (e == cudaSuccess)
-            e = launch(true, q8_tc_gemm_ts<E>, grid, dim3(kTsThreads), kTsSmem, stream, a, tc, (const __half*) tc_x,
-                       (const float*) tc_xunscale, tc_ws, split_stride, p.cps);
+            e = launch(true, q8_tc_gemm_ts<E, 64>, grid, dim3(kTsThreads), kTsSmem, stream, a, tc,
+                       (const __half*) tc_x, (const float*) tc_xunscale, tc_ws, split_stride, p.cps);
     }
     else
     {

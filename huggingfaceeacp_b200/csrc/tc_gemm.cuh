@@ -78,13 +78,23 @@ constexpr size_t kTcStageBytes = ((size_t) 2 * 128 * 128 + kTcBlockBytes + 1023)
 constexpr size_t kTcSmem = (size_t) 4 * kTcTileBytes + kTcStageBytes * kTcStages + 1024; // + alignment slack
 constexpr int kTcThreads = 352; // producer, 2 MMA issuers, 8 convert-and-drain warps
 
-// q8_tc_gemm_ts's shared memory: a ring of 8 load stages (x block, raw block).
-// Its TMEM: kTsBuffers converted weight tiles (64 columns each: hi, lo) and
-// kTsAccSets accumulator sets (128 columns each).
+// q8_tc_gemm_ts's shared memory: a ring of 8 load stages (x block of up to 64
+// rows, raw block). Its TMEM (512 columns): kTsBuffers converted weight tiles
+// (64 columns each: hi, lo) and kTsAccSets accumulator sets (2 NX columns
+// each).
+//
+// Measured on B200 (one CTA, A from TMEM, M = 128, K = 16 an instruction): an
+// MMA that accumulates into the result of the one before it waits about 94
+// cycles for it, whatever N up to 128; one issuing thread issues at most one
+// MMA every ~46 cycles (two threads together one every ~27); the tensor core
+// itself takes ~14 / 16 / 32 / 64 cycles at N = 16 / 32 / 64 / 128. Inside
+// this kernel a chunk's 8 MMAs issue at ~86 cycles each (traced), so two
+// independent chains a chunk (a third accumulator block for x_hi.w_lo) and
+// more sets were tried at NX = 16 and 32: no faster, not kept.
 constexpr int kTsStages = 8;
 constexpr int kTsBuffers = 4; // measured: 2 -> 4 buffers took a 71 MB product from 52.2 to 48.1 us
 constexpr int kTsAccSets = 2; // a third set measured no faster
-static_assert(64 * kTsBuffers + 128 * kTsAccSets <= 512, "TMEM holds 512 columns");
+static_assert(64 * kTsBuffers + 2 * 64 * kTsAccSets <= 512, "TMEM holds 512 columns");
 constexpr size_t kTsStageBytes = ((size_t) 2 * 64 * 128 + kTcBlockBytes + 1023) / 1024 * 1024;
 constexpr size_t kTsSmem = kTsStageBytes * kTsStages + 1024;
 constexpr int kTsThreads = 480; // producer, 2 MMA issuers, 8 converters, 4 drain warps
@@ -454,7 +464,7 @@ __device__ __forceinline__ void tc_drain(uint32_t large, uint32_t small_off, flo
 }
 
 // Drains q8_tc_gemm_ts's accumulator set at `d` (x_hi.w_hi at d, the small
-// products x_mid.w_hi + x_hi.w_lo 64 columns on) of one TMEM lane quarter
+// products x_mid.w_hi + x_hi.w_lo DN columns on) of one TMEM lane quarter
 // into sum.
 template <int DN>
 __device__ __forceinline__ void tc_drain2(uint32_t d, float (&sum)[DN])
@@ -464,7 +474,7 @@ __device__ __forceinline__ void tc_drain2(uint32_t d, float (&sum)[DN])
     {
         uint32_t u[16], v[16];
         tc_ld16(d + (uint32_t) j0, u);
-        tc_ld16(d + 64u + (uint32_t) j0, v);
+        tc_ld16(d + (uint32_t) (DN + j0), v);
         tc_wait_ld(u);
         tc_wait_ld(v);
 #pragma unroll
@@ -713,23 +723,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_trigger();
 }
 
-// The same product for a 64-row x tile, with the converted weight tiles in
-// TMEM as the MMA's A operand, and two MMAs per k-step instead of three: the
-// x block's hi and mid pieces are consecutive in shared memory, so one N = 128
-// MMA multiplies w_hi by both (the tensor core's full rate; N = 64 runs at
-// two thirds of it) into [x_hi.w_hi | x_mid.w_hi], and one N = 64 MMA adds
-// w_lo times x_hi into the second half, so the small products share one
-// accumulator apart from the large one. TMEM columns: tile buffer b (chunk i:
-// b = i % kTsBuffers) hi at 64 b, lo at 64 b + 32 (a 64-column chunk of fp16
-// is 32 columns); accumulator set c (chunk i: c = i % kTsAccSets) at
-// 64 kTsBuffers + 128 c. Four tile buffers let the converters run three
-// chunks ahead of the tensor core.
-template <Epi E>
+// The same product for an x tile of NX = 64, 32 or 16 rows, with the
+// converted weight tiles in TMEM as the MMA's A operand, and two MMAs per
+// k-step instead of three: the x block's hi and mid pieces are consecutive in
+// shared memory, so one N = 2 NX MMA multiplies w_hi by both into
+// [x_hi.w_hi | x_mid.w_hi], and one N = NX MMA adds w_lo times x_hi into the
+// second half, so the small products share one accumulator apart from the
+// large one. TMEM columns: tile buffer b (chunk i: b = i % kTsBuffers) hi at
+// 64 b, lo at 64 b + 32 (a 64-column chunk of fp16 is 32 columns);
+// accumulator set c (chunk i: c = i % kTsAccSets) at 64 kTsBuffers + 2 NX c.
+// Four tile buffers let the converters run three chunks ahead of the tensor
+// core. At NX = 64 a chunk's bulk copies (x block 256 NX bytes, weight block
+// 8.7 KB) set its pace (traced: a CTA's copies land at about 50 GB/s while
+// every SM streams), so fewer rows take a narrower x tile; at NX = 16 the
+// chunk's MMAs do.
+template <Epi E, int NX>
 __global__ void __launch_bounds__(kTsThreads, 1)
     q8_tc_gemm_ts(const GemvArgs a, const uint8_t* wblocks, const __half* xpieces, const float* xunscale, float* ws,
                   size_t split_stride, int chunks_per_split)
 {
-    constexpr int NX = 64, LS = kTsStages, NB = kTsBuffers, NA = kTsAccSets;
+    static_assert(NX == 16 || NX == 32 || NX == 64, "x tiles of 16, 32 or 64 rows");
+    constexpr int LS = kTsStages, NB = kTsBuffers, NA = kTsAccSets;
     constexpr size_t LSB = kTsStageBytes;
     constexpr int XB = 2 * NX * 128;
     constexpr uint32_t kAcc0 = 64u * NB; // first accumulator column
@@ -789,7 +803,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
     {
         if (lane == 0)
         {
-            const uint32_t idesc = tc_idesc(NX), idesc128 = tc_idesc(2 * NX);
+            const uint32_t idesc = tc_idesc(NX), idesc2 = tc_idesc(2 * NX);
             for (int i = warp == 1 ? 0 : 1; i < count; i += 2)
             {
                 const int s = i % LS, b = i % NB, c = i % NA;
@@ -802,14 +816,14 @@ __global__ void __launch_bounds__(kTsThreads, 1)
                 tc_fence_after();
                 const uint32_t xbase = smem_addr(loads + s * LSB);
                 const uint32_t a_hi = tmem + (uint32_t) (64 * b);
-                const uint32_t d = tmem + kAcc0 + (uint32_t) (128 * c);
-                const uint64_t b_both = tc_desc(xbase); // x_hi rows 0-63, x_mid rows 64-127
+                const uint32_t d = tmem + kAcc0 + (uint32_t) (2 * NX * c);
+                const uint64_t b_both = tc_desc(xbase); // x_hi rows 0 .. NX - 1, x_mid rows NX .. 2 NX - 1
 #pragma unroll
                 for (int k = 0; k < kTcChunk / 16; ++k)
                 {
                     // [x_hi.w_hi | x_mid.w_hi], then x_hi.w_lo into the second half (in issue order)
-                    tc_mma_ts(d, a_hi + 8u * k, b_both + 2 * k, idesc128, k > 0 ? 1u : 0u);
-                    tc_mma_ts(d + 64u, a_hi + 32u + 8u * k, b_both + 2 * k, idesc, 1u);
+                    tc_mma_ts(d, a_hi + 8u * k, b_both + 2 * k, idesc2, k > 0 ? 1u : 0u);
+                    tc_mma_ts(d + (uint32_t) NX, a_hi + 32u + 8u * k, b_both + 2 * k, idesc, 1u);
                 }
                 tc_commit(&empty[s]);
                 tc_commit(&a_free[b]);
@@ -878,7 +892,7 @@ __global__ void __launch_bounds__(kTsThreads, 1)
                 break;
             }
             tc_fence_after();
-            tc_drain2<NX>(tmem + lanes + kAcc0 + (uint32_t) (128 * c), sum);
+            tc_drain2<NX>(tmem + lanes + kAcc0 + (uint32_t) (2 * NX * c), sum);
             tc_fence_before();
             __syncwarp();
             if (lane == 0)

@@ -78,7 +78,7 @@ def test_config1_op_sweep_on_the_decoders_kernels(K, N, M):
     assert ob.worst_error(got, expected) <= ob.dot_product_tolerance(K)
 
 
-@pytest.mark.parametrize("M", [5, 8, 9, 40, 64, 130])
+@pytest.mark.parametrize("M", [5, 8, 9, 16, 20, 32, 40, 64, 130])
 @pytest.mark.parametrize("fold", ["bias", "gelu", "residual"])
 def test_prepared_linear_folds_on_every_path(M, fold):
     K, N = 2048, 512

@@ -28,7 +28,7 @@ def test_tensor_core_prefill_blocks_match_reference():
         prompt = native.synthetic_tokens(17, 429, SHAPE.vocab)
         first = 0
         try:
-            for rows in (300, 100, 20, 9):  # x tiles: 3 x 128, 128, 64 (split K), 64
+            for rows in (300, 100, 20, 9):  # x tiles: 3 x 128, 128, 32 (split K), 16
                 block = prompt[first:first + rows]
                 first += rows
                 logits, hidden = ctx.step(block)
