@@ -141,35 +141,40 @@ __device__ __forceinline__ int lane_of_head(int h)
     return lane;
 }
 
-// D = 256, QH query heads in one CTA's group (all reading kv head `kv_head`),
-// one CTA per (split, head group, row). A lane owns channels [8 lane, 8 lane + 8)
-// of every head of the group; K/V tiles of TILE keys are staged in shared
-// memory by the 256 threads at once, two tiles in flight (tile t + 1 lands
-// while tile t is scored); each warp takes TILE / 8 keys of a tile, scores
-// them for all heads, and keeps its own running (max, sum, row) per head; the
-// warps fold at the end. `sync` is the barrier of the 256 threads. The sums
-// run on the f32x2 pipe: the scores of two heads at once (each head's chain
-// over a lane's 8 channels in the same order as scalar FMAs), the rows two
-// channels at once.
-// Shared memory: max(4 TILE, 8 QH) x 256 floats + 16 QH.
+// D = 256, QH query heads (all reading kv head `kv_head`) in one CTA, one CTA
+// per (split, head group, row), GROUPS groups of 8 warps (256 GROUPS threads):
+// group g serves heads g QH / GROUPS .. of the CTA's QH, each group reading the
+// same staged K/V tiles. A lane owns channels [8 lane, 8 lane + 8) of every
+// head of its group; K/V tiles of TILE keys are staged in shared memory by all
+// threads at once, NBUF tiles in flight (tile t + NBUF - 1 lands while tile t
+// is scored); each warp of a group takes TILE / 8 keys of a tile, scores them
+// for its group's heads, and keeps its own running (max, sum, row) per head;
+// the warps fold at the end. `sync` is the barrier of all the CTA's threads.
+// The sums run on the f32x2 pipe: the scores of two heads at once (each
+// head's chain over a lane's 8 channels in the same order as scalar FMAs),
+// the rows two channels at once.
+// Shared memory: max(2 NBUF TILE, 8 QH) x 256 floats + 16 QH.
 //
 // `ready` waits for the kernels before this one (programmatic dependent
 // launch). A paged row's keys below its own position were written by earlier
 // steps (this step writes only key seq_pos[row]), and its position and page
-// table are set before the step, so its first tile is staged before `ready`
-// when that tile stops short of the newest key; the query is read after it.
-template <int QH, int TILE, typename Sync, typename Ready>
+// table are set before the step, so its first tiles are staged before `ready`
+// when they stop short of the newest key; the query is read after it.
+template <int QH, int TILE, int NBUF, int GROUPS, typename Sync, typename Ready>
 __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int head0, int kv_head, int split,
                           float* sm, Sync sync, Ready ready)
 {
     constexpr int D = 256;
+    constexpr int QG = QH / GROUPS;              // heads of a group
     constexpr int KPW = TILE / 8;                // keys of a tile per warp
-    constexpr int HP = QH >= 2 ? QH / 2 : 1;     // f32x2 head pairs (QH = 1: one head, the high half idle)
+    constexpr int HP = QG >= 2 ? QG / 2 : 1;     // f32x2 head pairs (QG = 1: one head, the high half idle)
+    constexpr int THREADS = 256 * GROUPS;
+    static_assert(QG * GROUPS == QH && NBUF >= 2, "whole head groups, at least two tile buffers");
     float* wacc = sm;               // after the loop: [8][QH][D] (reuses the tiles)
-    float* wm = sm + (4 * TILE > 8 * QH ? 4 * TILE : 8 * QH) * D; // [8][QH]
+    float* wm = sm + (2 * NBUF * TILE > 8 * QH ? 2 * NBUF * TILE : 8 * QH) * D; // [8][QH]
     float* wl = wm + 8 * QH;        // [8][QH]
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x, warp = (tid >> 5) & 7, group = tid >> 8, lane = tid & 31;
     const int H = a.heads;
     const int kvw = a.kv_heads * D;
     const int* table = a.page_table ? a.page_table + (size_t) row * a.table_stride : nullptr;
@@ -179,38 +184,45 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
     const int chunk = ((keys + a.nsplit - 1) / a.nsplit + TILE - 1) / TILE * TILE; // whole tiles
     const int k0 = min(keys, split * chunk);
     const int k1 = min(keys, k0 + chunk);
-    const int my_head = head_of_lane<QH>(lane);
+    const int my_head = head_of_lane<QG>(lane);   // within the group
+    const int g0 = group * QG;                    // the group's first head within the CTA's QH
 
     // The tile of keys [t0, t0 + TILE) into buffer `buf`: K then V rows. A
-    // thread keeps one 16-byte column of every fourth row; page sizes are
-    // powers of two.
+    // thread keeps one 16-byte column of every (THREADS / 64)-th row; page
+    // sizes are powers of two.
     const int page_shift = table ? __ffs(a.page_rows) - 1 : 0;
     const int col = (tid & (D / 4 - 1)) * 4;
     const float* k_col = k_cache + (size_t) kv_head * D + col;
     const float* v_col = v_cache + (size_t) kv_head * D + col;
     auto stage = [&](int t0, int buf) {
-        float* bk = sm + buf * 2 * TILE * D + col;
-        float* bv = bk + TILE * D;
-        const int nk = min(TILE, k1 - t0);
-        for (int r = tid / (D / 4); r < nk; r += 256 / (D / 4))
+        if (t0 < k1)
         {
-            const int key = t0 + r;
-            const size_t cache_row =
-                table ? ((size_t) table[key >> page_shift] << page_shift) + (key & (a.page_rows - 1)) : (size_t) key;
-            cp_async16(bk + r * D, k_col + cache_row * kvw);
-            cp_async16(bv + r * D, v_col + cache_row * kvw);
+            float* bk = sm + buf * 2 * TILE * D + col;
+            float* bv = bk + TILE * D;
+            const int nk = min(TILE, k1 - t0);
+            for (int r = tid / (D / 4); r < nk; r += THREADS / (D / 4))
+            {
+                const int key = t0 + r;
+                const size_t cache_row =
+                    table ? ((size_t) table[key >> page_shift] << page_shift) + (key & (a.page_rows - 1)) : (size_t) key;
+                cp_async16(bk + r * D, k_col + cache_row * kvw);
+                cp_async16(bv + r * D, v_col + cache_row * kvw);
+            }
         }
-        cp_async_commit();
+        cp_async_commit(); // an empty group past the range keeps the group count uniform
     };
 
-    const bool early = table && k0 < k1 && k0 + min(TILE, k1 - k0) < keys;
+    // Tiles 0 .. NBUF - 2 go out first; before `ready` as long as the newest
+    // key (written by this step) is past them.
+    const bool early = table && k0 + (NBUF - 1) * TILE < keys;
     if (early)
-        stage(k0, 0);
+        for (int b = 0; b < NBUF - 1; ++b)
+            stage(k0 + b * TILE, b);
     ready();
 
-    // q (scaled) as head pairs: qp[hp][d] = (head 2 hp, head 2 hp + 1) at channel d.
+    // q (scaled) as head pairs: qp[hp][d] = (head 2 hp, head 2 hp + 1) of the group at channel d.
     uint64_t qp[HP][8];
-    const float* qrow = a.q + (size_t) row * H * D + (size_t) head0 * D + lane * 8;
+    const float* qrow = a.q + (size_t) row * H * D + (size_t) (head0 + g0) * D + lane * 8;
 #pragma unroll
     for (int hp = 0; hp < HP; ++hp)
     {
@@ -218,7 +230,7 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
         const float4 a0 = __ldcg(reinterpret_cast<const float4*>(qrow + 2 * hp * D));
         const float4 b0 = __ldcg(reinterpret_cast<const float4*>(qrow + 2 * hp * D + 4));
         q0[0] = a0.x; q0[1] = a0.y; q0[2] = a0.z; q0[3] = a0.w; q0[4] = b0.x; q0[5] = b0.y; q0[6] = b0.z; q0[7] = b0.w;
-        if (QH >= 2)
+        if (QG >= 2)
         {
             const float4 a1 = __ldcg(reinterpret_cast<const float4*>(qrow + (2 * hp + 1) * D));
             const float4 b1 = __ldcg(reinterpret_cast<const float4*>(qrow + (2 * hp + 1) * D + 4));
@@ -230,28 +242,25 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
     }
 
     float m = -INFINITY, l = 0.f; // of head my_head, replicated across its lanes
-    uint64_t acc[QH][4];          // channel pairs (8 lane + 2 i, 8 lane + 2 i + 1)
+    uint64_t acc[QG][4];          // channel pairs (8 lane + 2 i, 8 lane + 2 i + 1)
 #pragma unroll
-    for (int h = 0; h < QH; ++h)
+    for (int h = 0; h < QG; ++h)
 #pragma unroll
         for (int i = 0; i < 4; ++i)
             acc[h][i] = 0; // (0.f, 0.f)
 
-    if (k0 < k1 && !early)
-        stage(k0, 0);
+    if (!early)
+        for (int b = 0; b < NBUF - 1; ++b)
+            stage(k0 + b * TILE, b);
     int buf = 0;
-    for (int t0 = k0; t0 < k1; t0 += TILE, buf ^= 1)
+    for (int t0 = k0; t0 < k1; t0 += TILE, buf = buf + 1 == NBUF ? 0 : buf + 1)
     {
         const int nk = min(TILE, k1 - t0);
-        // The next tile goes to the other buffer, read by the previous
-        // iteration before its closing barrier.
-        if (t0 + TILE < k1)
-        {
-            stage(t0 + TILE, buf ^ 1);
-            cp_async_wait_group<1>();
-        }
-        else
-            cp_async_wait_group<0>();
+        // The tile NBUF - 1 ahead goes to the buffer the previous iteration
+        // read (free since its closing barrier); then tile t0's group is the
+        // oldest of NBUF - 1 still in flight.
+        stage(t0 + (NBUF - 1) * TILE, buf == 0 ? NBUF - 1 : buf - 1);
+        cp_async_wait_group<NBUF - 1>();
         sync();
         const float* tk = sm + buf * 2 * TILE * D;
         const float* tv = tk + TILE * D;
@@ -277,16 +286,16 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
                 for (int hp = 0; hp < HP; ++hp)
                     v[hp] = fma2(qp[hp][d], kd, v[hp]);
             }
-            float part[QH];
+            float part[QG];
 #pragma unroll
             for (int hp = 0; hp < HP; ++hp)
             {
                 const float2 pr = unpack2(v[hp]);
                 part[2 * hp] = pr.x;
-                if (QH >= 2)
-                    part[(2 * hp + 1) % QH] = pr.y;
+                if (QG >= 2)
+                    part[(2 * hp + 1) % QG] = pr.y;
             }
-            const float total = transpose_reduce<QH>(part, lane);
+            const float total = transpose_reduce<QG>(part, lane);
             s[j] = r < nk ? total : -INFINITY;
         }
         float tile_max = s[0];
@@ -317,9 +326,9 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
 
         // ---- every lane needs every head's factors: rescale, then P V
 #pragma unroll
-        for (int h = 0; h < QH; ++h)
+        for (int h = 0; h < QG; ++h)
         {
-            const float c = __shfl_sync(0xFFFFFFFFu, carried, lane_of_head<QH>(h));
+            const float c = __shfl_sync(0xFFFFFFFFu, carried, lane_of_head<QG>(h));
             const uint64_t c2 = pack2(c, c);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -335,37 +344,40 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
             const ulonglong2 hi = *reinterpret_cast<const ulonglong2*>(tv + r * D + lane * 8 + 4);
             const uint64_t vv[4] = {lo.x, lo.y, hi.x, hi.y};
 #pragma unroll
-            for (int h = 0; h < QH; ++h)
+            for (int h = 0; h < QG; ++h)
             {
-                const float ph = __shfl_sync(0xFFFFFFFFu, p[j], lane_of_head<QH>(h));
+                const float ph = __shfl_sync(0xFFFFFFFFu, p[j], lane_of_head<QG>(h));
                 const uint64_t p2 = pack2(ph, ph);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
                     acc[h][i] = fma2(p2, vv[i], acc[h][i]);
             }
         }
-        sync(); // the tile is read before the stage two tiles on lands in its buffer
+        sync(); // the tile is read before a later stage lands in its buffer
     }
+    cp_async_wait_group<0>(); // the empty groups past the range
 
-    // ---- fold the 8 warps
+    // ---- fold the 8 warps of each group
 #pragma unroll
-    for (int h = 0; h < QH; ++h)
+    for (int h = 0; h < QG; ++h)
 #pragma unroll
         for (int i = 0; i < 4; i += 2)
         {
             const float2 x = unpack2(acc[h][i]), y = unpack2(acc[h][i + 1]);
-            *reinterpret_cast<float4*>(wacc + (warp * QH + h) * D + lane * 8 + 2 * i) = make_float4(x.x, x.y, y.x, y.y);
+            *reinterpret_cast<float4*>(wacc + (warp * QH + g0 + h) * D + lane * 8 + 2 * i) =
+                make_float4(x.x, x.y, y.x, y.y);
         }
-    if (lane == lane_of_head<QH>(my_head))
+    if (lane == lane_of_head<QG>(my_head))
     {
-        wm[warp * QH + my_head] = m;
-        wl[warp * QH + my_head] = l;
+        wm[warp * QH + g0 + my_head] = m;
+        wl[warp * QH + g0 + my_head] = l;
     }
     sync();
 
-    const int d = tid; // 256 threads, one channel each
-    for (int h = 0; h < QH; ++h)
+    const int d = tid & (D - 1); // one channel a thread, a group's heads a thread group
+    for (int hg = 0; hg < QG; ++hg)
     {
+        const int h = g0 + hg;
         float mx = -INFINITY;
 #pragma unroll
         for (int w = 0; w < 8; ++w)
@@ -417,7 +429,7 @@ __global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
         pdl_trigger();
     }
     const int head0 = blockIdx.y * QH; // QH divides the heads of one kv head
-    mqa_block<QH, kAttnFastTile>(a, position, blockIdx.z, head0, head0 / (a.heads / a.kv_heads), blockIdx.x, sm,
+    mqa_block<QH, kAttnFastTile, 2, 1>(a, position, blockIdx.z, head0, head0 / (a.heads / a.kv_heads), blockIdx.x, sm,
                                  [] { __syncthreads(); },
                                  [paged] {
                                      if (paged)
@@ -429,13 +441,46 @@ __global__ void __launch_bounds__(256) mqa_fast(const AttnArgs a)
 }
 
 
-// Shared memory of mqa_fast<QH>: the two K/V tiles, or the warp fold after them.
-template <int QH, int TILE = kAttnFastTile>
-constexpr size_t mqa_fast_smem()
+// Shared memory of mqa_block<QH, TILE, NBUF>: the K/V tiles in flight, or the
+// warp fold after them.
+template <int QH, int TILE, int NBUF>
+constexpr size_t mqa_block_smem()
 {
-    constexpr size_t tiles = 4 * TILE * 256;
+    constexpr size_t tiles = 2 * NBUF * TILE * 256;
     constexpr size_t fold = 8 * QH * 256;
     return ((tiles > fold ? tiles : fold) + 16 * QH) * sizeof(float);
+}
+
+template <int QH>
+constexpr size_t mqa_fast_smem()
+{
+    return mqa_block_smem<QH, kAttnFastTile, 2>();
+}
+
+// Batched decode steps (paged rows, every row its own sequence): grid
+// (nsplit, kv_heads, rows), one CTA of two 8-warp groups per (split, kv head,
+// sequence), each group QH / 2 of the kv head's query heads, so a K/V tile is
+// read once for all of them (against twice with two CTAs of QH / 2 heads);
+// 32-key tiles, three in flight; one CTA an SM (512 threads, 192 KiB).
+constexpr int kAttnPagesTile = 32;
+constexpr int kAttnPagesBuffers = 3;
+
+template <int QH>
+__global__ void __launch_bounds__(512, 1) mqa_pages(const AttnArgs a)
+{
+    extern __shared__ __align__(16) float sm[];
+    mqa_block<QH, kAttnPagesTile, kAttnPagesBuffers, 2>(a, 0u, blockIdx.z, blockIdx.y * QH, blockIdx.y, blockIdx.x, sm,
+                                                         [] { __syncthreads(); },
+                                                         [] {
+                                                             pdl_wait();
+                                                             pdl_trigger();
+                                                         });
+}
+
+template <int QH>
+constexpr size_t mqa_pages_smem()
+{
+    return mqa_block_smem<QH, kAttnPagesTile, kAttnPagesBuffers>();
 }
 
 // Folds the splits of mqa_fast: out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M).

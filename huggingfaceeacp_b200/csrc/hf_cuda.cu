@@ -181,6 +181,8 @@ void configure_kernels()
     cudaFuncSetAttribute(mqa_fast<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<4>());
     cudaFuncSetAttribute(mqa_fast<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<2>());
     cudaFuncSetAttribute(mqa_fast<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_fast_smem<1>());
+    cudaFuncSetAttribute(mqa_pages<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_pages_smem<8>());
+    cudaFuncSetAttribute(mqa_pages<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_pages_smem<4>());
     cudaFuncSetAttribute(mqa_generic, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(mqa_rows<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
     cudaFuncSetAttribute(mqa_rows<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
@@ -947,18 +949,28 @@ struct hf_ctx
     // attention split count serves every step.
     std::map<int, cudaGraphExec_t> batch_graphs;
 
+    // A batched step's attention: mqa_pages (a CTA of two head groups per kv
+    // head) where a kv head has 8 or 4 query heads, else mqa_fast.
+    bool batch_pages_kernel() const
+    {
+        const int QH = shape.heads / shape.kv_heads;
+        return fast && (QH == 8 || QH == 4);
+    }
+
     int enqueue_batch_step()
     {
         int keys = 1; // the longest context of this step
         for (int q = 0; q < sequences; ++q)
             keys = std::max(keys, seq_len[q] + 1);
         // Splits of a sequence's context: while the attention CTAs (sequences x
-        // head groups x splits, two resident an SM) still fit one wave.
-        // Measured at 64 sequences of ~520 keys: a step took 2.87 ms with 2
-        // splits, 2.98 with 4 and 3.08 with 8.
-        const int groups = shape.heads / std::min(4, shape.heads / shape.kv_heads);
+        // CTAs a split x splits) still fit one wave. Measured at 64 sequences
+        // of ~520 keys with two 256-thread CTAs an SM: a step took 2.87 ms
+        // with 2 splits, 2.98 with 4 and 3.08 with 8.
+        const bool pages_kernel = batch_pages_kernel();
+        const int per_split = pages_kernel ? shape.kv_heads : shape.heads / std::min(4, shape.heads / shape.kv_heads);
+        const int per_sm = pages_kernel ? 1 : 2;
         int splits = 1;
-        while (splits < batch_splits && splits * 64 < keys && sequences * groups * 2 * splits <= 2 * sms)
+        while (splits < batch_splits && splits * 64 < keys && sequences * per_split * 2 * splits <= per_sm * sms)
             splits *= 2;
         int rc = HF_OK;
         if (batch_graph_off)
@@ -1055,8 +1067,19 @@ struct hf_ctx
             at.nsplit = splits;
             at.state = state;
             at.err = err_word();
-            const int group = std::min(4, s.heads / s.kv_heads); // query heads a CTA serves
-            e = launch_attention(group, dim3(splits, s.heads / group, S), stream, at);
+            if (batch_pages_kernel())
+            {
+                const int QH = s.heads / s.kv_heads;
+                e = QH == 8 ? launch(true, mqa_pages<8>, dim3(splits, s.kv_heads, S), dim3(512), mqa_pages_smem<8>(),
+                                     stream, at)
+                            : launch(true, mqa_pages<4>, dim3(splits, s.kv_heads, S), dim3(512), mqa_pages_smem<4>(),
+                                     stream, at);
+            }
+            else
+            {
+                const int group = std::min(4, s.heads / s.kv_heads); // query heads a CTA serves
+                e = launch_attention(group, dim3(splits, s.heads / group, S), stream, at);
+            }
             if (e == cudaSuccess && splits > 1)
                 e = launch(true, mqa_merge, dim3((query_width() + 255) / 256, S), dim3(256), 0, stream, at);
             if (e != cudaSuccess)
