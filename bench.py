@@ -651,6 +651,61 @@ def run_profile_batched(args):
     return 0
 
 
+def run_profile_full(args):
+    """Full-size cases for launch lists and single-kernel ncu captures (not a
+    bench line), each with a profiler range (cudaProfilerStart/Stop) around
+    the launches to capture, so `ncu --profile-from-start off` sees only them:
+      batched-full  Gemma-2B, 64 sequences of 512-token seeded prompts (config
+                    3's), 3 warm-up batched steps, then `--steps` batched steps
+                    in the range (~3.5 GB on the device);
+      prefill-full  Gemma-2B, config 4's first 2048-token seeded prompt as one
+                    2048-row step, once to warm up, then once in the range.
+    Prints the case and the range's device time."""
+    import torch
+
+    from huggingfaceeacp_b200 import native
+
+    shape = native.GEMMA_2B.replace(max_step_rows=PREFILL_STEP_ROWS, max_positions=PREFILL_STEP_ROWS + 8)
+    batched = args.profile_case == "batched-full"
+    sequences = BATCH_SEQUENCES if batched else 1
+    pages = sequences * -(-(BATCH_PROMPT + 3 + args.steps + 1) // native.PAGE_ROWS) if batched else None
+    with native.Context(shape, sequences=sequences, pages=pages) as ctx:
+        ctx.load_synthetic(seed=SEED)
+        stream = torch.cuda.ExternalStream(ctx.stream)
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if batched:
+            prompts = np.stack([native.synthetic_tokens(BATCH_SEED + q, BATCH_PROMPT, shape.vocab)
+                                for q in range(sequences)])
+            ctx.prefill_batch_async(prompts)
+            ctx.decode_batch_async(3)
+            ctx.sync()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+            start.record(stream)
+            ctx.decode_batch_async(args.steps)
+            stop.record(stream)
+            ctx.sync()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+            case = f"Gemma-2B, {sequences} sequences of {BATCH_PROMPT}-token prompts, {args.steps} batched steps"
+        else:
+            prompt = native.synthetic_tokens(PREFILL_SEED, PREFILL_PROMPT, shape.vocab)
+            ctx.prefill_async(prompt)
+            ctx.begin_sequence()
+            ctx.sync()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+            start.record(stream)
+            ctx.prefill_async(prompt)
+            stop.record(stream)
+            ctx.sync()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+            case = f"Gemma-2B, one {PREFILL_PROMPT}-token prompt as one {PREFILL_STEP_ROWS}-row step"
+    print(json.dumps({"profile_case": case, "range_ms": start.elapsed_time(stop)}), flush=True)
+    return 0
+
+
 def run_profile_prefill(args):
     """A small case of prefill for ncu captures (not a bench line): Gemma-2B's
     layer and head shapes with 2 layers and a 64,000-token vocabulary, a
@@ -689,15 +744,19 @@ def main():
     parser.add_argument("--tp-prefill", action="store_true",
                         help="time tensor-parallel prefill of config 2's prompt over --gpus ranks (not the bench line)")
     parser.add_argument("--tp-rows", type=int, default=PREFILL_STEP_ROWS, help="prefill rows per step for --tp-prefill")
-    parser.add_argument("--profile-case", nargs="?", const="decode", choices=["decode", "batched", "prefill"],
-                        help="run a small ncu capture case instead of the bench: the decode kernel (default), "
-                             "a batched step's tensor-core products, or a prompt's prefill")
+    parser.add_argument("--profile-case", nargs="?", const="decode",
+                        choices=["decode", "batched", "prefill", "batched-full", "prefill-full"],
+                        help="run an ncu capture case instead of the bench: the decode kernel (default), a batched "
+                             "step's tensor-core products, a prompt's prefill (small cases), or a full-size batched "
+                             "step or 2048-row prefill step inside a profiler range")
     args = parser.parse_args()
     args.warmup = max(3, args.warmup)
     if args.profile_case == "batched":
         return run_profile_batched(args)
     if args.profile_case == "prefill":
         return run_profile_prefill(args)
+    if args.profile_case in ("batched-full", "prefill-full"):
+        return run_profile_full(args)
     if args.profile_case:
         return run_profile_case(args)
     if args.impl == "reference":
