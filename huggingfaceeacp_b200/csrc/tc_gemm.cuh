@@ -31,31 +31,29 @@
 //    per row undoing its power of two.
 //
 // The kernels (one output tile of 128 weight rows x NX rows of x, one K range):
-//  q8_tc_gemm_ts  NX = 64 (batched decode steps): the converted weight tiles
-//                 live in TMEM and are the MMA's A operand there
-//                 (tcgen05.mma ... [a-tmem]), so shared memory carries only
-//                 the bulk copies and the x operand;
+//  q8_tc_gemm_ts  NX = 16, 32 or 64 (batched decode steps, short prefills):
+//                 the converted weight tiles live in TMEM and are the MMA's A
+//                 operand there (tcgen05.mma ... [a-tmem]), so shared memory
+//                 carries only the bulk copies and the x operand;
 //  q8_tc_gemm     NX = 128 (prefill blocks): the converted tiles are in shared
 //                 memory (TMEM holds the 512 columns of accumulators).
-// Roles in both:
-//  warp 0 lane 0  producer: one bulk copy of the weight block and one of the
-//                 x block per load stage;
-//  MMA issuers   warp 1 (which also allocates TMEM) for even chunks, the last
-//                 warp for odd ones: lane 0 issues the chunk's 12 MMAs (4
-//                 k-steps x 3 products) into an accumulator set and commits
-//                 them to the load stage's, the weight tile's and the set's
-//                 barriers. Two issuers, because a barrier wait by a thread
-//                 with MMAs in flight stalls it for about 400 cycles: each
-//                 waits while the other's MMAs keep the tensor core busy;
-//  warps 2-9      convert chunk i's int8 weights into one of two fp16 hi/lo
-//                 tile buffers while the tensor core runs chunk i - 1;
+// Roles:
+//  producer       warp 0 lane 0: bulk copies of the weight blocks and the x
+//                 blocks (one ring in q8_tc_gemm_ts, a ring of each in
+//                 q8_tc_gemm);
+//  MMA issuers    two warps, lane 0, on alternating chunks: the chunk's MMAs
+//                 into an accumulator set, committed to the barriers of the
+//                 stage, the tile buffer and the set. Two issuers, because a
+//                 barrier wait by a thread with MMAs in flight stalls it for
+//                 about 400 cycles: each waits while the other's MMAs keep
+//                 the tensor core busy;
+//  converters     8 warps: chunk i's int8 weights into an fp16 hi/lo tile
+//                 buffer while the tensor core runs earlier chunks;
 //  drain          read each chunk's finished accumulators from TMEM into fp32
-//                 register sums, then apply the product's epilogue (or, when
-//                 K is split across CTAs, store the partial sums): warps
-//                 10-13 in q8_tc_gemm_ts (one per TMEM lane quarter, all 64
-//                 columns), warps 2-9 themselves in q8_tc_gemm (after
-//                 converting chunk i they drain chunk i - 1, each half of its
-//                 quarter's 128 columns).
+//                 register sums, then the whole CTA applies the product's
+//                 epilogue (or, when K is split across CTAs, stores the
+//                 partial sums): 4 warps in q8_tc_gemm_ts (one per TMEM lane
+//                 quarter, all NX columns), 16 in q8_tc_gemm (32 columns each).
 #pragma once
 
 #include "common.cuh"
@@ -71,12 +69,19 @@ constexpr int kTcBlockBytes = kTcQuantBytes + kTcRows * 2 * 2; // + two fp16 sca
 constexpr int kTcTileBytes = kTcRows * kTcChunk * 2;    // one fp16 A tile: 16 KiB
 
 // q8_tc_gemm's shared memory: two buffers of the converted fp16 weight tiles
-// (hi, lo), then a ring of 3 load stages, each the x block (hi, mid) and the
-// raw weight block, rounded to 1 KiB so every swizzle atom stays 1 KiB-aligned.
-constexpr int kTcStages = 3;
-constexpr size_t kTcStageBytes = ((size_t) 2 * 128 * 128 + kTcBlockBytes + 1023) / 1024 * 1024;
-constexpr size_t kTcSmem = (size_t) 4 * kTcTileBytes + kTcStageBytes * kTcStages + 1024; // + alignment slack
-constexpr int kTcThreads = 352; // producer, 2 MMA issuers, 8 convert-and-drain warps
+// (hi, lo), a ring of 4 x blocks (hi, mid: each held until its MMAs are done)
+// and a ring of 3 raw weight blocks (each held only until it is converted),
+// every stage a whole number of KiB so each swizzle atom stays 1 KiB-aligned.
+// Traced with one ring of 3 stages of both: each chunk's bytes were
+// requested only when the MMAs three chunks back were done and landed ~1 us
+// later, a chunk every ~1.0 us.
+constexpr int kTcXStages = 4;
+constexpr int kTcWStages = 3;
+constexpr size_t kTcXStageBytes = (size_t) 2 * 128 * 128;
+constexpr size_t kTcWStageBytes = ((size_t) kTcBlockBytes + 1023) / 1024 * 1024;
+constexpr size_t kTcSmem = (size_t) 4 * kTcTileBytes + kTcXStageBytes * kTcXStages + kTcWStageBytes * kTcWStages
+                           + 1024; // + alignment slack
+constexpr int kTcThreads = 864; // producer, 2 MMA issuers, 8 converters, 16 drain warps
 
 // q8_tc_gemm_ts's shared memory: a ring of 8 load stages (x block of up to 64
 // rows, raw block). Its TMEM (512 columns): kTsBuffers converted weight tiles
@@ -535,6 +540,38 @@ __device__ __forceinline__ void tc_produce(uint8_t* loads, size_t lsb, const uin
     }
 }
 
+// The producer lane of q8_tc_gemm: the raw weight blocks into their ring
+// (a stage free once the converters have read it) and the x blocks into
+// theirs (a stage free once its MMAs are done), chunk by chunk.
+__device__ __forceinline__ void tc_produce_split(uint8_t* wring, uint8_t* xring, const uint8_t* wblocks,
+                                                 const __half* xpieces, int t, int xt, int chunks, int c0, int count,
+                                                 uint64_t* w_full, uint64_t* w_empty, uint64_t* x_full,
+                                                 uint64_t* x_empty, unsigned* err)
+{
+    constexpr int XB = 2 * 128 * 128, WS = kTcWStages, XS = kTcXStages;
+    const uint64_t policy = evict_first_policy();
+    for (int i = 0; i < count; ++i)
+    {
+        const int ws = i % WS, xs = i % XS;
+        if (i >= WS && !mbar_wait(&w_empty[ws], ((i / WS) - 1) & 1u))
+        {
+            flag_error(err, kErrWaitTimeout);
+            break;
+        }
+        mbar_expect_tx(&w_full[ws], kTcBlockBytes);
+        bulk_load(wring + ws * kTcWStageBytes, wblocks + ((size_t) t * chunks + c0 + i) * kTcBlockBytes, kTcBlockBytes,
+                  &w_full[ws], policy);
+        if (i >= XS && !mbar_wait(&x_empty[xs], ((i / XS) - 1) & 1u))
+        {
+            flag_error(err, kErrWaitTimeout);
+            break;
+        }
+        mbar_expect_tx(&x_full[xs], XB);
+        bulk_load(xring + xs * kTcXStageBytes, xpieces + ((size_t) xt * chunks + c0 + i) * (XB / 2), XB, &x_full[xs],
+                  policy);
+    }
+}
+
 // y = x w^T for the tile (blockIdx.x: 128 weight rows, blockIdx.y: 128 rows of
 // x) over the K range blockIdx.z of `chunks_per_split` 64-column chunks, then
 // tc_epilogue. Converted weight tiles in shared memory.
@@ -547,22 +584,31 @@ __device__ __forceinline__ void tc_produce(uint8_t* loads, size_t lsb, const uin
 // x_hi.w_hi and the small ones (x_hi.w_lo, x_mid.w_hi, 2^-11 of them) have
 // separate accumulators, so the small ones do not truncate at the large
 // one's magnitude: each chunk's large sum sees 4 additions, not 12.
+//
+// Warps: 0 producer (lane 0), 1 and 2 MMA issuers (even, odd chunks; 1 also
+// owns TMEM), 3-10 converters (chunk i into tile buffer i & 1 as soon as
+// its bytes have landed and the buffer's MMAs are done), 11-26 drain (lane
+// quarter warp % 4, 32 of the 128 x columns each). Converting and draining
+// in separate warps lets the conversion of chunk i + 1 run while chunk i - 1
+// drains (traced with both in the same warps: a chunk every ~1.0 us, of
+// which ~0.3 us conversion and ~0.3 us drain after the MMAs).
 template <Epi E>
 __global__ void __launch_bounds__(kTcThreads, 1)
     q8_tc_gemm(const GemvArgs a, const uint8_t* wblocks, const __half* xpieces, const float* xunscale, float* ws,
                size_t split_stride, int chunks_per_split)
 {
-    constexpr int NX = 128, LS = kTcStages;
-    constexpr size_t LSB = kTcStageBytes;
+    constexpr int NX = 128, WS = kTcWStages, XS = kTcXStages;
     constexpr int XB = 2 * NX * 128; // bytes of one x block (hi + mid)
-    constexpr int DN = NX / 2;       // accumulator columns one drain thread keeps
+    constexpr int DN = 32;           // accumulator columns one drain thread keeps
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t full[LS], empty[LS], converted[2], a_free[2], acc_full[2], acc_empty[2];
+    __shared__ uint64_t w_full[WS], w_empty[WS], x_full[XS], x_empty[XS], converted[2], a_free[2], acc_full[2],
+        acc_empty[2];
     __shared__ uint32_t tmem_slot;
     __shared__ int tile_ok;
 
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
-    uint8_t* loads = smem + 4 * kTcTileBytes;
+    uint8_t* loads = smem + 4 * kTcTileBytes;              // the x ring; the tile's sums after the loop
+    uint8_t* wring = loads + kTcXStageBytes * XS;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t = blockIdx.x, xt = blockIdx.y;
     const int chunks = a.K / kTcChunk;
@@ -573,17 +619,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (tid == 0)
     {
         tile_ok = 1;
-        for (int s = 0; s < LS; ++s)
+        for (int s = 0; s < WS; ++s)
         {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&w_full[s], 1);
+            mbar_init(&w_empty[s], 8); // one arrival per converter warp
+        }
+        for (int s = 0; s < XS; ++s)
+        {
+            mbar_init(&x_full[s], 1);
+            mbar_init(&x_empty[s], 1);
         }
         for (int b = 0; b < 2; ++b)
         {
             mbar_init(&converted[b], 8); // one arrival per converter warp
             mbar_init(&a_free[b], 1);
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 8);
+            mbar_init(&acc_empty[b], 16); // one arrival per drain warp
         }
         mbar_fence_init();
     }
@@ -603,18 +654,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == 0)
     {
         if (lane == 0)
-            tc_produce<NX, LS>(loads, LSB, wblocks, xpieces, t, xt, chunks, c0, count, full, empty, err);
+            tc_produce_split(wring, loads, wblocks, xpieces, t, xt, chunks, c0, count, w_full, w_empty, x_full,
+                             x_empty, err);
         __syncwarp();
     }
-    else if (warp == 1 || warp == 10) // even chunks, odd chunks
+    else if (warp <= 2) // even chunks, odd chunks
     {
         if (lane == 0)
         {
             const uint32_t idesc = tc_idesc(NX);
             for (int i = warp == 1 ? 0 : 1; i < count; i += 2)
             {
-                const int s = i % LS, b = i & 1;
-                if (!mbar_wait(&converted[b], (i >> 1) & 1u)
+                const int xs = i % XS, b = i & 1;
+                if (!mbar_wait(&converted[b], (i >> 1) & 1u) || !mbar_wait(&x_full[xs], (i / XS) & 1u)
                     || (i >= 2 && !mbar_wait(&acc_empty[b], ((i >> 1) - 1) & 1u)))
                 {
                     flag_error(err, kErrWaitTimeout);
@@ -622,50 +674,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t abase = smem_addr(smem + b * 2 * kTcTileBytes);
-                const uint32_t xbase = smem_addr(loads + s * LSB);
+                const uint32_t xbase = smem_addr(loads + xs * kTcXStageBytes);
                 const uint32_t large = tmem + (uint32_t) (2 * b * NX);
                 tc_chunk_mmas<false>(large, large + NX, tc_desc(abase), tc_desc(abase + kTcTileBytes), 0, 0,
                                      tc_desc(xbase), tc_desc(xbase + XB / 2), idesc);
-                tc_commit(&empty[s]);
+                tc_commit(&x_empty[xs]);
                 tc_commit(&a_free[b]);
                 tc_commit(&acc_full[b]);
             }
         }
         __syncwarp();
     }
-    else
+    else if (warp <= 10)
     {
-        // ---- warps 2-9: convert chunk i into tile buffer i & 1, then drain
-        // chunk i - 1. TMEM lane block (warp % 4) * 32 is weight rows
-        // t * 128 + that block; warps 2-5 keep x columns [0, 64), 6-9 [64, 128).
-        const int ct = tid - 64; // 0 .. 255
-        const int quarter = warp & 3;
-        const int col0 = ((warp - 2) >> 2) * DN;
-        const uint32_t lanes = (uint32_t) (quarter * 32) << 16;
-        float sum[DN];
-#pragma unroll
-        for (int j = 0; j < DN; ++j)
-            sum[j] = 0.f;
-        auto drain = [&](int i) -> bool {
-            const int b = i & 1;
-            // warp-uniform: the TMEM loads are warp-collective
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[b], (i >> 1) & 1u)))
-                return false;
-            tc_fence_after();
-            tc_drain<DN>(tmem + lanes + (uint32_t) (2 * b * NX + col0), NX, sum);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0)
-                mbar_arrive(&acc_empty[b]);
-            return true;
-        };
-        auto convert = [&](int i) -> bool {
-            const int s = i % LS, b = i & 1;
+        // ---- converters: chunk i's int8 weights -> tile buffer i & 1 (fp16
+        // hi, lo), two 16-column groups of a row a thread
+        const int ct = tid - 96; // 0 .. 255
+        for (int i = 0; i < count; ++i)
+        {
+            const int ws = i % WS, b = i & 1;
             const bool ready =
-                mbar_wait(&full[s], (i / LS) & 1u) && (i < 2 || mbar_wait(&a_free[b], ((i >> 1) - 1) & 1u));
+                mbar_wait(&w_full[ws], (i / WS) & 1u) && (i < 2 || mbar_wait(&a_free[b], ((i >> 1) - 1) & 1u));
             if (!__all_sync(0xFFFFFFFFu, ready))
-                return false;
-            const uint8_t* raw = loads + s * LSB + XB;
+            {
+                flag_error(err, kErrWaitTimeout);
+                tile_ok = 0;
+                break;
+            }
+            const uint8_t* raw = wring + ws * kTcWStageBytes;
             uint8_t* atile = smem + b * 2 * kTcTileBytes;
 #pragma unroll
             for (int q = 0; q < 2; ++q)
@@ -686,14 +722,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             fence_proxy_async();
             __syncwarp();
             if (lane == 0)
+            {
                 mbar_arrive(&converted[b]);
-            return true;
-        };
+                mbar_arrive(&w_empty[ws]); // this warp's reads of the raw block are done
+            }
+        }
+    }
+    else
+    {
+        // ---- drain warps 11-26: TMEM lane quarter warp % 4 is weight rows
+        // t * 128 + that quarter; x columns 32 cb .. 32 cb + 31
+        const int quarter = warp & 3;
+        const int col0 = ((warp - 11) >> 2) * DN;
+        const uint32_t lanes = (uint32_t) (quarter * 32) << 16;
+        float sum[DN];
+#pragma unroll
+        for (int j = 0; j < DN; ++j)
+            sum[j] = 0.f;
         bool ok = true;
-        for (int i = 0; i < count && ok; ++i)
-            ok = convert(i) && (i == 0 || drain(i - 1));
-        if (ok && count > 0)
-            ok = drain(count - 1);
+        for (int i = 0; i < count; ++i)
+        {
+            const int b = i & 1;
+            // warp-uniform: the TMEM loads are warp-collective
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(&acc_full[b], (i >> 1) & 1u)))
+            {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            tc_drain<DN>(tmem + lanes + (uint32_t) (2 * b * NX + col0), NX, sum);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0)
+                mbar_arrive(&acc_empty[b]);
+        }
         if (!ok)
         {
             flag_error(err, kErrWaitTimeout);
