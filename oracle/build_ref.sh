@@ -1,10 +1,12 @@
 #!/bin/sh
 # TEST INFRASTRUCTURE ONLY. Compiles, unchanged and in place under the
 # reference tree, the reference's own Kernels/Int8Blocks.cpp,
-# Sampling/Sampler.cpp and Tests/Decoder/ReferenceDecoder.h (its scalar
+# Sampling/Sampler.cpp, Tokenizer/{Tokenizer,ByteFallback,Metaspace,
+# SpecialTokens}.cpp and Tests/Decoder/ReferenceDecoder.h (its scalar
 # double-precision forward pass) against the small shims in oracle/ref_shim
-# (eacp's fp16 helpers, ea_data_structures' Span/Vector, and a stand-in for
-# Tests/Decoder/Common.h), into oracle/_ref/libhf_ref.so. Nothing from the
+# (eacp's fp16 helpers, ea_data_structures' Span/Vector/Array, Miro's JSON
+# reader and UTF-8 decoder, and a stand-in for Tests/Decoder/Common.h), into
+# oracle/_ref/libhf_ref.so. Nothing from the
 # reference is copied into this repository; the output directory is
 # git-ignored.
 #
@@ -30,11 +32,16 @@ flags="-std=c++20 -O2 -fPIC"
 g++ $flags -I"$here/ref_shim" -I"$lib" -c "$lib/HuggingFaceEACP/Kernels/Int8Blocks.cpp" -o "$obj/int8_blocks.o"
 g++ $flags -I"$here/ref_shim" -I"$lib" -c "$lib/HuggingFaceEACP/Sampling/Sampler.cpp" -o "$obj/sampler.o"
 g++ $flags -I"$here/ref_shim" -I"$lib" -c "$here/ref_bridge.cpp" -o "$obj/ref_bridge.o"
+for part in Tokenizer ByteFallback Metaspace SpecialTokens; do
+    g++ $flags -I"$here/ref_shim" -I"$lib" -c "$lib/HuggingFaceEACP/Tokenizer/$part.cpp" -o "$obj/tokenizer_$part.o"
+done
+g++ $flags -I"$here/ref_shim" -I"$lib" -c "$here/ref_tokenizer_bridge.cpp" -o "$obj/ref_tokenizer_bridge.o"
 links="$out/links/Decoder"
 mkdir -p "$links"
 ln -sf "$ref/Tests/Decoder/ReferenceDecoder.h" "$links/ReferenceDecoder.h"
 ln -sf "$here/ref_shim/decoder/Common.h" "$links/Common.h"
 g++ $flags -I"$here/ref_shim" -I"$out/links" -c "$here/ref_decoder_bridge.cpp" -o "$obj/ref_decoder_bridge.o"
-g++ -shared -o "$out/libhf_ref.so" "$obj/int8_blocks.o" "$obj/sampler.o" "$obj/ref_bridge.o" "$obj/ref_decoder_bridge.o"
+g++ -shared -o "$out/libhf_ref.so" "$obj/int8_blocks.o" "$obj/sampler.o" "$obj/ref_bridge.o" "$obj/ref_decoder_bridge.o" \
+    "$obj"/tokenizer_*.o "$obj/ref_tokenizer_bridge.o"
 rm -f "$obj"/*.o "$links/ReferenceDecoder.h" "$links/Common.h"
 echo "built $out/libhf_ref.so"

@@ -1,8 +1,10 @@
 // TEST INFRASTRUCTURE ONLY. Minimal stand-ins for the ea_data_structures
-// containers the reference's Int8Blocks.cpp and Sampler.cpp name (EA::Span,
-// EA::Vector), so those files compile unchanged into oracle/_ref.
+// containers the reference's Int8Blocks.cpp, Sampler.cpp and Tokenizer/*.cpp
+// name (EA::Span, EA::Vector, EA::Array), so those files compile unchanged
+// into oracle/_ref.
 #pragma once
 #include <algorithm>
+#include <array>
 #include <cstddef>
 #include <memory>
 #include <vector>
@@ -47,7 +49,7 @@ public:
 };
 
 template <typename T, std::size_t N>
-using Array = T[N];
+using Array = std::array<T, N>;
 
 template <typename T>
 using OwningPointer = std::unique_ptr<T>;

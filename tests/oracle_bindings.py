@@ -96,8 +96,103 @@ def ref() -> ctypes.CDLL:
                                               ctypes.c_ulonglong, ctypes.c_int, _vp]
         lib.ref_reference_decode.argtypes = [_vp, ctypes.c_float, ctypes.c_double, ctypes.c_float, _vp, ctypes.c_int,
                                              _vp, ctypes.c_int, _vp, _vp]
+        lib.ref_tokenizer_from_json.restype = _vp
+        lib.ref_tokenizer_from_json.argtypes = [ctypes.c_char_p, ctypes.c_size_t]
+        lib.ref_tokenizer_free.argtypes = [_vp]
+        lib.ref_tokenizer_vocabulary.argtypes = [_vp]
+        lib.ref_tokenizer_encode.argtypes = [_vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int, _vp, ctypes.c_int]
+        lib.ref_tokenizer_decode.restype = ctypes.c_longlong
+        lib.ref_tokenizer_decode.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_char_p, ctypes.c_longlong]
         _ref = lib
     return _ref
+
+
+class RefTokenizer:
+    """The reference's own Tokenizer (Tokenizer/Tokenizer.h:32-124), compiled
+    unchanged into oracle/_ref: fromJsonText, encode / encodeWithBos, decode,
+    vocabularySize."""
+
+    def __init__(self, json_text: bytes):
+        self.lib = ref()
+        self.handle = self.lib.ref_tokenizer_from_json(json_text, len(json_text))
+        if not self.handle:
+            raise ValueError("the reference tokenizer refused the tokenizer.json")
+
+    def vocabulary(self) -> int:
+        return int(self.lib.ref_tokenizer_vocabulary(self.handle))
+
+    def encode(self, text: str, bos: bool = False) -> list[int]:
+        data = text.encode()
+        out = np.zeros(4 * len(data) + 8, dtype=np.int32)
+        n = self.lib.ref_tokenizer_encode(self.handle, data, len(data), int(bos), p(out), len(out))
+        if n < 0:
+            raise ValueError("the reference tokenizer refused the text")
+        return [int(t) for t in out[:n]]
+
+    def decode(self, tokens) -> bytes:
+        ids = np.ascontiguousarray(tokens, dtype=np.int32)
+        cap = 64 * max(1, len(ids)) + 64
+        buf = ctypes.create_string_buffer(cap)
+        n = self.lib.ref_tokenizer_decode(self.handle, p(ids), len(ids), buf, cap)
+        if n < 0 or n > cap:
+            raise ValueError("the reference tokenizer refused the tokens")
+        return buf.raw[:n]
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self.lib.ref_tokenizer_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
+SPACE_PIECE = "\u2581"  # a space as the vocabulary spells it (Tokenizer/Metaspace.h)
+
+
+def synthetic_tokenizer_json(size: int = 384) -> tuple[str, dict]:
+    """A small SentencePiece-BPE tokenizer.json in the form gemma-2b's file
+    takes (added special tokens, a Replace(" " -> U+2581) normalizer, byte
+    fallback, merges as "left right" strings), built here: pieces for a few
+    words out of single letters, the 256 byte pieces, and unused pieces up to
+    `size` tokens. Returns the JSON text and the vocabulary (piece -> id)."""
+    import json
+
+    vocab = {}
+
+    def add(piece):
+        if piece not in vocab:
+            vocab[piece] = len(vocab)
+        return piece
+
+    for special in ("<pad>", "<eos>", "<bos>", "<unk>"):
+        add(special)
+    for b in range(256):
+        add(f"<0x{b:02X}>")
+    add(SPACE_PIECE)
+    for c in "abcdefghijklmnopqrstuvwxyz":
+        add(c)
+    merges = []
+    for word in ("the", "cat", "sat", "on", "mat", "hat", "and", "dog", "in", "a"):
+        piece = word[0]
+        for c in word[1:]:
+            merges.append(f"{piece} {c}")
+            piece = add(piece + c)
+        merges.append(f"{SPACE_PIECE} {piece}")
+        add(SPACE_PIECE + piece)
+    k = 0
+    while len(vocab) < size:
+        add(f"<unused{k}>")
+        k += 1
+    added = [{"id": vocab[t], "content": t, "single_word": False, "lstrip": False, "rstrip": False,
+              "normalized": False, "special": True} for t in ("<pad>", "<eos>", "<bos>", "<unk>")]
+    doc = {"version": "1.0", "truncation": None, "padding": None, "added_tokens": added,
+           "normalizer": {"type": "Replace", "pattern": {"String": " "}, "content": SPACE_PIECE},
+           "pre_tokenizer": None, "post_processor": None, "decoder": None,
+           "model": {"type": "BPE", "dropout": None, "unk_token": "<unk>", "continuing_subword_prefix": None,
+                     "end_of_word_suffix": None, "fuse_unk": True, "byte_fallback": True, "vocab": vocab,
+                     "merges": merges}}
+    return json.dumps(doc, ensure_ascii=False), vocab
 
 
 def p(a):
