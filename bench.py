@@ -627,6 +627,32 @@ def run_profile_case(args):
     return 0
 
 
+def run_profile_long(args):
+    """A small case of the decode kernel at config 2's context (not a bench
+    line): Gemma-2B's layer and head shapes with 4 layers and a 32,000-token
+    vocabulary, config 2's 8064-token seeded prompt, then two launches of
+    `--steps` decode steps (keys 8065 on); capture the second launch
+    (`-k regex:decode_persistent -s 1 -c 1`). Prints the case's algorithmic
+    bytes per launch (weights + every step's K/V reads)."""
+    from huggingfaceeacp_b200 import native
+
+    shape = native.GEMMA_2B.replace(layers=4, vocab=32000, max_positions=LONG_PROMPT + 128, max_step_rows=2048)
+    with native.Context(shape) as ctx:
+        ctx.load_synthetic(seed=SEED)
+        prompt = native.synthetic_tokens(LONG_SEED, LONG_PROMPT, shape.vocab)
+        ctx.prefill_async(prompt)
+        ctx.decode_async(args.steps)
+        ctx.sync()
+        first = ctx.position
+        ctx.decode_async(args.steps)
+        ctx.sync()
+        launch_bytes = sum(native.decode_bytes(shape, first + i + 1) for i in range(args.steps))
+    print(json.dumps({"profile_case": f"Gemma-2B shapes, 4 layers, vocab 32000, {LONG_PROMPT}-token prompt",
+                      "steps_per_launch": args.steps, "first_keys": first + 1,
+                      "algorithmic_bytes_per_launch": launch_bytes}), flush=True)
+    return 0
+
+
 def run_profile_batched(args):
     """A small case of the batched decode step for ncu captures (not a bench
     line): Gemma-2B's layer and head shapes with 2 layers and a 64,000-token
@@ -745,7 +771,7 @@ def main():
                         help="time tensor-parallel prefill of config 2's prompt over --gpus ranks (not the bench line)")
     parser.add_argument("--tp-rows", type=int, default=PREFILL_STEP_ROWS, help="prefill rows per step for --tp-prefill")
     parser.add_argument("--profile-case", nargs="?", const="decode",
-                        choices=["decode", "batched", "prefill", "batched-full", "prefill-full"],
+                        choices=["decode", "decode-long", "batched", "prefill", "batched-full", "prefill-full"],
                         help="run an ncu capture case instead of the bench: the decode kernel (default), a batched "
                              "step's tensor-core products, a prompt's prefill (small cases), or a full-size batched "
                              "step or 2048-row prefill step inside a profiler range")
@@ -757,6 +783,8 @@ def main():
         return run_profile_prefill(args)
     if args.profile_case in ("batched-full", "prefill-full"):
         return run_profile_full(args)
+    if args.profile_case == "decode-long":
+        return run_profile_long(args)
     if args.profile_case:
         return run_profile_case(args)
     if args.impl == "reference":
