@@ -221,7 +221,7 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
     ready();
 
     // q (scaled) as head pairs: qp[hp][d] = (head 2 hp, head 2 hp + 1) of the group at channel d.
-    uint64_t qp[HP][8];
+    float2 qp[HP][8];
     const float* qrow = a.q + (size_t) row * H * D + (size_t) (head0 + g0) * D + lane * 8;
 #pragma unroll
     for (int hp = 0; hp < HP; ++hp)
@@ -238,16 +238,16 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
         }
 #pragma unroll
         for (int d = 0; d < 8; ++d)
-            qp[hp][d] = pack2(q0[d] * a.scale, q1[d] * a.scale);
+            qp[hp][d] = make_float2(q0[d] * a.scale, q1[d] * a.scale);
     }
 
     float m = -INFINITY, l = 0.f; // of head my_head, replicated across its lanes
-    uint64_t acc[QG][4];          // channel pairs (8 lane + 2 i, 8 lane + 2 i + 1)
+    float2 acc[QG][4];            // channel pairs (8 lane + 2 i, 8 lane + 2 i + 1)
 #pragma unroll
     for (int h = 0; h < QG; ++h)
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-            acc[h][i] = 0; // (0.f, 0.f)
+            acc[h][i] = make_float2(0.f, 0.f);
 
     if (!early)
         for (int b = 0; b < NBUF - 1; ++b)
@@ -274,23 +274,23 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
             const float4 lo = *reinterpret_cast<const float4*>(tk + (r < nk ? r : 0) * D + lane * 8);
             const float4 hi = *reinterpret_cast<const float4*>(tk + (r < nk ? r : 0) * D + lane * 8 + 4);
             const float kk[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-            uint64_t v[HP];
+            float2 v[HP];
 #pragma unroll
             for (int hp = 0; hp < HP; ++hp)
-                v[hp] = 0;
+                v[hp] = make_float2(0.f, 0.f);
 #pragma unroll
             for (int d = 0; d < 8; ++d)
             {
-                const uint64_t kd = pack2(kk[d], kk[d]);
+                const float2 kd = make_float2(kk[d], kk[d]);
 #pragma unroll
                 for (int hp = 0; hp < HP; ++hp)
-                    v[hp] = fma2(qp[hp][d], kd, v[hp]);
+                    v[hp] = __ffma2_rn(qp[hp][d], kd, v[hp]);
             }
             float part[QG];
 #pragma unroll
             for (int hp = 0; hp < HP; ++hp)
             {
-                const float2 pr = unpack2(v[hp]);
+                const float2 pr = v[hp];
                 part[2 * hp] = pr.x;
                 if (QG >= 2)
                     part[(2 * hp + 1) % QG] = pr.y;
@@ -329,10 +329,10 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
         for (int h = 0; h < QG; ++h)
         {
             const float c = __shfl_sync(0xFFFFFFFFu, carried, lane_of_head<QG>(h));
-            const uint64_t c2 = pack2(c, c);
+            const float2 c2 = make_float2(c, c);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-                acc[h][i] = mul2(acc[h][i], c2);
+                acc[h][i] = __fmul2_rn(acc[h][i], c2);
         }
 #pragma unroll
         for (int j = 0; j < KPW; ++j)
@@ -340,17 +340,18 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
             const int r = warp + 8 * j;
             if (r >= nk) // warp-uniform
                 break;
-            const ulonglong2 lo = *reinterpret_cast<const ulonglong2*>(tv + r * D + lane * 8);
-            const ulonglong2 hi = *reinterpret_cast<const ulonglong2*>(tv + r * D + lane * 8 + 4);
-            const uint64_t vv[4] = {lo.x, lo.y, hi.x, hi.y};
+            const float4 lo = *reinterpret_cast<const float4*>(tv + r * D + lane * 8);
+            const float4 hi = *reinterpret_cast<const float4*>(tv + r * D + lane * 8 + 4);
+            const float2 vv[4] = {make_float2(lo.x, lo.y), make_float2(lo.z, lo.w), make_float2(hi.x, hi.y),
+                                  make_float2(hi.z, hi.w)};
 #pragma unroll
             for (int h = 0; h < QG; ++h)
             {
                 const float ph = __shfl_sync(0xFFFFFFFFu, p[j], lane_of_head<QG>(h));
-                const uint64_t p2 = pack2(ph, ph);
+                const float2 p2 = make_float2(ph, ph);
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
-                    acc[h][i] = fma2(p2, vv[i], acc[h][i]);
+                    acc[h][i] = __ffma2_rn(p2, vv[i], acc[h][i]);
             }
         }
         sync(); // the tile is read before a later stage lands in its buffer
@@ -363,7 +364,7 @@ __device__ void mqa_block(const AttnArgs& a, unsigned position, int row, int hea
 #pragma unroll
         for (int i = 0; i < 4; i += 2)
         {
-            const float2 x = unpack2(acc[h][i]), y = unpack2(acc[h][i + 1]);
+            const float2 x = acc[h][i], y = acc[h][i + 1];
             *reinterpret_cast<float4*>(wacc + (warp * QH + g0 + h) * D + lane * 8 + 2 * i) =
                 make_float4(x.x, x.y, y.x, y.y);
         }

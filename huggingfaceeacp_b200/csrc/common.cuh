@@ -130,12 +130,6 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b)
     return d;
 }
 
-__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b)
-{
-    uint64_t d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
 
 // ---- Q8_0 unpacking -----------------------------------------------------------
 // A quantized byte b is the signed value (b ^ 0x80) - 128 (Int8Blocks.cpp:64-67).
