@@ -571,7 +571,9 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
     const int position = (int) *(volatile const unsigned*) a.state;
     pdl_trigger();
 
-    const int row0 = blockIdx.x * R;
+    // The causal triangle makes a block's work grow with its rows: the CTAs
+    // are handed out latest rows first, so the lightest blocks fill the tail.
+    const int row0 = (gridDim.x - 1 - blockIdx.x) * R;
     const int rows_here = min(R, a.rows - row0);
     const int head0 = blockIdx.y * QH;
     const int kvw = a.kv_heads * D;
