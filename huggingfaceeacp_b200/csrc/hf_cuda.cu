@@ -261,10 +261,14 @@ cudaError_t launch_attention(int QH, dim3 grid, cudaStream_t stream, const AttnA
 // records, in blocks of kRowsBlock rows.
 // How the tensor-core product tiles M rows of x against an [N, K] weight: the
 // x tile width (the fewest of 16, 32, 64 or 128 rows that hold M: a chunk's x
-// bytes set the batched kernel's pace), and a split of K when the
-// output tiles alone would leave SMs idle: the most splits that still fit in
-// one wave of CTAs (a second, nearly empty wave would double the time), each
-// keeping >= 4 chunks.
+// bytes set the batched kernel's pace), and a split of K: when the output
+// tiles alone would leave SMs idle, the most splits that still fit in one
+// wave of CTAs (a second, nearly empty wave would double the time), each
+// keeping >= 4 chunks; when they fill one wave or more and K is long (>= 128
+// chunks, so the partial sums stay small beside the work), 2 or 4 splits
+// where that packs the waves enough better to pay for the finish (counted as
+// 12 chunk times): a 2048-row down product's 256 tiles are 2 waves with the
+// second 73% full, and 4 splits make it 7 waves of a quarter of the chunks.
 struct TcPlan
 {
     int nx, tiles_m, tiles_n, splits, cps;
@@ -280,7 +284,17 @@ TcPlan tc_plan(int M, int N, int K, int sms)
     p.m_pad = (size_t) p.tiles_m * p.nx;
     const int chunks = K / kTcChunk;
     const int base = p.tiles_m * p.tiles_n;
-    const int splits = base >= sms ? 1 : std::max(1, std::min(sms / base, chunks / 4));
+    int splits = base >= sms ? 1 : std::max(1, std::min(sms / base, chunks / 4));
+    if (base >= sms && chunks >= 128)
+    {
+        auto cost = [&](int s) {
+            const int cps = (chunks + s - 1) / s;
+            return (long long) ((base * s + sms - 1) / sms) * cps + (s > 1 ? 12 : 0);
+        };
+        for (int s: {2, 4})
+            if (chunks / s >= 16 && cost(s) < cost(splits))
+                splits = s;
+    }
     p.cps = (chunks + splits - 1) / splits;
     p.splits = (chunks + p.cps - 1) / p.cps;
     return p;
