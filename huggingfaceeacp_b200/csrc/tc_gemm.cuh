@@ -255,9 +255,10 @@ __global__ void __launch_bounds__(kTcRows) build_tc_blocks(const uint8_t* quants
 // ---- x pieces (once per product input) --------------------------------------
 // One CTA of 256 threads per row of the padded tile set; thread t holds the
 // row's 8-column groups t, t + 256, ... (K / 2048 of them) in registers, so
-// the row is read once (twice with a norm). With `norm_w`, the row is first
-// RMS-normalised exactly as rms_norm_rows does it (the sum of squares in its
-// strided order, then x * (1 / sqrt(mean(x^2) + eps)) * (1 + w)). Then the
+// the row is read once. With `norm_w`, the row is first RMS-normalised:
+// x * (1 / sqrt(mean(x^2) + eps)) * (1 + w), the sum of squares taken over
+// the registers (each thread's groups in order, then the warps' in order;
+// fp32 like rms_norm_rows, whose strided order differs in rounding). Then the
 // row's power of two (max |x| = f 2^e is scaled to f 2^14), and the hi and mid
 // fp16 pieces of every group in their swizzled places. Rows >= M are zeros.
 template <int NX, int K>
@@ -271,22 +272,6 @@ __global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float
     const int m = blockIdx.x, tid = threadIdx.x;
     const bool live = m < M;
     const float* row = x + (size_t) m * K;
-    float scale = 1.f;
-    if (norm_w && live)
-    {
-        float s = 0.f;
-        for (int c = tid; c < K; c += 256)
-            s += row[c] * row[c];
-        s = warp_sum(s);
-        if ((tid & 31) == 0)
-            red[tid >> 5] = s;
-        __syncthreads();
-        float total = 0.f;
-        for (int w = 0; w < 8; ++w)
-            total += red[w];
-        scale = 1.f / sqrtf(total / (float) K + eps);
-        __syncthreads();
-    }
     float v[G][8];
 #pragma unroll
     for (int q = 0; q < G; ++q)
@@ -305,6 +290,25 @@ __global__ void __launch_bounds__(256) prep_x_pieces(const float* x, const float
             for (int i = 0; i < 8; ++i)
                 v[q][i] = 0.f;
         }
+    }
+    float scale = 1.f;
+    if (norm_w && live)
+    {
+        float sq = 0.f; // groups past K hold zeros
+#pragma unroll
+        for (int q = 0; q < G; ++q)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                sq = fmaf(v[q][i], v[q][i], sq);
+        sq = warp_sum(sq);
+        if ((tid & 31) == 0)
+            red[tid >> 5] = sq;
+        __syncthreads();
+        float total = 0.f;
+        for (int w = 0; w < 8; ++w)
+            total += red[w];
+        scale = 1.f / sqrtf(total / (float) K + eps);
+        __syncthreads();
     }
     float mx = 0.f;
 #pragma unroll
