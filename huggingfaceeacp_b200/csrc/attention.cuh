@@ -516,8 +516,8 @@ __global__ void __launch_bounds__(256) mqa_merge(const AttnArgs a)
 // mqa_fast gives every row its own CTA, so every row re-reads the whole
 // context from L2 and its scores and values are dot products folded across
 // the warp. mqa_rows gives a CTA kRowsPerCta consecutive rows x the 8 query
-// heads of a kv head: 32 queries share every 32-key K/V tile (double-buffered
-// with cp.async), and both products are register-blocked on fp32 FMAs.
+// heads of a kv head: 32 queries share every 32-key K/V tile (staged with
+// cp.async), and both products are register-blocked on fp32 FMAs.
 // Warp w owns the queries 4w .. 4w + 3: row w / 2, heads 4 (w % 2) .. + 3, so
 // a warp's causal limit is uniform.
 //  scores   lane (kb, c), kb = lane >> 2, c = lane & 3: keys 4 kb .. 4 kb + 3 of
@@ -545,9 +545,13 @@ constexpr int kRowsKFloats = kRowsTile * kRowsKStride;
 constexpr int kRowsVFloats = kRowsTile * 256;
 constexpr int kRowsBufFloats = kRowsKFloats + kRowsVFloats;
 
+// K/V tiles a CTA holds: one, so two CTAs (128 registers, 101 KiB each) share
+// an SM and one's tile loads while the other computes (measured: 43.7 -> 41.9 ms
+// a 2048-row prefill step against two buffers with one 164-register CTA an SM).
+constexpr int kRowsBuffers = 1;
 constexpr size_t mqa_rows_smem()
 {
-    return ((size_t) kRowsQueries * kRowsKStride + 2 * kRowsBufFloats + 8 * 4 * kRowsTile) * sizeof(float);
+    return ((size_t) kRowsQueries * kRowsKStride + kRowsBuffers * kRowsBufFloats + 8 * 4 * kRowsTile) * sizeof(float);
 }
 
 //
@@ -555,7 +559,7 @@ constexpr size_t mqa_rows_smem()
 // head): the CTA still holds 32 queries, now 32 / QH rows x QH heads; a warp's
 // four queries may then span rows, each with its own causal limit.
 template <int QH>
-__global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
+__global__ void __launch_bounds__(256, kRowsBuffers == 1 ? 2 : 1) mqa_rows(const AttnArgs a)
 {
     constexpr int D = 256, T = kRowsTile, KS = kRowsKStride;
     constexpr int R = kRowsQueries / QH; // rows per CTA
@@ -563,7 +567,7 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
     extern __shared__ __align__(16) float sm[];
     float* sq = sm;                                        // [32][KS] scaled queries
     float* bufs = sq + kRowsQueries * KS;                  // 2 x {K [T][KS], V [T][D]}
-    float* sp = bufs + 2 * kRowsBufFloats;                 // [8 warps][T keys][4 queries] probabilities
+    float* sp = bufs + kRowsBuffers * kRowsBufFloats;      // [8 warps][T keys][4 queries] probabilities
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int H = a.heads;
 
@@ -600,7 +604,7 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
     const int keys = base + rows_here;     // its last row sees keys [0, base + rows_here - 1]
     const int tiles = (keys + T - 1) / T;
     auto request = [&](int t) {
-        float* kb = bufs + (t & 1) * kRowsBufFloats;
+        float* kb = bufs + (t % kRowsBuffers) * kRowsBufFloats;
         float* vb = kb + kRowsKFloats;
         const int t0 = t * T, nk = min(T, keys - t0);
         for (int i = tid; i < nk * (D / 4); i += 256)
@@ -639,18 +643,16 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
             acc[i][c] = 0.f;
     }
 
-    if (tiles > 0)
-        request(0);
-    if (tiles > 1)
-        request(1);
+    for (int t = 0; t < kRowsBuffers && t < tiles; ++t)
+        request(t);
     for (int t = 0; t < tiles; ++t)
     {
-        if (t + 1 < tiles)
+        if (kRowsBuffers == 2 && t + 1 < tiles)
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         else
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         __syncthreads(); // tile t (and, at t = 0, the queries) visible to every warp
-        const float* kt = bufs + (t & 1) * kRowsBufFloats;
+        const float* kt = bufs + (t % kRowsBuffers) * kRowsBufFloats;
         const float* vt = kt + kRowsKFloats;
         const int t0 = t * T, nk = min(T, keys - t0);
         if (active && t0 <= limit)
@@ -768,9 +770,9 @@ __global__ void __launch_bounds__(256, 1) mqa_rows(const AttnArgs a)
             }
             __syncwarp(); // the probabilities are read before the next tile rewrites them
         }
-        __syncthreads(); // every warp is done with buffer t & 1
-        if (t + 2 < tiles)
-            request(t + 2);
+        __syncthreads(); // every warp is done with tile t's buffer
+        if (t + kRowsBuffers < tiles)
+            request(t + kRowsBuffers);
     }
 
     if (active)
