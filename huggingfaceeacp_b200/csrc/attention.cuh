@@ -47,6 +47,9 @@ struct AttnArgs
     int table_stride;
     int page_rows;
     int rows; // mqa_rows: the step's rows
+    // mqa_rows_tc: key tiles per chunk, and a ticket per row block (zero between launches)
+    int chunk_tiles;
+    unsigned* tickets;
 };
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src)

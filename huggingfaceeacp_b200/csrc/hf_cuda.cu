@@ -21,6 +21,7 @@
 #include <dlfcn.h>
 
 #include "attention.cuh"
+#include "attention_tc.cuh"
 #include "gemv.cuh"
 #include "misc.cuh"
 #include "persistent.cuh"
@@ -185,6 +186,7 @@ void configure_kernels()
     cudaFuncSetAttribute(mqa_pages<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_pages_smem<4>());
     cudaFuncSetAttribute(mqa_generic, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(mqa_rows<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
+    cudaFuncSetAttribute(mqa_rows_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_tc_smem());
     cudaFuncSetAttribute(mqa_rows<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
     cudaFuncSetAttribute(mqa_rows<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
     cudaFuncSetAttribute(mqa_rows<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) mqa_rows_smem());
@@ -474,6 +476,10 @@ struct hf_ctx
     unsigned* cand_idx = nullptr;
     float* attn_acc = nullptr;
     float* attn_ml = nullptr;
+    float* rows_acc = nullptr;        // mqa_rows_tc's chunk partials [kv][blocks][4][128][D]
+    float* rows_ml = nullptr;         // ... and their (max, sum)
+    unsigned* rows_tickets = nullptr; // [kv][blocks]
+    bool rows_tc_on = false;          // HF_ROWS_TC=1: long prefill steps' attention on mqa_rows_tc
     double* sample_uniforms = nullptr; // [max_positions + 1] a sampled run's uniforms
     float* sample_mask = nullptr;      // [vocab] hf_cuda_sample's mask row
     uint8_t* staging = nullptr;
@@ -1320,7 +1326,32 @@ struct hf_ctx
             at.nsplit = 1;
             at.state = state;
             at.err = err_word();
-            if (fast && QH == 8 && rows >= kRowsMinRows)
+            if (fast && QH == 8 && rows >= kTcaMinRows && rows_acc && rows_tc_on)
+            {
+                // long prefill steps, both products on the tensor cores (measured slower than
+                // mqa_rows: 830 against 720 us a 2048-row launch), each row block's keys cut into
+                // chunks sized from the whole causal triangle (~2 chunks an SM)
+                const int blocks = (rows + kTcaRows - 1) / kTcaRows;
+                long total = 0;
+                int most = 0;
+                for (int b = 0; b < blocks; ++b)
+                {
+                    const int block_tiles = (position + std::min((b + 1) * kTcaRows, rows) + kTcaTile - 1) / kTcaTile;
+                    total += block_tiles;
+                    most = std::max(most, block_tiles);
+                }
+                int chunk = (int) std::max<long>(kTcaMinChunk, (total + 2L * sms - 1) / (2L * sms));
+                chunk = std::max(chunk, (most + kTcaMaxSplits - 1) / kTcaMaxSplits);
+                at.rows = rows;
+                at.nsplit = (most + chunk - 1) / chunk;
+                at.chunk_tiles = chunk;
+                at.part_acc = rows_acc;
+                at.part_ml = rows_ml;
+                at.tickets = rows_tickets;
+                e = launch(true, mqa_rows_tc, dim3((unsigned) (blocks * at.nsplit), s.kv_heads), dim3(256),
+                           mqa_rows_tc_smem(), stream, at);
+            }
+            else if (fast && QH == 8 && rows >= kRowsMinRows)
             {
                 // many consecutive rows: the K/V tiles shared by a CTA's rows
                 at.rows = rows;
@@ -1689,6 +1720,8 @@ int create_context(int device, const hf_shape* shape, int sequences, int pages, 
         ctx->batch_graph_off = std::atoi(knob) == 0;
     if (const char* knob = std::getenv("HF_TC"))
         ctx->tc_off = std::atoi(knob) == 0;
+    if (const char* knob = std::getenv("HF_ROWS_TC"))
+        ctx->rows_tc_on = std::atoi(knob) != 0;
     if (const char* knob = std::getenv("HF_BATCH_SPLITS"))
         ctx->batch_splits = std::max(1, std::min(kBatchSplits, std::atoi(knob)));
     ctx->max_splits = 128;
@@ -1756,6 +1789,15 @@ int create_context(int device, const hf_shape* shape, int sequences, int pages, 
         || device_alloc(ctx, &ctx->sample_uniforms, P + 1, "sampling uniforms")
         || device_alloc(ctx, &ctx->sample_mask, V, "sampling mask"))
         return bail(HF_E_CUDA);
+    if (ctx->fast && QH == 8 && cap >= (size_t) kTcaMinRows && ctx->rows_tc_on)
+    {
+        const size_t blocks = (size_t) s.kv_heads * ((cap + kTcaRows - 1) / kTcaRows);
+        if (device_alloc(ctx, &ctx->rows_acc, blocks * kTcaMaxSplits * kTcaQueries * s.head_width, "attention chunk partials")
+            || device_alloc(ctx, &ctx->rows_ml, blocks * kTcaMaxSplits * kTcaQueries * 2, "attention chunk partials")
+            || device_alloc(ctx, &ctx->rows_tickets, blocks, "attention chunk tickets"))
+            return bail(HF_E_CUDA);
+        cudaMemset(ctx->rows_tickets, 0, blocks * sizeof(unsigned));
+    }
     ctx->single_slots = ctx->slot_base + (ctx->paged ? (size_t) sequences * (P + 1) : 0);
     cudaMemset(ctx->state, 0, 8 * sizeof(unsigned));
     cudaMemset(ctx->slot_base, 0, (ctx->paged ? sequences + 1 : 1) * (P + 1) * sizeof(unsigned));
@@ -1959,7 +2001,8 @@ void hf_cuda_destroy(hf_ctx* ctx)
     ctx->drop_tensor_parallel();
     void* buffers[] = {ctx->pool, ctx->record_pool, ctx->slice_pool, ctx->down_acc, ctx->act_ready, ctx->tc_pool, ctx->tc_x, ctx->tc_xunscale, ctx->tc_ws, ctx->final_norm, ctx->hidden, ctx->normed, ctx->qbuf, ctx->attended, ctx->act,
                        ctx->logits, ctx->kcache, ctx->vcache, ctx->rope_cos, ctx->rope_sin, ctx->slot_base, ctx->state,
-                       ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->staging, ctx->layer_dev,
+                       ctx->cand_val, ctx->cand_idx, ctx->attn_acc, ctx->attn_ml, ctx->rows_acc, ctx->rows_ml,
+                       ctx->rows_tickets, ctx->staging, ctx->layer_dev,
                        ctx->sample_uniforms, ctx->sample_mask, ctx->kpages, ctx->vpages, ctx->admit_k, ctx->admit_v,
                        ctx->page_table_dev, ctx->seq_pos_dev, ctx->seq_active_dev};
     for (void* b: buffers)

@@ -55,9 +55,14 @@ def test_tensor_core_batched_decode_matches_reference_per_sequence():
 LONG_BLOCK_TOLERANCE = 1e-5
 
 
-def test_tensor_core_prefill_blocks_of_1024_and_2048_rows_match_reference():
+@pytest.mark.parametrize("attention", ["mqa_rows", "mqa_rows_tc"])
+def test_tensor_core_prefill_blocks_of_1024_and_2048_rows_match_reference(attention, monkeypatch):
     """Prefill blocks of up to 2048 rows, the step capacity the bench's prefill runs at (one layer,
-    Gemma widths): 16 x tiles of 128 rows, the logits of the last rows and every hidden row checked."""
+    Gemma widths): 16 x tiles of 128 rows, the logits of the last rows and every hidden row checked.
+    The attention of such blocks runs on CUDA-core FMAs (mqa_rows, the default) or, with
+    HF_ROWS_TC=1, on the tensor cores in split tf32 (mqa_rows_tc), which cuts each late row block's
+    keys into 4 chunks (of 16 key tiles at position 0, of 24 at position 2048) and folds them."""
+    monkeypatch.setenv("HF_ROWS_TC", "1" if attention == "mqa_rows_tc" else "0")
     shape = SHAPE.replace(layers=1, max_positions=3200, max_step_rows=2048)
     with native.Context(shape) as ctx:
         tensors = ctx.load_synthetic(seed=19, keep=True)
